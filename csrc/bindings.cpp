@@ -1,0 +1,66 @@
+// Python bindings of the zeroq_b200 native extension (zeroq_b200._C).
+#include <torch/extension.h>
+
+#include <vector>
+
+// nf4.cu
+void nf4_quantize(at::Tensor x, at::Tensor packed, at::Tensor absmax, int64_t blocksize, int64_t qtype);
+void nf4_dequantize(at::Tensor packed, at::Tensor absmax, at::Tensor out, int64_t n, int64_t blocksize,
+                    int64_t qtype);
+// gemm_sm100.cu
+void gemm_bf16_tn(at::Tensor a, at::Tensor b, at::Tensor c);
+void gemm_bf16_tn_extra(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor a2, at::Tensor b2);
+std::vector<int64_t> gemm_status(int64_t device);
+void nf4_to_bf16(at::Tensor packed, at::Tensor absmax, at::Tensor out, int64_t rows, int64_t cols,
+                 int64_t blocksize, int64_t qtype, bool transpose);
+// elementwise.cu
+void add_rmsnorm_fwd(at::Tensor h, c10::optional<at::Tensor> d, at::Tensor w, at::Tensor hout,
+                     at::Tensor y, at::Tensor rstd, double eps);
+void rmsnorm_bwd(at::Tensor gy, at::Tensor x, at::Tensor w, at::Tensor rstd,
+                 c10::optional<at::Tensor> gh, at::Tensor dx, at::Tensor dw);
+void rope(at::Tensor x, at::Tensor out, double theta, double sign);
+void gelu_fwd(at::Tensor x, at::Tensor y);
+void gelu_bwd(at::Tensor g, at::Tensor x, at::Tensor dx);
+void swiglu_fwd(at::Tensor gate, at::Tensor up, at::Tensor y);
+void swiglu_bwd(at::Tensor g, at::Tensor gate, at::Tensor up, at::Tensor dgate, at::Tensor dup);
+void ce_fwd(at::Tensor logits, at::Tensor targets, at::Tensor loss, at::Tensor lse, at::Tensor count,
+            int64_t vocab, int64_t ignore_index);
+void ce_bwd(at::Tensor logits, at::Tensor targets, at::Tensor lse, at::Tensor scale, int64_t vocab,
+            int64_t ignore_index);
+void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> pbf16,
+                double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
+                double gscale);
+void lion_step(at::Tensor master, at::Tensor grad, at::Tensor mom, double lr, double b1, double b2,
+               double wd, int64_t seed);
+#ifdef ZQ_WITH_ATTENTION
+// attention.cu
+void attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, bool causal,
+              double scale);
+void attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse,
+              at::Tensor dq, at::Tensor dk, at::Tensor dv, bool causal, double scale);
+#endif
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "zeroq_b200 sm_100a kernels";
+  m.def("nf4_quantize", &nf4_quantize);
+  m.def("nf4_dequantize", &nf4_dequantize);
+  m.def("gemm_bf16_tn", &gemm_bf16_tn);
+  m.def("gemm_bf16_tn_extra", &gemm_bf16_tn_extra);
+  m.def("gemm_status", &gemm_status);
+  m.def("nf4_to_bf16", &nf4_to_bf16);
+  m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rope", &rope);
+  m.def("gelu_fwd", &gelu_fwd);
+  m.def("gelu_bwd", &gelu_bwd);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("ce_fwd", &ce_fwd);
+  m.def("ce_bwd", &ce_bwd);
+  m.def("adamw_step", &adamw_step);
+  m.def("lion_step", &lion_step);
+#ifdef ZQ_WITH_ATTENTION
+  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_bwd", &attn_bwd);
+#endif
+}

@@ -1,0 +1,486 @@
+// tcgen05 GEMM for sm_100a:  C[M,N] (bf16) = A[M,K] · B[N,K]^T  (+ A2[M,64] · B2[N,64]^T)
+//
+// Design (one CTA per SM, persistent over output tiles):
+//   warp 0      : TMA producer - one elected thread streams 128x64 A tiles and
+//                 BNx64 B tiles (128-byte swizzle) into a STAGES-deep ring.
+//   warp 1      : MMA issuer - allocates TMEM, one thread issues
+//                 tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16) and
+//                 commits to the ring's "empty" barriers and to the
+//                 accumulator's "full" barrier.
+//   warps 2..5  : epilogue - tcgen05.ld 32x32b.x32 from TMEM, fp32 -> bf16,
+//                 16-byte stores; then release the accumulator buffer.
+// Two accumulator buffers in TMEM (2 x BN fp32 columns) let the epilogue of
+// tile i overlap the MMAs of tile i+1.  Tiles are visited in groups of
+// kGroupM row-blocks so that concurrently running CTAs share A and B tiles in
+// L2.
+//
+// The optional second operand pair (A2, B2) is one extra K=64 slab appended to
+// the K loop; the NF4 linear layer uses it for the LoRA up-projection
+// (A2 = s·X·Aᵀ zero-padded to 64 columns, B2 = lora_B zero-padded).
+//
+// Every mbarrier wait is bounded (see common.cuh); on timeout the kernel
+// records an error in a device status word, stops its loops, and still frees
+// its TMEM before exiting.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace zq {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;          // one 128-byte swizzle atom of bf16
+constexpr int kGroupM = 8;
+constexpr int kGemmThreads = 192;
+
+enum GemmErr { kErrProducer = 101, kErrMma = 102, kErrMmaAcc = 103, kErrEpi = 104 };
+
+struct GemmArgs {
+  int M, N, K;           // main problem; K % 64 == 0
+  int extra_k16;         // number of K=16 MMA steps in the extra slab (0 = none)
+  int tiles_m, tiles_n;
+  __nv_bfloat16* C;
+  int64_t ldc;
+  DeviceStatus* status;
+};
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kBytes = kBarOffset + 256 + 1024;  // barriers + alignment slack
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
+  const int group_size = kGroupM * tiles_n;
+  const int g = tile / group_size;
+  const int first_m = g * kGroupM;
+  const int gm = min(tiles_m - first_m, kGroupM);
+  const int r = tile % group_size;
+  tm = first_m + r % gm;
+  tn = r / gm;
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
+               GemmArgs args) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = args.tiles_m * args.tiles_n;
+  const int k_tiles = args.K / kBK + (args.extra_k16 > 0 ? 1 : 0);
+  const int main_k_tiles = args.K / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 4 * 32);
+    }
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    if (args.extra_k16 > 0) {
+      prefetch_tmap(&tmA2);
+      prefetch_tmap(&tmB2);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      bool ok = true;
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int tm, tn;
+        tile_coords(tile, args.tiles_m, args.tiles_n, tm, tn);
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, args.status, kErrProducer)) { ok = false; break; }
+          uint8_t* sa = smem + stage * L::kStageBytes;
+          uint8_t* sb = sa + L::kABytes;
+          mbar_arrive_expect_tx(&full_bar[stage], L::kStageBytes);
+          if (kt < main_k_tiles) {
+            tma_load_2d(sa, &tmA, &full_bar[stage], kt * kBK, tm * kBM);
+            tma_load_2d(sb, &tmB, &full_bar[stage], kt * kBK, tn * BN);
+          } else {
+            tma_load_2d(sa, &tmA2, &full_bar[stage], 0, tm * kBM);
+            tma_load_2d(sb, &tmB2, &full_bar[stage], 0, tn * BN);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Drain: wait (bounded) until every load issued has landed, so no TMA
+      // write targets this CTA's shared memory after it exits.
+      for (int i = 0; i < STAGES; ++i) {
+        mbar_wait(&empty_bar[stage], phase ^ 1, nullptr, 0);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      bool ok = true;
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[buf], acc_phase ^ 1, args.status, kErrMmaAcc)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * 256);
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!mbar_wait(&full_bar[stage], phase, args.status, kErrMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
+          const uint32_t b_addr = a_addr + L::kABytes;
+          const int nk = kt < main_k_tiles ? kBK / 16 : args.extra_k16;
+          for (int kk = 0; kk < nk; ++kk) {
+            const uint64_t adesc = umma_desc_sw128_kmajor(a_addr + kk * 32);
+            const uint64_t bdesc = umma_desc_sw128_kmajor(b_addr + kk * 32);
+            umma_f16_ss(d_tmem, adesc, bdesc, idesc, (kt > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        umma_commit(&tfull_bar[buf]);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int q = warp & 3;                 // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int it = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++it) {
+      int tm, tn;
+      tile_coords(tile, args.tiles_m, args.tiles_n, tm, tn);
+      const int buf = it & 1;
+      if (!mbar_wait(&tfull_bar[buf], (it >> 1) & 1, args.status, kErrEpi)) { ok = false; break; }
+      tc_fence_after();
+      const int m = tm * kBM + row_in_tile;
+      const int n0 = tn * BN;
+      __nv_bfloat16* crow = args.C + (int64_t)m * args.ldc;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256 + c * 32), r);
+        tmem_ld_wait();
+        const int ncol = n0 + c * 32;
+        if (m < args.M) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const int nc = ncol + v * 8;
+            if (nc + 8 <= args.N) {
+              uint4 o;
+              o.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
+              o.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
+              o.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
+              o.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
+              *reinterpret_cast<uint4*>(crow + nc) = o;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// NF4 -> bf16 operand producers (memory-bound).  `transpose=false` writes
+// W [N,K] as is; `transpose=true` writes Wᵀ [K,N] (for the input-gradient GEMM)
+// through a 64x64 shared-memory tile so both the packed reads and the bf16
+// writes stay coalesced.
+// ----------------------------------------------------------------------------
+__constant__ float c_code_nf4[16] = {
+    -1.0f, -0.6961928009986877f, -0.5250730514526367f, -0.39491748809814453f,
+    -0.28444138169288635f, -0.18477343022823334f, -0.09105003625154495f, 0.0f,
+    0.07958029955625534f, 0.16093020141124725f, 0.24611230194568634f, 0.33791524171829224f,
+    0.44070982933044434f, 0.5626170039176941f, 0.7229568362236023f, 1.0f};
+__constant__ float c_code_fp4[16] = {0.0f, 0.005208333333f, 0.66666667f, 1.0f, 0.33333333f,
+                                     0.5f, 0.16666667f, 0.25f, -0.0f, -0.005208333333f,
+                                     -0.66666667f, -1.0f, -0.33333333f, -0.5f, -0.16666667f,
+                                     -0.25f};
+
+// 64x64 tile per CTA of 256 threads; each thread expands 16 values (8 bytes).
+__global__ void __launch_bounds__(256) nf4_to_bf16_tile_kernel(
+    const uint8_t* __restrict__ packed, const float* __restrict__ absmax,
+    __nv_bfloat16* __restrict__ out, int rows, int cols, int blocksize, int qtype, int transpose) {
+  __shared__ float lut[16];
+  __shared__ __align__(16) __nv_bfloat16 tile[64][64 + 8];
+  if (threadIdx.x < 16) lut[threadIdx.x] = qtype == 0 ? c_code_nf4[threadIdx.x] : c_code_fp4[threadIdx.x];
+  __syncthreads();
+  const int r0 = blockIdx.y * 64, c0 = blockIdx.x * 64;
+  const int tr = threadIdx.x >> 2;         // 0..63 row in tile
+  const int tc = (threadIdx.x & 3) * 16;   // 0,16,32,48
+  const int r = r0 + tr, c = c0 + tc;
+  float v[16];
+  if (r < rows && c + 16 <= cols) {
+    const int64_t e0 = (int64_t)r * cols + c;
+    const uint2 p = *reinterpret_cast<const uint2*>(packed + (e0 >> 1));
+    const float s = absmax[e0 / blocksize];
+    const uint32_t w[2] = {p.x, p.y};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t byte = (w[i >> 2] >> (8 * (i & 3))) & 0xFF;
+      v[2 * i] = lut[byte >> 4] * s;
+      v[2 * i + 1] = lut[byte & 0xF] * s;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      v[i] = 0.0f;
+      const int cc = c + i;
+      if (r < rows && cc < cols) {
+        const int64_t e = (int64_t)r * cols + cc;
+        const uint32_t byte = packed[e >> 1];
+        const uint32_t qv = (e & 1) ? (byte & 0xF) : (byte >> 4);
+        v[i] = lut[qv] * absmax[e / blocksize];
+      }
+    }
+  }
+  if (!transpose) {
+    if (r < rows) {
+      if (c + 16 <= cols) {
+        uint4 o0, o1;
+        o0.x = pack_bf16x2(v[0], v[1]);   o0.y = pack_bf16x2(v[2], v[3]);
+        o0.z = pack_bf16x2(v[4], v[5]);   o0.w = pack_bf16x2(v[6], v[7]);
+        o1.x = pack_bf16x2(v[8], v[9]);   o1.y = pack_bf16x2(v[10], v[11]);
+        o1.z = pack_bf16x2(v[12], v[13]); o1.w = pack_bf16x2(v[14], v[15]);
+        uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)r * cols + c);
+        dst[0] = o0;
+        dst[1] = o1;
+      } else {
+        for (int i = 0; i < 16 && c + i < cols; ++i) out[(int64_t)r * cols + c + i] = __float2bfloat16_rn(v[i]);
+      }
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) tile[tc + i][tr] = __float2bfloat16_rn(v[i]);
+  __syncthreads();
+  // write Wᵀ: out row = source column, 64 contiguous source rows per out row
+  const int oc = c0 + tr;           // out row (source column)
+  const int orow0 = r0 + tc;        // out column start (source row)
+  if (oc < cols) {
+    __nv_bfloat16* dst = out + (int64_t)oc * rows + orow0;
+    if (orow0 + 16 <= rows) {
+      uint4 o0, o1;
+      const uint32_t* s = reinterpret_cast<const uint32_t*>(&tile[tr][tc]);
+      o0 = make_uint4(s[0], s[1], s[2], s[3]);
+      o1 = make_uint4(s[4], s[5], s[6], s[7]);
+      reinterpret_cast<uint4*>(dst)[0] = o0;
+      reinterpret_cast<uint4*>(dst)[1] = o1;
+    } else {
+      for (int i = 0; i < 16 && orow0 + i < rows; ++i) dst[i] = tile[tr][tc + i];
+    }
+  }
+}
+
+}  // namespace zq
+
+using namespace zq;
+
+// ----------------------------------------------------------------------------
+// host side
+// ----------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (e == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  TORCH_CHECK(fn != nullptr, "cuTensorMapEncodeTiled is not available from the driver");
+  return fn;
+}
+
+// 2-D bf16 row-major [rows, cols] tensor map with a box of [box_rows, 64] and 128-B swizzle
+static CUtensorMap make_tmap_bf16(const void* base, int64_t rows, int64_t cols, int64_t row_stride_elems,
+                                  int box_rows) {
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA base must be 16-byte aligned");
+  TORCH_CHECK((row_stride_elems * 2) % 16 == 0, "TMA row pitch must be a multiple of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(row_stride_elems * 2)};
+  cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = get_encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", (int)r);
+  return map;
+}
+
+static DeviceStatus* status_buffer(int device) {
+  static DeviceStatus* bufs[64] = {nullptr};
+  static std::mutex mu;
+  std::lock_guard<std::mutex> g(mu);
+  if (bufs[device] == nullptr) {
+    C10_CUDA_CHECK(cudaMalloc(&bufs[device], sizeof(DeviceStatus)));
+    C10_CUDA_CHECK(cudaMemset(bufs[device], 0, sizeof(DeviceStatus)));
+  }
+  return bufs[device];
+}
+
+// Returns and clears the device error status (code, detail) of the GEMM kernels.
+std::vector<int64_t> gemm_status(int64_t device) {
+  DeviceStatus h{0, 0};
+  DeviceStatus* d = status_buffer((int)device);
+  C10_CUDA_CHECK(cudaMemcpy(&h, d, sizeof(h), cudaMemcpyDeviceToHost));
+  C10_CUDA_CHECK(cudaMemset(d, 0, sizeof(DeviceStatus)));
+  return {h.code, h.detail};
+}
+
+template <int BN, int STAGES>
+static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2,
+                        const CUtensorMap& tb2, GemmArgs args, cudaStream_t stream, int sms) {
+  using L = GemmSmem<BN, STAGES>;
+  static bool configured[64] = {false};
+  int dev;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  if (!configured[dev]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_tn_kernel<BN, STAGES>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+    configured[dev] = true;
+  }
+  const int tiles = args.tiles_m * args.tiles_n;
+  const int grid = std::min(tiles, sms);
+  gemm_tn_kernel<BN, STAGES><<<grid, kGemmThreads, L::kBytes, stream>>>(ta, tb, ta2, tb2, args);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Pick the N tile that minimises wave quantisation over the SMs.
+static int choose_bn(int M, int N, int sms) {
+  const int tm = (M + kBM - 1) / kBM;
+  double best = 1e30;
+  int best_bn = 256;
+  for (int bn : {256, 192, 128}) {
+    const int tn = (N + bn - 1) / bn;
+    const int tiles = tm * tn;
+    const int waves = (tiles + sms - 1) / sms;
+    // cost ~ waves * per-tile time (proportional to bn); small penalty for narrow tiles
+    const double cost = (double)waves * bn * (bn == 128 ? 1.15 : 1.0);
+    if (cost < best - 1e-9) { best = cost; best_bn = bn; }
+  }
+  return best_bn;
+}
+
+static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
+                      const c10::optional<at::Tensor>& a2, const c10::optional<at::Tensor>& b2) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: CUDA tensors");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 &&
+                  c.scalar_type() == at::kBFloat16, "gemm: bf16 operands");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm: 2-D operands");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && c.stride(1) == 1, "gemm: row-major operands");
+  const int64_t M = a.size(0), K = a.size(1), N = b.size(0);
+  TORCH_CHECK(b.size(1) == K, "gemm: K mismatch");
+  TORCH_CHECK(c.size(0) == M && c.size(1) == N, "gemm: C shape");
+  TORCH_CHECK(K % 64 == 0 && K > 0, "gemm: K must be a positive multiple of 64");
+  TORCH_CHECK(N % 8 == 0, "gemm: N must be a multiple of 8");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(c.data_ptr()) & 15) == 0 && (c.stride(0) % 8) == 0,
+              "gemm: C must be 16-byte aligned with a row pitch multiple of 8");
+  TORCH_CHECK(M < (1LL << 31) && N < (1LL << 31), "gemm: dims too large");
+  const at::cuda::CUDAGuard guard(a.device());
+  const int dev = a.get_device();
+  const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  const int bn = choose_bn((int)M, (int)N, sms);
+
+  GemmArgs args;
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.extra_k16 = 0;
+  args.tiles_m = (int)((M + kBM - 1) / kBM);
+  args.tiles_n = (int)((N + bn - 1) / bn);
+  args.C = reinterpret_cast<__nv_bfloat16*>(c.data_ptr<at::BFloat16>());
+  args.ldc = c.stride(0);
+  args.status = status_buffer(dev);
+
+  CUtensorMap ta = make_tmap_bf16(a.data_ptr(), M, K, a.stride(0), kBM);
+  CUtensorMap tb = make_tmap_bf16(b.data_ptr(), N, K, b.stride(0), bn);
+  CUtensorMap ta2 = ta, tb2 = tb;
+  if (a2.has_value() && a2->defined()) {
+    TORCH_CHECK(b2.has_value() && b2->defined(), "gemm: extra slab needs both operands");
+    const at::Tensor& x2 = *a2;
+    const at::Tensor& y2 = *b2;
+    TORCH_CHECK(x2.scalar_type() == at::kBFloat16 && y2.scalar_type() == at::kBFloat16, "extra slab bf16");
+    TORCH_CHECK(x2.size(0) == M && y2.size(0) == N && x2.size(1) == 64 && y2.size(1) == 64 &&
+                    x2.stride(1) == 1 && y2.stride(1) == 1,
+                "extra slab operands must be [M,64] and [N,64] row-major");
+    ta2 = make_tmap_bf16(x2.data_ptr(), M, 64, x2.stride(0), kBM);
+    tb2 = make_tmap_bf16(y2.data_ptr(), N, 64, y2.stride(0), bn);
+    args.extra_k16 = 4;
+  }
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (bn == 256) launch_gemm<256, 4>(ta, tb, ta2, tb2, args, stream, sms);
+  else if (bn == 192) launch_gemm<192, 5>(ta, tb, ta2, tb2, args, stream, sms);
+  else launch_gemm<128, 6>(ta, tb, ta2, tb2, args, stream, sms);
+}
+
+void gemm_bf16_tn(at::Tensor a, at::Tensor b, at::Tensor c) {
+  gemm_impl(a, b, c, c10::nullopt, c10::nullopt);
+}
+
+void gemm_bf16_tn_extra(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor a2, at::Tensor b2) {
+  gemm_impl(a, b, c, a2, b2);
+}
+
+// NF4 weight [rows, cols] -> bf16 [rows, cols] (transpose=false) or [cols, rows].
+void nf4_to_bf16(at::Tensor packed, at::Tensor absmax, at::Tensor out, int64_t rows, int64_t cols,
+                 int64_t blocksize, int64_t qtype, bool transpose) {
+  TORCH_CHECK(packed.is_cuda() && packed.scalar_type() == at::kByte, "nf4_to_bf16: uint8 packed");
+  TORCH_CHECK(absmax.scalar_type() == at::kFloat, "nf4_to_bf16: fp32 absmax");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() == rows * cols,
+              "nf4_to_bf16: out bf16 [rows*cols]");
+  TORCH_CHECK(cols % 16 == 0 && (!transpose || rows % 16 == 0), "nf4_to_bf16: 16-aligned dims");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(packed.data_ptr()) & 7) == 0, "nf4_to_bf16: packed 8-byte aligned");
+  const at::cuda::CUDAGuard guard(out.device());
+  dim3 grid((unsigned)((cols + 63) / 64), (unsigned)((rows + 63) / 64));
+  nf4_to_bf16_tile_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      packed.data_ptr<uint8_t>(), absmax.data_ptr<float>(),
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()), (int)rows, (int)cols,
+      (int)blocksize, (int)qtype, transpose ? 1 : 0);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

@@ -1,0 +1,221 @@
+"""Numerics of each sm_100a kernel against a plain PyTorch fp32 reference of the same op."""
+
+import math
+
+import pytest
+import torch
+
+from zeroq_b200.ops import _ext
+from zeroq_b200.ops.nf4 import (dequantize_4bit_reference, quantize_4bit,
+                                quantize_4bit_reference)
+
+pytestmark = pytest.mark.gpu
+
+
+def _status_ok(dev):
+    code, detail = _ext.ext().gemm_status(dev.index or 0)
+    assert code == 0, f"device status error {code} (detail {detail})"
+
+
+@pytest.mark.parametrize("quant_type", ["nf4", "fp4"])
+@pytest.mark.parametrize("blocksize", [64, 256, 1024])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_quantize_matches_oracle_bit_exact(cuda, quant_type, blocksize, dtype):
+    torch.manual_seed(0)
+    x = (torch.randn(1000003, dtype=torch.float32) * 0.02).to(dtype)
+    x[:blocksize] = 0  # an all-zero block
+    p_ref, a_ref = quantize_4bit_reference(x, blocksize, quant_type)
+    p, st = quantize_4bit(x.to(cuda), blocksize, quant_type)
+    assert torch.equal(p.cpu(), p_ref)
+    assert torch.equal(st.absmax.cpu(), a_ref)
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_dequantize_matches_oracle(cuda, out_dtype):
+    torch.manual_seed(1)
+    x = torch.randn(4096 * 33 + 7) * 0.02
+    p, a = quantize_4bit_reference(x, 64, "nf4")
+    ref = dequantize_4bit_reference(p, a, x.numel(), 64, "nf4", out_dtype)
+    out = torch.empty(x.numel(), dtype=out_dtype, device=cuda)
+    _ext.ext().nf4_dequantize(p.to(cuda), a.to(cuda), out, x.numel(), 64, 0)
+    assert torch.equal(out.cpu(), ref)
+
+
+@pytest.mark.parametrize("shape", [(128, 256, 64), (256, 512, 128), (1000, 768, 320),
+                                   (8192 // 4, 3072, 3072), (333, 200, 64), (4096, 12288, 3072)])
+def test_gemm_bf16_tn(cuda, shape):
+    M, N, K = shape
+    torch.manual_seed(2)
+    a = torch.randn(M, K, device=cuda, dtype=torch.bfloat16)
+    b = torch.randn(N, K, device=cuda, dtype=torch.bfloat16)
+    c = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+    _ext.ext().gemm_bf16_tn(a, b, c)
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    ref = a.float() @ b.float().t()
+    err = (c.float() - ref).abs().max().item()
+    tol = 2e-2 * math.sqrt(K) + 1e-2 * ref.abs().max().item()
+    assert err < tol, (err, tol)
+
+
+def test_gemm_extra_slab(cuda):
+    M, N, K = 640, 448, 192
+    torch.manual_seed(3)
+    a = torch.randn(M, K, device=cuda, dtype=torch.bfloat16)
+    b = torch.randn(N, K, device=cuda, dtype=torch.bfloat16)
+    a2 = torch.zeros(M, 64, device=cuda, dtype=torch.bfloat16)
+    b2 = torch.zeros(N, 64, device=cuda, dtype=torch.bfloat16)
+    a2[:, :16] = torch.randn(M, 16, device=cuda).bfloat16()
+    b2[:, :16] = torch.randn(N, 16, device=cuda).bfloat16()
+    c = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+    _ext.ext().gemm_bf16_tn_extra(a, b, c, a2, b2)
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    ref = a.float() @ b.float().t() + a2.float() @ b2.float().t()
+    assert (c.float() - ref).abs().max().item() < 0.5
+
+
+@pytest.mark.parametrize("transpose", [False, True])
+def test_nf4_to_bf16(cuda, transpose):
+    R, C = 384, 1280
+    w = torch.randn(R, C) * 0.02
+    p, a = quantize_4bit_reference(w, 64, "nf4")
+    ref = dequantize_4bit_reference(p, a, R * C, 64, "nf4", torch.bfloat16).view(R, C)
+    out = torch.empty(R * C, dtype=torch.bfloat16, device=cuda)
+    _ext.ext().nf4_to_bf16(p.to(cuda), a.to(cuda), out, R, C, 64, 0, transpose)
+    got = out.view(C, R).t() if transpose else out.view(R, C)
+    assert torch.equal(got.cpu(), ref)
+
+
+def test_add_rmsnorm_fwd_bwd(cuda):
+    from zeroq_b200.ops.norm import add_rmsnorm
+
+    torch.manual_seed(4)
+    M, D = 300, 3072
+    h = torch.randn(M, D, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    d = torch.randn(M, D, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(D, device=cuda)).requires_grad_(True)
+    hn, y = add_rmsnorm(h, d, w, 1e-6)
+    g_h = torch.randn_like(hn)
+    g_y = torch.randn_like(y)
+    (hn.float() * g_h.float()).sum().add((y.float() * g_y.float()).sum()).backward()
+    hr = h.detach().float().requires_grad_(True)
+    dr = d.detach().float().requires_grad_(True)
+    wr = w.detach().clone().requires_grad_(True)
+    s = (hr + dr).bfloat16().float()
+    yr = s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + 1e-6) * wr
+    ((hr + dr) * g_h.float()).sum().add((yr * g_y.float()).sum()).backward()
+    assert (y.float() - yr).abs().max() < 3e-2
+    assert (h.grad.float() - hr.grad).abs().max() < 5e-2
+    assert (d.grad.float() - dr.grad).abs().max() < 5e-2
+    assert (w.grad - wr.grad).abs().max() / wr.grad.abs().max() < 1e-2
+
+
+def test_rope(cuda):
+    from zeroq_b200.ops.rope import apply_rope, rope_reference
+
+    q = torch.randn(2, 64, 4, 128, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(2, 64, 2, 128, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    qo, ko = apply_rope(q, k, 1e6)
+    assert (qo.float() - rope_reference(q.detach(), 1e6).float()).abs().max() < 2e-2
+    assert (ko.float() - rope_reference(k.detach(), 1e6).float()).abs().max() < 2e-2
+    (qo.float().sum() + ko.float().sum()).backward()
+    qr = q.detach().float().requires_grad_(True)
+    rope_reference(qr, 1e6).sum().backward()
+    assert (q.grad.float() - qr.grad).abs().max() < 3e-2
+
+
+def test_gelu_swiglu(cuda):
+    from zeroq_b200.ops.activations import gelu, swiglu
+
+    x = torch.randn(4096, 1024, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    u = torch.randn(4096, 1024, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    y = gelu(x)
+    xr = x.detach().float().requires_grad_(True)
+    yr = torch.nn.functional.gelu(xr)
+    assert (y.float() - yr).abs().max() < 2e-2
+    y.float().sum().backward()
+    yr.sum().backward()
+    assert (x.grad.float() - xr.grad).abs().max() < 2e-2
+    x.grad = None
+    z = swiglu(x, u)
+    xr2 = x.detach().float().requires_grad_(True)
+    ur2 = u.detach().float().requires_grad_(True)
+    zr = torch.nn.functional.silu(xr2) * ur2
+    assert (z.float() - zr).abs().max() < 5e-2
+    z.float().sum().backward()
+    zr.sum().backward()
+    assert (x.grad.float() - xr2.grad).abs().max() < 5e-2
+    assert (u.grad.float() - ur2.grad).abs().max() < 5e-2
+
+
+def test_cross_entropy(cuda):
+    from zeroq_b200.ops.cross_entropy import cross_entropy
+
+    torch.manual_seed(5)
+    M, V, Vp = 257, 50257, 50304
+    logits = torch.randn(M, Vp, device=cuda, dtype=torch.bfloat16) * 3
+    t = torch.randint(0, V, (M,), device=cuda)
+    t[5] = -100
+    lg = logits.clone().requires_grad_(True)
+    loss = cross_entropy(lg, t, vocab=V)
+    lr = logits[:, :V].float().requires_grad_(True)
+    ref = torch.nn.functional.cross_entropy(lr, t, ignore_index=-100)
+    assert abs(loss.item() - ref.item()) < 1e-3
+    loss.backward()
+    ref.backward()
+    g = lg.grad.float()
+    assert (g[:, :V] - lr.grad).abs().max() < 1e-4
+    assert g[:, V:].abs().max() == 0
+
+
+def test_adamw_lion(cuda):
+    from zeroq_b200.ops.optim import adamw_step, lion_step
+
+    n = 100003
+    p = torch.randn(n, device=cuda)
+    g = torch.randn(n, device=cuda)
+    m = torch.zeros(n, device=cuda)
+    v = torch.zeros(n, device=cuda)
+    pc, gc, mc, vc = p.cpu(), g.cpu(), m.cpu(), v.cpu()
+    for step in (1, 2):
+        adamw_step(p, g, m, v, lr=1e-3, weight_decay=0.1, step=step, grad_scale=0.5)
+        adamw_step(pc, gc, mc, vc, lr=1e-3, weight_decay=0.1, step=step, grad_scale=0.5)
+    assert (p.cpu() - pc).abs().max() < 1e-6
+    mom = torch.zeros(n, device=cuda)
+    mom_c = mom.cpu()
+    w = torch.randn(n, device=cuda)
+    wc = w.cpu()
+    lion_step(w, g, mom, lr=1e-3, wd=0.01, seed=7)
+    lion_step(wc, gc, mom_c, lr=1e-3, wd=0.01, seed=7)
+    assert (w.cpu() - wc).abs().max() < 1e-6
+    # fp16 master: stochastic rounding stays within one fp16 ulp of the fp32 update
+    w16 = torch.randn(n, device=cuda).half()
+    ref = w16.float().cpu()
+    m16 = torch.zeros(n, device=cuda)
+    lion_step(w16, g, m16, lr=1e-3, wd=0.0, seed=3)
+    upd = ref - 1e-3 * torch.sign(0.1 * g.cpu())
+    assert ((w16.float().cpu() - upd).abs() <= upd.abs() * 2e-3 + 1e-4).all()
+
+
+@pytest.mark.parametrize("cfg", [(2, 256, 4, 4, 128), (1, 512, 8, 2, 128), (2, 128, 4, 4, 64),
+                                 (1, 384, 6, 3, 64)])
+@pytest.mark.parametrize("causal", [True, False])
+def test_flash_attention_fwd_bwd(cuda, cfg, causal):
+    from zeroq_b200.ops.attention import attention_reference, flash_attention
+
+    B, S, Hq, Hk, D = cfg
+    torch.manual_seed(6)
+    q = torch.randn(B, S, Hq, D, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(B, S, Hk, D, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn(B, S, Hk, D, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    o = flash_attention(q, k, v, causal=causal)
+    qr, kr, vr = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    orf = attention_reference(qr, kr, vr, causal=causal)
+    assert (o.float() - orf).abs().max().item() < 2e-2
+    go = torch.randn_like(o)
+    o.backward(go)
+    orf.backward(go.float())
+    for a, r in ((q.grad, qr.grad), (k.grad, kr.grad), (v.grad, vr.grad)):
+        err = (a.float() - r).abs().max().item()
+        assert err < 5e-2 * max(1.0, r.abs().max().item()), err

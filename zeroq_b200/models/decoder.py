@@ -1,0 +1,299 @@
+"""Decoder-only language models built on this framework's kernels.
+
+One module family covers every model shape the framework is measured on:
+
+* ``tiny``      - vocab 1024, d 256, 4 layers, 4 heads of 64, SwiGLU 688 (plumbing).
+* ``4.7b``      - d 3072, 40 layers, 24 heads of 128, explicit Q/K/V/O, GELU FFN
+                  12288, vocab 50257 (the compiled-hybrid-lm decoder shape the
+                  reference quotes in ``README.md:33-45``), tied embeddings.
+* ``qwen2.5-7b``  - d 3584, 28 layers, 28 Q / 4 KV heads of 128, SwiGLU 18944,
+                    vocab 152064, RoPE theta 1e6.
+* ``qwen2.5-32b`` - d 5120, 64 layers, 40 Q / 8 KV heads of 128, SwiGLU 27648,
+                    vocab 152064, RoPE theta 1e6.
+
+Every projection is a :class:`zeroq_b200.ops.qlinear.Linear4bit`; it holds a
+frozen full-precision ``weight`` (before quantisation, or while a gather/release
+coordinator has it gathered) or resident NF4 data (4-bit compute).  Weights are
+random N(0, std) and can be generated layer by layer straight into NF4
+(``init_nf4_``), so a 4.7B model never exists in bf16 on the device.
+
+The vocabulary is padded to a multiple of 128 so logits rows are 16-byte
+aligned for the tcgen05 GEMM's TMA store; the padded rows of the embedding are
+zero and the loss ignores the padded columns.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import asdict, dataclass, field, replace
+from typing import Optional, Tuple
+
+import torch
+import torch.nn as nn
+import torch.utils.checkpoint as ckpt
+
+from ..ops.activations import gelu, swiglu
+from ..ops.attention import flash_attention
+from ..ops.cross_entropy import cross_entropy
+from ..ops.gemm import LMHeadFunction
+from ..ops.norm import add_rmsnorm
+from ..ops.qlinear import Linear4bit
+from ..ops.rope import apply_rope
+
+
+@dataclass
+class DecoderConfig:
+    vocab_size: int = 1024
+    d_model: int = 256
+    n_layers: int = 4
+    n_heads: int = 4
+    n_kv_heads: int = 4
+    head_dim: int = 64
+    ffn_dim: int = 688
+    ffn_act: str = "swiglu"  # "swiglu" | "gelu"
+    rope_theta: float = 10000.0
+    norm_eps: float = 1e-6
+    tie_embeddings: bool = True
+    vocab_pad_multiple: int = 128
+    # LoRA (PEFT naming); targets are projection names
+    lora_r: int = 0
+    lora_alpha: float = 32.0
+    lora_targets: Tuple[str, ...] = ("q_proj", "k_proj", "v_proj", "o_proj")
+    # quantisation of the frozen projections
+    blocksize: int = 64
+    quant_type: str = "nf4"
+    # memory
+    activation_checkpointing: bool = False
+    train_norms: bool = True
+    train_embeddings: bool = False
+
+    @property
+    def vocab_padded(self) -> int:
+        m = self.vocab_pad_multiple
+        return (self.vocab_size + m - 1) // m * m
+
+    def num_params(self) -> int:
+        d, L = self.d_model, self.n_layers
+        attn = d * self.n_heads * self.head_dim * 2 + d * self.n_kv_heads * self.head_dim * 2
+        mlp = d * self.ffn_dim * (3 if self.ffn_act == "swiglu" else 2)
+        emb = self.vocab_size * d * (1 if self.tie_embeddings else 2)
+        return L * (attn + mlp + 2 * d) + emb + d
+
+    def to_dict(self) -> dict:
+        return asdict(self)
+
+
+PRESETS = {
+    "tiny": DecoderConfig(),
+    "4.7b": DecoderConfig(vocab_size=50257, d_model=3072, n_layers=40, n_heads=24,
+                          n_kv_heads=24, head_dim=128, ffn_dim=12288, ffn_act="gelu",
+                          rope_theta=10000.0, tie_embeddings=True,
+                          lora_targets=("q_proj", "k_proj", "v_proj", "o_proj",
+                                        "up_proj", "down_proj")),
+    "qwen2.5-7b": DecoderConfig(vocab_size=152064, d_model=3584, n_layers=28, n_heads=28,
+                                n_kv_heads=4, head_dim=128, ffn_dim=18944, ffn_act="swiglu",
+                                rope_theta=1e6, tie_embeddings=False,
+                                lora_targets=("q_proj", "k_proj", "v_proj", "o_proj")),
+    "qwen2.5-32b": DecoderConfig(vocab_size=152064, d_model=5120, n_layers=64, n_heads=40,
+                                 n_kv_heads=8, head_dim=128, ffn_dim=27648, ffn_act="swiglu",
+                                 rope_theta=1e6, tie_embeddings=False,
+                                 activation_checkpointing=True,
+                                 lora_targets=("q_proj", "k_proj", "v_proj", "o_proj",
+                                               "gate_proj", "up_proj", "down_proj")),
+}
+
+
+def get_config(name: str, **overrides) -> DecoderConfig:
+    if name not in PRESETS:
+        raise KeyError(f"unknown model preset {name!r}; choose from {sorted(PRESETS)}")
+    return replace(PRESETS[name], **overrides)
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, d: int, eps: float, device=None, trainable: bool = True):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(d, device=device, dtype=torch.float32),
+                                   requires_grad=trainable)
+
+
+class DecoderLayer(nn.Module):
+    def __init__(self, cfg: DecoderConfig, device=None, dtype=torch.bfloat16):
+        super().__init__()
+        self.cfg = cfg
+        d, hd = cfg.d_model, cfg.head_dim
+
+        def lin(name, i, o):
+            r = cfg.lora_r if name in cfg.lora_targets else 0
+            return Linear4bit(i, o, bias=False, blocksize=cfg.blocksize,
+                              quant_type=cfg.quant_type, lora_r=r, lora_alpha=cfg.lora_alpha,
+                              device=device, dtype=dtype)
+
+        self.attn_norm = RMSNorm(d, cfg.norm_eps, device, cfg.train_norms)
+        self.q_proj = lin("q_proj", d, cfg.n_heads * hd)
+        self.k_proj = lin("k_proj", d, cfg.n_kv_heads * hd)
+        self.v_proj = lin("v_proj", d, cfg.n_kv_heads * hd)
+        self.o_proj = lin("o_proj", cfg.n_heads * hd, d)
+        self.mlp_norm = RMSNorm(d, cfg.norm_eps, device, cfg.train_norms)
+        if cfg.ffn_act == "swiglu":
+            self.gate_proj = lin("gate_proj", d, cfg.ffn_dim)
+        else:
+            self.gate_proj = None
+        self.up_proj = lin("up_proj", d, cfg.ffn_dim)
+        self.down_proj = lin("down_proj", cfg.ffn_dim, d)
+
+    def projections(self):
+        out = [("q_proj", self.q_proj), ("k_proj", self.k_proj), ("v_proj", self.v_proj),
+               ("o_proj", self.o_proj)]
+        if self.gate_proj is not None:
+            out.append(("gate_proj", self.gate_proj))
+        out += [("up_proj", self.up_proj), ("down_proj", self.down_proj)]
+        return out
+
+    def forward(self, h: torch.Tensor, delta: Optional[torch.Tensor]):
+        """``h`` is the residual stream, ``delta`` the previous block's output that
+        still has to be added (fused into this layer's first norm)."""
+        cfg = self.cfg
+        B, S, d = h.shape
+        h, x = add_rmsnorm(h, delta, self.attn_norm.weight, self.attn_norm.eps)
+        q = self.q_proj(x).view(B, S, cfg.n_heads, cfg.head_dim)
+        k = self.k_proj(x).view(B, S, cfg.n_kv_heads, cfg.head_dim)
+        v = self.v_proj(x).view(B, S, cfg.n_kv_heads, cfg.head_dim)
+        q, k = apply_rope(q, k, cfg.rope_theta)
+        o = flash_attention(q, k, v, causal=True)
+        a = self.o_proj(o.view(B, S, cfg.n_heads * cfg.head_dim))
+        h, x = add_rmsnorm(h, a, self.mlp_norm.weight, self.mlp_norm.eps)
+        if self.gate_proj is not None:
+            f = swiglu(self.gate_proj(x), self.up_proj(x))
+        else:
+            f = gelu(self.up_proj(x))
+        return h, self.down_proj(f)
+
+
+class DecoderLM(nn.Module):
+    def __init__(self, cfg: DecoderConfig, device=None, dtype=torch.bfloat16):
+        super().__init__()
+        self.cfg = cfg
+        self.dtype = dtype
+        V = cfg.vocab_padded
+        self.embed_tokens = nn.Embedding(V, cfg.d_model, device=device, dtype=dtype)
+        self.embed_tokens.weight.requires_grad_(cfg.train_embeddings)
+        self.layers = nn.ModuleList([DecoderLayer(cfg, device, dtype) for _ in range(cfg.n_layers)])
+        self.norm = RMSNorm(cfg.d_model, cfg.norm_eps, device, cfg.train_norms)
+        if cfg.tie_embeddings:
+            self.lm_head = None
+        else:
+            self.lm_head = nn.Linear(cfg.d_model, V, bias=False, device=device, dtype=dtype)
+            self.lm_head.weight.requires_grad_(cfg.train_embeddings)
+        self._head_t = None  # cached transpose of the (frozen) head matrix
+
+    # -- weights ---------------------------------------------------------------
+    def head_weight(self) -> torch.Tensor:
+        return self.embed_tokens.weight if self.lm_head is None else self.lm_head.weight
+
+    def _zero_vocab_padding(self):
+        with torch.no_grad():
+            self.embed_tokens.weight[self.cfg.vocab_size:].zero_()
+            if self.lm_head is not None:
+                self.lm_head.weight[self.cfg.vocab_size:].zero_()
+
+    def init_dense_(self, std: float = 0.02, seed: int = 0):
+        """Random N(0, std) full-precision projection weights (before partitioning)."""
+        g = torch.Generator(device=self.embed_tokens.weight.device).manual_seed(seed)
+        with torch.no_grad():
+            self.embed_tokens.weight.normal_(0.0, std, generator=g)
+            if self.lm_head is not None:
+                self.lm_head.weight.normal_(0.0, std, generator=g)
+            for layer in self.layers:
+                for _, m in layer.projections():
+                    w = torch.empty(m.out_features, m.in_features, device=m.weight.device,
+                                    dtype=self.dtype)
+                    w.normal_(0.0, std, generator=g)
+                    m.weight = nn.Parameter(w, requires_grad=False)
+        self._zero_vocab_padding()
+        self._head_t = None
+        return self
+
+    def init_nf4_(self, std: float = 0.02, seed: int = 0):
+        """Random N(0, std) weights generated one projection at a time and
+        quantised straight to NF4 (the bf16 model is never materialised)."""
+        dev = self.embed_tokens.weight.device
+        g = torch.Generator(device=dev).manual_seed(seed)
+        with torch.no_grad():
+            self.embed_tokens.weight.normal_(0.0, std, generator=g)
+            if self.lm_head is not None:
+                self.lm_head.weight.normal_(0.0, std, generator=g)
+            for layer in self.layers:
+                for _, m in layer.projections():
+                    w = torch.empty(m.out_features, m.in_features, device=dev, dtype=self.dtype)
+                    w.normal_(0.0, std, generator=g)
+                    m.quantize_from(w)
+                    del w
+        self._zero_vocab_padding()
+        self._head_t = None
+        return self
+
+    def convert_to_4bit_(self):
+        """Quantise every projection that still holds a dense weight (4-bit compute)."""
+        for layer in self.layers:
+            for _, m in layer.projections():
+                if not m.has_nf4 and m.weight.numel():
+                    m.quantize_from(m.weight.data)
+                    m.weight = nn.Parameter(torch.empty(0, device=m.weight.device,
+                                                        dtype=m.weight.dtype), requires_grad=False)
+        return self
+
+    def refresh_head_cache(self):
+        self._head_t = None
+
+    def _head_transposed(self):
+        W = self.head_weight()
+        if W.requires_grad or not W.is_cuda:
+            return None
+        if self._head_t is None or self._head_t.shape != (W.shape[1], W.shape[0]):
+            self._head_t = W.detach().t().contiguous()
+        return self._head_t
+
+    # -- forward -----------------------------------------------------------------
+    def _layer_call(self, layer, h, delta):
+        if self.cfg.activation_checkpointing and self.training and torch.is_grad_enabled():
+            if delta is None:
+                return ckpt.checkpoint(lambda hh: layer(hh, None), h, use_reentrant=False)
+            return ckpt.checkpoint(layer, h, delta, use_reentrant=False)
+        return layer(h, delta)
+
+    def forward(self, input_ids: torch.Tensor, targets: Optional[torch.Tensor] = None,
+                ignore_index: int = -100):
+        B, S = input_ids.shape
+        h = self.embed_tokens(input_ids)
+        delta = None
+        for layer in self.layers:
+            h, delta = self._layer_call(layer, h, delta)
+        _, x = add_rmsnorm(h, delta, self.norm.weight, self.norm.eps)
+        W = self.head_weight()
+        logits = LMHeadFunction.apply(x, W, self._head_transposed())
+        if targets is None:
+            return logits.view(B, S, -1)[..., : self.cfg.vocab_size]
+        return cross_entropy(logits, targets.reshape(-1), vocab=self.cfg.vocab_size,
+                             ignore_index=ignore_index)
+
+    # -- bookkeeping ---------------------------------------------------------------
+    def trainable_parameters(self):
+        return [p for p in self.parameters() if p.requires_grad]
+
+    def flops_per_token(self, seq_len: int) -> float:
+        """Training FLOPs per token: frozen projections run forward + input-grad
+        (4·params), the head likewise, attention fwd (causal) + bwd (2.5x fwd);
+        LoRA adds 6·r·(in+out) per adapted projection."""
+        c = self.cfg
+        proj = 0
+        lora = 0
+        for name, m in self.layers[0].projections():
+            proj += m.in_features * m.out_features
+            if m.lora_r:
+                lora += m.lora_r * (m.in_features + m.out_features)
+        proj *= c.n_layers
+        lora *= c.n_layers
+        head = c.d_model * c.vocab_padded
+        attn_fwd = 2 * 2 * seq_len * c.n_heads * c.head_dim * c.n_layers * 0.5
+        return 4 * proj + 4 * head + 6 * lora + attn_fwd * 3.5

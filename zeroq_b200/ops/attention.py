@@ -1,0 +1,67 @@
+"""Causal (GQA-capable) flash attention, forward and backward.
+
+Tensors keep the projection layout ``[B, S, H, D]`` (``D = 128``) so no
+transposes surround the kernels.  The forward (``csrc/attention.cu``) streams
+K/V tiles with online softmax and writes ``O`` plus the row log-sum-exp ``L``;
+the backward recomputes probabilities from ``L``, accumulates ``dK``/``dV`` per
+key tile in registers and ``dQ`` in fp32 with atomics, after a small kernel that
+forms ``delta = rowsum(dO * O)``.
+
+CPU tensors use PyTorch's SDPA (the oracle).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from . import _ext
+
+
+def attention_reference(q, k, v, causal: bool = True, scale=None):
+    B, S, Hq, D = q.shape
+    Hk = k.shape[2]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    qt = q.transpose(1, 2).float()
+    kt = k.transpose(1, 2).float()
+    vt = v.transpose(1, 2).float()
+    if Hk != Hq:
+        rep = Hq // Hk
+        kt = kt.repeat_interleave(rep, dim=1)
+        vt = vt.repeat_interleave(rep, dim=1)
+    o = F.scaled_dot_product_attention(qt, kt, vt, is_causal=causal, scale=scale)
+    return o.transpose(1, 2).to(q.dtype)
+
+
+class _FlashAttn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, causal, scale):
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        B, S, Hq, D = q.shape
+        o = torch.empty_like(q)
+        lse = torch.empty(B, Hq, S, dtype=torch.float32, device=q.device)
+        _ext.ext().attn_fwd(q, k, v, o, lse, bool(causal), float(scale))
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.causal, ctx.scale = causal, scale
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse = ctx.saved_tensors
+        do = do.contiguous()
+        dq = torch.empty_like(q)
+        dk = torch.empty_like(k)
+        dv = torch.empty_like(v)
+        _ext.ext().attn_bwd(do, q, k, v, o, lse, dq, dk, dv, bool(ctx.causal), float(ctx.scale))
+        return dq, dk, dv, None, None
+
+
+def flash_attention(q, k, v, causal: bool = True, scale=None):
+    if scale is None:
+        scale = 1.0 / math.sqrt(q.shape[-1])
+    if q.is_cuda and q.dtype == torch.bfloat16:
+        return _FlashAttn.apply(q, k, v, causal, scale)
+    return attention_reference(q, k, v, causal, scale)

@@ -1,0 +1,92 @@
+"""RMSNorm with an optional fused residual add.
+
+``add_rmsnorm(h, delta, w)`` returns ``(h + delta, rmsnorm(h + delta) * w)`` in
+one kernel (``csrc/elementwise.cu``); its backward adds the incoming residual
+gradient to the norm's input gradient in the same kernel and accumulates the
+weight gradient with one atomic per column per CTA.  On CPU the PyTorch
+expressions below are used; they are also the numerics oracle.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _ext
+
+
+def rmsnorm_reference(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    r = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return (xf * r * w.float()).to(x.dtype)
+
+
+class _AddRMSNorm(torch.autograd.Function):
+    """``(h + delta, rmsnorm(h + delta))`` in one kernel."""
+
+    @staticmethod
+    def forward(ctx, h, delta, w, eps):
+        D = h.shape[-1]
+        h2 = h.reshape(-1, D).contiguous()
+        d2 = delta.reshape(-1, D).contiguous()
+        M = h2.shape[0]
+        hout = torch.empty_like(h2)
+        y = torch.empty_like(h2)
+        rstd = torch.empty(M, dtype=torch.float32, device=h.device)
+        _ext.ext().add_rmsnorm_fwd(h2, d2, w, hout, y, rstd, float(eps))
+        ctx.save_for_backward(hout, w, rstd)
+        ctx.shape = h.shape
+        return hout.view(h.shape), y.view(h.shape)
+
+    @staticmethod
+    def backward(ctx, g_h, g_y):
+        hout, w, rstd = ctx.saved_tensors
+        dx, dw = _norm_bwd(g_y, g_h, hout, w, rstd)
+        dx = dx.view(ctx.shape)
+        return dx, dx, dw.to(w.dtype), None
+
+
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        D = x.shape[-1]
+        x2 = x.reshape(-1, D).contiguous()
+        y = torch.empty_like(x2)
+        rstd = torch.empty(x2.shape[0], dtype=torch.float32, device=x.device)
+        _ext.ext().add_rmsnorm_fwd(x2, None, w, x2, y, rstd, float(eps))
+        ctx.save_for_backward(x2, w, rstd)
+        ctx.shape = x.shape
+        return y.view(x.shape)
+
+    @staticmethod
+    def backward(ctx, g_y):
+        x2, w, rstd = ctx.saved_tensors
+        dx, dw = _norm_bwd(g_y, None, x2, w, rstd)
+        return dx.view(ctx.shape), dw.to(w.dtype), None
+
+
+def _norm_bwd(g_y, g_h, x2, w, rstd):
+    D = x2.shape[-1]
+    gy2 = g_y.reshape(-1, D).contiguous() if g_y is not None else torch.zeros_like(x2)
+    gh2 = g_h.reshape(-1, D).contiguous() if g_h is not None else None
+    dx = torch.empty_like(x2)
+    dw = torch.zeros(D, dtype=torch.float32, device=x2.device)
+    _ext.ext().rmsnorm_bwd(gy2, x2, w, rstd, gh2, dx, dw)
+    return dx, dw
+
+
+def add_rmsnorm(h: torch.Tensor, delta: Optional[torch.Tensor], w: torch.Tensor,
+                eps: float = 1e-6):
+    """Returns ``(h_new, y)`` with ``h_new = h + delta`` (or ``h``) and
+    ``y = h_new / rms(h_new) * w``."""
+    if h.is_cuda and h.dtype == torch.bfloat16:
+        if delta is None:
+            return h, _RMSNorm.apply(h, w, eps)
+        return _AddRMSNorm.apply(h, delta, w, eps)
+    hn = h + delta if delta is not None else h
+    return hn, rmsnorm_reference(hn, w, eps)
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    return add_rmsnorm(x, None, w, eps)[1]

@@ -1,0 +1,219 @@
+"""NF4 linear layer with a fused LoRA path (4-bit compute mode).
+
+``Linear4bit`` replaces bitsandbytes' ``Linear4bit``/``matmul_4bit`` that the
+reference relies on (``src/hetero/zeroq_hetero.py:477-500``).  Its frozen weight
+``W [out, in]`` is stored as NF4 (packed bytes + fp32 absmax, bitsandbytes
+layout) and never expanded to a full-precision copy in HBM:
+
+* forward ``Y = X Wᵀ + s·(X Aᵀ) Bᵀ`` runs as ONE sm_100a kernel
+  (``csrc/gemm_sm100.cu``): producer warps dequantise NF4 tiles straight into
+  shared memory in the tcgen05 operand layout, and the LoRA up-projection is one
+  extra K=16 slab of the same MMA chain (operands ``U = s·X Aᵀ`` and ``B``);
+* input gradient ``dX = dY W + s·(dY B) A`` runs as the transposed-producer
+  variant of the same kernel;
+* ``A``/``B`` gradients (rank ``r`` skinny products) and ``U``/``V`` are small
+  GEMMs.
+
+LoRA parameter names follow PEFT (``lora_A [r, in]``, ``lora_B [out, r]``,
+``scaling = alpha / r``, ``B`` zero-initialised) so ``prepare_model_for_zeroq``'s
+``'lora_'`` rule trains them.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from . import _ext
+from .nf4 import QUANT_TYPE_ID, QuantState, dequantize_4bit, quantize_4bit
+
+
+def _fused_ok(x: torch.Tensor, K: int, N: int, blocksize: int) -> bool:
+    return (x.is_cuda and x.dtype == torch.bfloat16 and K % 64 == 0 and N % 16 == 0
+            and blocksize % 64 == 0)
+
+
+def _dequant_weight(packed, absmax, N, K, blocksize, quant_type, dtype):
+    st = QuantState(absmax=absmax, shape=torch.Size([N, K]), dtype=dtype, blocksize=blocksize,
+                    quant_type=quant_type)
+    return dequantize_4bit(packed, st, out_dtype=dtype)
+
+
+class NF4LinearFunction(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, packed, absmax, lora_A, lora_B, bias, N, K, blocksize, quant_type,
+                scaling, backend):
+        shp = x.shape
+        x2 = x.reshape(-1, K)
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        M = x2.shape[0]
+        has_lora = lora_A is not None and lora_B is not None
+        U = None
+        fused = backend != "torch" and _fused_ok(x2, K, N, blocksize)
+        if has_lora:
+            U = (x2 @ lora_A.t().to(x2.dtype)) * scaling
+            if fused:
+                U = U.to(torch.bfloat16).contiguous()
+        if fused:
+            y = torch.empty(M, N, dtype=x2.dtype, device=x2.device)
+            _ext.ext().nf4_linear_fwd(x2, packed, absmax, y, N, K, blocksize,
+                                      QUANT_TYPE_ID[quant_type], U,
+                                      lora_B.to(torch.bfloat16).contiguous() if has_lora else None)
+        else:
+            w = _dequant_weight(packed, absmax, N, K, blocksize, quant_type, torch.float32)
+            y = x2.float() @ w.t()
+            if has_lora:
+                y = y + U.float() @ lora_B.float().t()
+            y = y.to(x2.dtype)
+        if bias is not None:
+            y = y + bias.to(y.dtype)
+        ctx.save_for_backward(x2 if has_lora else None, packed, absmax, lora_A, lora_B, U)
+        ctx.meta = (shp, N, K, blocksize, quant_type, scaling, fused, bias is not None, has_lora)
+        return y.view(*shp[:-1], N)
+
+    @staticmethod
+    def backward(ctx, gy):
+        x2, packed, absmax, lora_A, lora_B, U = ctx.saved_tensors
+        shp, N, K, blocksize, quant_type, scaling, fused, has_bias, has_lora = ctx.meta
+        gy2 = gy.reshape(-1, N)
+        if not gy2.is_contiguous():
+            gy2 = gy2.contiguous()
+        M = gy2.shape[0]
+        V = None
+        if has_lora:
+            V = (gy2 @ lora_B.to(gy2.dtype)) * scaling
+        gx = None
+        if ctx.needs_input_grad[0]:
+            if fused:
+                gx = torch.empty(M, K, dtype=gy2.dtype, device=gy2.device)
+                _ext.ext().nf4_linear_dgrad(
+                    gy2, packed, absmax, gx, N, K, blocksize, QUANT_TYPE_ID[quant_type],
+                    V.to(torch.bfloat16).contiguous() if has_lora else None,
+                    lora_A.to(torch.bfloat16).contiguous() if has_lora else None)
+            else:
+                w = _dequant_weight(packed, absmax, N, K, blocksize, quant_type, torch.float32)
+                g = gy2.float() @ w
+                if has_lora:
+                    g = g + V.float() @ lora_A.float()
+                gx = g.to(gy2.dtype)
+            gx = gx.view(*shp[:-1], K)
+        gA = gB = gbias = None
+        if has_lora:
+            if ctx.needs_input_grad[3]:
+                gA = (V.t().to(x2.dtype) @ x2).to(lora_A.dtype)
+            if ctx.needs_input_grad[4]:
+                gB = (gy2.t() @ U.to(gy2.dtype)).to(lora_B.dtype)
+        if has_bias and ctx.needs_input_grad[5]:
+            gbias = gy2.float().sum(0)
+        return gx, None, None, gA, gB, gbias, None, None, None, None, None, None
+
+
+def nf4_linear(x, packed, absmax, out_features: int, in_features: int, bias=None,
+               lora_A=None, lora_B=None, scaling: float = 1.0, blocksize: int = 64,
+               quant_type: str = "nf4", backend: str = "auto"):
+    if backend == "auto":
+        backend = "fused" if x.is_cuda else "torch"
+    return NF4LinearFunction.apply(x, packed, absmax, lora_A, lora_B, bias, out_features,
+                                   in_features, blocksize, quant_type, scaling, backend)
+
+
+class Linear4bit(nn.Module):
+    """Frozen NF4 weight + optional bias + optional LoRA adapter.
+
+    The module can hold its NF4 data permanently (4-bit compute, "gather once")
+    or receive it from the coordinator before each use (gather/release with
+    ``compute_in_4bit``) through :meth:`set_nf4` / :meth:`clear_nf4`.
+    """
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = False,
+                 blocksize: int = 64, quant_type: str = "nf4", lora_r: int = 0,
+                 lora_alpha: float = 16.0, device=None, dtype=torch.bfloat16,
+                 backend: str = "auto"):
+        super().__init__()
+        self.in_features = in_features
+        self.out_features = out_features
+        self.blocksize = blocksize
+        self.quant_type = quant_type
+        self.compute_dtype = dtype
+        self.backend = backend
+        self.weight = nn.Parameter(torch.empty(0, device=device, dtype=dtype), requires_grad=False)
+        self.register_buffer("weight_packed", None)
+        self.register_buffer("weight_absmax", None)
+        self.bias = nn.Parameter(torch.zeros(out_features, device=device, dtype=dtype)) \
+            if bias else None
+        self.lora_r = lora_r
+        if lora_r > 0:
+            self.scaling = lora_alpha / lora_r
+            self.lora_A = nn.Parameter(torch.empty(lora_r, in_features, device=device,
+                                                   dtype=torch.float32))
+            self.lora_B = nn.Parameter(torch.zeros(out_features, lora_r, device=device,
+                                                   dtype=torch.float32))
+            nn.init.kaiming_uniform_(self.lora_A, a=math.sqrt(5))
+        else:
+            self.scaling = 0.0
+            self.lora_A = None
+            self.lora_B = None
+
+    # -- weight management ---------------------------------------------------
+    @classmethod
+    def from_linear(cls, lin: nn.Linear, blocksize: int = 64, quant_type: str = "nf4",
+                    lora_r: int = 0, lora_alpha: float = 16.0, dtype=torch.bfloat16,
+                    quantize: bool = True):
+        m = cls(lin.in_features, lin.out_features, bias=lin.bias is not None,
+                blocksize=blocksize, quant_type=quant_type, lora_r=lora_r,
+                lora_alpha=lora_alpha, device=lin.weight.device, dtype=dtype)
+        if lin.bias is not None:
+            m.bias.data.copy_(lin.bias.data)
+        if quantize and lin.weight.numel():
+            m.quantize_from(lin.weight.data)
+        return m
+
+    def quantize_from(self, w: torch.Tensor):
+        """Quantise a full-precision ``[out, in]`` weight into resident NF4 storage.
+
+        The weight is cast to fp16 first, as the reference does before calling
+        bitsandbytes (``src/coordinator.py:166-168``)."""
+        if tuple(w.shape) != (self.out_features, self.in_features):
+            raise ValueError(f"weight shape {tuple(w.shape)} != "
+                             f"{(self.out_features, self.in_features)}")
+        packed, st = quantize_4bit(w.detach().to(torch.float16), self.blocksize, self.quant_type)
+        self.set_nf4(packed, st.absmax)
+
+    def set_nf4(self, packed: torch.Tensor, absmax: torch.Tensor, meta: Optional[dict] = None):
+        self.weight_packed = packed.reshape(-1)
+        self.weight_absmax = absmax.reshape(-1).float()
+
+    def clear_nf4(self):
+        self.weight_packed = None
+        self.weight_absmax = None
+
+    @property
+    def has_nf4(self) -> bool:
+        return self.weight_packed is not None
+
+    def dequantized_weight(self, dtype=torch.float32) -> torch.Tensor:
+        return _dequant_weight(self.weight_packed, self.weight_absmax, self.out_features,
+                               self.in_features, self.blocksize, self.quant_type, dtype)
+
+    # -- forward -------------------------------------------------------------
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.weight_packed is None:
+            if self.weight.numel() == 0:
+                raise RuntimeError("Linear4bit has no weight: neither NF4 data nor a "
+                                   "gathered full-precision weight is present")
+            y = torch.nn.functional.linear(x, self.weight.to(x.dtype),
+                                           None if self.bias is None else self.bias.to(x.dtype))
+            if self.lora_r:
+                y = y + (x @ self.lora_A.t().to(x.dtype)) @ self.lora_B.t().to(x.dtype) * self.scaling
+            return y
+        return nf4_linear(x, self.weight_packed, self.weight_absmax, self.out_features,
+                          self.in_features, self.bias, self.lora_A, self.lora_B,
+                          self.scaling, self.blocksize, self.quant_type, self.backend)
+
+    def extra_repr(self) -> str:
+        return (f"in_features={self.in_features}, out_features={self.out_features}, "
+                f"quant={self.quant_type}/{self.blocksize}, lora_r={self.lora_r}")

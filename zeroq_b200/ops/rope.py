@@ -1,0 +1,51 @@
+"""Rotary position embedding (rotate-half convention: pairs ``(i, i + D/2)``).
+
+``apply_rope(q, k, theta)`` rotates ``q [B,S,Hq,D]`` and ``k [B,S,Hk,D]`` by
+position-dependent angles ``pos * theta^(-2i/D)``; the backward is the rotation
+by the negated angle.  CUDA tensors run ``csrc/elementwise.cu``'s kernel, which
+computes the angles in fp32 per element (no cos/sin table in HBM).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _ext
+
+
+def rope_reference(x: torch.Tensor, theta: float, sign: float = 1.0) -> torch.Tensor:
+    B, S, H, D = x.shape
+    half = D // 2
+    inv = theta ** (-torch.arange(0, half, dtype=torch.float64, device=x.device) * 2.0 / D)
+    pos = torch.arange(S, dtype=torch.float64, device=x.device)
+    ang = (pos[:, None] * inv[None, :]).float()
+    cos = torch.cos(ang)[None, :, None, :]
+    sin = torch.sin(ang)[None, :, None, :] * sign
+    xf = x.float()
+    x1, x2 = xf[..., :half], xf[..., half:]
+    return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1).to(x.dtype)
+
+
+class _Rope(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, theta):
+        qo = torch.empty_like(q)
+        ko = torch.empty_like(k)
+        _ext.ext().rope(q.contiguous(), qo, float(theta), 1.0)
+        _ext.ext().rope(k.contiguous(), ko, float(theta), 1.0)
+        ctx.theta = theta
+        return qo, ko
+
+    @staticmethod
+    def backward(ctx, gq, gk):
+        dq = torch.empty_like(gq)
+        dk = torch.empty_like(gk)
+        _ext.ext().rope(gq.contiguous(), dq, float(ctx.theta), -1.0)
+        _ext.ext().rope(gk.contiguous(), dk, float(ctx.theta), -1.0)
+        return dq, dk, None
+
+
+def apply_rope(q: torch.Tensor, k: torch.Tensor, theta: float = 10000.0):
+    if q.is_cuda and q.dtype == torch.bfloat16:
+        return _Rope.apply(q, k, theta)
+    return rope_reference(q, theta), rope_reference(k, theta)
