@@ -1,0 +1,192 @@
+#!/usr/bin/env python
+"""Training-throughput benchmark: the 4.7B NF4 decoder in 4-bit compute mode.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+For N > 1 launch one rank per GPU with torchrun (``--master-addr 127.0.0.1``);
+RANK / LOCAL_RANK / WORLD_SIZE come from the environment.
+
+Workload (weak scaling, per GPU): batch 8 x seq 1024 uniform random token ids,
+next-token cross-entropy, decoder d=3072, 40 layers, 24 heads of 128, explicit
+Q/K/V/O, GELU FFN 12288, vocab 50257, random N(0, 0.02) weights quantised to NF4
+(block 64, fp32 absmax) through the public ``initialize`` API with
+``compute_in_4bit=True``; LoRA r=16 (alpha 32) on every projection and the RMSNorm
+weights train under AdamW (reduce-scatter + sharded update + all-gather across
+ranks).  The embedding (tied LM head) stays bf16 and frozen.
+
+Reported (rank 0, one JSON line):
+* ``value``: tokens/s over all ranks, device-timed with CUDA events around K
+  steps (barrier + synchronize on both sides, max over ranks); inputs resident.
+* ``e2e``: the same through ``Trainer.step`` - pinned host -> device copy of the
+  batch and a device -> host read of the loss every step.
+* ``gpu_launches``: this framework's kernel launches inside the timed region.
+* ``clocks``: nvidia-smi SM clock median and throttle reasons sampled during it.
+The step's working set (NF4 weights, activations, logits) is tens of GB, far
+larger than the 126 MB L2, so no explicit L2 flush is needed between steps.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import sys
+
+BASELINE_TOK_S = 23.7  # reference README.md:41, 2x Tesla M40
+METRIC = "train tokens/sec (device-timed, max over ranks) at 1/2/4/8 B200; fused-path % roofline"
+
+
+def _measured_peaks():
+    p = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except Exception:
+        return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0,
+                "source": "fallback"}
+
+
+def run_reference(args):
+    """The reference's engine cannot be constructed on this image (see reason)."""
+    ref = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
+    reason = None
+    if not os.path.isdir(os.path.join(ref, "zero_q")):
+        reason = "reference not installed under baseline/_ref"
+    else:
+        sys.path.insert(0, ref)
+        try:
+            import zero_q  # noqa: F401
+            import zero_q.coordinator  # noqa: F401  (needs bitsandbytes)
+        except Exception as e:
+            reason = (f"reference 4-bit engine unavailable: zero_q.coordinator imports bitsandbytes "
+                      f"(src/coordinator.py:14), which is not installed and not in the offline "
+                      f"wheelhouse ({type(e).__name__}: {e})")
+    if reason is None:
+        reason = "reference 4.7B decoder (compiled-hybrid-lm) is not part of the reference repo"
+    rank = int(os.environ.get("RANK", "0"))
+    if rank == 0:
+        print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--model", default="4.7b")
+    ap.add_argument("--batch", type=int, default=8)
+    ap.add_argument("--seq", type=int, default=1024)
+    ap.add_argument("--lora-r", type=int, default=16)
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from zeroq_b200 import ShardedAdamW, ZeroQConfig, initialize
+    from zeroq_b200.models import DecoderLM, get_config
+    from zeroq_b200.ops import _ext
+    from zeroq_b200.train import ClockSampler, Trainer, device_time_ms, synthetic_batch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(minutes=10),
+                                device_id=device)
+    if world != args.gpus and rank == 0:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
+    _ext.ext()
+
+    cfg = get_config(args.model, lora_r=args.lora_r, lora_alpha=2.0 * args.lora_r)
+    model = DecoderLM(cfg, device=device)
+    model.init_dense_(std=0.02, seed=1234)  # identical on every rank
+    zq = ZeroQConfig(compute_dtype=torch.bfloat16, compute_in_4bit=True, double_quant=False,
+                     exclude_modules=["lm_head", "embed_tokens"], backend="auto")
+    initialize(model, zq, trainable_patterns=("lora_", "norm"))
+    torch.cuda.empty_cache()
+    opt = ShardedAdamW(model.trainable_parameters(), lr=1e-4, betas=(0.9, 0.999),
+                       weight_decay=0.0)
+    trainer = Trainer(model, opt, device)
+
+    B, S = args.batch, args.seq
+    x_host, y_host = synthetic_batch(B, S, cfg.vocab_size, seed=1000 + rank)
+    x_dev, y_dev = x_host.to(device), y_host.to(device)
+
+    losses = []
+    for _ in range(args.warmup):
+        losses.append(trainer.step_device(x_dev, y_dev))
+    torch.cuda.synchronize()
+
+    with ClockSampler(local) as clk, _ext.LaunchCounter() as lc:
+        ms = device_time_ms(lambda: trainer.step_device(x_dev, y_dev), args.steps)
+    e2e_ms = None
+    if not args.no_e2e:
+        e2e_ms = device_time_ms(lambda: losses.append(trainer.step(x_host, y_host)), args.steps)
+
+    tokens = B * S * world * args.steps
+    value = tokens / (ms / 1000.0)
+    peaks = _measured_peaks()
+    fpt = model.flops_per_token(S)
+    tflops_per_gpu = fpt * value / world / 1e12
+    mem_gb = torch.cuda.max_memory_allocated(device) / 1e9
+    first_loss = float(losses[0]) if losses else float("nan")
+    last_loss = float(losses[-1]) if losses else float("nan")
+    out = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": round(value / BASELINE_TOK_S, 1),
+        "dtype": "bf16",
+        "data": "synthetic (uniform random token ids; random-init N(0,0.02) weights)",
+        "impl": "ours",
+        "config": {
+            "model": f"{args.model} decoder (d={cfg.d_model}, {cfg.n_layers} layers, "
+                     f"{cfg.n_heads}x{cfg.head_dim} heads, {cfg.ffn_act} FFN {cfg.ffn_dim}, "
+                     f"vocab {cfg.vocab_size}), NF4 4-bit compute, LoRA r={args.lora_r} on "
+                     f"{'/'.join(cfg.lora_targets)} + RMSNorm weights, AdamW",
+            "global_batch": B * world,
+            "seq_len": S,
+            "parallelism": f"dp{world}",
+            "l2": "no flush: per-step working set (NF4 weights + activations) >> 126 MB L2",
+        },
+        "e2e": None if e2e_ms is None else {
+            "value": round(tokens / (e2e_ms / 1000.0), 1),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": int(x_host.numel() * x_host.element_size()
+                                      + y_host.numel() * y_host.element_size()),
+            "d2h_bytes_per_step": 4,
+        },
+        "gpu_launches": lc.count,
+        "clocks": clk.summary(),
+        "achieved_tflops_per_gpu": round(tflops_per_gpu, 1),
+        "frac_of_measured_bf16_sustained": round(tflops_per_gpu / peaks["bf16_tflops_sustained"], 3),
+        "peak_mem_gb": round(mem_gb, 1),
+        "loss_first_last": [round(first_loss, 4), round(last_loss, 4)],
+    }
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -15,6 +15,7 @@ import importlib
 import os
 
 _EXT = None
+_COUNTED = None
 _EXT_ERR: Exception | None = None
 
 
@@ -26,6 +27,8 @@ def _load():
         import torch  # noqa: F401  (the extension links against libtorch)
 
         _EXT = importlib.import_module("zeroq_b200._C")
+        global _COUNTED
+        _COUNTED = _Counted(_EXT)
     except Exception as e:  # pragma: no cover - depends on the build
         _EXT_ERR = e
 
@@ -33,6 +36,48 @@ def _load():
 def available() -> bool:
     _load()
     return _EXT is not None
+
+
+# kernels launched per call of each binding (bindings not listed launch one)
+_KERNELS_PER_CALL = {"attn_bwd": 3, "gemm_status": 0}
+
+
+class LaunchCounter:
+    """Counts this extension's kernel launches while active (``with LaunchCounter() as c``)."""
+
+    active = None
+
+    def __init__(self):
+        self.count = 0
+        self.by_name = {}
+
+    def __enter__(self):
+        LaunchCounter.active = self
+        return self
+
+    def __exit__(self, *exc):
+        LaunchCounter.active = None
+        return False
+
+
+class _Counted:
+    def __init__(self, mod):
+        self._mod = mod
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if not callable(fn):
+            return fn
+        k = _KERNELS_PER_CALL.get(name, 1)
+
+        def call(*args, **kwargs):
+            c = LaunchCounter.active
+            if c is not None:
+                c.count += k
+                c.by_name[name] = c.by_name.get(name, 0) + k
+            return fn(*args, **kwargs)
+
+        return call
 
 
 def ext():
@@ -44,7 +89,7 @@ def ext():
             f"{_EXT_ERR!r}. Build it with `python -c 'import __graft_entry__ as g; g.build()'` "
             "or `python setup.py build_ext --inplace`."
         )
-    return _EXT
+    return _COUNTED if LaunchCounter.active is not None else _EXT
 
 
 def so_path() -> str | None:

@@ -3,16 +3,18 @@
 ``Linear4bit`` replaces bitsandbytes' ``Linear4bit``/``matmul_4bit`` that the
 reference relies on (``src/hetero/zeroq_hetero.py:477-500``).  Its frozen weight
 ``W [out, in]`` is stored as NF4 (packed bytes + fp32 absmax, bitsandbytes
-layout) and never expanded to a full-precision copy in HBM:
+layout); no full-precision copy of it is kept between uses.
 
-* forward ``Y = X Wᵀ + s·(X Aᵀ) Bᵀ`` runs as ONE sm_100a kernel
-  (``csrc/gemm_sm100.cu``): producer warps dequantise NF4 tiles straight into
-  shared memory in the tcgen05 operand layout, and the LoRA up-projection is one
-  extra K=16 slab of the same MMA chain (operands ``U = s·X Aᵀ`` and ``B``);
-* input gradient ``dX = dY W + s·(dY B) A`` runs as the transposed-producer
-  variant of the same kernel;
-* ``A``/``B`` gradients (rank ``r`` skinny products) and ``U``/``V`` are small
-  GEMMs.
+CUDA path, per call (``csrc/gemm_sm100.cu``):
+
+* the NF4 operand kernel expands ``W`` (forward) or ``Wᵀ`` (input gradient) to a
+  transient bf16 operand that stays L2-resident for the GEMM that follows;
+* the tcgen05/TMEM GEMM computes ``Y = X Wᵀ`` and, in the same MMA chain, the
+  LoRA up-projection as one extra 64-wide K slab (``U = s·X Aᵀ`` against
+  ``B``, both zero-padded to rank 64); the input gradient
+  ``dX = dY W + (s·dY B) A`` is the same GEMM with the transposed operand;
+* ``U``/``V`` (rank-64 padded) run on the same GEMM; the ``A``/``B`` weight
+  gradients (contractions over tokens) are small cuBLAS GEMMs.
 
 LoRA parameter names follow PEFT (``lora_A [r, in]``, ``lora_B [out, r]``,
 ``scaling = alpha / r``, ``B`` zero-initialised) so ``prepare_model_for_zeroq``'s
@@ -32,7 +34,7 @@ from .nf4 import QUANT_TYPE_ID, QuantState, dequantize_4bit, quantize_4bit
 
 
 def _fused_ok(x: torch.Tensor, K: int, N: int, blocksize: int) -> bool:
-    return (x.is_cuda and x.dtype == torch.bfloat16 and K % 64 == 0 and N % 16 == 0
+    return (x.is_cuda and x.dtype == torch.bfloat16 and K % 64 == 0 and N % 64 == 0
             and blocksize % 64 == 0)
 
 
@@ -42,7 +44,34 @@ def _dequant_weight(packed, absmax, N, K, blocksize, quant_type, dtype):
     return dequantize_4bit(packed, st, out_dtype=dtype)
 
 
+def _nf4_operand(packed, absmax, N, K, blocksize, quant_type, transpose: bool):
+    """bf16 GEMM operand from NF4: ``W [N, K]`` or ``Wᵀ [K, N]`` (``csrc/gemm_sm100.cu``)."""
+    w = torch.empty(N * K, dtype=torch.bfloat16, device=packed.device)
+    _ext.ext().nf4_to_bf16(packed, absmax, w, N, K, blocksize, QUANT_TYPE_ID[quant_type],
+                           transpose)
+    return w.view(K, N) if transpose else w.view(N, K)
+
+
+def _pad_cols(t: torch.Tensor, width: int = 64) -> torch.Tensor:
+    out = torch.zeros(t.shape[0], width, dtype=torch.bfloat16, device=t.device)
+    out[:, : t.shape[1]] = t
+    return out
+
+
+def _pad_rows(t: torch.Tensor, height: int = 64) -> torch.Tensor:
+    out = torch.zeros(height, t.shape[1], dtype=torch.bfloat16, device=t.device)
+    out[: t.shape[0]] = t
+    return out
+
+
 class NF4LinearFunction(torch.autograd.Function):
+    """``y = x Wᵀ + s (x Aᵀ) Bᵀ (+ bias)`` with ``W`` frozen NF4.
+
+    CUDA path: the NF4 operand is produced in the tcgen05 operand layout and the
+    LoRA up-projection rides as the extra 64-wide K slab of the same GEMM
+    (``U = s·x·Aᵀ`` and ``B``, zero-padded to rank 64).
+    """
+
     @staticmethod
     def forward(ctx, x, packed, absmax, lora_A, lora_B, bias, N, K, blocksize, quant_type,
                 scaling, backend):
@@ -52,61 +81,83 @@ class NF4LinearFunction(torch.autograd.Function):
             x2 = x2.contiguous()
         M = x2.shape[0]
         has_lora = lora_A is not None and lora_B is not None
+        r = lora_A.shape[0] if has_lora else 0
+        fused = backend != "torch" and _fused_ok(x2, K, N, blocksize) and r <= 64
         U = None
-        fused = backend != "torch" and _fused_ok(x2, K, N, blocksize)
-        if has_lora:
-            U = (x2 @ lora_A.t().to(x2.dtype)) * scaling
-            if fused:
-                U = U.to(torch.bfloat16).contiguous()
         if fused:
+            E = _ext.ext()
+            w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
             y = torch.empty(M, N, dtype=x2.dtype, device=x2.device)
-            _ext.ext().nf4_linear_fwd(x2, packed, absmax, y, N, K, blocksize,
-                                      QUANT_TYPE_ID[quant_type], U,
-                                      lora_B.to(torch.bfloat16).contiguous() if has_lora else None)
+            if has_lora:
+                a_pad = _pad_rows(lora_A.detach().to(torch.bfloat16) * scaling)
+                U = torch.empty(M, 64, dtype=torch.bfloat16, device=x2.device)
+                E.gemm_bf16_tn(x2, a_pad, U)
+                E.gemm_bf16_tn_extra(x2, w, y, U, _pad_cols(lora_B.detach().to(torch.bfloat16)))
+            else:
+                E.gemm_bf16_tn(x2, w, y)
+            del w
         else:
             w = _dequant_weight(packed, absmax, N, K, blocksize, quant_type, torch.float32)
             y = x2.float() @ w.t()
             if has_lora:
-                y = y + U.float() @ lora_B.float().t()
+                U = (x2.float() @ lora_A.float().t()) * scaling
+                y = y + U @ lora_B.float().t()
             y = y.to(x2.dtype)
         if bias is not None:
             y = y + bias.to(y.dtype)
         ctx.save_for_backward(x2 if has_lora else None, packed, absmax, lora_A, lora_B, U)
-        ctx.meta = (shp, N, K, blocksize, quant_type, scaling, fused, bias is not None, has_lora)
+        ctx.meta = (shp, N, K, blocksize, quant_type, scaling, fused, bias is not None, has_lora, r)
         return y.view(*shp[:-1], N)
 
     @staticmethod
     def backward(ctx, gy):
         x2, packed, absmax, lora_A, lora_B, U = ctx.saved_tensors
-        shp, N, K, blocksize, quant_type, scaling, fused, has_bias, has_lora = ctx.meta
+        shp, N, K, blocksize, quant_type, scaling, fused, has_bias, has_lora, r = ctx.meta
         gy2 = gy.reshape(-1, N)
         if not gy2.is_contiguous():
             gy2 = gy2.contiguous()
         M = gy2.shape[0]
-        V = None
-        if has_lora:
-            V = (gy2 @ lora_B.to(gy2.dtype)) * scaling
-        gx = None
-        if ctx.needs_input_grad[0]:
-            if fused:
-                gx = torch.empty(M, K, dtype=gy2.dtype, device=gy2.device)
-                _ext.ext().nf4_linear_dgrad(
-                    gy2, packed, absmax, gx, N, K, blocksize, QUANT_TYPE_ID[quant_type],
-                    V.to(torch.bfloat16).contiguous() if has_lora else None,
-                    lora_A.to(torch.bfloat16).contiguous() if has_lora else None)
-            else:
+        gx = gA = gB = gbias = None
+        if fused:
+            E = _ext.ext()
+            gy2 = gy2.to(torch.bfloat16)
+            V = None
+            if has_lora:
+                bt_pad = _pad_rows(lora_B.detach().t().to(torch.bfloat16) * scaling)
+                V = torch.empty(M, 64, dtype=torch.bfloat16, device=gy2.device)
+                if N % 64 == 0:
+                    E.gemm_bf16_tn(gy2, bt_pad, V)
+                else:
+                    V.copy_(gy2 @ bt_pad.t())
+            if ctx.needs_input_grad[0]:
+                wt = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, True)
+                gx = torch.empty(M, K, dtype=torch.bfloat16, device=gy2.device)
+                if has_lora:
+                    E.gemm_bf16_tn_extra(gy2, wt, gx, V, _pad_cols(lora_A.detach().t().to(torch.bfloat16)))
+                else:
+                    E.gemm_bf16_tn(gy2, wt, gx)
+                del wt
+                gx = gx.view(*shp[:-1], K)
+            if has_lora:
+                if ctx.needs_input_grad[3]:
+                    gA = (V[:, :r].t() @ x2).to(lora_A.dtype)
+                if ctx.needs_input_grad[4]:
+                    gB = (gy2.t() @ U[:, :r]).to(lora_B.dtype)
+        else:
+            Vf = None
+            if has_lora:
+                Vf = (gy2.float() @ lora_B.float()) * scaling
+            if ctx.needs_input_grad[0]:
                 w = _dequant_weight(packed, absmax, N, K, blocksize, quant_type, torch.float32)
                 g = gy2.float() @ w
                 if has_lora:
-                    g = g + V.float() @ lora_A.float()
-                gx = g.to(gy2.dtype)
-            gx = gx.view(*shp[:-1], K)
-        gA = gB = gbias = None
-        if has_lora:
-            if ctx.needs_input_grad[3]:
-                gA = (V.t().to(x2.dtype) @ x2).to(lora_A.dtype)
-            if ctx.needs_input_grad[4]:
-                gB = (gy2.t() @ U.to(gy2.dtype)).to(lora_B.dtype)
+                    g = g + Vf @ lora_A.float()
+                gx = g.to(gy.dtype).view(*shp[:-1], K)
+            if has_lora:
+                if ctx.needs_input_grad[3]:
+                    gA = (Vf.t() @ x2.float()).to(lora_A.dtype)
+                if ctx.needs_input_grad[4]:
+                    gB = (gy2.float().t() @ U.float()).to(lora_B.dtype)
         if has_bias and ctx.needs_input_grad[5]:
             gbias = gy2.float().sum(0)
         return gx, None, None, gA, gB, gbias, None, None, None, None, None, None

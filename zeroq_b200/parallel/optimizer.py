@@ -1,0 +1,163 @@
+"""Flat-buffer optimizers for the trainable surface (LoRA adapters, norms).
+
+:class:`FlatParams` moves a list of fp32 parameters into one contiguous fp32
+buffer (each parameter becomes a view of it) and pre-assigns every ``.grad`` as
+a view of one contiguous gradient buffer; autograd accumulates into those views
+in place.  One kernel launch then updates every parameter, and one collective
+moves every gradient.
+
+:class:`ShardedAdamW` is the data-parallel AdamW of the reference's training
+loops (``examples/train_32b_maxwell.py:472-475`` all-reduces each LoRA grad,
+then steps torch's AdamW), restructured ZeRO-style:
+
+* world size 1: one fused AdamW kernel over the flat buffer;
+* world size W, backend ``nccl``: one ``reduce_scatter_tensor`` of the flat
+  gradient, AdamW on this rank's 1/W shard (moments are sharded too, with the
+  1/W averaging folded into the kernel's ``grad_scale``), one
+  ``all_gather_into_tensor`` of the updated shard;
+* backend ``fused``: the same three steps with the reduce-scatter done by the
+  peer-memory kernel of ``zeroq_b200.parallel.peer`` (it sums the peers' slices
+  over NVLink and applies AdamW in the same pass).
+
+Optional global-norm gradient clipping scales the gradient inside the kernel.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Iterable, List, Optional
+
+import torch
+import torch.distributed as dist
+
+from ..ops.optim import adamw_step
+
+
+class FlatParams:
+    def __init__(self, params: Iterable[torch.nn.Parameter], pad_to: int = 1, device=None):
+        self.params: List[torch.nn.Parameter] = [p for p in params]
+        if not self.params:
+            raise ValueError("FlatParams needs at least one parameter")
+        for p in self.params:
+            if p.dtype != torch.float32:
+                raise TypeError(f"FlatParams holds fp32 parameters; got {p.dtype}")
+        device = device or self.params[0].device
+        self.numel = sum(p.numel() for p in self.params)
+        self.padded = (self.numel + pad_to - 1) // pad_to * pad_to
+        self.data = torch.zeros(self.padded, dtype=torch.float32, device=device)
+        self.grad = torch.zeros(self.padded, dtype=torch.float32, device=device)
+        self.offsets = []
+        off = 0
+        with torch.no_grad():
+            for p in self.params:
+                n = p.numel()
+                self.data[off:off + n].copy_(p.data.reshape(-1))
+                p.data = self.data[off:off + n].view(p.shape)
+                p.grad = self.grad[off:off + n].view(p.shape)
+                self.offsets.append(off)
+                off += n
+
+    def zero_grad(self):
+        self.grad.zero_()
+        # autograd may have replaced a .grad (e.g. after a set_to_none elsewhere): rebind
+        for p, off in zip(self.params, self.offsets):
+            if p.grad is None or p.grad.data_ptr() != self.grad[off:].data_ptr():
+                p.grad = self.grad[off:off + p.numel()].view(p.shape)
+
+    def grads_bound(self) -> bool:
+        return all(p.grad is not None and p.grad.data_ptr() == self.grad[off:].data_ptr()
+                   for p, off in zip(self.params, self.offsets))
+
+
+class ShardedAdamW:
+    """AdamW over a :class:`FlatParams`, data-parallel across the process group."""
+
+    def __init__(self, params, lr: float = 1e-4, betas=(0.9, 0.999), eps: float = 1e-8,
+                 weight_decay: float = 0.0, process_group: Optional[dist.ProcessGroup] = None,
+                 backend: str = "auto", max_grad_norm: Optional[float] = None):
+        self.pg = process_group
+        self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(process_group) if dist.is_initialized() else 0
+        self.flat = FlatParams(params, pad_to=self.world)
+        self.lr, self.betas, self.eps, self.wd = lr, betas, eps, weight_decay
+        self.max_grad_norm = max_grad_norm
+        self.shard = self.flat.padded // self.world
+        dev = self.flat.data.device
+        self.exp_avg = torch.zeros(self.shard, dtype=torch.float32, device=dev)
+        self.exp_avg_sq = torch.zeros(self.shard, dtype=torch.float32, device=dev)
+        self.grad_shard = torch.zeros(self.shard, dtype=torch.float32, device=dev) \
+            if self.world > 1 else None
+        self.step_count = 0
+        if backend == "auto":
+            backend = "fused" if dev.type == "cuda" and self.world > 1 else "nccl"
+        self.backend = backend
+        self._peer = None
+        self.last_grad_norm: Optional[torch.Tensor] = None
+
+    @property
+    def params(self):
+        return self.flat.params
+
+    def zero_grad(self, set_to_none: bool = False):
+        self.flat.zero_grad()
+
+    def _clip_scale(self, g: torch.Tensor, already_averaged_scale: float) -> float:
+        if self.max_grad_norm is None:
+            return 1.0
+        sq = (g.float() * already_averaged_scale).pow(2).sum()
+        if self.world > 1:
+            dist.all_reduce(sq, group=self.pg)
+        norm = sq.sqrt()
+        self.last_grad_norm = norm
+        # device-side factor would avoid this sync; clipping is off on the bench path
+        return float(torch.clamp(self.max_grad_norm / (norm + 1e-6), max=1.0))
+
+    @torch.no_grad()
+    def step(self):
+        self.step_count += 1
+        b1, b2 = self.betas
+        if self.world == 1:
+            scale = self._clip_scale(self.flat.grad, 1.0)
+            adamw_step(self.flat.data, self.flat.grad, self.exp_avg, self.exp_avg_sq, lr=self.lr,
+                       beta1=b1, beta2=b2, eps=self.eps, weight_decay=self.wd,
+                       step=self.step_count, grad_scale=scale)
+            return
+        lo = self.rank * self.shard
+        mine = self.flat.data[lo:lo + self.shard]
+        if self.backend == "fused" and self._peer_ready():
+            self._peer.reduce_scatter_adamw(self, mine)
+        else:
+            dist.reduce_scatter_tensor(self.grad_shard, self.flat.grad, op=dist.ReduceOp.SUM,
+                                       group=self.pg)
+            scale = self._clip_scale(self.grad_shard, 1.0 / self.world) / self.world
+            adamw_step(mine, self.grad_shard, self.exp_avg, self.exp_avg_sq, lr=self.lr,
+                       beta1=b1, beta2=b2, eps=self.eps, weight_decay=self.wd,
+                       step=self.step_count, grad_scale=scale)
+        # NCCL gathers in place when the input is this rank's slice of the output;
+        # other backends get a private copy of the shard.
+        src = mine if self.flat.data.is_cuda else mine.clone()
+        dist.all_gather_into_tensor(self.flat.data, src, group=self.pg)
+
+    def _peer_ready(self) -> bool:
+        if self._peer is None:
+            try:
+                from .peer import PeerReduceScatterAdamW
+
+                self._peer = PeerReduceScatterAdamW.create(self.flat.grad, self.pg)
+            except Exception as e:  # no peer access / extension: stay on NCCL
+                self._peer = False
+                self._peer_error = repr(e)
+        return bool(self._peer)
+
+    def state_dict(self) -> dict:
+        return {"step": self.step_count, "exp_avg": self.exp_avg.detach().cpu(),
+                "exp_avg_sq": self.exp_avg_sq.detach().cpu(), "lr": self.lr,
+                "betas": self.betas, "eps": self.eps, "weight_decay": self.wd,
+                "world": self.world, "rank": self.rank, "shard": self.shard}
+
+    def load_state_dict(self, st: dict):
+        if st["shard"] != self.shard:
+            raise ValueError("optimizer shard size differs (different world size or params)")
+        self.step_count = int(st["step"])
+        self.exp_avg.copy_(st["exp_avg"])
+        self.exp_avg_sq.copy_(st["exp_avg_sq"])
