@@ -81,6 +81,8 @@ def main():
     ap.add_argument("--seq", type=int, default=1024)
     ap.add_argument("--lora-r", type=int, default=16)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--torch-profile", default=None,
+                    help="after timing, profile one more step and write a per-kernel table here")
     args = ap.parse_args()
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
@@ -134,6 +136,16 @@ def main():
     e2e_ms = None
     if not args.no_e2e:
         e2e_ms = device_time_ms(lambda: losses.append(trainer.step(x_host, y_host)), args.steps)
+
+    if args.torch_profile and rank == 0:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            trainer.step_device(x_dev, y_dev)
+            torch.cuda.synchronize()
+        with open(args.torch_profile, "w") as f:
+            f.write(prof.key_averages().table(sort_by="cuda_time_total", row_limit=60,
+                                              max_name_column_width=90))
 
     tokens = B * S * world * args.steps
     value = tokens / (ms / 1000.0)

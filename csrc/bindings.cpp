@@ -17,8 +17,8 @@ void nf4_to_bf16(at::Tensor packed, at::Tensor absmax, at::Tensor out, int64_t r
 void add_rmsnorm_fwd(at::Tensor h, c10::optional<at::Tensor> d, at::Tensor w, at::Tensor hout,
                      at::Tensor y, at::Tensor rstd, double eps);
 void rmsnorm_bwd(at::Tensor gy, at::Tensor x, at::Tensor w, at::Tensor rstd,
-                 c10::optional<at::Tensor> gh, at::Tensor dx, at::Tensor dw);
-void rope(at::Tensor x, at::Tensor out, double theta, double sign);
+                 c10::optional<at::Tensor> gh, at::Tensor dx, at::Tensor dw_part);
+void rope(at::Tensor x, at::Tensor out, at::Tensor cs, double sign);
 void gelu_fwd(at::Tensor x, at::Tensor y);
 void gelu_bwd(at::Tensor g, at::Tensor x, at::Tensor dx);
 void swiglu_fwd(at::Tensor gate, at::Tensor up, at::Tensor y);

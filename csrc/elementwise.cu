@@ -96,8 +96,8 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_fwd_kernel(
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
     const __nv_bfloat16* __restrict__ gy, const __nv_bfloat16* __restrict__ x,
     const float* __restrict__ w, const float* __restrict__ rstd,
-    const __nv_bfloat16* __restrict__ gh, __nv_bfloat16* __restrict__ dx, float* __restrict__ dw,
-    int64_t M, int D) {
+    const __nv_bfloat16* __restrict__ gh, __nv_bfloat16* __restrict__ dx,
+    float* __restrict__ dw_part, int64_t M, int D) {
   __shared__ float red[4];
   const int nch = D >> 3;
   float dwacc[kNormMaxChunks][8];
@@ -145,36 +145,49 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
       }
     }
   }
+  // this CTA's partial weight gradient: one row of dw_part (summed on the host side)
+  float* dst = dw_part + (int64_t)blockIdx.x * D;
 #pragma unroll
   for (int c = 0; c < kNormMaxChunks; ++c) {
     const int ch = c * kNormThreads + threadIdx.x;
     if (ch < nch) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) atomicAdd(dw + ch * 8 + i, dwacc[c][i]);
+      float4* d4 = reinterpret_cast<float4*>(dst + ch * 8);
+      d4[0] = make_float4(dwacc[c][0], dwacc[c][1], dwacc[c][2], dwacc[c][3]);
+      d4[1] = make_float4(dwacc[c][4], dwacc[c][5], dwacc[c][6], dwacc[c][7]);
     }
   }
 }
 
 // ----------------------------------------------------------------------------
-// RoPE, rotate-half convention; x [rows = B*S*H, D], position = (row / H) % S
+// RoPE, rotate-half convention; x [rows = B*S*H, D], position = (row / H) % S.
+// cs: [S, D/2] float2 (cos, sin) table; each thread rotates 8 pairs with
+// 16-byte loads/stores from both halves of the row.
 // ----------------------------------------------------------------------------
 __global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ out,
-                            const double* __restrict__ inv_freq, int64_t rows, int S, int H,
-                            int D, float sign) {
+                            const float2* __restrict__ cs, int64_t rows, int S, int H, int D,
+                            float sign) {
   const int half = D >> 1;
+  const int groups = half >> 3;
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= rows * half) return;
-  const int64_t row = t / half;
-  const int i = (int)(t % half);
+  if (t >= rows * groups) return;
+  const int64_t row = t / groups;
+  const int i0 = (int)(t % groups) * 8;
   const int pos = (int)((row / H) % S);
-  const float ang = (float)((double)pos * inv_freq[i]);
-  float s, c;
-  sincosf(ang, &s, &c);
-  s *= sign;
-  const float x1 = __bfloat162float(x[row * D + i]);
-  const float x2 = __bfloat162float(x[row * D + i + half]);
-  out[row * D + i] = __float2bfloat16_rn(x1 * c - x2 * s);
-  out[row * D + i + half] = __float2bfloat16_rn(x2 * c + x1 * s);
+  float a[8], b[8], oa[8], ob[8];
+  bf16x8_to_f32(*reinterpret_cast<const uint4*>(x + row * D + i0), a);
+  bf16x8_to_f32(*reinterpret_cast<const uint4*>(x + row * D + half + i0), b);
+  const float4* c4 = reinterpret_cast<const float4*>(cs + (int64_t)pos * half + i0);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float4 v = c4[j];  // (cos, sin) of pairs 2j and 2j+1
+    const float c0 = v.x, s0 = v.y * sign, c1 = v.z, s1 = v.w * sign;
+    oa[2 * j] = a[2 * j] * c0 - b[2 * j] * s0;
+    ob[2 * j] = b[2 * j] * c0 + a[2 * j] * s0;
+    oa[2 * j + 1] = a[2 * j + 1] * c1 - b[2 * j + 1] * s1;
+    ob[2 * j + 1] = b[2 * j + 1] * c1 + a[2 * j + 1] * s1;
+  }
+  *reinterpret_cast<uint4*>(out + row * D + i0) = f32_to_bf16x8(oa);
+  *reinterpret_cast<uint4*>(out + row * D + half + i0) = f32_to_bf16x8(ob);
 }
 
 // ----------------------------------------------------------------------------
@@ -429,8 +442,9 @@ void add_rmsnorm_fwd(at::Tensor h, c10::optional<at::Tensor> d, at::Tensor w, at
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// dw_part: [grid, D] fp32 partial sums, grid = dw_part.size(0); caller sums over rows
 void rmsnorm_bwd(at::Tensor gy, at::Tensor x, at::Tensor w, at::Tensor rstd,
-                 c10::optional<at::Tensor> gh, at::Tensor dx, at::Tensor dw) {
+                 c10::optional<at::Tensor> gh, at::Tensor dx, at::Tensor dw_part) {
   check_bf16(gy, "gy");
   check_bf16(x, "x");
   check_bf16(dx, "dx");
@@ -442,28 +456,30 @@ void rmsnorm_bwd(at::Tensor gy, at::Tensor x, at::Tensor w, at::Tensor rstd,
     check_bf16(*gh, "gh");
     ghp = cbf(*gh);
   }
-  int dev_sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
-  const int64_t grid = std::min<int64_t>(M, (int64_t)dev_sms * 8);
+  TORCH_CHECK(dw_part.dim() == 2 && dw_part.size(1) == D && dw_part.is_contiguous() &&
+                  dw_part.scalar_type() == at::kFloat, "dw_part must be fp32 [grid, D]");
+  const int64_t grid = std::min<int64_t>(M, dw_part.size(0));
   rmsnorm_bwd_kernel<<<(unsigned)grid, kNormThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       cbf(gy), cbf(x), w.data_ptr<float>(), rstd.data_ptr<float>(), ghp, bf(dx),
-      dw.data_ptr<float>(), M, (int)D);
+      dw_part.data_ptr<float>(), M, (int)D);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void rope(at::Tensor x, at::Tensor out, double theta, double sign) {
+void rope(at::Tensor x, at::Tensor out, at::Tensor cs, double sign) {
   check_bf16(x, "x");
   check_bf16(out, "out");
   TORCH_CHECK(x.dim() == 4, "rope: x must be [B, S, H, D]");
   const int64_t B = x.size(0), S = x.size(1), H = x.size(2), D = x.size(3);
-  TORCH_CHECK(D % 2 == 0, "rope: even head dim");
+  TORCH_CHECK(D % 16 == 0, "rope: head dim must be a multiple of 16");
+  TORCH_CHECK(cs.scalar_type() == at::kFloat && cs.is_contiguous() && cs.numel() >= S * D,
+              "rope: cos/sin table must be fp32 [S, D/2, 2]");
   const at::cuda::CUDAGuard guard(x.device());
-  auto inv = at::arange(0, D / 2, x.options().dtype(at::kDouble));
-  inv = at::pow(at::full({}, theta, inv.options()), inv * (-2.0 / (double)D));
   const int64_t rows = B * S * H;
-  const int64_t total = rows * (D / 2);
+  const int64_t total = rows * (D / 16);
   const int bs = 256;
   rope_kernel<<<(unsigned)((total + bs - 1) / bs), bs, 0, at::cuda::getCurrentCUDAStream()>>>(
-      cbf(x), bf(out), inv.data_ptr<double>(), rows, (int)S, (int)H, (int)D, (float)sign);
+      cbf(x), bf(out), reinterpret_cast<const float2*>(cs.data_ptr<float>()), rows, (int)S,
+      (int)H, (int)D, (float)sign);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -71,9 +71,20 @@ def _norm_bwd(g_y, g_h, x2, w, rstd):
     gy2 = g_y.reshape(-1, D).contiguous() if g_y is not None else torch.zeros_like(x2)
     gh2 = g_h.reshape(-1, D).contiguous() if g_h is not None else None
     dx = torch.empty_like(x2)
-    dw = torch.zeros(D, dtype=torch.float32, device=x2.device)
-    _ext.ext().rmsnorm_bwd(gy2, x2, w, rstd, gh2, dx, dw)
-    return dx, dw
+    grid = min(x2.shape[0], _num_sms(x2.device) * 2)
+    dw_part = torch.empty(grid, D, dtype=torch.float32, device=x2.device)
+    _ext.ext().rmsnorm_bwd(gy2, x2, w, rstd, gh2, dx, dw_part)
+    return dx, dw_part.sum(0)
+
+
+_SMS = {}
+
+
+def _num_sms(device) -> int:
+    i = device.index if device.index is not None else torch.cuda.current_device()
+    if i not in _SMS:
+        _SMS[i] = torch.cuda.get_device_properties(i).multi_processor_count
+    return _SMS[i]
 
 
 def add_rmsnorm(h: torch.Tensor, delta: Optional[torch.Tensor], w: torch.Tensor,

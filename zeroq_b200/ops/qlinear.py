@@ -13,8 +13,8 @@ CUDA path, per call (``csrc/gemm_sm100.cu``):
   LoRA up-projection as one extra 64-wide K slab (``U = s·X Aᵀ`` against
   ``B``, both zero-padded to rank 64); the input gradient
   ``dX = dY W + (s·dY B) A`` is the same GEMM with the transposed operand;
-* ``U``/``V`` (rank-64 padded) run on the same GEMM; the ``A``/``B`` weight
-  gradients (contractions over tokens) are small cuBLAS GEMMs.
+* ``U``/``V`` (rank-64 padded, skinny) and the ``A``/``B`` weight gradients
+  (contractions over tokens) are small cuBLAS GEMMs.
 
 LoRA parameter names follow PEFT (``lora_A [r, in]``, ``lora_B [out, r]``,
 ``scaling = alpha / r``, ``B`` zero-initialised) so ``prepare_model_for_zeroq``'s
@@ -90,8 +90,7 @@ class NF4LinearFunction(torch.autograd.Function):
             y = torch.empty(M, N, dtype=x2.dtype, device=x2.device)
             if has_lora:
                 a_pad = _pad_rows(lora_A.detach().to(torch.bfloat16) * scaling)
-                U = torch.empty(M, 64, dtype=torch.bfloat16, device=x2.device)
-                E.gemm_bf16_tn(x2, a_pad, U)
+                U = x2 @ a_pad.t()  # [M, 64] skinny product: cuBLAS
                 E.gemm_bf16_tn_extra(x2, w, y, U, _pad_cols(lora_B.detach().to(torch.bfloat16)))
             else:
                 E.gemm_bf16_tn(x2, w, y)
@@ -124,11 +123,7 @@ class NF4LinearFunction(torch.autograd.Function):
             V = None
             if has_lora:
                 bt_pad = _pad_rows(lora_B.detach().t().to(torch.bfloat16) * scaling)
-                V = torch.empty(M, 64, dtype=torch.bfloat16, device=gy2.device)
-                if N % 64 == 0:
-                    E.gemm_bf16_tn(gy2, bt_pad, V)
-                else:
-                    V.copy_(gy2 @ bt_pad.t())
+                V = gy2 @ bt_pad.t()  # [M, 64] skinny product: cuBLAS
             if ctx.needs_input_grad[0]:
                 wt = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, True)
                 gx = torch.empty(M, K, dtype=torch.bfloat16, device=gy2.device)

@@ -26,22 +26,42 @@ def rope_reference(x: torch.Tensor, theta: float, sign: float = 1.0) -> torch.Te
     return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1).to(x.dtype)
 
 
+_TABLES = {}
+
+
+def rope_table(S: int, D: int, theta: float, device) -> torch.Tensor:
+    """fp32 ``[S, D/2, 2]`` (cos, sin) of the angles ``pos * theta^(-2i/D)``; the
+    angle is formed in fp64 and rounded to fp32 before cos/sin, as in
+    :func:`rope_reference`.  Cached per (S, D, theta, device)."""
+    key = (S, D, float(theta), str(device))
+    t = _TABLES.get(key)
+    if t is None:
+        half = D // 2
+        inv = theta ** (-torch.arange(0, half, dtype=torch.float64, device=device) * 2.0 / D)
+        pos = torch.arange(S, dtype=torch.float64, device=device)
+        ang = (pos[:, None] * inv[None, :]).float()
+        t = torch.stack([torch.cos(ang), torch.sin(ang)], dim=-1).contiguous()
+        _TABLES[key] = t
+    return t
+
+
 class _Rope(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, theta):
+        cs = rope_table(q.shape[1], q.shape[3], theta, q.device)
         qo = torch.empty_like(q)
         ko = torch.empty_like(k)
-        _ext.ext().rope(q.contiguous(), qo, float(theta), 1.0)
-        _ext.ext().rope(k.contiguous(), ko, float(theta), 1.0)
-        ctx.theta = theta
+        _ext.ext().rope(q.contiguous(), qo, cs, 1.0)
+        _ext.ext().rope(k.contiguous(), ko, cs, 1.0)
+        ctx.cs = cs
         return qo, ko
 
     @staticmethod
     def backward(ctx, gq, gk):
         dq = torch.empty_like(gq)
         dk = torch.empty_like(gk)
-        _ext.ext().rope(gq.contiguous(), dq, float(ctx.theta), -1.0)
-        _ext.ext().rope(gk.contiguous(), dk, float(ctx.theta), -1.0)
+        _ext.ext().rope(gq.contiguous(), dq, ctx.cs, -1.0)
+        _ext.ext().rope(gk.contiguous(), dk, ctx.cs, -1.0)
         return dq, dk, None
 
 
