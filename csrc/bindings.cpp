@@ -11,6 +11,7 @@ void nf4_dequantize(at::Tensor packed, at::Tensor absmax, at::Tensor out, int64_
 void gemm_bf16_tn(at::Tensor a, at::Tensor b, at::Tensor c);
 void gemm_bf16_tn_extra(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor a2, at::Tensor b2);
 std::vector<int64_t> gemm_status(int64_t device);
+void set_gemm_pair_mode(int64_t mode);
 void nf4_to_bf16(at::Tensor packed, at::Tensor absmax, at::Tensor out, int64_t rows, int64_t cols,
                  int64_t blocksize, int64_t qtype, bool transpose);
 // elementwise.cu
@@ -32,6 +33,25 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::opt
                 double gscale);
 void lion_step(at::Tensor master, at::Tensor grad, at::Tensor mom, double lr, double b1, double b2,
                double wd, int64_t seed);
+// p2p.cu
+std::vector<int64_t> peer_alloc(int64_t bytes);
+at::Tensor peer_handle(int64_t ptr);
+int64_t peer_open(at::Tensor handle);
+void peer_close(int64_t ptr);
+void peer_free(int64_t ptr);
+at::Tensor tensor_from_ptr(int64_t ptr, int64_t numel, at::ScalarType dtype, int64_t device);
+std::vector<int64_t> peer_status_read(int64_t flags_ptr);
+int64_t peer_flag_words();
+void rs_adamw(std::vector<int64_t> grads, std::vector<int64_t> params, std::vector<int64_t> flags,
+              int64_t rank, int64_t epoch, int64_t lo, int64_t n, at::Tensor m, at::Tensor v,
+              int64_t grad_is_bf16, double lr, double b1, double b2, double eps, double wd,
+              double bc1, double bc2, double gscale, bool push, int64_t timeout_ms);
+void plan_gather(std::vector<int64_t> src, std::vector<int64_t> flags, int64_t rank, int64_t epoch,
+                 std::vector<int64_t> offsets, std::vector<int64_t> lengths, at::Tensor out,
+                 int64_t timeout_ms);
+void plan_gather_dequant(std::vector<int64_t> psrc, std::vector<int64_t> pstarts,
+                         std::vector<int64_t> asrc, std::vector<int64_t> astarts, int64_t rows,
+                         int64_t cols, int64_t blocksize, int64_t qtype, bool transpose, at::Tensor out);
 #ifdef ZQ_WITH_ATTENTION
 // attention.cu
 void attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, bool causal,
@@ -47,6 +67,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16_tn", &gemm_bf16_tn);
   m.def("gemm_bf16_tn_extra", &gemm_bf16_tn_extra);
   m.def("gemm_status", &gemm_status);
+  m.def("set_gemm_pair_mode", &set_gemm_pair_mode);
   m.def("nf4_to_bf16", &nf4_to_bf16);
   m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
@@ -59,6 +80,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ce_bwd", &ce_bwd);
   m.def("adamw_step", &adamw_step);
   m.def("lion_step", &lion_step);
+  m.def("peer_alloc", &peer_alloc);
+  m.def("peer_handle", &peer_handle);
+  m.def("peer_open", &peer_open);
+  m.def("peer_close", &peer_close);
+  m.def("peer_free", &peer_free);
+  m.def("tensor_from_ptr", &tensor_from_ptr);
+  m.def("peer_status_read", &peer_status_read);
+  m.def("peer_flag_words", &peer_flag_words);
+  m.def("rs_adamw", &rs_adamw);
+  m.def("plan_gather", &plan_gather);
+  m.def("plan_gather_dequant", &plan_gather_dequant);
 #ifdef ZQ_WITH_ATTENTION
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_bwd", &attn_bwd);

@@ -225,6 +225,192 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 }
 
 // ----------------------------------------------------------------------------
+// CTA-pair variant (cluster of 2, tcgen05 cta_group::2): one MMA of M=256 x BN
+// per k-step, issued by the leader CTA.  Each CTA stages its own 128 rows of A
+// and its own BN/2 rows of B (so every SM reads half of B from its shared
+// memory), and holds its 128 rows x BN accumulator columns in its own TMEM.
+//   full[s]   (leader): one arrive.expect_tx by the leader's producer for both
+//             CTAs' bytes; both CTAs' TMA loads complete_tx on it.
+//   empty[s]  (each CTA): the leader's commits (one per CTA address) free the
+//             stage in both CTAs.
+//   tfull[b]  (each CTA): the leader's commits after a tile's last k-step.
+//   tempty[b] (leader): 2 x 128 epilogue threads of both CTAs arrive.
+// ----------------------------------------------------------------------------
+template <int BN, int STAGES>
+struct PairSmem {
+  static constexpr int kABytes = kBM * kBK * 2;           // this CTA's 128 rows of A
+  static constexpr int kBBytes = (BN / 2) * kBK * 2;      // this CTA's half of B
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kBytes = kBarOffset + 256 + 1024;
+};
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
+                    GemmArgs args) {
+  using L = PairSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;
+  uint64_t* tempty_bar = tfull_bar + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t cr = cluster_ctarank();        // 0 = leader
+  const uint32_t peer = cr ^ 1u;
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+  const int num_tiles = args.tiles_m * args.tiles_n;  // tiles of 256 x BN
+  const int main_k_tiles = args.K / kBK;
+  const int k_tiles = main_k_tiles + (args.extra_k16 > 0 ? 1 : 0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 2 * 4 * 32);
+    }
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    if (args.extra_k16 > 0) {
+      prefetch_tmap(&tmA2);
+      prefetch_tmap(&tmB2);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer (both CTAs)
+    if (lane == 0) {
+      bool ok = true;
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
+        int tm, tn;
+        tile_coords(tile, args.tiles_m, args.tiles_n, tm, tn);
+        const int arow = tm * (2 * kBM) + (int)cr * kBM;
+        const int brow = tn * BN + (int)cr * (BN / 2);
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, args.status, kErrProducer)) { ok = false; break; }
+          uint8_t* sa = smem + stage * L::kStageBytes;
+          uint8_t* sb = sa + L::kABytes;
+          const uint32_t leader_full = map_to_cta(smem_u32(&full_bar[stage]), 0);
+          if (cr == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * L::kStageBytes);
+          if (kt < main_k_tiles) {
+            tma_load_2d_pair(sa, &tmA, leader_full, kt * kBK, arow);
+            tma_load_2d_pair(sb, &tmB, leader_full, kt * kBK, brow);
+          } else {
+            tma_load_2d_pair(sa, &tmA2, leader_full, 0, arow);
+            tma_load_2d_pair(sb, &tmB2, leader_full, 0, brow);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+      for (int i = 0; i < STAGES; ++i) {  // drain: every issued load has landed
+        mbar_wait(&empty_bar[stage], phase ^ 1, nullptr, 0);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer (leader only)
+    if (lane == 0 && cr == 0) {
+      bool ok = true;
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      constexpr uint32_t idesc = umma_idesc_bf16(2 * kBM, BN);
+      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters, ++it) {
+        const int buf = it & 1;
+        if (!mbar_wait(&tempty_bar[buf], ((it >> 1) & 1) ^ 1, args.status, kErrMmaAcc)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * 256);
+        for (int kt = 0; kt < k_tiles; ++kt) {
+          if (!mbar_wait(&full_bar[stage], phase, args.status, kErrMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
+          const uint32_t b_addr = a_addr + L::kABytes;
+          const int nk = kt < main_k_tiles ? kBK / 16 : args.extra_k16;
+          for (int kk = 0; kk < nk; ++kk) {
+            umma_f16_ss_pair(d_tmem, umma_desc_sw128_kmajor(a_addr + kk * 32),
+                             umma_desc_sw128_kmajor(b_addr + kk * 32), idesc,
+                             (kt > 0 || kk > 0) ? 1u : 0u);
+          }
+          const uint32_t e = smem_u32(&empty_bar[stage]);
+          umma_commit_pair(map_to_cta(e, 0));
+          umma_commit_pair(map_to_cta(e, 1));
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        const uint32_t f = smem_u32(&tfull_bar[buf]);
+        umma_commit_pair(map_to_cta(f, 0));
+        umma_commit_pair(map_to_cta(f, 1));
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (both CTAs)
+    const int q = warp & 3;
+    const int row_in_tile = (int)cr * kBM + q * 32 + lane;
+    int it = 0;
+    bool ok = true;
+    for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters, ++it) {
+      int tm, tn;
+      tile_coords(tile, args.tiles_m, args.tiles_n, tm, tn);
+      const int buf = it & 1;
+      if (!mbar_wait(&tfull_bar[buf], (it >> 1) & 1, args.status, kErrEpi)) { ok = false; break; }
+      tc_fence_after();
+      const int m = tm * (2 * kBM) + row_in_tile;
+      const int n0 = tn * BN;
+      __nv_bfloat16* crow = args.C + (int64_t)m * args.ldc;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256 + c * 32), r);
+        tmem_ld_wait();
+        const int ncol = n0 + c * 32;
+        if (m < args.M) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            const int nc = ncol + v * 8;
+            if (nc + 8 <= args.N) {
+              uint4 o;
+              o.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
+              o.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
+              o.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
+              o.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
+              *reinterpret_cast<uint4*>(crow + nc) = o;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(map_to_cta(smem_u32(&tempty_bar[buf]), 0));
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its pair may still touch its smem/TMEM
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 512);
+  }
+}
+
+// ----------------------------------------------------------------------------
 // NF4 -> bf16 operand producers (memory-bound).  `transpose=false` writes
 // W [N,K] as is; `transpose=true` writes Wᵀ [K,N] (for the input-gradient GEMM)
 // through a 64x64 shared-memory tile so both the packed reads and the bf16
@@ -391,6 +577,35 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+template <int BN, int STAGES>
+static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2,
+                             const CUtensorMap& tb2, GemmArgs args, cudaStream_t stream, int sms) {
+  using L = PairSmem<BN, STAGES>;
+  static bool configured[64] = {false};
+  int dev;
+  C10_CUDA_CHECK(cudaGetDevice(&dev));
+  if (!configured[dev]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_tn_pair_kernel<BN, STAGES>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
+    configured[dev] = true;
+  }
+  const int tiles = args.tiles_m * args.tiles_n;
+  const int clusters = std::max(1, std::min(tiles, sms / 2));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = L::kBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tn_pair_kernel<BN, STAGES>, ta, tb, ta2, tb2, args));
+}
+
 // Pick the N tile that minimises wave quantisation over the SMs.
 static int choose_bn(int M, int N, int sms) {
   const int tm = (M + kBM - 1) / kBM;
@@ -406,6 +621,27 @@ static int choose_bn(int M, int N, int sms) {
   }
   return best_bn;
 }
+
+static int g_pair_mode = 1;  // 1: use the CTA-pair kernel when M >= 256 (set_gemm_pair_mode)
+
+// CTA-pair tiles are 256 x BN; BN in {256, 192, 128} (BN/2 rows of B per CTA)
+static int choose_bn_pair(int M, int N, int sms) {
+  const int tm = (M + 2 * kBM - 1) / (2 * kBM);
+  const int pairs = std::max(1, sms / 2);
+  double best = 1e30;
+  int best_bn = 256;
+  // measured on B200: 256x192 pair tiles run slower per tile than 256x256, so
+  // only 256 and 128 are considered
+  for (int bn : {256, 128}) {
+    const int tn = (N + bn - 1) / bn;
+    const int waves = (tm * tn + pairs - 1) / pairs;
+    const double cost = (double)waves * bn * (bn == 128 ? 1.1 : 1.0);
+    if (cost < best - 1e-9) { best = cost; best_bn = bn; }
+  }
+  return best_bn;
+}
+
+void set_gemm_pair_mode(int64_t mode) { g_pair_mode = (int)mode; }
 
 static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
                       const c10::optional<at::Tensor>& a2, const c10::optional<at::Tensor>& b2) {
@@ -425,21 +661,23 @@ static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
   const at::cuda::CUDAGuard guard(a.device());
   const int dev = a.get_device();
   const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
-  const int bn = choose_bn((int)M, (int)N, sms);
+  const bool pair = g_pair_mode != 0 && M >= 2 * kBM;
+  const int bn = pair ? choose_bn_pair((int)M, (int)N, sms) : choose_bn((int)M, (int)N, sms);
 
   GemmArgs args;
   args.M = (int)M;
   args.N = (int)N;
   args.K = (int)K;
   args.extra_k16 = 0;
-  args.tiles_m = (int)((M + kBM - 1) / kBM);
+  args.tiles_m = pair ? (int)((M + 2 * kBM - 1) / (2 * kBM)) : (int)((M + kBM - 1) / kBM);
   args.tiles_n = (int)((N + bn - 1) / bn);
   args.C = reinterpret_cast<__nv_bfloat16*>(c.data_ptr<at::BFloat16>());
   args.ldc = c.stride(0);
   args.status = status_buffer(dev);
 
   CUtensorMap ta = make_tmap_bf16(a.data_ptr(), M, K, a.stride(0), kBM);
-  CUtensorMap tb = make_tmap_bf16(b.data_ptr(), N, K, b.stride(0), bn);
+  const int b_box = pair ? bn / 2 : bn;
+  CUtensorMap tb = make_tmap_bf16(b.data_ptr(), N, K, b.stride(0), b_box);
   CUtensorMap ta2 = ta, tb2 = tb;
   if (a2.has_value() && a2->defined()) {
     TORCH_CHECK(b2.has_value() && b2->defined(), "gemm: extra slab needs both operands");
@@ -450,10 +688,16 @@ static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
                     x2.stride(1) == 1 && y2.stride(1) == 1,
                 "extra slab operands must be [M,64] and [N,64] row-major");
     ta2 = make_tmap_bf16(x2.data_ptr(), M, 64, x2.stride(0), kBM);
-    tb2 = make_tmap_bf16(y2.data_ptr(), N, 64, y2.stride(0), bn);
+    tb2 = make_tmap_bf16(y2.data_ptr(), N, 64, y2.stride(0), b_box);
     args.extra_k16 = 4;
   }
   auto stream = at::cuda::getCurrentCUDAStream();
+  if (pair) {
+    if (bn == 256) launch_gemm_pair<256, 7>(ta, tb, ta2, tb2, args, stream, sms);
+    else if (bn == 192) launch_gemm_pair<192, 8>(ta, tb, ta2, tb2, args, stream, sms);
+    else launch_gemm_pair<128, 9>(ta, tb, ta2, tb2, args, stream, sms);
+    return;
+  }
   if (bn == 256) launch_gemm<256, 4>(ta, tb, ta2, tb2, args, stream, sms);
   else if (bn == 192) launch_gemm<192, 5>(ta, tb, ta2, tb2, args, stream, sms);
   else launch_gemm<128, 6>(ta, tb, ta2, tb2, args, stream, sms);

@@ -1,0 +1,157 @@
+"""Peer-memory kernels over NVLink: the fused reduce-scatter + AdamW + all-gather and
+the plan-driven NF4 gather / gather+dequantise, against the NCCL path.  Multi-GPU
+cases run as one process per GPU and skip with fewer than two GPUs; the bounded-wait
+case runs on one GPU with a peer flag that nothing ever sets."""
+
+import datetime
+import os
+import socket
+import tempfile
+import time
+import traceback
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _spawn_worker(rank, world, port, fn_name, errfile):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    try:
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", rank))
+        globals()[fn_name](rank, world)
+        dist.barrier()
+    except BaseException:
+        with open(f"{errfile}.{rank}", "w") as f:
+            f.write(traceback.format_exc())
+        raise
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def _run(fn_name, world=2):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+
+    err = tempfile.mktemp()
+    try:
+        mp.spawn(_spawn_worker, args=(world, _free_port(), fn_name, err), nprocs=world, join=True)
+    except Exception:
+        msgs = [open(f"{err}.{r}").read() for r in range(world) if os.path.exists(f"{err}.{r}")]
+        raise AssertionError("\n".join(msgs) or "worker failed")
+
+
+def w_fused_adamw(rank, world):
+    import zeroq_b200 as zq
+
+    torch.manual_seed(0)
+    shapes = [(333, 7), (1001,), (16, 64)]
+    init = [torch.randn(s, device="cuda") for s in shapes]
+    pf = [torch.nn.Parameter(t.clone()) for t in init]
+    pn = [torch.nn.Parameter(t.clone()) for t in init]
+    fused = zq.ShardedAdamW(pf, lr=1e-2, weight_decay=0.05, backend="fused")
+    nccl = zq.ShardedAdamW(pn, lr=1e-2, weight_decay=0.05, backend="nccl")
+    assert fused.backend == "fused", fused._peer_error
+    for step in range(3):
+        g = torch.Generator(device="cuda").manual_seed(10 * step + rank)
+        for a, b in zip(pf, pn):
+            gr = torch.randn(a.shape, device="cuda", generator=g)
+            a.grad.copy_(gr)
+            b.grad.copy_(gr)
+        fused.step()
+        nccl.step()
+        fused.zero_grad()
+        nccl.zero_grad()
+    torch.cuda.synchronize()
+    fused._peer.flags.check()
+    for a, b in zip(pf, pn):
+        assert torch.allclose(a.detach(), b.detach(), atol=1e-6, rtol=1e-5)
+
+
+def w_peer_gather(rank, world):
+    import zeroq_b200 as zq
+    from zeroq_b200.ops.qlinear import Linear4bit
+    from zeroq_b200.parallel.peer import PeerShardPool
+
+    for hetero in (False, True):
+        torch.manual_seed(1)
+        m = torch.nn.Sequential(Linear4bit(512, 384, device="cuda"), Linear4bit(384, 320, device="cuda"))
+        for lin in m:
+            lin.weight = torch.nn.Parameter(torch.randn(lin.out_features, lin.in_features,
+                                                        device="cuda") * 0.02, requires_grad=False)
+        cfg = zq.ZeroQConfig(exclude_modules=[], backend="nccl")
+        if hetero:
+            coord = zq.HeteroZeroQCoordinator(cfg, rank_weights=[3.0, 1.0])
+            zq.HeteroZeroQModuleWrapper(m, coord).partition()
+        else:
+            coord = zq.ZeroQCoordinator(cfg)
+            zq.ZeroQModuleWrapper(m, coord).partition()
+        ref = {}
+        from zeroq_b200.parallel import comm
+        for p in coord._params.values():
+            ref[p.param_id] = comm.gather_nf4(p, async_op=False).wait()
+        pool = PeerShardPool(coord)
+        for p in coord._params.values():
+            pk, am = pool.gather(p).wait()
+            assert torch.equal(pk, ref[p.param_id][0]) and torch.equal(am, ref[p.param_id][1])
+            rows, cols = p.original_shape
+            for transpose in (False, True):
+                op = pool.gather_dequant(p, rows, cols, transpose)
+                full = torch.empty(rows * cols, dtype=torch.bfloat16, device="cuda")
+                from zeroq_b200.ops import _ext
+                _ext.ext().nf4_to_bf16(pk, am, full, rows, cols, 64, 0, transpose)
+                assert torch.equal(op.reshape(-1), full)
+        torch.cuda.synchronize()
+        pool.close()
+
+
+def test_fused_reduce_scatter_adamw_matches_nccl():
+    _run("w_fused_adamw", 2)
+
+
+def test_peer_gather_and_gather_dequant_match_nccl():
+    _run("w_peer_gather", 2)
+
+
+def test_peer_wait_times_out_with_error_status(cuda):
+    """A barrier whose peer never signals: the kernel gives up after ~1 s, records
+    an error code the host reads, and the context stays usable."""
+    from zeroq_b200.ops import _ext
+
+    E = _ext.ext()
+    flags = int(E.peer_alloc(4 * E.peer_flag_words())[0])
+    grads = torch.zeros(1024, device=cuda)
+    params = torch.zeros(1024, device=cuda)
+    m = torch.zeros(512, device=cuda)
+    v = torch.zeros(512, device=cuda)
+    try:
+        t0 = time.time()
+        # world 2, but "rank 1" is this same flag block: nothing ever sets slot 1
+        E.rs_adamw([grads.data_ptr()] * 2, [params.data_ptr()] * 2, [flags, flags], 0, 1, 0, 512,
+                   m, v, 0, 1e-3, 0.9, 0.999, 1e-8, 0.0, 0.1, 0.001, 0.5, True, 1000)
+        torch.cuda.synchronize()
+        elapsed = time.time() - t0
+        code, detail = E.peer_status_read(flags)
+        assert code == 201 and detail == 1, (code, detail)
+        assert elapsed < 30
+        assert torch.all(params == 0)  # no update after a failed barrier
+        x = torch.ones(10, device=cuda)
+        assert float((x * 2).sum()) == 20.0  # the context is still usable
+    finally:
+        E.peer_free(flags)

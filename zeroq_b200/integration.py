@@ -141,6 +141,12 @@ def prepare_model_for_zeroq(model: nn.Module, config: Optional[ZeroQConfig] = No
     wrapper.partition()
     if hetero:
         coordinator.verify_registration_consistency()
+    if (config.resolved_backend() == "fused" and coordinator.world_size > 1
+            and torch.cuda.is_available() and dist.is_initialized()
+            and dist.get_backend(process_group) == "nccl"):
+        from .parallel.peer import PeerShardPool
+
+        coordinator.peer_pool = PeerShardPool(coordinator, process_group)
     if getattr(config, "compute_in_4bit", False):
         convert_to_4bit_compute(model, coordinator, wrapper)
         wrapper = None

@@ -34,7 +34,11 @@ from ..ops.optim import adamw_step
 
 
 class FlatParams:
-    def __init__(self, params: Iterable[torch.nn.Parameter], pad_to: int = 1, device=None):
+    """``alloc(numel, dtype, role)`` (role ``"data"`` then ``"grad"``) may place the
+    buffers elsewhere, e.g. in peer memory for the fused optimizer."""
+
+    def __init__(self, params: Iterable[torch.nn.Parameter], pad_to: int = 1, device=None,
+                 alloc=None):
         self.params: List[torch.nn.Parameter] = [p for p in params]
         if not self.params:
             raise ValueError("FlatParams needs at least one parameter")
@@ -44,8 +48,12 @@ class FlatParams:
         device = device or self.params[0].device
         self.numel = sum(p.numel() for p in self.params)
         self.padded = (self.numel + pad_to - 1) // pad_to * pad_to
-        self.data = torch.zeros(self.padded, dtype=torch.float32, device=device)
-        self.grad = torch.zeros(self.padded, dtype=torch.float32, device=device)
+        if alloc is None:
+            self.data = torch.zeros(self.padded, dtype=torch.float32, device=device)
+            self.grad = torch.zeros(self.padded, dtype=torch.float32, device=device)
+        else:
+            self.data = alloc(self.padded, torch.float32, "data")
+            self.grad = alloc(self.padded, torch.float32, "grad")
         self.offsets = []
         off = 0
         with torch.no_grad():
@@ -78,7 +86,22 @@ class ShardedAdamW:
         self.pg = process_group
         self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(process_group) if dist.is_initialized() else 0
-        self.flat = FlatParams(params, pad_to=self.world)
+        params = list(params)
+        on_cuda = bool(params) and params[0].is_cuda
+        if backend == "auto":
+            backend = "fused" if on_cuda and self.world > 1 else "nccl"
+        alloc = None
+        self._peer_error = None
+        if backend == "fused" and self.world > 1:
+            try:
+                from .peer import peer_flat_allocator
+
+                alloc = peer_flat_allocator(process_group)
+            except Exception as e:  # no IPC / extension: NCCL path
+                self._peer_error = repr(e)
+                backend = "nccl"
+        # pad so that every rank's shard is a whole number of 16-byte vectors
+        self.flat = FlatParams(params, pad_to=self.world * 4, alloc=alloc)
         self.lr, self.betas, self.eps, self.wd = lr, betas, eps, weight_decay
         self.max_grad_norm = max_grad_norm
         self.shard = self.flat.padded // self.world
@@ -88,10 +111,10 @@ class ShardedAdamW:
         self.grad_shard = torch.zeros(self.shard, dtype=torch.float32, device=dev) \
             if self.world > 1 else None
         self.step_count = 0
-        if backend == "auto":
-            backend = "fused" if dev.type == "cuda" and self.world > 1 else "nccl"
         self.backend = backend
-        self._peer = None
+        self._peer = getattr(self.flat.grad, "_zq_peer", None) if backend == "fused" else None
+        if backend == "fused" and self._peer is None:
+            self.backend = "nccl"
         self.last_grad_norm: Optional[torch.Tensor] = None
 
     @property
@@ -124,30 +147,23 @@ class ShardedAdamW:
             return
         lo = self.rank * self.shard
         mine = self.flat.data[lo:lo + self.shard]
-        if self.backend == "fused" and self._peer_ready():
+        if self.backend == "fused":
+            if self.max_grad_norm is not None:
+                raise NotImplementedError("gradient clipping runs on the nccl backend")
+            # one kernel: peers' gradient slices summed over NVLink, AdamW, and the
+            # updated shard written into every peer's parameter buffer
             self._peer.reduce_scatter_adamw(self, mine)
-        else:
-            dist.reduce_scatter_tensor(self.grad_shard, self.flat.grad, op=dist.ReduceOp.SUM,
-                                       group=self.pg)
-            scale = self._clip_scale(self.grad_shard, 1.0 / self.world) / self.world
-            adamw_step(mine, self.grad_shard, self.exp_avg, self.exp_avg_sq, lr=self.lr,
-                       beta1=b1, beta2=b2, eps=self.eps, weight_decay=self.wd,
-                       step=self.step_count, grad_scale=scale)
+            return
+        dist.reduce_scatter_tensor(self.grad_shard, self.flat.grad, op=dist.ReduceOp.SUM,
+                                   group=self.pg)
+        scale = self._clip_scale(self.grad_shard, 1.0 / self.world) / self.world
+        adamw_step(mine, self.grad_shard, self.exp_avg, self.exp_avg_sq, lr=self.lr,
+                   beta1=b1, beta2=b2, eps=self.eps, weight_decay=self.wd,
+                   step=self.step_count, grad_scale=scale)
         # NCCL gathers in place when the input is this rank's slice of the output;
         # other backends get a private copy of the shard.
         src = mine if self.flat.data.is_cuda else mine.clone()
         dist.all_gather_into_tensor(self.flat.data, src, group=self.pg)
-
-    def _peer_ready(self) -> bool:
-        if self._peer is None:
-            try:
-                from .peer import PeerReduceScatterAdamW
-
-                self._peer = PeerReduceScatterAdamW.create(self.flat.grad, self.pg)
-            except Exception as e:  # no peer access / extension: stay on NCCL
-                self._peer = False
-                self._peer_error = repr(e)
-        return bool(self._peer)
 
     def state_dict(self) -> dict:
         return {"step": self.step_count, "exp_avg": self.exp_avg.detach().cpu(),

@@ -1,0 +1,234 @@
+"""Peer memory over NVLink / NVSwitch: IPC-shared buffers and the kernels that use them.
+
+:class:`PeerBuffer` is one ``cudaMalloc`` allocation per rank, opened on every
+other rank of the node through CUDA IPC handles that are exchanged once over
+the process group.  The kernels in ``csrc/p2p.cu`` then read and write peers'
+buffers with ordinary loads and stores.
+
+* :class:`PeerReduceScatterAdamW` - the optimizer path of
+  :class:`~zeroq_b200.parallel.optimizer.ShardedAdamW` with ``backend="fused"``:
+  one kernel per rank sums every peer's gradient slice of its shard, scales by
+  1/W, applies AdamW, and writes the updated shard into every peer's parameter
+  buffer (reduce-scatter + update + all-gather in one pass).  It replaces the
+  reference's per-tensor NCCL all-reduce + torch AdamW
+  (``examples/train_32b_maxwell.py:472-475``, ``src/gradient_sync.py:489-532``).
+* :class:`PeerShardPool` - holds every NF4 shard of a coordinator in one peer
+  buffer per rank; ``gather(zq)`` assembles a parameter's packed bytes and absmax
+  straight from the owners' buffers by their shard plans (uniform or weighted),
+  with no padding, staging or unpad copies (reference
+  ``src/coordinator.py:385-533``, ``src/hetero/zeroq_hetero.py:312-452``), and
+  ``gather_dequant(zq)`` additionally expands to the bf16 GEMM operand in the
+  same kernel.
+
+Cross-rank synchronisation is by epoch flags with bounded waits; a timeout
+leaves an error code that :meth:`PeerFlags.check` raises on the host.
+"""
+
+from __future__ import annotations
+
+from typing import Dict, List, Optional
+
+import torch
+import torch.distributed as dist
+
+from ..ops import _ext
+
+
+def _group_info(group):
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+class PeerBuffer:
+    """A device buffer of ``nbytes`` on every rank, mapped into every rank."""
+
+    def __init__(self, nbytes: int, group=None):
+        E = _ext.ext()
+        self.group = group
+        self.rank, self.world = _group_info(group)
+        self.nbytes = max(16, (int(nbytes) + 255) // 256 * 256)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.local_ptr = int(E.peer_alloc(self.nbytes)[0])
+        handle = bytes(E.peer_handle(self.local_ptr).numpy().tobytes())
+        handles: List[bytes] = [b""] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self.ptrs: List[int] = []
+        for q, h in enumerate(handles):
+            if q == self.rank:
+                self.ptrs.append(self.local_ptr)
+            else:
+                t = torch.frombuffer(bytearray(h), dtype=torch.uint8)
+                self.ptrs.append(int(E.peer_open(t)))
+        self._closed = False
+
+    def tensor(self, numel: int, dtype: torch.dtype, byte_offset: int = 0) -> torch.Tensor:
+        esz = torch.empty(0, dtype=dtype).element_size()
+        if byte_offset % esz or byte_offset + numel * esz > self.nbytes:
+            raise ValueError("view outside the peer buffer")
+        return _ext.ext().tensor_from_ptr(self.local_ptr + byte_offset, numel, dtype,
+                                          self.device.index)
+
+    def close(self):
+        if self._closed:
+            return
+        E = _ext.ext()
+        torch.cuda.synchronize()
+        for q, p in enumerate(self.ptrs):
+            if q != self.rank:
+                E.peer_close(p)
+        E.peer_free(self.local_ptr)
+        self._closed = True
+
+
+class PeerFlags(PeerBuffer):
+    """Flag words for the cross-rank barriers of the peer kernels."""
+
+    def __init__(self, group=None):
+        super().__init__(4 * int(_ext.ext().peer_flag_words()), group)
+        self.epoch = 0
+
+    def next_epoch(self) -> int:
+        self.epoch += 1
+        return self.epoch
+
+    def check(self):
+        code, detail = _ext.ext().peer_status_read(self.local_ptr)
+        if code:
+            raise RuntimeError(f"peer collective on rank {self.rank} failed: code {code} "
+                               f"(detail {detail}); a peer did not arrive within the wait limit")
+
+
+class PeerReduceScatterAdamW:
+    """Fused reduce-scatter + AdamW + all-gather over peer memory."""
+
+    def __init__(self, grad_buf: PeerBuffer, param_buf: PeerBuffer, flags: PeerFlags,
+                 grad_is_bf16: bool = False):
+        self.grad_buf, self.param_buf, self.flags = grad_buf, param_buf, flags
+        self.grad_is_bf16 = grad_is_bf16
+
+    @classmethod
+    def create(cls, flat_grad: torch.Tensor, group):
+        owner = getattr(flat_grad, "_zq_peer", None)
+        if owner is None:
+            raise RuntimeError("flat gradient is not in peer memory")
+        return owner
+
+    def run(self, lo: int, n: int, m: torch.Tensor, v: torch.Tensor, *, lr, beta1, beta2, eps,
+            weight_decay, step, grad_scale, push: bool = True, timeout_ms: int = 0):
+        bc1 = 1.0 - beta1 ** step
+        bc2 = 1.0 - beta2 ** step
+        _ext.ext().rs_adamw(self.grad_buf.ptrs, self.param_buf.ptrs, self.flags.ptrs,
+                            self.flags.rank, self.flags.next_epoch(), int(lo), int(n), m, v,
+                            1 if self.grad_is_bf16 else 0, float(lr), float(beta1), float(beta2),
+                            float(eps), float(weight_decay), float(bc1), float(bc2),
+                            float(grad_scale), bool(push), int(timeout_ms))
+
+    def reduce_scatter_adamw(self, opt, mine: torch.Tensor):
+        b1, b2 = opt.betas
+        lo = opt.rank * opt.shard
+        self.run(lo, opt.shard, opt.exp_avg, opt.exp_avg_sq, lr=opt.lr, beta1=b1, beta2=b2,
+                 eps=opt.eps, weight_decay=opt.wd, step=opt.step_count,
+                 grad_scale=1.0 / opt.world, push=True)
+
+
+def peer_flat_allocator(group):
+    """Allocator for :class:`FlatParams`: data and grad in peer memory, plus the fused
+    optimizer object attached to the grad tensor."""
+    state: Dict[str, PeerBuffer] = {}
+
+    def alloc(numel: int, dtype: torch.dtype, role: str) -> torch.Tensor:
+        buf = PeerBuffer(numel * torch.empty(0, dtype=dtype).element_size(), group)
+        state[role] = buf
+        t = buf.tensor(numel, dtype)
+        t.zero_()
+        t._zq_peer_buffer = buf
+        if role == "grad" and "data" in state:
+            t._zq_peer = PeerReduceScatterAdamW(buf, state["data"], PeerFlags(group))
+        return t
+
+    return alloc
+
+
+class PeerShardPool:
+    """Every NF4 shard of a coordinator, in one peer buffer per rank.
+
+    Shard byte offsets are computed identically on every rank from the shard
+    plans (which every rank knows), so rank ``q``'s piece of parameter ``p``
+    lives at ``ptrs[q] + offset_q(p)`` with no per-parameter exchange.
+    """
+
+    ALIGN = 16
+
+    def __init__(self, coordinator, group=None):
+        self.group = group if group is not None else coordinator.process_group
+        self.rank, self.world = _group_info(self.group)
+        params = [p for p in coordinator._params.values() if p.local_packed is not None]
+        self.offsets: Dict[int, List[List[int]]] = {}   # pid -> [rank] -> [packed_off, absmax_off]
+        ends = [0] * self.world
+        for zq in params:
+            entry = []
+            for q in range(self.world):
+                po = ends[q]
+                ends[q] = (po + zq.packed_plan.lengths[q] + self.ALIGN - 1) // self.ALIGN * self.ALIGN
+                ao = ends[q]
+                ends[q] = (ao + 4 * zq.absmax_plan.lengths[q] + self.ALIGN - 1) // self.ALIGN * self.ALIGN
+                entry.append([po, ao])
+            self.offsets[zq.param_id] = entry
+        self.buf = PeerBuffer(max(ends + [16]), self.group)
+        self.flags = PeerFlags(self.group)
+        for zq in params:
+            po, ao = self.offsets[zq.param_id][self.rank]
+            pk = self.buf.tensor(zq.local_packed.numel(), torch.uint8, po)
+            am = self.buf.tensor(zq.local_absmax.numel(), torch.float32, ao)
+            pk.copy_(zq.local_packed)
+            am.copy_(zq.local_absmax)
+            zq.local_packed, zq.local_absmax = pk, am
+            zq._peer_pool = self
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+
+    def _segments(self, zq, which: int):
+        plan = zq.packed_plan if which == 0 else zq.absmax_plan
+        esz = 1 if which == 0 else 4
+        src = [self.buf.ptrs[q] + self.offsets[zq.param_id][q][which] for q in range(self.world)]
+        offs = [o * esz for o in plan.offsets]
+        lens = [n * esz for n in plan.lengths]
+        return src, offs, lens
+
+    def gather(self, zq):
+        """Assembled ``(packed, absmax)`` of ``zq`` (shards are static between
+        re-quantisations, so no barrier is needed)."""
+        from .comm import GatherHandle
+
+        E = _ext.ext()
+        packed = torch.empty(zq.packed_plan.total, dtype=torch.uint8, device=zq.local_packed.device)
+        absmax = torch.empty(zq.absmax_plan.total, dtype=torch.float32, device=zq.local_packed.device)
+        for which, out in ((0, packed), (1, absmax)):
+            src, offs, lens = self._segments(zq, which)
+            E.plan_gather(src, self.flags.ptrs, self.rank, 0, offs, lens, out, 0)
+        return GatherHandle([lambda: packed, lambda: absmax])
+
+    def gather_dequant(self, zq, rows: int, cols: int, transpose: bool = False,
+                       out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """bf16 operand ``W [rows, cols]`` (or ``Wᵀ``) read straight from the owners'
+        NF4 shards over NVLink: the gather and the dequantisation are one kernel."""
+        from ..ops.nf4 import QUANT_TYPE_ID
+
+        psrc, _, _ = self._segments(zq, 0)
+        asrc, _, _ = self._segments(zq, 1)
+        if out is None:
+            out = torch.empty(rows * cols, dtype=torch.bfloat16, device=zq.local_packed.device)
+        m = zq._quant_meta
+        _ext.ext().plan_gather_dequant(psrc, list(zq.packed_plan.offsets), asrc,
+                                       list(zq.absmax_plan.offsets), rows, cols,
+                                       int(m["blocksize"]), QUANT_TYPE_ID[m["quant_type"]],
+                                       bool(transpose), out)
+        return out.view(cols, rows) if transpose else out.view(rows, cols)
+
+    def sync_after_update(self):
+        """Barrier after shards were re-quantised in place (training mode)."""
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+
+    def close(self):
+        self.buf.close()
+        self.flags.close()
