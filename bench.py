@@ -48,6 +48,25 @@ def _measured_peaks():
                 "source": "fallback"}
 
 
+# name -> (model preset, lora r, lora targets or None, batch, seq, mode, description)
+CONFIGS = {
+    "4.7b": ("4.7b", 16, None, 8, 1024, "4bit-once",
+             "NF4 4-bit compute (weights gathered once, resident), LoRA r=16 on every "
+             "projection + RMSNorm weights, AdamW"),
+    "qwen7b-hetero": ("qwen2.5-7b", 16, ("q_proj", "k_proj", "v_proj", "o_proj"), 4, 2048,
+                      "hetero",
+                      "Qwen2.5-7B shape, frozen NF4 base sharded by rank weights "
+                      "[2,2,1,1,1,1,1,1] and gathered per use (peer plan gather), LoRA r=16 "
+                      "alpha 32 on q/k/v/o, AdamW"),
+    "qwen32b-gather": ("qwen2.5-32b", 64, ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj",
+                                          "up_proj", "down_proj"), 2, 4096, "gather",
+                       "Qwen2.5-32B shape, NF4 shards gathered per layer with one layer of "
+                       "prefetch and released after use, activation checkpointing, LoRA r=64 "
+                       "on all linears, AdamW"),
+}
+HETERO_WEIGHTS = [2.0, 2.0, 1.0, 1.0, 1.0, 1.0, 1.0, 1.0]
+
+
 def run_reference(args):
     """The reference's engine cannot be constructed on this image (see reason)."""
     ref = os.path.join(os.path.dirname(os.path.abspath(__file__)), "baseline", "_ref")
@@ -76,10 +95,11 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--model", default="4.7b")
-    ap.add_argument("--batch", type=int, default=8)
-    ap.add_argument("--seq", type=int, default=1024)
-    ap.add_argument("--lora-r", type=int, default=16)
+    ap.add_argument("--config", default="4.7b", choices=sorted(CONFIGS),
+                    help="4.7b: the headline; qwen7b-hetero / qwen32b-gather: the other "
+                         "model configs (gather/release paths)")
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--seq", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--torch-profile", default=None,
                     help="after timing, profile one more step and write a per-kernel table here")
@@ -111,18 +131,26 @@ def main():
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}", file=sys.stderr)
     _ext.ext()
 
-    cfg = get_config(args.model, lora_r=args.lora_r, lora_alpha=2.0 * args.lora_r)
+    preset, lora_r, targets, B0, S0, mode, desc = CONFIGS[args.config]
+    overrides = dict(lora_r=lora_r, lora_alpha=2.0 * lora_r)
+    if targets is not None:
+        overrides["lora_targets"] = targets
+    cfg = get_config(preset, **overrides)
     model = DecoderLM(cfg, device=device)
     model.init_dense_(std=0.02, seed=1234)  # identical on every rank
     zq = ZeroQConfig(compute_dtype=torch.bfloat16, compute_in_4bit=True, double_quant=False,
+                     gather_once=(mode == "4bit-once"), prefetch_count=1, async_gather=True,
                      exclude_modules=["lm_head", "embed_tokens"], backend="auto")
-    initialize(model, zq, trainable_patterns=("lora_", "norm"))
+    rank_weights = HETERO_WEIGHTS[:world] if mode == "hetero" else None
+    trainable = ("lora_", "norm") if mode == "4bit-once" else ("lora_",)
+    initialize(model, zq, trainable_patterns=trainable, rank_weights=rank_weights)
     torch.cuda.empty_cache()
     opt = ShardedAdamW(model.trainable_parameters(), lr=1e-4, betas=(0.9, 0.999),
                        weight_decay=0.0)
     trainer = Trainer(model, opt, device)
 
-    B, S = args.batch, args.seq
+    B = args.batch or B0
+    S = args.seq or S0
     x_host, y_host = synthetic_batch(B, S, cfg.vocab_size, seed=1000 + rank)
     x_dev, y_dev = x_host.to(device), y_host.to(device)
 
@@ -165,15 +193,16 @@ def main():
         "ms_per_step": round(ms / args.steps, 3),
         "higher_is_better": True,
         "scaling": "weak",
-        "vs_baseline": round(value / BASELINE_TOK_S, 1),
+        "vs_baseline": round(value / BASELINE_TOK_S, 1) if args.config == "4.7b" else None,
         "dtype": "bf16",
         "data": "synthetic (uniform random token ids; random-init N(0,0.02) weights)",
         "impl": "ours",
         "config": {
-            "model": f"{args.model} decoder (d={cfg.d_model}, {cfg.n_layers} layers, "
-                     f"{cfg.n_heads}x{cfg.head_dim} heads, {cfg.ffn_act} FFN {cfg.ffn_dim}, "
-                     f"vocab {cfg.vocab_size}), NF4 4-bit compute, LoRA r={args.lora_r} on "
-                     f"{'/'.join(cfg.lora_targets)} + RMSNorm weights, AdamW",
+            "model": f"{preset} decoder (d={cfg.d_model}, {cfg.n_layers} layers, "
+                     f"{cfg.n_heads}/{cfg.n_kv_heads} heads of {cfg.head_dim}, {cfg.ffn_act} FFN "
+                     f"{cfg.ffn_dim}, vocab {cfg.vocab_size}); {desc}",
+            "config_name": args.config,
+            "rank_weights": rank_weights,
             "global_batch": B * world,
             "seq_len": S,
             "parallelism": f"dp{world}",

@@ -51,7 +51,8 @@ void plan_gather(std::vector<int64_t> src, std::vector<int64_t> flags, int64_t r
                  int64_t timeout_ms);
 void plan_gather_dequant(std::vector<int64_t> psrc, std::vector<int64_t> pstarts,
                          std::vector<int64_t> asrc, std::vector<int64_t> astarts, int64_t rows,
-                         int64_t cols, int64_t blocksize, int64_t qtype, bool transpose, at::Tensor out);
+                         int64_t cols, int64_t row0, int64_t blocksize, int64_t qtype, bool transpose,
+                         at::Tensor out);
 #ifdef ZQ_WITH_ATTENTION
 // attention.cu
 void attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, bool causal,

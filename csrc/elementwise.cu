@@ -428,12 +428,16 @@ void add_rmsnorm_fwd(at::Tensor h, c10::optional<at::Tensor> d, at::Tensor w, at
   check_bf16(y, "y");
   TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous(), "norm weight must be fp32");
   const int64_t D = h.size(-1), M = h.numel() / D;
+  TORCH_CHECK(w.numel() == D, "norm weight has ", w.numel(), " elements, expected ", D);
+  TORCH_CHECK(y.numel() == h.numel() && rstd.numel() >= M && rstd.scalar_type() == at::kFloat,
+              "norm output / rstd sizes");
   TORCH_CHECK(D % 8 == 0 && D <= 8 * kNormThreads * kNormMaxChunks, "D must be %8 and <= 8192");
   const at::cuda::CUDAGuard guard(h.device());
   const __nv_bfloat16* dp = nullptr;
   if (d.has_value() && d->defined()) {
     check_bf16(*d, "delta");
     check_bf16(hout, "hout");
+    TORCH_CHECK(d->numel() == h.numel() && hout.numel() == h.numel(), "add_rmsnorm: sizes");
     dp = cbf(*d);
   }
   add_rmsnorm_fwd_kernel<<<(unsigned)M, kNormThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
@@ -450,10 +454,14 @@ void rmsnorm_bwd(at::Tensor gy, at::Tensor x, at::Tensor w, at::Tensor rstd,
   check_bf16(dx, "dx");
   const int64_t D = x.size(-1), M = x.numel() / D;
   TORCH_CHECK(D % 8 == 0 && D <= 8 * kNormThreads * kNormMaxChunks, "D must be %8 and <= 8192");
+  TORCH_CHECK(w.numel() == D && w.scalar_type() == at::kFloat, "norm weight must be fp32 [D]");
+  TORCH_CHECK(gy.numel() == x.numel() && dx.numel() == x.numel() && rstd.numel() >= M,
+              "rmsnorm_bwd: tensor sizes");
   const at::cuda::CUDAGuard guard(x.device());
   const __nv_bfloat16* ghp = nullptr;
   if (gh.has_value() && gh->defined()) {
     check_bf16(*gh, "gh");
+    TORCH_CHECK(gh->numel() == x.numel(), "rmsnorm_bwd: gh size");
     ghp = cbf(*gh);
   }
   TORCH_CHECK(dw_part.dim() == 2 && dw_part.size(1) == D && dw_part.is_contiguous() &&
@@ -469,6 +477,7 @@ void rope(at::Tensor x, at::Tensor out, at::Tensor cs, double sign) {
   check_bf16(x, "x");
   check_bf16(out, "out");
   TORCH_CHECK(x.dim() == 4, "rope: x must be [B, S, H, D]");
+  TORCH_CHECK(out.numel() == x.numel(), "rope: out size");
   const int64_t B = x.size(0), S = x.size(1), H = x.size(2), D = x.size(3);
   TORCH_CHECK(D % 16 == 0, "rope: head dim must be a multiple of 16");
   TORCH_CHECK(cs.scalar_type() == at::kFloat && cs.is_contiguous() && cs.numel() >= S * D,
@@ -488,7 +497,7 @@ static inline unsigned ew_grid(int64_t n8) { return (unsigned)((n8 + 255) / 256)
 void gelu_fwd(at::Tensor x, at::Tensor y) {
   check_bf16(x, "x");
   check_bf16(y, "y");
-  TORCH_CHECK(x.numel() % 8 == 0, "gelu: numel % 8");
+  TORCH_CHECK(x.numel() % 8 == 0 && y.numel() == x.numel(), "gelu: numel % 8 and equal sizes");
   const int64_t n8 = x.numel() / 8;
   const at::cuda::CUDAGuard guard(x.device());
   gelu_fwd_kernel<<<ew_grid(n8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(cbf(x), bf(y), n8);
@@ -499,7 +508,8 @@ void gelu_bwd(at::Tensor g, at::Tensor x, at::Tensor dx) {
   check_bf16(g, "g");
   check_bf16(x, "x");
   check_bf16(dx, "dx");
-  TORCH_CHECK(x.numel() % 8 == 0, "gelu: numel % 8");
+  TORCH_CHECK(x.numel() % 8 == 0 && g.numel() == x.numel() && dx.numel() == x.numel(),
+              "gelu: numel % 8 and equal sizes");
   const int64_t n8 = x.numel() / 8;
   const at::cuda::CUDAGuard guard(x.device());
   gelu_bwd_kernel<<<ew_grid(n8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(cbf(g), cbf(x), bf(dx), n8);
@@ -510,7 +520,8 @@ void swiglu_fwd(at::Tensor gate, at::Tensor up, at::Tensor y) {
   check_bf16(gate, "gate");
   check_bf16(up, "up");
   check_bf16(y, "y");
-  TORCH_CHECK(gate.numel() % 8 == 0, "swiglu: numel % 8");
+  TORCH_CHECK(gate.numel() % 8 == 0 && up.numel() == gate.numel() && y.numel() == gate.numel(),
+              "swiglu: numel % 8 and equal sizes");
   const int64_t n8 = gate.numel() / 8;
   const at::cuda::CUDAGuard guard(gate.device());
   swiglu_fwd_kernel<<<ew_grid(n8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(cbf(gate), cbf(up), bf(y), n8);
@@ -523,6 +534,9 @@ void swiglu_bwd(at::Tensor g, at::Tensor gate, at::Tensor up, at::Tensor dgate, 
   check_bf16(up, "up");
   check_bf16(dgate, "dgate");
   check_bf16(dup, "dup");
+  TORCH_CHECK(gate.numel() % 8 == 0 && g.numel() == gate.numel() && up.numel() == gate.numel() &&
+                  dgate.numel() == gate.numel() && dup.numel() == gate.numel(),
+              "swiglu_bwd: numel % 8 and equal sizes");
   const int64_t n8 = gate.numel() / 8;
   const at::cuda::CUDAGuard guard(gate.device());
   swiglu_bwd_kernel<<<ew_grid(n8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
@@ -536,7 +550,7 @@ void ce_fwd(at::Tensor logits, at::Tensor targets, at::Tensor loss, at::Tensor l
   TORCH_CHECK(targets.scalar_type() == at::kLong && targets.is_contiguous(), "targets int64");
   const int64_t M = logits.size(0), Vpad = logits.size(1);
   TORCH_CHECK(Vpad % 8 == 0 && vocab <= Vpad, "ce: Vpad % 8 and vocab <= Vpad");
-  TORCH_CHECK(targets.numel() == M, "ce: one target per row");
+  TORCH_CHECK(targets.numel() == M && loss.numel() >= M && lse.numel() >= M, "ce: one target per row");
   const at::cuda::CUDAGuard guard(logits.device());
   ce_fwd_kernel<<<(unsigned)M, kCEThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       cbf(logits), targets.data_ptr<int64_t>(), loss.data_ptr<float>(), lse.data_ptr<float>(),
@@ -548,6 +562,9 @@ void ce_bwd(at::Tensor logits, at::Tensor targets, at::Tensor lse, at::Tensor sc
             int64_t vocab, int64_t ignore_index) {
   check_bf16(logits, "logits");
   const int64_t M = logits.size(0), Vpad = logits.size(1);
+  TORCH_CHECK(Vpad % 8 == 0 && vocab <= Vpad && targets.numel() == M && lse.numel() >= M &&
+                  targets.scalar_type() == at::kLong && scale.numel() >= 1,
+              "ce_bwd: sizes");
   const at::cuda::CUDAGuard guard(logits.device());
   ce_bwd_kernel<<<(unsigned)M, kCEThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       bf(logits), targets.data_ptr<int64_t>(), lse.data_ptr<float>(), scale.data_ptr<float>(),

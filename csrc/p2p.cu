@@ -168,37 +168,55 @@ __global__ void __launch_bounds__(256) rs_adamw_kernel(PeerTable grads, PeerTabl
     const float inv_sqrt_bc2 = rsqrtf(bc2);
     float* master = reinterpret_cast<float*>(params.ptr[rank]) + lo;
     const int64_t n4 = n >> 2;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
-         i += (int64_t)gridDim.x * blockDim.x) {
-      const int64_t e = i * 4;
-      float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int q = 0; q < world; ++q) {
-        const float4 t = load4<G>(reinterpret_cast<const G*>(grads.ptr[q]) + lo + e);
-        g.x += t.x; g.y += t.y; g.z += t.z; g.w += t.w;
-      }
-      float4 p = *reinterpret_cast<const float4*>(master + e);
-      float4 mm = *reinterpret_cast<const float4*>(m + e);
-      float4 vv = *reinterpret_cast<const float4*>(v + e);
-      float* pp = &p.x;
-      float* mp = &mm.x;
-      float* vp = &vv.x;
-      const float* gp = &g.x;
+    constexpr int U = 4;  // independent 4-element groups in flight per thread
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t base = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < n4; base += stride * U) {
+      float4 g[U];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float gi = gp[j] * gscale;
-        float pi = pp[j] * (1.0f - lr * wd);
-        mp[j] = b1 * mp[j] + (1.0f - b1) * gi;
-        vp[j] = b2 * vp[j] + (1.0f - b2) * gi * gi;
-        pi -= step_size * mp[j] / (sqrtf(vp[j]) * inv_sqrt_bc2 + eps);
-        pp[j] = pi;
+      for (int u = 0; u < U; ++u) g[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      // issue every peer load of the U groups before using any of them
+      for (int q = 0; q < world; ++q) {
+        const G* gq = reinterpret_cast<const G*>(grads.ptr[q]) + lo;
+        float4 t[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t i = base + u * stride;
+          t[u] = i < n4 ? load4<G>(gq + i * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          g[u].x += t[u].x; g[u].y += t[u].y; g[u].z += t[u].z; g[u].w += t[u].w;
+        }
       }
-      *reinterpret_cast<float4*>(m + e) = mm;
-      *reinterpret_cast<float4*>(v + e) = vv;
-      *reinterpret_cast<float4*>(master + e) = p;
-      if (push) {
-        for (int q = 0; q < world; ++q) {
-          if (q == rank) continue;
-          *reinterpret_cast<float4*>(reinterpret_cast<float*>(params.ptr[q]) + lo + e) = p;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t i = base + u * stride;
+        if (i >= n4) break;
+        const int64_t e = i * 4;
+        float4 p = *reinterpret_cast<const float4*>(master + e);
+        float4 mm = *reinterpret_cast<const float4*>(m + e);
+        float4 vv = *reinterpret_cast<const float4*>(v + e);
+        float* pp = &p.x;
+        float* mp = &mm.x;
+        float* vp = &vv.x;
+        const float* gp = &g[u].x;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float gi = gp[j] * gscale;
+          float pi = pp[j] * (1.0f - lr * wd);
+          mp[j] = b1 * mp[j] + (1.0f - b1) * gi;
+          vp[j] = b2 * vp[j] + (1.0f - b2) * gi * gi;
+          pi -= step_size * mp[j] / (sqrtf(vp[j]) * inv_sqrt_bc2 + eps);
+          pp[j] = pi;
+        }
+        *reinterpret_cast<float4*>(m + e) = mm;
+        *reinterpret_cast<float4*>(v + e) = vv;
+        *reinterpret_cast<float4*>(master + e) = p;
+        if (push) {
+          for (int q = 0; q < world; ++q) {
+            if (q == rank) continue;
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(params.ptr[q]) + lo + e) = p;
+          }
         }
       }
     }
@@ -261,7 +279,7 @@ __device__ __forceinline__ uint8_t peer_byte(const PeerTable& src, const PeerTab
 
 __global__ void __launch_bounds__(256) plan_gather_dequant_kernel(
     PeerTable psrc, PeerTable pstart, PeerTable asrc, PeerTable astart, int world, int rows,
-    int cols, int blocksize, int qtype, int transpose, __nv_bfloat16* __restrict__ out) {
+    int cols, int64_t row0, int blocksize, int qtype, int transpose, __nv_bfloat16* __restrict__ out) {
   __shared__ float lut[16];
   __shared__ __align__(16) __nv_bfloat16 tile[64][64 + 8];
   if (threadIdx.x < 16) lut[threadIdx.x] = c_p2p_code[qtype][threadIdx.x];
@@ -273,7 +291,7 @@ __global__ void __launch_bounds__(256) plan_gather_dequant_kernel(
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = 0.0f;
   if (r < rows && c < cols) {
-    const int64_t e0 = (int64_t)r * cols + c;
+    const int64_t e0 = (row0 + r) * (int64_t)cols + c;
     const int64_t b0 = e0 >> 1;
     const int qa = plan_owner(astart, world, e0 / blocksize);
     const float s = reinterpret_cast<const float*>(asrc.ptr[qa])[e0 / blocksize - astart.ptr[qa]];
@@ -385,10 +403,14 @@ static unsigned long long wait_ns(int64_t timeout_ms) {
   return timeout_ms > 0 ? (unsigned long long)timeout_ms * 1000000ull : kPeerWaitNsDefault;
 }
 
-static int resident_grid(int threads) {
+// Largest grid whose CTAs are all resident at once (the kernels' CTAs wait on
+// CTA 0's barrier, so every CTA must be running).
+template <typename K>
+static int resident_grid(K kernel, int threads) {
   const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
-  (void)threads;
-  return sms;  // one CTA of 256 threads per SM: always co-resident
+  int per_sm = 0;
+  C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0));
+  return sms * std::max(1, std::min(per_sm, 4));
 }
 
 void rs_adamw(std::vector<int64_t> grads, std::vector<int64_t> params, std::vector<int64_t> flags,
@@ -402,7 +424,8 @@ void rs_adamw(std::vector<int64_t> grads, std::vector<int64_t> params, std::vect
   TORCH_CHECK(m.numel() >= n && v.numel() >= n, "rs_adamw: moments too small");
   const at::cuda::CUDAGuard guard(m.device());
   auto stream = at::cuda::getCurrentCUDAStream();
-  const int grid = resident_grid(256);
+  const int grid = grad_is_bf16 ? resident_grid(rs_adamw_kernel<__nv_bfloat16>, 256)
+                                : resident_grid(rs_adamw_kernel<float>, 256);
   if (grad_is_bf16) {
     rs_adamw_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
         table_from(grads), table_from(params), table_from(flags), (int)rank, world, (int)epoch, lo, n,
@@ -429,17 +452,19 @@ void plan_gather(std::vector<int64_t> src, std::vector<int64_t> flags, int64_t r
   TORCH_CHECK(out.is_cuda() && out.is_contiguous() && out.numel() * out.element_size() >= total,
               "plan_gather: output too small");
   const at::cuda::CUDAGuard guard(out.device());
-  plan_gather_kernel<<<resident_grid(256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  plan_gather_kernel<<<resident_grid(plan_gather_kernel, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       table_from(src), table_from(flags), (int)rank, world, (int)epoch, table_from(offsets),
       table_from(lengths), reinterpret_cast<uint8_t*>(out.data_ptr()), wait_ns(timeout_ms));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// Peer NF4 shards -> bf16 operand W [rows, cols] (or Wᵀ when transpose).
+// Peer NF4 shards -> bf16 operand: rows [row0, row0+rows) of the [*, cols] weight as
+// [rows, cols] (or transposed [cols, rows]).
 // pstarts/astarts: global start index of each rank's packed bytes / absmax values.
 void plan_gather_dequant(std::vector<int64_t> psrc, std::vector<int64_t> pstarts,
                          std::vector<int64_t> asrc, std::vector<int64_t> astarts, int64_t rows,
-                         int64_t cols, int64_t blocksize, int64_t qtype, bool transpose, at::Tensor out) {
+                         int64_t cols, int64_t row0, int64_t blocksize, int64_t qtype, bool transpose,
+                         at::Tensor out) {
   const int world = (int)psrc.size();
   TORCH_CHECK(world >= 1 && world <= kMaxRanks && (int)pstarts.size() == world &&
                   (int)asrc.size() == world && (int)astarts.size() == world,
@@ -452,7 +477,7 @@ void plan_gather_dequant(std::vector<int64_t> psrc, std::vector<int64_t> pstarts
   dim3 grid((unsigned)((cols + 63) / 64), (unsigned)((rows + 63) / 64));
   plan_gather_dequant_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       table_from(psrc), table_from(pstarts), table_from(asrc), table_from(astarts), world, (int)rows,
-      (int)cols, (int)blocksize, (int)qtype, transpose ? 1 : 0,
+      (int)cols, row0, (int)blocksize, (int)qtype, transpose ? 1 : 0,
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -140,7 +140,7 @@ class TestModel:
         torch.manual_seed(0)
         m = DecoderLM(cfg).init_dense_(seed=3)
         x = torch.randint(0, cfg.vocab_size, (2, 32))
-        zq.initialize(m, zq.ZeroQConfig(compute_in_4bit=True,
+        zq.initialize(m, zq.ZeroQConfig(compute_in_4bit=True, gather_once=True,
                                         exclude_modules=["lm_head", "embed_tokens"]))
         assert all(mod.has_nf4 for mod in m.modules() if isinstance(mod, Linear4bit))
         logits = m(x)
@@ -180,7 +180,7 @@ class TestModel:
 
     def test_sharded_checkpoint_roundtrip(self, cfg, tmp_path):
         m = DecoderLM(cfg).init_dense_(seed=1)
-        zq.initialize(m, zq.ZeroQConfig(compute_in_4bit=True,
+        zq.initialize(m, zq.ZeroQConfig(compute_in_4bit=True, gather_once=True,
                                         exclude_modules=["lm_head", "embed_tokens"]),
                       trainable_patterns=("lora_", "norm"))
         opt = zq.ShardedAdamW(m.trainable_parameters(), lr=1e-3)
@@ -190,7 +190,7 @@ class TestModel:
         zq.save_sharded_checkpoint(str(tmp_path / "ck"), m, opt, step=7)
         out_ref = m(x).detach()
         m2 = DecoderLM(cfg).init_dense_(seed=99)
-        zq.initialize(m2, zq.ZeroQConfig(compute_in_4bit=True,
+        zq.initialize(m2, zq.ZeroQConfig(compute_in_4bit=True, gather_once=True,
                                          exclude_modules=["lm_head", "embed_tokens"]),
                       trainable_patterns=("lora_", "norm"))
         m2.embed_tokens.weight.data.copy_(m.embed_tokens.weight.data)
@@ -223,3 +223,22 @@ def test_inject_lora_into_plain_model():
     out = m(torch.randn(3, 64))
     out.sum().backward()
     assert m.fc1.lora_A.grad is not None
+
+
+def test_gather_release_with_frozen_sharded_norms():
+    """Frozen norm weights are sharded too; the decoder must reach them through the
+    norm modules so the gather hooks run (a bare ``.weight`` would be empty)."""
+    cfg = get_config("tiny", lora_r=4, n_layers=2)
+    m = DecoderLM(cfg).init_dense_(seed=0)
+    zq.initialize(m, zq.ZeroQConfig(compute_in_4bit=True, gather_once=False,
+                                    exclude_modules=["lm_head", "embed_tokens"]),
+                  trainable_patterns=("lora_",))
+    coord = m._zeroq_coordinator
+    norm_params = [p for p in coord._params.values() if "norm" in (p.module_path or "")]
+    assert norm_params, "norm weights should be registered and sharded"
+    assert m.layers[0].attn_norm.weight.numel() == 0  # released between uses
+    x = torch.randint(0, cfg.vocab_size, (2, 32))
+    loss = m(x, x)
+    loss.backward()
+    assert torch.isfinite(loss)
+    assert m.layers[0].q_proj.lora_B.grad is not None

@@ -87,6 +87,10 @@ class ZeroQConfig:
     # 4-bit compute: frozen Linear weights stay NF4 and run through the fused
     # NF4-dequant GEMM instead of being dequantised to a full-precision copy.
     compute_in_4bit: bool = False
+    # With compute_in_4bit: gather every weight once, keep it resident and drop
+    # the gather/release hooks (True), or keep gathering per use (False, the
+    # reference's hetero ``compute_in_4bit`` behaviour).
+    gather_once: bool = False
 
     # Train-from-scratch: shard parameters as fp32 masters (no quantisation)
     training_mode: bool = False

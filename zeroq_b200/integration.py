@@ -2,7 +2,8 @@
 
 * :func:`prepare_model_for_zeroq` - freeze the base, unfreeze adapters, build a
   coordinator + hook wrapper, quantise and shard (reference :35-90).  With
-  ``config.compute_in_4bit`` it then switches the model to 4-bit compute: every
+  ``config.compute_in_4bit`` gathered Linear4bit weights stay NF4 per use; with
+  ``gather_once`` as well it switches the model to resident 4-bit compute: every
   :class:`~zeroq_b200.ops.qlinear.Linear4bit` gathers its full NF4 weight ONCE and
   keeps it resident, other sharded params are gathered once and kept, and the
   gather/release hooks are removed - the mode the reference's README describes
@@ -147,7 +148,7 @@ def prepare_model_for_zeroq(model: nn.Module, config: Optional[ZeroQConfig] = No
         from .parallel.peer import PeerShardPool
 
         coordinator.peer_pool = PeerShardPool(coordinator, process_group)
-    if getattr(config, "compute_in_4bit", False):
+    if getattr(config, "compute_in_4bit", False) and getattr(config, "gather_once", False):
         convert_to_4bit_compute(model, coordinator, wrapper)
         wrapper = None
     model._zeroq_wrapper = wrapper

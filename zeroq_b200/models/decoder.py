@@ -110,11 +110,22 @@ def get_config(name: str, **overrides) -> DecoderConfig:
 
 
 class RMSNorm(nn.Module):
+    """RMSNorm; ``forward(h, delta)`` fuses the residual add and returns
+    ``(h + delta, norm(h + delta))``, ``forward(h)`` returns ``norm(h)``.
+
+    Called as a module (never by reaching into ``.weight``) so that a
+    gather/release coordinator's hooks gather a sharded weight first."""
+
     def __init__(self, d: int, eps: float, device=None, trainable: bool = True):
         super().__init__()
         self.eps = eps
         self.weight = nn.Parameter(torch.ones(d, device=device, dtype=torch.float32),
                                    requires_grad=trainable)
+
+    def forward(self, h: torch.Tensor, delta: Optional[torch.Tensor] = None):
+        if delta is None:
+            return add_rmsnorm(h, None, self.weight, self.eps)[1]
+        return add_rmsnorm(h, delta, self.weight, self.eps)
 
 
 class DecoderLayer(nn.Module):
@@ -155,14 +166,17 @@ class DecoderLayer(nn.Module):
         still has to be added (fused into this layer's first norm)."""
         cfg = self.cfg
         B, S, d = h.shape
-        h, x = add_rmsnorm(h, delta, self.attn_norm.weight, self.attn_norm.eps)
+        if delta is None:
+            x = self.attn_norm(h)
+        else:
+            h, x = self.attn_norm(h, delta)
         q = self.q_proj(x).view(B, S, cfg.n_heads, cfg.head_dim)
         k = self.k_proj(x).view(B, S, cfg.n_kv_heads, cfg.head_dim)
         v = self.v_proj(x).view(B, S, cfg.n_kv_heads, cfg.head_dim)
         q, k = apply_rope(q, k, cfg.rope_theta)
         o = flash_attention(q, k, v, causal=True)
         a = self.o_proj(o.view(B, S, cfg.n_heads * cfg.head_dim))
-        h, x = add_rmsnorm(h, a, self.mlp_norm.weight, self.mlp_norm.eps)
+        h, x = self.mlp_norm(h, a)
         if self.gate_proj is not None:
             f = swiglu(self.gate_proj(x), self.up_proj(x))
         else:
@@ -269,8 +283,11 @@ class DecoderLM(nn.Module):
         delta = None
         for layer in self.layers:
             h, delta = self._layer_call(layer, h, delta)
-        _, x = add_rmsnorm(h, delta, self.norm.weight, self.norm.eps)
+        x = self.norm(h) if delta is None else self.norm(h, delta)[1]
         W = self.head_weight()
+        if W.numel() == 0:
+            raise RuntimeError("the LM head weight is sharded and not gathered here; keep "
+                               "'embed_tokens' and 'lm_head' in exclude_modules")
         logits = LMHeadFunction.apply(x, W, self._head_transposed())
         if targets is None:
             return logits.view(B, S, -1)[..., : self.cfg.vocab_size]

@@ -208,9 +208,10 @@ class PeerShardPool:
         return GatherHandle([lambda: packed, lambda: absmax])
 
     def gather_dequant(self, zq, rows: int, cols: int, transpose: bool = False,
-                       out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """bf16 operand ``W [rows, cols]`` (or ``Wᵀ``) read straight from the owners'
-        NF4 shards over NVLink: the gather and the dequantisation are one kernel."""
+                       out: Optional[torch.Tensor] = None, row0: int = 0) -> torch.Tensor:
+        """bf16 operand: rows ``[row0, row0+rows)`` of ``W [*, cols]`` (or their
+        transpose) read straight from the owners' NF4 shards over NVLink: the
+        gather and the dequantisation are one kernel."""
         from ..ops.nf4 import QUANT_TYPE_ID
 
         psrc, _, _ = self._segments(zq, 0)
@@ -219,7 +220,7 @@ class PeerShardPool:
             out = torch.empty(rows * cols, dtype=torch.bfloat16, device=zq.local_packed.device)
         m = zq._quant_meta
         _ext.ext().plan_gather_dequant(psrc, list(zq.packed_plan.offsets), asrc,
-                                       list(zq.absmax_plan.offsets), rows, cols,
+                                       list(zq.absmax_plan.offsets), rows, cols, int(row0),
                                        int(m["blocksize"]), QUANT_TYPE_ID[m["quant_type"]],
                                        bool(transpose), out)
         return out.view(cols, rows) if transpose else out.view(rows, cols)
