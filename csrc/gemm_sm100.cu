@@ -236,21 +236,27 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 //   tfull[b]  (each CTA): the leader's commits after a tile's last k-step.
 //   tempty[b] (leader): 2 x 128 epilogue threads of both CTAs arrive.
 // ----------------------------------------------------------------------------
-template <int BN, int STAGES>
+template <int BN, int STAGES, int KB>
 struct PairSmem {
-  static constexpr int kABytes = kBM * kBK * 2;           // this CTA's 128 rows of A
-  static constexpr int kBBytes = (BN / 2) * kBK * 2;      // this CTA's half of B
+  // KB 128-byte-wide K atoms per stage (BK = 64 * KB): 8 MMAs per commit at
+  // KB = 2, which measured markedly lower pipeline overhead than KB = 1
+  static constexpr int kAAtom = kBM * kBK * 2;             // 128 rows x 64 K of A
+  static constexpr int kBAtom = (BN / 2) * kBK * 2;        // BN/2 rows x 64 K of B
+  static constexpr int kABytes = kAAtom * KB;              // this CTA's 128 rows of A
+  static constexpr int kBBytes = kBAtom * KB;              // this CTA's half of B
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kEpiOffset = STAGES * kStageBytes;         // 2 x [128 rows][32 cols] bf16
+  static constexpr int kEpiBytes = 128 * 32 * 2;
+  static constexpr int kBarOffset = kEpiOffset + 2 * kEpiBytes;
   static constexpr int kBytes = kBarOffset + 256 + 1024;
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int KB>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
-                    GemmArgs args) {
-  using L = PairSmem<BN, STAGES>;
+                    const __grid_constant__ CUtensorMap tmC, GemmArgs args) {
+  using L = PairSmem<BN, STAGES, KB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
@@ -266,7 +272,7 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   const int cluster_id = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
   const int num_tiles = args.tiles_m * args.tiles_n;  // tiles of 256 x BN
-  const int main_k_tiles = args.K / kBK;
+  const int main_k_tiles = args.K / (kBK * KB);
   const int k_tiles = main_k_tiles + (args.extra_k16 > 0 ? 1 : 0);
 
   if (threadIdx.x == 0) {
@@ -311,11 +317,15 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           uint8_t* sa = smem + stage * L::kStageBytes;
           uint8_t* sb = sa + L::kABytes;
           const uint32_t leader_full = map_to_cta(smem_u32(&full_bar[stage]), 0);
-          if (cr == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * L::kStageBytes);
           if (kt < main_k_tiles) {
-            tma_load_2d_pair(sa, &tmA, leader_full, kt * kBK, arow);
-            tma_load_2d_pair(sb, &tmB, leader_full, kt * kBK, brow);
-          } else {
+            if (cr == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * L::kStageBytes);
+            for (int kb = 0; kb < KB; ++kb) {
+              const int kc = (kt * KB + kb) * kBK;
+              tma_load_2d_pair(sa + kb * L::kAAtom, &tmA, leader_full, kc, arow);
+              tma_load_2d_pair(sb + kb * L::kBAtom, &tmB, leader_full, kc, brow);
+            }
+          } else {  // extra 64-wide slab: first atom of the stage only
+            if (cr == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * (L::kAAtom + L::kBAtom));
             tma_load_2d_pair(sa, &tmA2, leader_full, 0, arow);
             tma_load_2d_pair(sb, &tmB2, leader_full, 0, brow);
           }
@@ -345,10 +355,12 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
           const uint32_t b_addr = a_addr + L::kABytes;
-          const int nk = kt < main_k_tiles ? kBK / 16 : args.extra_k16;
+          const int nk = kt < main_k_tiles ? KB * (kBK / 16) : args.extra_k16;
           for (int kk = 0; kk < nk; ++kk) {
-            umma_f16_ss_pair(d_tmem, umma_desc_sw128_kmajor(a_addr + kk * 32),
-                             umma_desc_sw128_kmajor(b_addr + kk * 32), idesc,
+            const uint32_t ao = (uint32_t)((kk >> 2) * L::kAAtom + (kk & 3) * 32);
+            const uint32_t bo = (uint32_t)((kk >> 2) * L::kBAtom + (kk & 3) * 32);
+            umma_f16_ss_pair(d_tmem, umma_desc_sw128_kmajor(a_addr + ao),
+                             umma_desc_sw128_kmajor(b_addr + bo), idesc,
                              (kt > 0 || kk > 0) ? 1u : 0u);
           }
           const uint32_t e = smem_u32(&empty_bar[stage]);
@@ -363,43 +375,53 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     }
   } else {
     // ---------------------------------------------------------------- epilogue (both CTAs)
+    // TMEM -> registers -> bf16 -> 64-byte-swizzled staging tile in shared
+    // memory -> one TMA tensor store per 128 x 32 chunk (double-buffered).
     const int q = warp & 3;
-    const int row_in_tile = (int)cr * kBM + q * 32 + lane;
-    int it = 0;
+    const int row = q * 32 + lane;                 // row within this CTA's 128 rows
+    const bool leader_thread = (warp == 2 && lane == 0);
+    uint8_t* epi = smem + L::kEpiOffset;
+    int it = 0, chunk_no = 0;
     bool ok = true;
     for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters, ++it) {
       int tm, tn;
       tile_coords(tile, args.tiles_m, args.tiles_n, tm, tn);
       const int buf = it & 1;
-      if (!mbar_wait(&tfull_bar[buf], (it >> 1) & 1, args.status, kErrEpi)) { ok = false; break; }
+      const bool got = mbar_wait(&tfull_bar[buf], (it >> 1) & 1, args.status, kErrEpi);
+      if (!named_barrier_and(1, 128, got)) { ok = false; break; }  // same decision in all 128
       tc_fence_after();
-      const int m = tm * (2 * kBM) + row_in_tile;
+      const int m0 = tm * (2 * kBM) + (int)cr * kBM;
       const int n0 = tn * BN;
-      __nv_bfloat16* crow = args.C + (int64_t)m * args.ldc;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = 0; c < BN / 32; ++c, ++chunk_no) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256 + c * 32), r);
         tmem_ld_wait();
-        const int ncol = n0 + c * 32;
-        if (m < args.M) {
+        uint8_t* st = epi + (chunk_no & 1) * L::kEpiBytes;
+        // the store that last used this staging buffer (two chunks ago) must have read it
+        if (leader_thread) bulk_wait_group_read<1>();
+        named_barrier(1, 128);
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const int nc = ncol + v * 8;
-            if (nc + 8 <= args.N) {
-              uint4 o;
-              o.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
-              o.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
-              o.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
-              o.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
-              *reinterpret_cast<uint4*>(crow + nc) = o;
-            }
-          }
+        for (int j = 0; j < 4; ++j) {
+          uint4 o;
+          o.x = pack_bf16x2(__uint_as_float(r[j * 8 + 0]), __uint_as_float(r[j * 8 + 1]));
+          o.y = pack_bf16x2(__uint_as_float(r[j * 8 + 2]), __uint_as_float(r[j * 8 + 3]));
+          o.z = pack_bf16x2(__uint_as_float(r[j * 8 + 4]), __uint_as_float(r[j * 8 + 5]));
+          o.w = pack_bf16x2(__uint_as_float(r[j * 8 + 6]), __uint_as_float(r[j * 8 + 7]));
+          const int pj = j ^ ((row >> 1) & 3);   // 64-byte swizzle
+          *reinterpret_cast<uint4*>(st + row * 64 + pj * 16) = o;
+        }
+        fence_proxy_async_smem();
+        named_barrier(1, 128);
+        if (leader_thread) {
+          tma_store_2d(&tmC, st, n0 + c * 32, m0);
+          bulk_commit_group();
         }
       }
       tc_fence_before();
       mbar_arrive_cluster(map_to_cta(smem_u32(&tempty_bar[buf]), 0));
     }
+    if (leader_thread) bulk_wait_group<0>();
   }
 
   tc_fence_before();
@@ -539,6 +561,25 @@ static CUtensorMap make_tmap_bf16(const void* base, int64_t rows, int64_t cols, 
   return map;
 }
 
+// [rows, cols] bf16 output tensor map for the epilogue's TMA store: box of 128
+// rows x 32 columns, 64-byte swizzle (matches the staging tile layout)
+static CUtensorMap make_tmap_store_bf16(const void* base, int64_t rows, int64_t cols,
+                                        int64_t row_stride_elems) {
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "TMA store base must be 16-byte aligned");
+  TORCH_CHECK((row_stride_elems * 2) % 16 == 0, "TMA store row pitch must be a multiple of 16 bytes");
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(row_stride_elems * 2)};
+  cuuint32_t box[2] = {32u, 128u};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = get_encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (store) failed with code ", (int)r);
+  return map;
+}
+
 static DeviceStatus* status_buffer(int device) {
   static DeviceStatus* bufs[64] = {nullptr};
   static std::mutex mu;
@@ -577,15 +618,16 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int KB>
 static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2,
-                             const CUtensorMap& tb2, GemmArgs args, cudaStream_t stream, int sms) {
-  using L = PairSmem<BN, STAGES>;
+                             const CUtensorMap& tb2, const CUtensorMap& tc, GemmArgs args,
+                             cudaStream_t stream, int sms) {
+  using L = PairSmem<BN, STAGES, KB>;
   static bool configured[64] = {false};
   int dev;
   C10_CUDA_CHECK(cudaGetDevice(&dev));
   if (!configured[dev]) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_tn_pair_kernel<BN, STAGES>,
+    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_tn_pair_kernel<BN, STAGES, KB>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
     configured[dev] = true;
   }
@@ -603,7 +645,7 @@ static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tn_pair_kernel<BN, STAGES>, ta, tb, ta2, tb2, args));
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tn_pair_kernel<BN, STAGES, KB>, ta, tb, ta2, tb2, tc, args));
 }
 
 // Pick the N tile that minimises wave quantisation over the SMs.
@@ -693,9 +735,15 @@ static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
   }
   auto stream = at::cuda::getCurrentCUDAStream();
   if (pair) {
-    if (bn == 256) launch_gemm_pair<256, 7>(ta, tb, ta2, tb2, args, stream, sms);
-    else if (bn == 192) launch_gemm_pair<192, 8>(ta, tb, ta2, tb2, args, stream, sms);
-    else launch_gemm_pair<128, 9>(ta, tb, ta2, tb2, args, stream, sms);
+    const CUtensorMap tc = make_tmap_store_bf16(c.data_ptr(), M, N, c.stride(0));
+    const bool k128 = (K % 128) == 0;
+    if (bn == 256) {
+      if (k128) launch_gemm_pair<256, 3, 2>(ta, tb, ta2, tb2, tc, args, stream, sms);
+      else launch_gemm_pair<256, 6, 1>(ta, tb, ta2, tb2, tc, args, stream, sms);
+    } else {
+      if (k128) launch_gemm_pair<128, 4, 2>(ta, tb, ta2, tb2, tc, args, stream, sms);
+      else launch_gemm_pair<128, 8, 1>(ta, tb, ta2, tb2, tc, args, stream, sms);
+    }
     return;
   }
   if (bn == 256) launch_gemm<256, 4>(ta, tb, ta2, tb2, args, stream, sms);

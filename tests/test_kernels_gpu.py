@@ -42,7 +42,8 @@ def test_dequantize_matches_oracle(cuda, out_dtype):
 
 
 @pytest.mark.parametrize("shape", [(128, 256, 64), (256, 512, 128), (1000, 768, 320),
-                                   (8192 // 4, 3072, 3072), (333, 200, 64), (4096, 12288, 3072)])
+                                   (8192 // 4, 3072, 3072), (333, 200, 64), (4096, 12288, 3072),
+                                   (300, 136, 256), (2048, 50304, 128)])
 def test_gemm_bf16_tn(cuda, shape):
     M, N, K = shape
     torch.manual_seed(2)
@@ -52,14 +53,21 @@ def test_gemm_bf16_tn(cuda, shape):
     _ext.ext().gemm_bf16_tn(a, b, c)
     torch.cuda.synchronize()
     _status_ok(cuda)
+    # strided output (a column block of a wider matrix) through the TMA-store epilogue
+    wide = torch.zeros(M, N + 64, device=cuda, dtype=torch.bfloat16)
+    _ext.ext().gemm_bf16_tn(a, b, wide[:, 32:32 + N])
+    torch.cuda.synchronize()
+    assert torch.equal(wide[:, 32:32 + N], c)
+    assert torch.all(wide[:, :32] == 0) and torch.all(wide[:, 32 + N:] == 0)
     ref = a.float() @ b.float().t()
     err = (c.float() - ref).abs().max().item()
     tol = 2e-2 * math.sqrt(K) + 1e-2 * ref.abs().max().item()
     assert err < tol, (err, tol)
 
 
-def test_gemm_extra_slab(cuda):
-    M, N, K = 640, 448, 192
+@pytest.mark.parametrize("K", [192, 256, 3072])
+def test_gemm_extra_slab(cuda, K):
+    M, N = 640, 448
     torch.manual_seed(3)
     a = torch.randn(M, K, device=cuda, dtype=torch.bfloat16)
     b = torch.randn(N, K, device=cuda, dtype=torch.bfloat16)
@@ -72,7 +80,8 @@ def test_gemm_extra_slab(cuda):
     torch.cuda.synchronize()
     _status_ok(cuda)
     ref = a.float() @ b.float().t() + a2.float() @ b2.float().t()
-    assert (c.float() - ref).abs().max().item() < 0.5
+    tol = 2e-2 * math.sqrt(K) + 1e-2 * ref.abs().max().item()
+    assert (c.float() - ref).abs().max().item() < tol
 
 
 @pytest.mark.parametrize("transpose", [False, True])
