@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Run one hot kernel a few times on one GPU - the small cases profiled with ncu.
 
-    python benchmarks/kernel_case.py gemm --m 8192 --n 3072 --k 3072 [--pair 0|1]
+    python benchmarks/kernel_case.py gemm --m 8192 --n 3072 --k 3072 [--pair 0|1] [--nn]
     python benchmarks/kernel_case.py attention --b 8 --s 1024 --h 24 --d 128
     python benchmarks/kernel_case.py nf4_operand --n 12288 --k 3072 [--transpose]
     python benchmarks/kernel_case.py rmsnorm --m 8192 --d 3072
@@ -45,6 +45,7 @@ def main():
     ap.add_argument("--h", type=int, default=24)
     ap.add_argument("--d", type=int, default=128)
     ap.add_argument("--transpose", action="store_true")
+    ap.add_argument("--nn", action="store_true", help="gemm: B given as [K, N] (MN-major read)")
     ap.add_argument("--reps", type=int, default=4)
     a = ap.parse_args()
 
@@ -55,10 +56,14 @@ def main():
     if a.case == "gemm":
         E.set_gemm_pair_mode(a.pair)
         x = torch.randn(a.m, a.k, device=dev, dtype=torch.bfloat16)
-        w = torch.randn(a.n, a.k, device=dev, dtype=torch.bfloat16)
         y = torch.empty(a.m, a.n, device=dev, dtype=torch.bfloat16)
-        ms = _time(lambda: E.gemm_bf16_tn(x, w, y), a.reps)
-        print(f"gemm {a.m}x{a.n}x{a.k} pair={a.pair}: {ms:.4f} ms, "
+        if a.nn:
+            w = torch.randn(a.k, a.n, device=dev, dtype=torch.bfloat16)
+            ms = _time(lambda: E.gemm_bf16_nn(x, w, y, None, None), a.reps)
+        else:
+            w = torch.randn(a.n, a.k, device=dev, dtype=torch.bfloat16)
+            ms = _time(lambda: E.gemm_bf16_tn(x, w, y), a.reps)
+        print(f"gemm {a.m}x{a.n}x{a.k} pair={a.pair} nn={a.nn}: {ms:.4f} ms, "
               f"{2 * a.m * a.n * a.k / ms / 1e9:.0f} TFLOP/s, status {E.gemm_status(0)}")
     elif a.case == "attention":
         from zeroq_b200.ops.attention import flash_attention

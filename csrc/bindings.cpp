@@ -10,6 +10,8 @@ void nf4_dequantize(at::Tensor packed, at::Tensor absmax, at::Tensor out, int64_
 // gemm_sm100.cu
 void gemm_bf16_tn(at::Tensor a, at::Tensor b, at::Tensor c);
 void gemm_bf16_tn_extra(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor a2, at::Tensor b2);
+void gemm_bf16_nn(at::Tensor a, at::Tensor b, at::Tensor c, c10::optional<at::Tensor> a2,
+                  c10::optional<at::Tensor> b2);
 std::vector<int64_t> gemm_status(int64_t device);
 void set_gemm_pair_mode(int64_t mode);
 void nf4_to_bf16(at::Tensor packed, at::Tensor absmax, at::Tensor out, int64_t rows, int64_t cols,
@@ -67,6 +69,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nf4_dequantize", &nf4_dequantize);
   m.def("gemm_bf16_tn", &gemm_bf16_tn);
   m.def("gemm_bf16_tn_extra", &gemm_bf16_tn_extra);
+  m.def("gemm_bf16_nn", &gemm_bf16_nn);
   m.def("gemm_status", &gemm_status);
   m.def("set_gemm_pair_mode", &set_gemm_pair_mode);
   m.def("nf4_to_bf16", &nf4_to_bf16);

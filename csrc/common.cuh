@@ -253,6 +253,19 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_kmajor(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory descriptor for an MN-major operand stored as TMA boxes of
+// 64 MN-elements (128 B, 128-byte swizzle) x K rows: 8-row K groups are 1024 B
+// apart (SBO) and 64-element MN chunks are `lbo_bytes` apart (LBO).
+__device__ __forceinline__ uint64_t umma_desc_sw128_mnmajor(uint32_t smem_addr, uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr & 0x3FFFF) >> 4);      // start address
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;  // LBO: MN-chunk stride
+  d |= (uint64_t)(1024 >> 4) << 32;                  // SBO: 8-row K-group stride
+  d |= (uint64_t)1 << 46;                            // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;                            // SWIZZLE_128B
+  return d;
+}
+
 // Instruction descriptor: kind::f16, A/B bf16, D fp32, both K-major.
 __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
   return (1u << 4)                        // D format: f32
@@ -260,6 +273,11 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
          | (1u << 10)                     // B format: bf16
          | ((uint32_t)(N >> 3) << 17)     // N >> 3
          | ((uint32_t)(M >> 4) << 24);    // M >> 4
+}
+
+// Same with B MN-major (b_major bit 16).
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_bmn(int M, int N) {
+  return umma_idesc_bf16(M, N) | (1u << 16);
 }
 
 // ----------------------------------------------------------------------------

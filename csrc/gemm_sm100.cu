@@ -251,7 +251,7 @@ struct PairSmem {
   static constexpr int kBytes = kBarOffset + 256 + 1024;
 };
 
-template <int BN, int STAGES, int KB>
+template <int BN, int STAGES, int KB, bool BMN>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
@@ -322,12 +322,24 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             for (int kb = 0; kb < KB; ++kb) {
               const int kc = (kt * KB + kb) * kBK;
               tma_load_2d_pair(sa + kb * L::kAAtom, &tmA, leader_full, kc, arow);
-              tma_load_2d_pair(sb + kb * L::kBAtom, &tmB, leader_full, kc, brow);
+              if (BMN) {
+                // B is [K, N] row-major: boxes of 64 N-columns x 64 K-rows
+                for (int ch = 0; ch < BN / 128; ++ch)
+                  tma_load_2d_pair(sb + kb * L::kBAtom + ch * 8192, &tmB, leader_full,
+                                   brow + ch * 64, kc);
+              } else {
+                tma_load_2d_pair(sb + kb * L::kBAtom, &tmB, leader_full, kc, brow);
+              }
             }
           } else {  // extra 64-wide slab: first atom of the stage only
             if (cr == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * (L::kAAtom + L::kBAtom));
             tma_load_2d_pair(sa, &tmA2, leader_full, 0, arow);
-            tma_load_2d_pair(sb, &tmB2, leader_full, 0, brow);
+            if (BMN) {
+              for (int ch = 0; ch < BN / 128; ++ch)
+                tma_load_2d_pair(sb + ch * 8192, &tmB2, leader_full, brow + ch * 64, 0);
+            } else {
+              tma_load_2d_pair(sb, &tmB2, leader_full, 0, brow);
+            }
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -344,7 +356,7 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
-      constexpr uint32_t idesc = umma_idesc_bf16(2 * kBM, BN);
+      constexpr uint32_t idesc = BMN ? umma_idesc_bf16_bmn(2 * kBM, BN) : umma_idesc_bf16(2 * kBM, BN);
       for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters, ++it) {
         const int buf = it & 1;
         if (!mbar_wait(&tempty_bar[buf], ((it >> 1) & 1) ^ 1, args.status, kErrMmaAcc)) { ok = false; break; }
@@ -358,9 +370,15 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           const int nk = kt < main_k_tiles ? KB * (kBK / 16) : args.extra_k16;
           for (int kk = 0; kk < nk; ++kk) {
             const uint32_t ao = (uint32_t)((kk >> 2) * L::kAAtom + (kk & 3) * 32);
-            const uint32_t bo = (uint32_t)((kk >> 2) * L::kBAtom + (kk & 3) * 32);
-            umma_f16_ss_pair(d_tmem, umma_desc_sw128_kmajor(a_addr + ao),
-                             umma_desc_sw128_kmajor(b_addr + bo), idesc,
+            uint64_t bdesc;
+            if (BMN) {  // 16 K-rows per MMA = 2048 B within a 64-row K atom
+              const uint32_t bo = (uint32_t)((kk >> 2) * L::kBAtom + (kk & 3) * 2048);
+              bdesc = umma_desc_sw128_mnmajor(b_addr + bo, 8192);
+            } else {
+              const uint32_t bo = (uint32_t)((kk >> 2) * L::kBAtom + (kk & 3) * 32);
+              bdesc = umma_desc_sw128_kmajor(b_addr + bo);
+            }
+            umma_f16_ss_pair(d_tmem, umma_desc_sw128_kmajor(a_addr + ao), bdesc, idesc,
                              (kt > 0 || kk > 0) ? 1u : 0u);
           }
           const uint32_t e = smem_u32(&empty_bar[stage]);
@@ -618,7 +636,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-template <int BN, int STAGES, int KB>
+template <int BN, int STAGES, int KB, bool BMN>
 static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2,
                              const CUtensorMap& tb2, const CUtensorMap& tc, GemmArgs args,
                              cudaStream_t stream, int sms) {
@@ -627,7 +645,7 @@ static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const
   int dev;
   C10_CUDA_CHECK(cudaGetDevice(&dev));
   if (!configured[dev]) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_tn_pair_kernel<BN, STAGES, KB>,
+    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_tn_pair_kernel<BN, STAGES, KB, BMN>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
     configured[dev] = true;
   }
@@ -645,7 +663,7 @@ static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tn_pair_kernel<BN, STAGES, KB>, ta, tb, ta2, tb2, tc, args));
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tn_pair_kernel<BN, STAGES, KB, BMN>, ta, tb, ta2, tb2, tc, args));
 }
 
 // Pick the N tile that minimises wave quantisation over the SMs.
@@ -685,15 +703,17 @@ static int choose_bn_pair(int M, int N, int sms) {
 
 void set_gemm_pair_mode(int64_t mode) { g_pair_mode = (int)mode; }
 
+// b_mn = false: B is [N, K] row-major (C = A·Bᵀ); true: B is [K, N] row-major (C = A·B)
 static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
-                      const c10::optional<at::Tensor>& a2, const c10::optional<at::Tensor>& b2) {
+                      const c10::optional<at::Tensor>& a2, const c10::optional<at::Tensor>& b2,
+                      bool b_mn = false) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: CUDA tensors");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 &&
                   c.scalar_type() == at::kBFloat16, "gemm: bf16 operands");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm: 2-D operands");
   TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && c.stride(1) == 1, "gemm: row-major operands");
-  const int64_t M = a.size(0), K = a.size(1), N = b.size(0);
-  TORCH_CHECK(b.size(1) == K, "gemm: K mismatch");
+  const int64_t M = a.size(0), K = a.size(1), N = b_mn ? b.size(1) : b.size(0);
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "gemm: K mismatch");
   TORCH_CHECK(c.size(0) == M && c.size(1) == N, "gemm: C shape");
   TORCH_CHECK(K % 64 == 0 && K > 0, "gemm: K must be a positive multiple of 64");
   TORCH_CHECK(N % 8 == 0, "gemm: N must be a multiple of 8");
@@ -703,7 +723,9 @@ static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
   const at::cuda::CUDAGuard guard(a.device());
   const int dev = a.get_device();
   const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
-  const bool pair = g_pair_mode != 0 && M >= 2 * kBM;
+  const bool pair = (g_pair_mode != 0 || b_mn) && M >= 2 * kBM;
+  TORCH_CHECK(!b_mn || pair, "gemm: B as [K, N] needs M >= 256");
+  TORCH_CHECK(!b_mn || N % 64 == 0, "gemm: B as [K, N] needs N % 64 == 0");
   const int bn = pair ? choose_bn_pair((int)M, (int)N, sms) : choose_bn((int)M, (int)N, sms);
 
   GemmArgs args;
@@ -719,30 +741,49 @@ static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
 
   CUtensorMap ta = make_tmap_bf16(a.data_ptr(), M, K, a.stride(0), kBM);
   const int b_box = pair ? bn / 2 : bn;
-  CUtensorMap tb = make_tmap_bf16(b.data_ptr(), N, K, b.stride(0), b_box);
+  // [K, N] operands are read as boxes of 64 N-columns x 64 K-rows
+  CUtensorMap tb = b_mn ? make_tmap_bf16(b.data_ptr(), K, N, b.stride(0), 64)
+                        : make_tmap_bf16(b.data_ptr(), N, K, b.stride(0), b_box);
   CUtensorMap ta2 = ta, tb2 = tb;
   if (a2.has_value() && a2->defined()) {
     TORCH_CHECK(b2.has_value() && b2->defined(), "gemm: extra slab needs both operands");
     const at::Tensor& x2 = *a2;
     const at::Tensor& y2 = *b2;
     TORCH_CHECK(x2.scalar_type() == at::kBFloat16 && y2.scalar_type() == at::kBFloat16, "extra slab bf16");
-    TORCH_CHECK(x2.size(0) == M && y2.size(0) == N && x2.size(1) == 64 && y2.size(1) == 64 &&
-                    x2.stride(1) == 1 && y2.stride(1) == 1,
-                "extra slab operands must be [M,64] and [N,64] row-major");
+    if (b_mn) {
+      TORCH_CHECK(x2.size(0) == M && x2.size(1) == 64 && y2.size(0) == 64 && y2.size(1) == N &&
+                      x2.stride(1) == 1 && y2.stride(1) == 1,
+                  "extra slab operands must be [M,64] and [64,N] row-major");
+    } else {
+      TORCH_CHECK(x2.size(0) == M && y2.size(0) == N && x2.size(1) == 64 && y2.size(1) == 64 &&
+                      x2.stride(1) == 1 && y2.stride(1) == 1,
+                  "extra slab operands must be [M,64] and [N,64] row-major");
+    }
     ta2 = make_tmap_bf16(x2.data_ptr(), M, 64, x2.stride(0), kBM);
-    tb2 = make_tmap_bf16(y2.data_ptr(), N, 64, y2.stride(0), b_box);
+    tb2 = b_mn ? make_tmap_bf16(y2.data_ptr(), 64, N, y2.stride(0), 64)
+               : make_tmap_bf16(y2.data_ptr(), N, 64, y2.stride(0), b_box);
     args.extra_k16 = 4;
   }
   auto stream = at::cuda::getCurrentCUDAStream();
   if (pair) {
     const CUtensorMap tc = make_tmap_store_bf16(c.data_ptr(), M, N, c.stride(0));
     const bool k128 = (K % 128) == 0;
+    if (b_mn) {
+      if (bn == 256) {
+        if (k128) launch_gemm_pair<256, 3, 2, true>(ta, tb, ta2, tb2, tc, args, stream, sms);
+        else launch_gemm_pair<256, 6, 1, true>(ta, tb, ta2, tb2, tc, args, stream, sms);
+      } else {
+        if (k128) launch_gemm_pair<128, 4, 2, true>(ta, tb, ta2, tb2, tc, args, stream, sms);
+        else launch_gemm_pair<128, 8, 1, true>(ta, tb, ta2, tb2, tc, args, stream, sms);
+      }
+      return;
+    }
     if (bn == 256) {
-      if (k128) launch_gemm_pair<256, 3, 2>(ta, tb, ta2, tb2, tc, args, stream, sms);
-      else launch_gemm_pair<256, 6, 1>(ta, tb, ta2, tb2, tc, args, stream, sms);
+      if (k128) launch_gemm_pair<256, 3, 2, false>(ta, tb, ta2, tb2, tc, args, stream, sms);
+      else launch_gemm_pair<256, 6, 1, false>(ta, tb, ta2, tb2, tc, args, stream, sms);
     } else {
-      if (k128) launch_gemm_pair<128, 4, 2>(ta, tb, ta2, tb2, tc, args, stream, sms);
-      else launch_gemm_pair<128, 8, 1>(ta, tb, ta2, tb2, tc, args, stream, sms);
+      if (k128) launch_gemm_pair<128, 4, 2, false>(ta, tb, ta2, tb2, tc, args, stream, sms);
+      else launch_gemm_pair<128, 8, 1, false>(ta, tb, ta2, tb2, tc, args, stream, sms);
     }
     return;
   }
@@ -757,6 +798,12 @@ void gemm_bf16_tn(at::Tensor a, at::Tensor b, at::Tensor c) {
 
 void gemm_bf16_tn_extra(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor a2, at::Tensor b2) {
   gemm_impl(a, b, c, a2, b2);
+}
+
+// C[M,N] = A[M,K] · B[K,N] (+ A2[M,64] · B2[64,N]); B read MN-major by the tensor core
+void gemm_bf16_nn(at::Tensor a, at::Tensor b, at::Tensor c, c10::optional<at::Tensor> a2,
+                  c10::optional<at::Tensor> b2) {
+  gemm_impl(a, b, c, a2, b2, true);
 }
 
 // NF4 weight [rows, cols] -> bf16 [rows, cols] (transpose=false) or [cols, rows].

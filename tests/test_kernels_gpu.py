@@ -228,3 +228,92 @@ def test_flash_attention_fwd_bwd(cuda, cfg, causal):
     for a, r in ((q.grad, qr.grad), (k.grad, kr.grad), (v.grad, vr.grad)):
         err = (a.float() - r).abs().max().item()
         assert err < 5e-2 * max(1.0, r.abs().max().item()), err
+
+
+@pytest.mark.parametrize("shape", [(256, 128, 64), (512, 384, 192), (1000, 768, 320),
+                                   (2048, 3072, 3072), (8192, 3072, 12288)])
+@pytest.mark.parametrize("extra", [False, True])
+def test_gemm_bf16_nn_mn_major_b(cuda, shape, extra):
+    """C = A @ B with B row-major [K, N] (the tensor core reads B MN-major)."""
+    M, N, K = shape
+    torch.manual_seed(8)
+    a = torch.randn(M, K, device=cuda, dtype=torch.bfloat16)
+    b = torch.randn(K, N, device=cuda, dtype=torch.bfloat16)
+    c = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+    a2 = b2 = None
+    if extra:
+        a2 = torch.zeros(M, 64, device=cuda, dtype=torch.bfloat16)
+        b2 = torch.zeros(64, N, device=cuda, dtype=torch.bfloat16)
+        a2[:, :16] = torch.randn(M, 16, device=cuda).bfloat16()
+        b2[:16] = torch.randn(16, N, device=cuda).bfloat16()
+    _ext.ext().gemm_bf16_nn(a, b, c, a2, b2)
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    ref = a.float() @ b.float()
+    if extra:
+        ref = ref + a2.float() @ b2.float()
+    tol = 2e-2 * math.sqrt(K) + 1e-2 * ref.abs().max().item()
+    assert (c.float() - ref).abs().max().item() < tol
+
+
+@pytest.mark.parametrize("M", [96, 512, 2048])
+@pytest.mark.parametrize("lora_r", [0, 16])
+def test_nf4_linear_fwd_bwd_vs_fp32(cuda, M, lora_r):
+    """Fused NF4 linear (operand kernel + tcgen05 GEMM + LoRA slab) against the
+    fp32 oracle of the same op: output, input gradient and LoRA gradients."""
+    from zeroq_b200.ops.qlinear import Linear4bit
+
+    torch.manual_seed(11)
+    K, N = 768, 1280
+    lin = Linear4bit(K, N, lora_r=lora_r, lora_alpha=32.0, device=cuda)
+    lin.quantize_from(torch.randn(N, K, device=cuda) * 0.05)
+    if lora_r:
+        with torch.no_grad():
+            lin.lora_B.normal_(0.0, 0.05)
+    x = torch.randn(M, K, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    gy = torch.randn(M, N, device=cuda, dtype=torch.bfloat16)
+    y = lin(x)
+    y.backward(gy)
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+
+    w = lin.dequantized_weight(torch.float32)
+    xf = x.detach().float().requires_grad_(True)
+    params = []
+    yr = xf @ w.t()
+    if lora_r:
+        A = lin.lora_A.detach().clone().requires_grad_(True)
+        B = lin.lora_B.detach().clone().requires_grad_(True)
+        params = [A, B]
+        yr = yr + (xf @ A.t()) @ B.t() * lin.scaling
+    yr.backward(gy.float())
+
+    def close(a, b, rel):
+        return (a.float() - b).abs().max().item() <= rel * b.abs().max().item() + 1e-3
+
+    assert close(y, yr.detach(), 2e-2)
+    assert close(x.grad, xf.grad, 2e-2)
+    if lora_r:
+        assert close(lin.lora_A.grad, params[0].grad, 3e-2)
+        assert close(lin.lora_B.grad, params[1].grad, 3e-2)
+
+
+def test_lm_head_grad_vs_fp32(cuda):
+    """Tied LM head: logits = h·Eᵀ and dh = dlogits·E (E read MN-major in place)."""
+    from zeroq_b200.ops.gemm import LMHeadFunction
+
+    torch.manual_seed(12)
+    M, d, V = 1024, 512, 4096
+    h = torch.randn(M, d, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    E = (torch.randn(V, d, device=cuda) * 0.05).bfloat16().requires_grad_(True)
+    g = torch.randn(M, V, device=cuda, dtype=torch.bfloat16)
+    logits = LMHeadFunction.apply(h, E)
+    logits.backward(g)
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    hf, Ef = h.detach().float(), E.detach().float()
+    ref_dh = g.float() @ Ef
+    ref_dE = g.float().t() @ hf
+    assert (logits.float() - hf @ Ef.t()).abs().max().item() < 2e-2 * (hf @ Ef.t()).abs().max().item() + 1e-2
+    assert (h.grad.float() - ref_dh).abs().max().item() < 2e-2 * ref_dh.abs().max().item() + 1e-2
+    assert (E.grad.float() - ref_dE).abs().max().item() < 2e-2 * ref_dE.abs().max().item() + 1e-2

@@ -118,8 +118,6 @@ def convert_to_4bit_compute(model: nn.Module, coordinator: ZeroQCoordinator,
         count += 1
     if wrapper is not None:
         wrapper.remove_hooks()
-    if hasattr(model, "refresh_head_cache"):
-        model.refresh_head_cache()
     return count
 
 

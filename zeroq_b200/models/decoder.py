@@ -199,7 +199,6 @@ class DecoderLM(nn.Module):
         else:
             self.lm_head = nn.Linear(cfg.d_model, V, bias=False, device=device, dtype=dtype)
             self.lm_head.weight.requires_grad_(cfg.train_embeddings)
-        self._head_t = None  # cached transpose of the (frozen) head matrix
 
     # -- weights ---------------------------------------------------------------
     def head_weight(self) -> torch.Tensor:
@@ -225,7 +224,6 @@ class DecoderLM(nn.Module):
                     w.normal_(0.0, std, generator=g)
                     m.weight = nn.Parameter(w, requires_grad=False)
         self._zero_vocab_padding()
-        self._head_t = None
         return self
 
     def init_nf4_(self, std: float = 0.02, seed: int = 0):
@@ -244,7 +242,6 @@ class DecoderLM(nn.Module):
                     m.quantize_from(w)
                     del w
         self._zero_vocab_padding()
-        self._head_t = None
         return self
 
     def convert_to_4bit_(self):
@@ -256,17 +253,6 @@ class DecoderLM(nn.Module):
                     m.weight = nn.Parameter(torch.empty(0, device=m.weight.device,
                                                         dtype=m.weight.dtype), requires_grad=False)
         return self
-
-    def refresh_head_cache(self):
-        self._head_t = None
-
-    def _head_transposed(self):
-        W = self.head_weight()
-        if W.requires_grad or not W.is_cuda:
-            return None
-        if self._head_t is None or self._head_t.shape != (W.shape[1], W.shape[0]):
-            self._head_t = W.detach().t().contiguous()
-        return self._head_t
 
     # -- forward -----------------------------------------------------------------
     def _layer_call(self, layer, h, delta):
@@ -288,7 +274,7 @@ class DecoderLM(nn.Module):
         if W.numel() == 0:
             raise RuntimeError("the LM head weight is sharded and not gathered here; keep "
                                "'embed_tokens' and 'lm_head' in exclude_modules")
-        logits = LMHeadFunction.apply(x, W, self._head_transposed())
+        logits = LMHeadFunction.apply(x, W)
         if targets is None:
             return logits.view(B, S, -1)[..., : self.cfg.vocab_size]
         return cross_entropy(logits, targets.reshape(-1), vocab=self.cfg.vocab_size,

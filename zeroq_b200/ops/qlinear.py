@@ -7,12 +7,13 @@ layout); no full-precision copy of it is kept between uses.
 
 CUDA path, per call (``csrc/gemm_sm100.cu``):
 
-* the NF4 operand kernel expands ``W`` (forward) or ``Wᵀ`` (input gradient) to a
-  transient bf16 operand that stays L2-resident for the GEMM that follows;
+* the NF4 operand kernel expands ``W`` to a transient bf16 operand ``[N, K]``
+  that stays L2-resident for the GEMM that follows;
 * the tcgen05/TMEM GEMM computes ``Y = X Wᵀ`` and, in the same MMA chain, the
   LoRA up-projection as one extra 64-wide K slab (``U = s·X Aᵀ`` against
   ``B``, both zero-padded to rank 64); the input gradient
-  ``dX = dY W + (s·dY B) A`` is the same GEMM with the transposed operand;
+  ``dX = dY W + (s·dY B) A`` reads the same ``[N, K]`` operand MN-major
+  (``gemm_bf16_nn``), so no transposed operand is produced;
 * ``U``/``V`` (rank-64 padded, skinny) and the ``A``/``B`` weight gradients
   (contractions over tokens) are small cuBLAS GEMMs.
 
@@ -125,13 +126,19 @@ class NF4LinearFunction(torch.autograd.Function):
                 bt_pad = _pad_rows(lora_B.detach().t().to(torch.bfloat16) * scaling)
                 V = gy2 @ bt_pad.t()  # [M, 64] skinny product: cuBLAS
             if ctx.needs_input_grad[0]:
-                wt = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, True)
                 gx = torch.empty(M, K, dtype=torch.bfloat16, device=gy2.device)
-                if has_lora:
-                    E.gemm_bf16_tn_extra(gy2, wt, gx, V, _pad_cols(lora_A.detach().t().to(torch.bfloat16)))
-                else:
-                    E.gemm_bf16_tn(gy2, wt, gx)
-                del wt
+                if M >= 256:  # W [N, K] read MN-major: dX = dY · W
+                    w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
+                    E.gemm_bf16_nn(gy2, w, gx, V if has_lora else None,
+                                   _pad_rows(lora_A.detach().to(torch.bfloat16)) if has_lora else None)
+                else:  # short inputs: single-CTA kernel on the transposed operand
+                    w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, True)
+                    if has_lora:
+                        E.gemm_bf16_tn_extra(gy2, w, gx, V,
+                                             _pad_cols(lora_A.detach().t().to(torch.bfloat16)))
+                    else:
+                        E.gemm_bf16_tn(gy2, w, gx)
+                del w
                 gx = gx.view(*shp[:-1], K)
             if has_lora:
                 if ctx.needs_input_grad[3]:
