@@ -5,6 +5,7 @@
     python benchmarks/kernel_case.py attention --b 8 --s 1024 --h 24 --d 128
     python benchmarks/kernel_case.py nf4_operand --n 12288 --k 3072 [--transpose]
     python benchmarks/kernel_case.py rmsnorm --m 8192 --d 3072
+    python benchmarks/kernel_case.py gelu --m 8192 --n 12288
 
 Each case allocates at most a few GB, runs ``--reps`` launches (default 4) and
 prints the mean CUDA-event time of the last ``--reps - 1`` launches.
@@ -21,9 +22,19 @@ import torch
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 
+_PROFILE = False
+
+
 def _time(fn, reps):
     fn()
     torch.cuda.synchronize()
+    if _PROFILE:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            fn()
+            torch.cuda.synchronize()
+        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=10))
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     s.record()
     for _ in range(reps - 1):
@@ -35,7 +46,7 @@ def _time(fn, reps):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attention", "nf4_operand", "rmsnorm"])
+    ap.add_argument("case", choices=["gemm", "attention", "nf4_operand", "rmsnorm", "gelu"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=3072)
@@ -47,7 +58,10 @@ def main():
     ap.add_argument("--transpose", action="store_true")
     ap.add_argument("--nn", action="store_true", help="gemm: B given as [K, N] (MN-major read)")
     ap.add_argument("--reps", type=int, default=4)
+    ap.add_argument("--profile", action="store_true", help="print one call's kernels (torch profiler)")
     a = ap.parse_args()
+    global _PROFILE
+    _PROFILE = a.profile
 
     from zeroq_b200.ops import _ext
 
@@ -90,6 +104,17 @@ def main():
         ms = _time(lambda: E.nf4_to_bf16(packed, st.absmax, out, a.n, a.k, 64, 0, a.transpose), a.reps)
         byts = a.n * a.k * (0.5 + 4 / 64 + 2)
         print(f"nf4_operand {a.n}x{a.k} transpose={a.transpose}: {ms:.4f} ms, {byts / ms / 1e6:.0f} GB/s")
+    elif a.case == "gelu":
+        from zeroq_b200.ops.activations import gelu
+
+        x = torch.randn(a.m, a.n, device=dev, dtype=torch.bfloat16, requires_grad=True)
+        g = torch.randn_like(x)
+
+        def step():
+            gelu(x).backward(g)
+
+        ms = _time(step, a.reps)
+        print(f"gelu fwd+bwd {a.m}x{a.n}: {ms:.4f} ms, {5 * 2 * a.m * a.n / ms / 1e6:.0f} GB/s (5 passes)")
     elif a.case == "rmsnorm":
         from zeroq_b200.ops.norm import add_rmsnorm
 

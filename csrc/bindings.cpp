@@ -9,6 +9,8 @@ void nf4_dequantize(at::Tensor packed, at::Tensor absmax, at::Tensor out, int64_
                     int64_t qtype);
 // gemm_sm100.cu
 void gemm_bf16_tn(at::Tensor a, at::Tensor b, at::Tensor c);
+void lora_pack(at::Tensor A, at::Tensor B, double scaling, at::Tensor a_pad, at::Tensor b_pad);
+void matmul_accum_f32(at::Tensor A, at::Tensor B, at::Tensor C, double alpha, double beta);
 void gemm_bf16_tn_extra(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor a2, at::Tensor b2);
 void gemm_bf16_nn(at::Tensor a, at::Tensor b, at::Tensor c, c10::optional<at::Tensor> a2,
                   c10::optional<at::Tensor> b2);
@@ -23,6 +25,7 @@ void rmsnorm_bwd(at::Tensor gy, at::Tensor x, at::Tensor w, at::Tensor rstd,
                  c10::optional<at::Tensor> gh, at::Tensor dx, at::Tensor dw_part);
 void rope(at::Tensor x, at::Tensor out, at::Tensor cs, double sign);
 void gelu_fwd(at::Tensor x, at::Tensor y);
+void gelu_cdf_pdf(at::Tensor x, at::Tensor cdf, at::Tensor pdf);
 void gelu_bwd(at::Tensor g, at::Tensor x, at::Tensor dx);
 void swiglu_fwd(at::Tensor gate, at::Tensor up, at::Tensor y);
 void swiglu_bwd(at::Tensor g, at::Tensor gate, at::Tensor up, at::Tensor dgate, at::Tensor dup);
@@ -70,6 +73,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16_tn", &gemm_bf16_tn);
   m.def("gemm_bf16_tn_extra", &gemm_bf16_tn_extra);
   m.def("gemm_bf16_nn", &gemm_bf16_nn);
+  m.def("lora_pack", &lora_pack);
+  m.def("matmul_accum_f32", &matmul_accum_f32);
   m.def("gemm_status", &gemm_status);
   m.def("set_gemm_pair_mode", &set_gemm_pair_mode);
   m.def("nf4_to_bf16", &nf4_to_bf16);
@@ -78,6 +83,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope", &rope);
   m.def("gelu_fwd", &gelu_fwd);
   m.def("gelu_bwd", &gelu_bwd);
+  m.def("gelu_cdf_pdf", &gelu_cdf_pdf);
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("ce_fwd", &ce_fwd);

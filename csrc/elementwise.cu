@@ -2,7 +2,7 @@
 // (forward/backward), RoPE, GELU, SwiGLU, fused cross-entropy, AdamW and Lion
 // on flat buffers.  All read bf16/fp32 with 16-byte vector accesses where the
 // layout allows and compute in fp32.  erf/exp/sin/cos/rsqrt are CUDA's own
-// functions.
+// functions, except the GELU CDF (a named published approximation, below).
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -12,11 +12,14 @@
 namespace zq {
 
 // ----------------------------------------------------------------------------
-// RMSNorm (+ residual add).  One CTA of 128 threads per row; each thread owns
-// up to 8 chunks of 8 bf16 (D <= 8192, D % 8 == 0).
+// RMSNorm (+ residual add).  A team of TPR lanes (32, 64 or 128) owns one row;
+// each lane owns NC chunks of 8 bf16 (D <= 8 * TPR * NC, D % 8 == 0) and
+// issues all of its loads before the first use, so a 256-thread CTA keeps
+// 256 * NC * 16 B (x2-3 tensors) in flight.  Teams of one warp reduce with
+// shuffles only; wider teams add one shared-memory exchange.
 // ----------------------------------------------------------------------------
-constexpr int kNormThreads = 128;
-constexpr int kNormMaxChunks = 8;
+constexpr int kNormThreads = 256;
+constexpr int kNormMaxD = 8192;
 
 __device__ __forceinline__ void bf16x8_to_f32(const uint4& u, float (&f)[8]) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -37,125 +40,178 @@ __device__ __forceinline__ uint4 f32_to_bf16x8(const float (&f)[8]) {
   return u;
 }
 
-__device__ __forceinline__ float block_sum_128(float v, float* red) {
+// Sum of v over the TPR lanes of this thread's team.  Every thread of the CTA
+// must call it (it contains __syncthreads when TPR > 32).
+template <int TPR>
+__device__ __forceinline__ float team_sum(float v, float* red) {
   v = warp_sum(v);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  float r = red[0] + red[1] + red[2] + red[3];
-  __syncthreads();
-  return r;
+  if constexpr (TPR == 32) {
+    return v;
+  } else {
+    constexpr int W = TPR / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    const int base = (warp / W) * W;
+    float r = 0.0f;
+#pragma unroll
+    for (int i = 0; i < W; ++i) r += red[base + i];
+    __syncthreads();
+    return r;
+  }
 }
 
+template <int NC, int TPR>
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_fwd_kernel(
     const __nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ d,
     const float* __restrict__ w, __nv_bfloat16* __restrict__ hout, __nv_bfloat16* __restrict__ y,
-    float* __restrict__ rstd, int D, float eps) {
-  __shared__ float red[4];
-  const int64_t row = blockIdx.x;
+    float* __restrict__ rstd, int64_t M, int D, float eps) {
+  __shared__ float red[kNormThreads / 32];
+  constexpr int R = kNormThreads / TPR;
+  const int team = threadIdx.x / TPR, tl = threadIdx.x % TPR;
+  const int64_t row = (int64_t)blockIdx.x * R + team;
+  const bool live = row < M;
   const int nch = D >> 3;
-  float v[kNormMaxChunks][8];
+  uint4 hv[NC], dv[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int ch = c * TPR + tl;
+    if (live && ch < nch) {
+      hv[c] = *reinterpret_cast<const uint4*>(h + row * D + (int64_t)ch * 8);
+      if (d != nullptr) dv[c] = *reinterpret_cast<const uint4*>(d + row * D + (int64_t)ch * 8);
+    }
+  }
+  float v[NC][8];
   float ss = 0.0f;
 #pragma unroll
-  for (int c = 0; c < kNormMaxChunks; ++c) {
-    const int ch = c * kNormThreads + threadIdx.x;
-    if (ch < nch) {
-      const int64_t off = row * D + (int64_t)ch * 8;
-      bf16x8_to_f32(*reinterpret_cast<const uint4*>(h + off), v[c]);
+  for (int c = 0; c < NC; ++c) {
+    const int ch = c * TPR + tl;
+    if (live && ch < nch) {
+      bf16x8_to_f32(hv[c], v[c]);
       if (d != nullptr) {
         float t[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(d + off), t);
+        bf16x8_to_f32(dv[c], t);
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[c][i] += t[i];
         // round the residual stream to bf16, exactly what is stored and reused
-        uint4 packed = f32_to_bf16x8(v[c]);
-        *reinterpret_cast<uint4*>(hout + off) = packed;
+        const uint4 packed = f32_to_bf16x8(v[c]);
+        *reinterpret_cast<uint4*>(hout + row * D + (int64_t)ch * 8) = packed;
         bf16x8_to_f32(packed, v[c]);
       }
 #pragma unroll
       for (int i = 0; i < 8; ++i) ss += v[c][i] * v[c][i];
     }
   }
-  const float tot = block_sum_128(ss, red);
+  const float tot = team_sum<TPR>(ss, red);
+  if (!live) return;
   const float r = rsqrtf(tot / (float)D + eps);
-  if (threadIdx.x == 0) rstd[row] = r;
+  if (tl == 0) rstd[row] = r;
 #pragma unroll
-  for (int c = 0; c < kNormMaxChunks; ++c) {
-    const int ch = c * kNormThreads + threadIdx.x;
+  for (int c = 0; c < NC; ++c) {
+    const int ch = c * TPR + tl;
     if (ch < nch) {
-      const int64_t off = row * D + (int64_t)ch * 8;
+      const float4 w0 = reinterpret_cast<const float4*>(w)[ch * 2];
+      const float4 w1 = reinterpret_cast<const float4*>(w)[ch * 2 + 1];
+      const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
       float o[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = v[c][i] * r * w[ch * 8 + i];
-      *reinterpret_cast<uint4*>(y + off) = f32_to_bf16x8(o);
+      for (int i = 0; i < 8; ++i) o[i] = v[c][i] * r * ww[i];
+      *reinterpret_cast<uint4*>(y + row * D + (int64_t)ch * 8) = f32_to_bf16x8(o);
     }
   }
 }
 
-// dx = r * (g*w - xhat * mean(g*w*xhat)) [+ gh];  dw += sum_rows g * xhat
+// dx = r * (g*w - xhat * mean(g*w*xhat)) [+ gh];  dw += sum_rows g * xhat.
+// Teams walk rows with a grid stride and keep their dw share in registers; the
+// teams of a CTA combine through shared memory into one row of dw_part.
+template <int NC, int TPR>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
     const __nv_bfloat16* __restrict__ gy, const __nv_bfloat16* __restrict__ x,
     const float* __restrict__ w, const float* __restrict__ rstd,
     const __nv_bfloat16* __restrict__ gh, __nv_bfloat16* __restrict__ dx,
     float* __restrict__ dw_part, int64_t M, int D) {
-  __shared__ float red[4];
+  __shared__ float red[kNormThreads / 32];
+  extern __shared__ float sdw[];  // [D]
+  constexpr int R = kNormThreads / TPR;
+  const int team = threadIdx.x / TPR, tl = threadIdx.x % TPR;
   const int nch = D >> 3;
-  float dwacc[kNormMaxChunks][8];
+  for (int i = threadIdx.x; i < D; i += kNormThreads) sdw[i] = 0.0f;
+  float dwacc[NC][8];
 #pragma unroll
-  for (int c = 0; c < kNormMaxChunks; ++c)
+  for (int c = 0; c < NC; ++c)
 #pragma unroll
     for (int i = 0; i < 8; ++i) dwacc[c][i] = 0.0f;
-  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
-    const float r = rstd[row];
-    float xh[kNormMaxChunks][8], gw[kNormMaxChunks][8];
+  const float4* w4 = reinterpret_cast<const float4*>(w);  // [D/4], L1-resident
+  const int64_t groups = (M + R - 1) / R;
+  for (int64_t gidx = blockIdx.x; gidx < groups; gidx += gridDim.x) {
+    const int64_t row = gidx * R + team;
+    const bool live = row < M;
+    uint4 xv[NC], gv[NC], hv[NC];
+#pragma unroll
+    for (int c = 0; c < NC; ++c) {
+      const int ch = c * TPR + tl;
+      if (live && ch < nch) {
+        const int64_t off = row * D + (int64_t)ch * 8;
+        xv[c] = *reinterpret_cast<const uint4*>(x + off);
+        gv[c] = *reinterpret_cast<const uint4*>(gy + off);
+        if (gh != nullptr) hv[c] = *reinterpret_cast<const uint4*>(gh + off);
+      }
+    }
+    const float r = live ? rstd[row] : 0.0f;
     float dot = 0.0f;
 #pragma unroll
-    for (int c = 0; c < kNormMaxChunks; ++c) {
-      const int ch = c * kNormThreads + threadIdx.x;
-      if (ch < nch) {
-        const int64_t off = row * D + (int64_t)ch * 8;
-        float g[8];
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(x + off), xh[c]);
-        bf16x8_to_f32(*reinterpret_cast<const uint4*>(gy + off), g);
+    for (int c = 0; c < NC; ++c) {
+      const int ch = c * TPR + tl;
+      if (live && ch < nch) {
+        float xf[8], gf[8];
+        bf16x8_to_f32(xv[c], xf);
+        bf16x8_to_f32(gv[c], gf);
+        const float4 w0 = __ldg(w4 + ch * 2), w1 = __ldg(w4 + ch * 2 + 1);
+        const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          xh[c][i] *= r;
-          gw[c][i] = g[i] * w[ch * 8 + i];
-          dot += gw[c][i] * xh[c][i];
-          dwacc[c][i] += g[i] * xh[c][i];
+          const float xh = xf[i] * r;
+          dot += gf[i] * ww[i] * xh;
+          dwacc[c][i] += gf[i] * xh;
         }
       }
     }
-    const float mean = block_sum_128(dot, red) / (float)D;
+    const float mean = team_sum<TPR>(dot, red) / (float)D;
+    if (live) {
 #pragma unroll
-    for (int c = 0; c < kNormMaxChunks; ++c) {
-      const int ch = c * kNormThreads + threadIdx.x;
-      if (ch < nch) {
-        const int64_t off = row * D + (int64_t)ch * 8;
-        float o[8];
+      for (int c = 0; c < NC; ++c) {
+        const int ch = c * TPR + tl;
+        if (ch < nch) {
+          float xf[8], gf[8], o[8];
+          bf16x8_to_f32(xv[c], xf);
+          bf16x8_to_f32(gv[c], gf);
+          const float4 w0 = __ldg(w4 + ch * 2), w1 = __ldg(w4 + ch * 2 + 1);
+          const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = r * (gw[c][i] - xh[c][i] * mean);
-        if (gh != nullptr) {
-          float t[8];
-          bf16x8_to_f32(*reinterpret_cast<const uint4*>(gh + off), t);
+          for (int i = 0; i < 8; ++i) o[i] = r * (gf[i] * ww[i] - xf[i] * r * mean);
+          if (gh != nullptr) {
+            float t[8];
+            bf16x8_to_f32(hv[c], t);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) o[i] += t[i];
+            for (int i = 0; i < 8; ++i) o[i] += t[i];
+          }
+          *reinterpret_cast<uint4*>(dx + row * D + (int64_t)ch * 8) = f32_to_bf16x8(o);
         }
-        *reinterpret_cast<uint4*>(dx + off) = f32_to_bf16x8(o);
       }
     }
   }
-  // this CTA's partial weight gradient: one row of dw_part (summed on the host side)
-  float* dst = dw_part + (int64_t)blockIdx.x * D;
+  __syncthreads();
 #pragma unroll
-  for (int c = 0; c < kNormMaxChunks; ++c) {
-    const int ch = c * kNormThreads + threadIdx.x;
+  for (int c = 0; c < NC; ++c) {
+    const int ch = c * TPR + tl;
     if (ch < nch) {
-      float4* d4 = reinterpret_cast<float4*>(dst + ch * 8);
-      d4[0] = make_float4(dwacc[c][0], dwacc[c][1], dwacc[c][2], dwacc[c][3]);
-      d4[1] = make_float4(dwacc[c][4], dwacc[c][5], dwacc[c][6], dwacc[c][7]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) atomicAdd(&sdw[ch * 8 + i], dwacc[c][i]);
     }
   }
+  __syncthreads();
+  float* dst = dw_part + (int64_t)blockIdx.x * D;
+  for (int i = threadIdx.x; i < D; i += kNormThreads) dst[i] = sdw[i];
 }
 
 // ----------------------------------------------------------------------------
@@ -193,31 +249,96 @@ __global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* 
 // ----------------------------------------------------------------------------
 // GELU (erf form) and SwiGLU
 // ----------------------------------------------------------------------------
+// Gaussian CDF and PDF for GELU.  erf uses the rational approximation of
+// Abramowitz & Stegun, Handbook of Mathematical Functions (1964), formula
+// 7.1.26 (Hastings): for a >= 0,
+//   erf(a) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-a^2) + e(a),
+//   t = 1 / (1 + p a),  |e(a)| <= 1.5e-7.
+// With a = |x| / sqrt(2), exp(-a^2) = exp(-x^2 / 2) is also the unnormalised
+// PDF, so one reciprocal and one exponential give both.
+struct GeluCP {
+  float cdf, pdf;
+};
+
+__device__ __forceinline__ GeluCP gelu_cdf_pdf(float x) {
+  constexpr float kP = 0.3275911f;
+  constexpr float kA1 = 0.254829592f, kA2 = -0.284496736f, kA3 = 1.421413741f,
+                  kA4 = -1.453152027f, kA5 = 1.061405429f;
+  constexpr float kInvSqrt2 = 0.70710678118654752f, kInvSqrt2Pi = 0.39894228040143268f;
+  const float a = fabsf(x) * kInvSqrt2;
+  const float t = __fdividef(1.0f, fmaf(kP, a, 1.0f));
+  const float e = __expf(-0.5f * x * x);
+  const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, kA5, kA4), kA3), kA2), kA1);
+  const float tail = 0.5f * poly * e;  // = (1 - erf(a)) / 2
+  GeluCP r;
+  r.cdf = x >= 0.0f ? 1.0f - tail : tail;
+  r.pdf = e * kInvSqrt2Pi;
+  return r;
+}
+
+// Each thread handles kEwIlp chunks of 8 elements, kEwIlp * blockDim apart, and
+// issues all loads before computing.
+constexpr int kEwIlp = 4;
+
 __global__ void gelu_fwd_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y,
                                 int64_t n8) {
-  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= n8) return;
-  float v[8], o[8];
-  bf16x8_to_f32(reinterpret_cast<const uint4*>(x)[t], v);
+  const int64_t base = (int64_t)blockIdx.x * blockDim.x * kEwIlp + threadIdx.x;
+  uint4 in[kEwIlp];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) o[i] = 0.5f * v[i] * (1.0f + erff(v[i] * 0.70710678118654752f));
-  reinterpret_cast<uint4*>(y)[t] = f32_to_bf16x8(o);
+  for (int j = 0; j < kEwIlp; ++j) {
+    const int64_t t = base + (int64_t)j * blockDim.x;
+    if (t < n8) in[j] = reinterpret_cast<const uint4*>(x)[t];
+  }
+#pragma unroll
+  for (int j = 0; j < kEwIlp; ++j) {
+    const int64_t t = base + (int64_t)j * blockDim.x;
+    if (t < n8) {
+      float v[8], o[8];
+      bf16x8_to_f32(in[j], v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = v[i] * gelu_cdf_pdf(v[i]).cdf;
+      reinterpret_cast<uint4*>(y)[t] = f32_to_bf16x8(o);
+    }
+  }
 }
 
 __global__ void gelu_bwd_kernel(const __nv_bfloat16* __restrict__ g, const __nv_bfloat16* __restrict__ x,
                                 __nv_bfloat16* __restrict__ dx, int64_t n8) {
-  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= n8) return;
-  float v[8], gg[8], o[8];
-  bf16x8_to_f32(reinterpret_cast<const uint4*>(x)[t], v);
-  bf16x8_to_f32(reinterpret_cast<const uint4*>(g)[t], gg);
+  const int64_t base = (int64_t)blockIdx.x * blockDim.x * kEwIlp + threadIdx.x;
+  uint4 xin[kEwIlp], gin[kEwIlp];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float cdf = 0.5f * (1.0f + erff(v[i] * 0.70710678118654752f));
-    const float pdf = expf(-0.5f * v[i] * v[i]) * 0.39894228040143268f;
-    o[i] = gg[i] * (cdf + v[i] * pdf);
+  for (int j = 0; j < kEwIlp; ++j) {
+    const int64_t t = base + (int64_t)j * blockDim.x;
+    if (t < n8) {
+      xin[j] = reinterpret_cast<const uint4*>(x)[t];
+      gin[j] = reinterpret_cast<const uint4*>(g)[t];
+    }
   }
-  reinterpret_cast<uint4*>(dx)[t] = f32_to_bf16x8(o);
+#pragma unroll
+  for (int j = 0; j < kEwIlp; ++j) {
+    const int64_t t = base + (int64_t)j * blockDim.x;
+    if (t < n8) {
+      float v[8], gg[8], o[8];
+      bf16x8_to_f32(xin[j], v);
+      bf16x8_to_f32(gin[j], gg);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const GeluCP c = gelu_cdf_pdf(v[i]);
+        o[i] = gg[i] * (c.cdf + v[i] * c.pdf);
+      }
+      reinterpret_cast<uint4*>(dx)[t] = f32_to_bf16x8(o);
+    }
+  }
+}
+
+// fp32 GELU CDF/PDF of the approximation above, for checking its error bound
+__global__ void gelu_cdf_pdf_kernel(const float* __restrict__ x, float* __restrict__ cdf,
+                                    float* __restrict__ pdf, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const GeluCP c = gelu_cdf_pdf(x[i]);
+  cdf[i] = c.cdf;
+  pdf[i] = c.pdf;
 }
 
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gate,
@@ -422,6 +543,32 @@ static void check_bf16(const at::Tensor& t, const char* name) {
   TORCH_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0, name, ": 16-byte alignment");
 }
 
+// Team width and chunks per lane for a row of D bf16: the narrowest team whose
+// lanes need at most 8 chunks, then the smallest instantiated chunk count.
+static void norm_shape(int64_t D, int* tpr, int* nc) {
+  const int64_t chunks = D / 8;
+  *tpr = chunks <= 32 * 8 ? 32 : (chunks <= 64 * 8 ? 64 : 128);
+  const int64_t need = (chunks + *tpr - 1) / *tpr;
+  *nc = need <= 1 ? 1 : need <= 2 ? 2 : need <= 4 ? 4 : need <= 6 ? 6 : 8;
+}
+
+#define ZQ_NORM_DISPATCH(TPR, NC, KERNEL, ...)                                     \
+  do {                                                                            \
+    if (TPR == 32) {                                                              \
+      if (NC == 1) KERNEL<1, 32>__VA_ARGS__;                                      \
+      else if (NC == 2) KERNEL<2, 32>__VA_ARGS__;                                 \
+      else if (NC == 4) KERNEL<4, 32>__VA_ARGS__;                                 \
+      else if (NC == 6) KERNEL<6, 32>__VA_ARGS__;                                 \
+      else KERNEL<8, 32>__VA_ARGS__;                                              \
+    } else if (TPR == 64) {                                                       \
+      if (NC == 6) KERNEL<6, 64>__VA_ARGS__;                                      \
+      else KERNEL<8, 64>__VA_ARGS__;                                              \
+    } else {                                                                      \
+      if (NC == 6) KERNEL<6, 128>__VA_ARGS__;                                     \
+      else KERNEL<8, 128>__VA_ARGS__;                                             \
+    }                                                                             \
+  } while (0)
+
 void add_rmsnorm_fwd(at::Tensor h, c10::optional<at::Tensor> d, at::Tensor w, at::Tensor hout,
                      at::Tensor y, at::Tensor rstd, double eps) {
   check_bf16(h, "h");
@@ -431,7 +578,8 @@ void add_rmsnorm_fwd(at::Tensor h, c10::optional<at::Tensor> d, at::Tensor w, at
   TORCH_CHECK(w.numel() == D, "norm weight has ", w.numel(), " elements, expected ", D);
   TORCH_CHECK(y.numel() == h.numel() && rstd.numel() >= M && rstd.scalar_type() == at::kFloat,
               "norm output / rstd sizes");
-  TORCH_CHECK(D % 8 == 0 && D <= 8 * kNormThreads * kNormMaxChunks, "D must be %8 and <= 8192");
+  TORCH_CHECK(D % 8 == 0 && D <= kNormMaxD, "D must be %8 and <= 8192");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(w.data_ptr()) & 15) == 0, "norm weight: 16-byte alignment");
   const at::cuda::CUDAGuard guard(h.device());
   const __nv_bfloat16* dp = nullptr;
   if (d.has_value() && d->defined()) {
@@ -440,21 +588,53 @@ void add_rmsnorm_fwd(at::Tensor h, c10::optional<at::Tensor> d, at::Tensor w, at
     TORCH_CHECK(d->numel() == h.numel() && hout.numel() == h.numel(), "add_rmsnorm: sizes");
     dp = cbf(*d);
   }
-  add_rmsnorm_fwd_kernel<<<(unsigned)M, kNormThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      cbf(h), dp, w.data_ptr<float>(), dp ? bf(hout) : nullptr, bf(y), rstd.data_ptr<float>(),
-      (int)D, (float)eps);
+  if (M == 0) return;
+  int tpr, nc;
+  norm_shape(D, &tpr, &nc);
+  const int rows_per_cta = kNormThreads / tpr;
+  const unsigned grid = (unsigned)((M + rows_per_cta - 1) / rows_per_cta);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  ZQ_NORM_DISPATCH(tpr, nc, add_rmsnorm_fwd_kernel, <<<grid, kNormThreads, 0, stream>>>(
+      cbf(h), dp, w.data_ptr<float>(), dp ? bf(hout) : nullptr, bf(y), rstd.data_ptr<float>(), M,
+      (int)D, (float)eps));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-// dw_part: [grid, D] fp32 partial sums, grid = dw_part.size(0); caller sums over rows
+namespace zq {
+// Raw-pointer launcher of the backward kernel, shared by the ATen wrapper below
+// and the allocation-free entry point (noalloc.cu).  Writes one row of dw_part
+// per CTA for at most max_grid CTAs and returns the number of rows written in
+// *grid_out.  Allocates nothing.
+cudaError_t launch_rmsnorm_bwd(const __nv_bfloat16* gy, const __nv_bfloat16* x, const float* w,
+                               const float* rstd, const __nv_bfloat16* gh, __nv_bfloat16* dx,
+                               float* dw_part, int64_t M, int D, int64_t max_grid,
+                               cudaStream_t stream, int64_t* grid_out) {
+  if (M < 1 || D < 8 || D % 8 != 0 || D > kNormMaxD || max_grid < 1) return cudaErrorInvalidValue;
+  int tpr, nc;
+  norm_shape(D, &tpr, &nc);
+  const int rows_per_cta = kNormThreads / tpr;
+  const int64_t groups = (M + rows_per_cta - 1) / rows_per_cta;
+  const int64_t grid = std::min<int64_t>(groups, max_grid);
+  const size_t smem = (size_t)D * sizeof(float);
+  ZQ_NORM_DISPATCH(tpr, nc, rmsnorm_bwd_kernel, <<<(unsigned)grid, kNormThreads, smem, stream>>>(
+      gy, x, w, rstd, gh, dx, dw_part, M, D));
+  *grid_out = grid;
+  return cudaGetLastError();
+}
+}  // namespace zq
+
+// dw_part: [G, D] fp32 partial sums; rows past the grid are zeroed, so the
+// caller's sum over all G rows is the weight gradient.
 void rmsnorm_bwd(at::Tensor gy, at::Tensor x, at::Tensor w, at::Tensor rstd,
                  c10::optional<at::Tensor> gh, at::Tensor dx, at::Tensor dw_part) {
   check_bf16(gy, "gy");
   check_bf16(x, "x");
   check_bf16(dx, "dx");
   const int64_t D = x.size(-1), M = x.numel() / D;
-  TORCH_CHECK(D % 8 == 0 && D <= 8 * kNormThreads * kNormMaxChunks, "D must be %8 and <= 8192");
-  TORCH_CHECK(w.numel() == D && w.scalar_type() == at::kFloat, "norm weight must be fp32 [D]");
+  TORCH_CHECK(D % 8 == 0 && D <= kNormMaxD, "D must be %8 and <= 8192");
+  TORCH_CHECK(w.numel() == D && w.scalar_type() == at::kFloat && w.is_contiguous(),
+              "norm weight must be fp32 [D]");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(w.data_ptr()) & 15) == 0, "norm weight: 16-byte alignment");
   TORCH_CHECK(gy.numel() == x.numel() && dx.numel() == x.numel() && rstd.numel() >= M,
               "rmsnorm_bwd: tensor sizes");
   const at::cuda::CUDAGuard guard(x.device());
@@ -466,11 +646,15 @@ void rmsnorm_bwd(at::Tensor gy, at::Tensor x, at::Tensor w, at::Tensor rstd,
   }
   TORCH_CHECK(dw_part.dim() == 2 && dw_part.size(1) == D && dw_part.is_contiguous() &&
                   dw_part.scalar_type() == at::kFloat, "dw_part must be fp32 [grid, D]");
-  const int64_t grid = std::min<int64_t>(M, dw_part.size(0));
-  rmsnorm_bwd_kernel<<<(unsigned)grid, kNormThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      cbf(gy), cbf(x), w.data_ptr<float>(), rstd.data_ptr<float>(), ghp, bf(dx),
-      dw_part.data_ptr<float>(), M, (int)D);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (M == 0) {
+    dw_part.zero_();
+    return;
+  }
+  int64_t grid = 0;
+  C10_CUDA_CHECK(zq::launch_rmsnorm_bwd(cbf(gy), cbf(x), w.data_ptr<float>(), rstd.data_ptr<float>(),
+                                    ghp, bf(dx), dw_part.data_ptr<float>(), M, (int)D,
+                                    dw_part.size(0), at::cuda::getCurrentCUDAStream(), &grid));
+  if (grid < dw_part.size(0)) dw_part.narrow(0, grid, dw_part.size(0) - grid).zero_();
 }
 
 void rope(at::Tensor x, at::Tensor out, at::Tensor cs, double sign) {
@@ -500,7 +684,22 @@ void gelu_fwd(at::Tensor x, at::Tensor y) {
   TORCH_CHECK(x.numel() % 8 == 0 && y.numel() == x.numel(), "gelu: numel % 8 and equal sizes");
   const int64_t n8 = x.numel() / 8;
   const at::cuda::CUDAGuard guard(x.device());
-  gelu_fwd_kernel<<<ew_grid(n8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(cbf(x), bf(y), n8);
+  gelu_fwd_kernel<<<ew_grid((n8 + kEwIlp - 1) / kEwIlp), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      cbf(x), bf(y), n8);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gelu_cdf_pdf(at::Tensor x, at::Tensor cdf, at::Tensor pdf) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kFloat && x.is_contiguous() &&
+                  cdf.sizes() == x.sizes() && pdf.sizes() == x.sizes() && cdf.is_contiguous() &&
+                  pdf.is_contiguous() && cdf.scalar_type() == at::kFloat &&
+                  pdf.scalar_type() == at::kFloat,
+              "gelu_cdf_pdf: contiguous fp32 CUDA tensors of one shape");
+  const at::cuda::CUDAGuard guard(x.device());
+  const int64_t n = x.numel();
+  if (n == 0) return;
+  gelu_cdf_pdf_kernel<<<(unsigned)((n + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      x.data_ptr<float>(), cdf.data_ptr<float>(), pdf.data_ptr<float>(), n);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -512,7 +711,8 @@ void gelu_bwd(at::Tensor g, at::Tensor x, at::Tensor dx) {
               "gelu: numel % 8 and equal sizes");
   const int64_t n8 = x.numel() / 8;
   const at::cuda::CUDAGuard guard(x.device());
-  gelu_bwd_kernel<<<ew_grid(n8), 256, 0, at::cuda::getCurrentCUDAStream()>>>(cbf(g), cbf(x), bf(dx), n8);
+  gelu_bwd_kernel<<<ew_grid((n8 + kEwIlp - 1) / kEwIlp), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      cbf(g), cbf(x), bf(dx), n8);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -1,0 +1,110 @@
+// LoRA support for the NF4 linear layer:
+//  * lora_pack: the padded, pre-scaled bf16 operands that ride as the extra
+//    64-wide K slab of the tcgen05 GEMM (one launch per module per optimizer
+//    step, rows/columns past the rank stay zero);
+//  * matmul_accum_f32: C (fp32) = beta * C + alpha * A @ B for bf16 A, B, so the
+//    LoRA weight gradients accumulate straight into the fp32 .grad buffers with
+//    no cast or add kernel.  This is a plain library GEMM (cuBLAS, bf16 inputs,
+//    fp32 accumulate and output).
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cublas_v2.h>
+
+#include "common.cuh"
+
+namespace zq {
+
+// a_pad[i, k] = s * A[i, k] for i < r; b_pad[n, j] = B[n, j] for j < r.
+__global__ void lora_pack_kernel(const float* __restrict__ A, const float* __restrict__ B,
+                                 __nv_bfloat16* __restrict__ a_pad, int64_t a_ld,
+                                 __nv_bfloat16* __restrict__ b_pad, int64_t b_ld, int r, int64_t K,
+                                 int64_t N, float s) {
+  const int64_t na = (int64_t)r * K, nb = N * r;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < na + nb;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    if (i < na) {
+      const int64_t row = i / K, col = i % K;
+      a_pad[row * a_ld + col] = __float2bfloat16_rn(s * A[i]);
+    } else {
+      const int64_t j = i - na, row = j / r, col = j % r;
+      b_pad[row * b_ld + col] = __float2bfloat16_rn(B[j]);
+    }
+  }
+}
+
+}  // namespace zq
+
+using namespace zq;
+
+void lora_pack(at::Tensor A, at::Tensor B, double scaling, at::Tensor a_pad, at::Tensor b_pad) {
+  TORCH_CHECK(A.is_cuda() && A.scalar_type() == at::kFloat && A.is_contiguous() && A.dim() == 2,
+              "lora_pack: A must be contiguous fp32 [r, K]");
+  TORCH_CHECK(B.is_cuda() && B.scalar_type() == at::kFloat && B.is_contiguous() && B.dim() == 2,
+              "lora_pack: B must be contiguous fp32 [N, r]");
+  const int64_t r = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == r, "lora_pack: rank mismatch");
+  TORCH_CHECK(a_pad.scalar_type() == at::kBFloat16 && a_pad.dim() == 2 && a_pad.size(0) >= r &&
+                  a_pad.size(1) == K && a_pad.stride(1) == 1,
+              "lora_pack: a_pad must be bf16 [>= r, K] with unit column stride");
+  TORCH_CHECK(b_pad.scalar_type() == at::kBFloat16 && b_pad.dim() == 2 && b_pad.size(0) == N &&
+                  b_pad.size(1) >= r && b_pad.stride(1) == 1,
+              "lora_pack: b_pad must be bf16 [N, >= r] with unit column stride");
+  const at::cuda::CUDAGuard guard(A.device());
+  const int64_t total = r * K + N * r;
+  if (total == 0) return;
+  const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 8);
+  lora_pack_kernel<<<(unsigned)blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      A.data_ptr<float>(), B.data_ptr<float>(),
+      reinterpret_cast<__nv_bfloat16*>(a_pad.data_ptr()), a_pad.stride(0),
+      reinterpret_cast<__nv_bfloat16*>(b_pad.data_ptr()), b_pad.stride(0), (int)r, K, N,
+      (float)scaling);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Operand of a row-major product as cuBLAS (column-major) sees it: a matrix
+// whose last dimension is contiguous is "row-major" with leading dimension
+// stride(0); one whose first dimension is contiguous is "column-major" with
+// leading dimension stride(1).
+static bool row_major(const at::Tensor& t, int64_t* ld) {
+  if (t.stride(1) == 1 && t.stride(0) >= std::max<int64_t>(1, t.size(1))) {
+    *ld = t.stride(0);
+    return true;
+  }
+  TORCH_CHECK(t.stride(0) == 1 && t.stride(1) >= std::max<int64_t>(1, t.size(0)),
+              "matmul_accum_f32: operands must have one unit stride");
+  *ld = t.stride(1);
+  return false;
+}
+
+// C[m, n] (fp32, row-major contiguous) = beta * C + alpha * A[m, k] @ B[k, n].
+void matmul_accum_f32(at::Tensor A, at::Tensor B, at::Tensor C, double alpha, double beta) {
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && C.is_cuda(), "matmul_accum_f32: CUDA tensors");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16,
+              "matmul_accum_f32: A and B must be bf16");
+  TORCH_CHECK(C.scalar_type() == at::kFloat && C.is_contiguous(), "matmul_accum_f32: C fp32 contiguous");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "matmul_accum_f32: 2-D operands");
+  const int64_t m = A.size(0), k = A.size(1), n = B.size(1);
+  TORCH_CHECK(B.size(0) == k && C.size(0) == m && C.size(1) == n, "matmul_accum_f32: shapes");
+  if (m == 0 || n == 0) return;
+  const at::cuda::CUDAGuard guard(C.device());
+  if (k == 0) {
+    C.mul_(beta);
+    return;
+  }
+  int64_t lda = 0, ldb = 0;
+  const bool a_rm = row_major(A, &lda);
+  const bool b_rm = row_major(B, &ldb);
+  // row-major C = column-major C^T [n, m] = B^T [n, k] @ A^T [k, m]
+  const cublasOperation_t opB = b_rm ? CUBLAS_OP_N : CUBLAS_OP_T;
+  const cublasOperation_t opA = a_rm ? CUBLAS_OP_N : CUBLAS_OP_T;
+  const float al = (float)alpha, be = (float)beta;
+  cublasHandle_t h = at::cuda::getCurrentCUDABlasHandle();
+  TORCH_CHECK(m <= INT32_MAX && n <= INT32_MAX && k <= INT32_MAX, "matmul_accum_f32: size");
+  const cublasStatus_t st = cublasGemmEx(
+      h, opB, opA, (int)n, (int)m, (int)k, &al, B.data_ptr(), CUDA_R_16BF, (int)ldb, A.data_ptr(),
+      CUDA_R_16BF, (int)lda, &be, C.data_ptr(), CUDA_R_32F, (int)n, CUBLAS_COMPUTE_32F,
+      CUBLAS_GEMM_DEFAULT);
+  TORCH_CHECK(st == CUBLAS_STATUS_SUCCESS, "matmul_accum_f32: cublasGemmEx failed with status ",
+              (int)st);
+}

@@ -9,12 +9,12 @@
 #include "noalloc.cuh"
 
 namespace zq {
-// defined in elementwise.cu: per-CTA partial weight gradients into dw_part[gridDim.x][D]
-__global__ void __launch_bounds__(128) rmsnorm_bwd_kernel(
-    const __nv_bfloat16* __restrict__ gy, const __nv_bfloat16* __restrict__ x,
-    const float* __restrict__ w, const float* __restrict__ rstd,
-    const __nv_bfloat16* __restrict__ gh, __nv_bfloat16* __restrict__ dx,
-    float* __restrict__ dw_part, int64_t M, int D);
+// defined in elementwise.cu: per-CTA partial weight gradients into dw_part[grid][D],
+// grid <= max_grid returned in *grid_out; allocates nothing
+cudaError_t launch_rmsnorm_bwd(const __nv_bfloat16* gy, const __nv_bfloat16* x, const float* w,
+                               const float* rstd, const __nv_bfloat16* gh, __nv_bfloat16* dx,
+                               float* dw_part, int64_t M, int D, int64_t max_grid,
+                               cudaStream_t stream, int64_t* grid_out);
 }  // namespace zq
 
 namespace {
@@ -62,8 +62,8 @@ extern "C" int zq_rmsnorm_bwd_noalloc(const void* gy, const void* x, const float
                 "static scratch");
   if (!gy || !x || !w || !rstd || !dx || !dw)
     return fail(cudaErrorInvalidValue, "zq_rmsnorm_bwd_noalloc: a required pointer is NULL");
-  if (!aligned16(gy) || !aligned16(x) || !aligned16(dx) || (gh && !aligned16(gh)))
-    return fail(cudaErrorInvalidValue, "zq_rmsnorm_bwd_noalloc: bf16 buffers must be 16-byte aligned");
+  if (!aligned16(gy) || !aligned16(x) || !aligned16(dx) || (gh && !aligned16(gh)) || !aligned16(w))
+    return fail(cudaErrorInvalidValue, "zq_rmsnorm_bwd_noalloc: buffers must be 16-byte aligned");
 
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -83,14 +83,16 @@ extern "C" int zq_rmsnorm_bwd_noalloc(const void* gy, const void* x, const float
   int sms = 0;
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return fail(e, "zq_rmsnorm_bwd_noalloc: cudaDeviceGetAttribute failed");
-  long long grid = 2ll * sms;
-  if (grid > M) grid = M;
+  long long max_grid = 2ll * sms;
   const long long cap = kScratchFloats / D;  // partial rows that fit in the scratch
-  if (grid > cap) grid = cap;
+  if (max_grid > cap) max_grid = cap;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  zq::rmsnorm_bwd_kernel<<<(unsigned)grid, 128, 0, s>>>(
+  int64_t grid = 0;
+  e = zq::launch_rmsnorm_bwd(
       static_cast<const __nv_bfloat16*>(gy), static_cast<const __nv_bfloat16*>(x), w, rstd,
-      static_cast<const __nv_bfloat16*>(gh), static_cast<__nv_bfloat16*>(dx), scratch, (int64_t)M, D);
+      static_cast<const __nv_bfloat16*>(gh), static_cast<__nv_bfloat16*>(dx), scratch, (int64_t)M, D,
+      max_grid, s, &grid);
+  if (e != cudaSuccess) return fail(e, "zq_rmsnorm_bwd_noalloc: kernel launch failed");
   sum_partial_rows_kernel<<<(unsigned)((D + 255) / 256), 256, 0, s>>>(scratch, (int)grid, D, dw);
   e = cudaGetLastError();
   if (e != cudaSuccess) return fail(e, "zq_rmsnorm_bwd_noalloc: kernel launch failed");

@@ -35,8 +35,8 @@ extern "C" {
 
 // dx[M,D] (bf16) and dw[D] (fp32, overwritten) from gy[M,D], x[M,D] (bf16),
 // w[D] and rstd[M] (fp32), plus an optional residual gradient gh[M,D] (bf16,
-// may be NULL) that is added to dx.  Pointers to bf16 data must be 16-byte
-// aligned.  `stream` is a cudaStream_t (NULL = legacy default stream).
+// may be NULL) that is added to dx.  Pointers to bf16 data and w must be
+// 16-byte aligned.  `stream` is a cudaStream_t (NULL = legacy default stream).
 // Returns 0 on success or a cudaError_t code.
 int zq_rmsnorm_bwd_noalloc(const void* gy, const void* x, const float* w, const float* rstd,
                            const void* gh, void* dx, float* dw, long long M, int D, void* stream);

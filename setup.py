@@ -32,6 +32,7 @@ setup(
             name="zeroq_b200._C",
             sources=SOURCES,
             extra_compile_args={"cxx": ["-O3", "-std=c++17"] + DEFINES, "nvcc": NVCC_FLAGS},
+            libraries=["cublas"],
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},

@@ -96,11 +96,13 @@ def test_nf4_to_bf16(cuda, transpose):
     assert torch.equal(got.cpu(), ref)
 
 
-def test_add_rmsnorm_fwd_bwd(cuda):
+@pytest.mark.parametrize("M,D", [(300, 3072), (1001, 256), (77, 2056), (513, 3584), (130, 5120),
+                                 (64, 8192), (4099, 3072)])
+def test_add_rmsnorm_fwd_bwd(cuda, M, D):
+    """Every team width (32/64/128 lanes) and chunk count, ragged row counts."""
     from zeroq_b200.ops.norm import add_rmsnorm
 
     torch.manual_seed(4)
-    M, D = 300, 3072
     h = torch.randn(M, D, device=cuda, dtype=torch.bfloat16, requires_grad=True)
     d = torch.randn(M, D, device=cuda, dtype=torch.bfloat16, requires_grad=True)
     w = (1 + 0.1 * torch.randn(D, device=cuda)).requires_grad_(True)
@@ -132,6 +134,38 @@ def test_rope(cuda):
     qr = q.detach().float().requires_grad_(True)
     rope_reference(qr, 1e6).sum().backward()
     assert (q.grad.float() - qr.grad).abs().max() < 3e-2
+
+
+def test_gelu_cdf_pdf_error_bound(cuda):
+    """The GELU CDF (Abramowitz & Stegun 7.1.26 erf, |e| <= 1.5e-7) and PDF in
+    fp32 against CUDA's erf/exp as called by PyTorch."""
+    x = torch.linspace(-12.0, 12.0, 1 << 20, device=cuda)
+    cdf = torch.empty_like(x)
+    pdf = torch.empty_like(x)
+    _ext.ext().gelu_cdf_pdf(x, cdf, pdf)
+    torch.cuda.synchronize()
+    xd = x.double()
+    ref_cdf = 0.5 * (1.0 + torch.special.erf(xd / math.sqrt(2.0)))
+    ref_pdf = torch.exp(-0.5 * xd * xd) / math.sqrt(2.0 * math.pi)
+    assert (cdf.double() - ref_cdf).abs().max().item() < 1e-6
+    rel = ((pdf.double() - ref_pdf).abs() / ref_pdf.clamp_min(1e-30))[ref_pdf > 1e-30]
+    assert rel.max().item() < 1e-5
+
+
+@pytest.mark.parametrize("n", [8, 8 * 1023, 8 * 4097, 3 * 1024 * 1024])
+def test_gelu_ragged_sizes(cuda, n):
+    from zeroq_b200.ops.activations import gelu
+
+    torch.manual_seed(5)
+    x = torch.randn(n, device=cuda, dtype=torch.bfloat16, requires_grad=True)
+    y = gelu(x)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xr = x.detach().float().requires_grad_(True)
+    yr = torch.nn.functional.gelu(xr)
+    yr.backward(g.float())
+    assert (y.float() - yr).abs().max().item() < 2e-2
+    assert (x.grad.float() - xr.grad).abs().max().item() < 3e-2
 
 
 def test_gelu_swiglu(cuda):
@@ -317,3 +351,48 @@ def test_lm_head_grad_vs_fp32(cuda):
     assert (logits.float() - hf @ Ef.t()).abs().max().item() < 2e-2 * (hf @ Ef.t()).abs().max().item() + 1e-2
     assert (h.grad.float() - ref_dh).abs().max().item() < 2e-2 * ref_dh.abs().max().item() + 1e-2
     assert (E.grad.float() - ref_dE).abs().max().item() < 2e-2 * ref_dE.abs().max().item() + 1e-2
+
+
+def test_nf4_linear_flat_grads_and_lora_cache(cuda):
+    """FlatParams-bound LoRA weights: gradients accumulate in place in fp32 over
+    two backward passes, and the cached padded operands follow an update
+    written by a kernel once the optimizer marks the buffers updated."""
+    from zeroq_b200.ops.qlinear import Linear4bit
+    from zeroq_b200.parallel.optimizer import FlatParams
+
+    torch.manual_seed(13)
+    K, N, M = 512, 768, 512
+    lin = Linear4bit(K, N, lora_r=8, lora_alpha=16.0, device=cuda)
+    lin.quantize_from(torch.randn(N, K, device=cuda) * 0.05)
+    with torch.no_grad():
+        lin.lora_B.normal_(0.0, 0.05)
+    flat = FlatParams([lin.lora_A, lin.lora_B])
+    w = lin.dequantized_weight(torch.float32)
+
+    def ref_grads(x, gy):
+        xf = x.float()
+        A = lin.lora_A.detach().clone().requires_grad_(True)
+        B = lin.lora_B.detach().clone().requires_grad_(True)
+        y = xf @ w.t() + (xf @ A.t()) @ B.t() * lin.scaling
+        y.backward(gy.float())
+        return y.detach(), A.grad, B.grad
+
+    x = torch.randn(M, K, device=cuda, dtype=torch.bfloat16)
+    gy = torch.randn(M, N, device=cuda, dtype=torch.bfloat16)
+    _, rA, rB = ref_grads(x, gy)
+    for _ in range(2):
+        lin(x).backward(gy)
+    torch.cuda.synchronize()
+    assert lin.lora_A.grad.data_ptr() == flat.grad.data_ptr()
+    tolA = 3e-2 * rA.abs().max().item()
+    tolB = 3e-2 * rB.abs().max().item()
+    assert (lin.lora_A.grad - 2 * rA).abs().max().item() < 2 * tolA
+    assert (lin.lora_B.grad - 2 * rB).abs().max().item() < 2 * tolB
+
+    # an update that bypasses autograd's counters, then the optimizer's notice
+    with torch.no_grad():
+        flat.data.mul_(1.5)
+    flat.mark_updated()
+    y = lin(x)
+    yr, _, _ = ref_grads(x, gy)
+    assert (y.float() - yr).abs().max().item() < 2e-2 * yr.abs().max().item()

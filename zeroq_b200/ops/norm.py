@@ -2,8 +2,8 @@
 
 ``add_rmsnorm(h, delta, w)`` returns ``(h + delta, rmsnorm(h + delta) * w)`` in
 one kernel (``csrc/elementwise.cu``); its backward adds the incoming residual
-gradient to the norm's input gradient in the same kernel and accumulates the
-weight gradient with one atomic per column per CTA.  On CPU the PyTorch
+gradient to the norm's input gradient in the same kernel and writes one row of
+per-CTA weight-gradient partial sums, reduced here.  On CPU the PyTorch
 expressions below are used; they are also the numerics oracle.
 """
 

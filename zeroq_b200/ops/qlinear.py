@@ -15,7 +15,15 @@ CUDA path, per call (``csrc/gemm_sm100.cu``):
   ``dX = dY W + (s·dY B) A`` reads the same ``[N, K]`` operand MN-major
   (``gemm_bf16_nn``), so no transposed operand is produced;
 * ``U``/``V`` (rank-64 padded, skinny) and the ``A``/``B`` weight gradients
-  (contractions over tokens) are small cuBLAS GEMMs.
+  (contractions over tokens) are small cuBLAS GEMMs; the weight gradients
+  accumulate straight into fp32 ``.grad`` buffers bound by ``FlatParams``.
+
+The padded bf16 LoRA operands (``s·A`` as ``[64, in]`` and ``B`` as
+``[out, 64]``) are cached per module and rebuilt by one kernel when the
+parameters' version counters change (every in-place update by an optimizer
+bumps them; ``ShardedAdamW`` bumps them after its kernels).  Writes through
+``.data`` bypass the counters: call :meth:`Linear4bit.refresh_lora_cache`
+after those.
 
 LoRA parameter names follow PEFT (``lora_A [r, in]``, ``lora_B [out, r]``,
 ``scaling = alpha / r``, ``B`` zero-initialised) so ``prepare_model_for_zeroq``'s
@@ -65,17 +73,25 @@ def _pad_rows(t: torch.Tensor, height: int = 64) -> torch.Tensor:
     return out
 
 
+def _direct_grad(p: Optional[torch.Tensor]) -> bool:
+    """True when ``p``'s gradient is accumulated in place into its bound fp32
+    ``.grad`` (parameters bound by ``FlatParams``) instead of returned to autograd."""
+    return (p is not None and getattr(p, "_zq_flat_grad", False) and p.grad is not None
+            and p.grad.dtype == torch.float32 and p.grad.is_contiguous())
+
+
 class NF4LinearFunction(torch.autograd.Function):
     """``y = x Wᵀ + s (x Aᵀ) Bᵀ (+ bias)`` with ``W`` frozen NF4.
 
     CUDA path: the NF4 operand is produced in the tcgen05 operand layout and the
     LoRA up-projection rides as the extra 64-wide K slab of the same GEMM
-    (``U = s·x·Aᵀ`` and ``B``, zero-padded to rank 64).
+    (``U = x·(s·A)ᵀ`` against ``B``, zero-padded to rank 64).  ``lora_ops`` is
+    the cached pair ``(s·A padded [64, K], B padded [N, 64])`` in bf16.
     """
 
     @staticmethod
     def forward(ctx, x, packed, absmax, lora_A, lora_B, bias, N, K, blocksize, quant_type,
-                scaling, backend):
+                scaling, backend, lora_ops=None):
         shp = x.shape
         x2 = x.reshape(-1, K)
         if not x2.is_contiguous():
@@ -85,14 +101,17 @@ class NF4LinearFunction(torch.autograd.Function):
         r = lora_A.shape[0] if has_lora else 0
         fused = backend != "torch" and _fused_ok(x2, K, N, blocksize) and r <= 64
         U = None
+        a_pad = b_pad = None
         if fused:
             E = _ext.ext()
             w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
             y = torch.empty(M, N, dtype=x2.dtype, device=x2.device)
             if has_lora:
-                a_pad = _pad_rows(lora_A.detach().to(torch.bfloat16) * scaling)
+                if lora_ops is None:
+                    lora_ops = _pack_lora(lora_A.detach(), lora_B.detach(), scaling)
+                a_pad, b_pad = lora_ops
                 U = x2 @ a_pad.t()  # [M, 64] skinny product: cuBLAS
-                E.gemm_bf16_tn_extra(x2, w, y, U, _pad_cols(lora_B.detach().to(torch.bfloat16)))
+                E.gemm_bf16_tn_extra(x2, w, y, U, b_pad)
             else:
                 E.gemm_bf16_tn(x2, w, y)
             del w
@@ -105,13 +124,14 @@ class NF4LinearFunction(torch.autograd.Function):
             y = y.to(x2.dtype)
         if bias is not None:
             y = y + bias.to(y.dtype)
-        ctx.save_for_backward(x2 if has_lora else None, packed, absmax, lora_A, lora_B, U)
+        ctx.save_for_backward(x2 if has_lora else None, packed, absmax, lora_A, lora_B, U,
+                              a_pad, b_pad)
         ctx.meta = (shp, N, K, blocksize, quant_type, scaling, fused, bias is not None, has_lora, r)
         return y.view(*shp[:-1], N)
 
     @staticmethod
     def backward(ctx, gy):
-        x2, packed, absmax, lora_A, lora_B, U = ctx.saved_tensors
+        x2, packed, absmax, lora_A, lora_B, U, a_pad, b_pad = ctx.saved_tensors
         shp, N, K, blocksize, quant_type, scaling, fused, has_bias, has_lora, r = ctx.meta
         gy2 = gy.reshape(-1, N)
         if not gy2.is_contiguous():
@@ -123,28 +143,36 @@ class NF4LinearFunction(torch.autograd.Function):
             gy2 = gy2.to(torch.bfloat16)
             V = None
             if has_lora:
-                bt_pad = _pad_rows(lora_B.detach().t().to(torch.bfloat16) * scaling)
-                V = gy2 @ bt_pad.t()  # [M, 64] skinny product: cuBLAS
+                V = gy2 @ b_pad  # [M, 64] = dY·B (unscaled), skinny product: cuBLAS
             if ctx.needs_input_grad[0]:
                 gx = torch.empty(M, K, dtype=torch.bfloat16, device=gy2.device)
-                if M >= 256:  # W [N, K] read MN-major: dX = dY · W
+                if M >= 256:  # W [N, K] read MN-major: dX = dY·W + V·(s·A)
                     w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
-                    E.gemm_bf16_nn(gy2, w, gx, V if has_lora else None,
-                                   _pad_rows(lora_A.detach().to(torch.bfloat16)) if has_lora else None)
+                    E.gemm_bf16_nn(gy2, w, gx, V, a_pad)
                 else:  # short inputs: single-CTA kernel on the transposed operand
                     w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, True)
                     if has_lora:
-                        E.gemm_bf16_tn_extra(gy2, w, gx, V,
-                                             _pad_cols(lora_A.detach().t().to(torch.bfloat16)))
+                        E.gemm_bf16_tn_extra(gy2, w, gx, V, a_pad.t().contiguous())
                     else:
                         E.gemm_bf16_tn(gy2, w, gx)
                 del w
                 gx = gx.view(*shp[:-1], K)
             if has_lora:
+                # dA = s·Vᵀ·X, dB = dYᵀ·U: bf16 operands, fp32 accumulation
                 if ctx.needs_input_grad[3]:
-                    gA = (V[:, :r].t() @ x2).to(lora_A.dtype)
+                    if _direct_grad(lora_A):
+                        E.matmul_accum_f32(V[:, :r].t(), x2, lora_A.grad, scaling, 1.0)
+                    else:
+                        gA = torch.empty(r, K, dtype=torch.float32, device=gy2.device)
+                        E.matmul_accum_f32(V[:, :r].t(), x2, gA, scaling, 0.0)
+                        gA = gA.to(lora_A.dtype)
                 if ctx.needs_input_grad[4]:
-                    gB = (gy2.t() @ U[:, :r]).to(lora_B.dtype)
+                    if _direct_grad(lora_B):
+                        E.matmul_accum_f32(gy2.t(), U[:, :r], lora_B.grad, 1.0, 1.0)
+                    else:
+                        gB = torch.empty(N, r, dtype=torch.float32, device=gy2.device)
+                        E.matmul_accum_f32(gy2.t(), U[:, :r], gB, 1.0, 0.0)
+                        gB = gB.to(lora_B.dtype)
         else:
             Vf = None
             if has_lora:
@@ -162,16 +190,33 @@ class NF4LinearFunction(torch.autograd.Function):
                     gB = (gy2.float().t() @ U.float()).to(lora_B.dtype)
         if has_bias and ctx.needs_input_grad[5]:
             gbias = gy2.float().sum(0)
-        return gx, None, None, gA, gB, gbias, None, None, None, None, None, None
+        return gx, None, None, gA, gB, gbias, None, None, None, None, None, None, None
+
+
+def _pack_lora(A: torch.Tensor, B: torch.Tensor, scaling: float, out=None):
+    """``(s·A padded to [64, K], B padded to [N, 64])`` in bf16; ``out`` reuses buffers
+    whose padding is already zero."""
+    r, K = A.shape
+    N = B.shape[0]
+    if out is None:
+        out = (torch.zeros(64, K, dtype=torch.bfloat16, device=A.device),
+               torch.zeros(N, 64, dtype=torch.bfloat16, device=A.device))
+    a_pad, b_pad = out
+    if A.is_cuda and A.dtype == torch.float32 and B.dtype == torch.float32:
+        _ext.ext().lora_pack(A.contiguous(), B.contiguous(), float(scaling), a_pad, b_pad)
+    else:
+        a_pad[:r].copy_(A.float() * scaling)
+        b_pad[:, :r].copy_(B)
+    return a_pad, b_pad
 
 
 def nf4_linear(x, packed, absmax, out_features: int, in_features: int, bias=None,
                lora_A=None, lora_B=None, scaling: float = 1.0, blocksize: int = 64,
-               quant_type: str = "nf4", backend: str = "auto"):
+               quant_type: str = "nf4", backend: str = "auto", lora_ops=None):
     if backend == "auto":
         backend = "fused" if x.is_cuda else "torch"
     return NF4LinearFunction.apply(x, packed, absmax, lora_A, lora_B, bias, out_features,
-                                   in_features, blocksize, quant_type, scaling, backend)
+                                   in_features, blocksize, quant_type, scaling, backend, lora_ops)
 
 
 class Linear4bit(nn.Module):
@@ -210,6 +255,8 @@ class Linear4bit(nn.Module):
             self.scaling = 0.0
             self.lora_A = None
             self.lora_B = None
+        self._lora_ops = None
+        self._lora_key = None
 
     # -- weight management ---------------------------------------------------
     @classmethod
@@ -252,6 +299,28 @@ class Linear4bit(nn.Module):
         return _dequant_weight(self.weight_packed, self.weight_absmax, self.out_features,
                                self.in_features, self.blocksize, self.quant_type, dtype)
 
+    # -- LoRA operand cache ------------------------------------------------------
+    def refresh_lora_cache(self):
+        """Drop the cached padded LoRA operands (after writes through ``.data``)."""
+        self._lora_key = None
+
+    def _lora_operands(self):
+        A, B = self.lora_A, self.lora_B
+        if A is None or B is None or not A.is_cuda or A.shape[0] > 64:
+            return None
+        key = (A._version, B._version, A.data_ptr(), B.data_ptr(), float(self.scaling),
+               tuple(A.shape), tuple(B.shape))
+        if self._lora_key != key:
+            reuse = self._lora_ops
+            if reuse is not None and (reuse[0].shape != (64, A.shape[1])
+                                      or reuse[1].shape != (B.shape[0], 64)
+                                      or reuse[0].device != A.device):
+                reuse = None
+            with torch.no_grad():
+                self._lora_ops = _pack_lora(A.detach(), B.detach(), self.scaling, reuse)
+            self._lora_key = key
+        return self._lora_ops
+
     # -- forward -------------------------------------------------------------
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self.weight_packed is None:
@@ -263,9 +332,10 @@ class Linear4bit(nn.Module):
             if self.lora_r:
                 y = y + (x @ self.lora_A.t().to(x.dtype)) @ self.lora_B.t().to(x.dtype) * self.scaling
             return y
+        ops = self._lora_operands() if (self.lora_r and x.is_cuda) else None
         return nf4_linear(x, self.weight_packed, self.weight_absmax, self.out_features,
                           self.in_features, self.bias, self.lora_A, self.lora_B,
-                          self.scaling, self.blocksize, self.quant_type, self.backend)
+                          self.scaling, self.blocksize, self.quant_type, self.backend, ops)
 
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, "

@@ -62,6 +62,9 @@ class FlatParams:
                 self.data[off:off + n].copy_(p.data.reshape(-1))
                 p.data = self.data[off:off + n].view(p.shape)
                 p.grad = self.grad[off:off + n].view(p.shape)
+                # layers may accumulate this parameter's gradient in place into
+                # the bound fp32 .grad instead of returning it to autograd
+                p._zq_flat_grad = True
                 self.offsets.append(off)
                 off += n
 
@@ -71,6 +74,11 @@ class FlatParams:
         for p, off in zip(self.params, self.offsets):
             if p.grad is None or p.grad.data_ptr() != self.grad[off:].data_ptr():
                 p.grad = self.grad[off:off + p.numel()].view(p.shape)
+
+    def mark_updated(self):
+        """Bump every parameter's version counter after the buffers were written by
+        kernels (caches keyed on ``_version`` then see the update)."""
+        torch.autograd.graph.increment_version(self.params)
 
     def grads_bound(self) -> bool:
         return all(p.grad is not None and p.grad.data_ptr() == self.grad[off:].data_ptr()
@@ -137,6 +145,10 @@ class ShardedAdamW:
 
     @torch.no_grad()
     def step(self):
+        self._step()
+        self.flat.mark_updated()
+
+    def _step(self):
         self.step_count += 1
         b1, b2 = self.betas
         if self.world == 1:
