@@ -1,19 +1,24 @@
 #!/usr/bin/env python
-"""Run one hot kernel a few times on one GPU - the small cases profiled with ncu.
+"""Run one hot kernel on one GPU: CUDA-event timings and the small cases profiled with ncu.
 
-    python benchmarks/kernel_case.py gemm --m 8192 --n 3072 --k 3072 [--pair 0|1] [--nn]
+    python benchmarks/kernel_case.py gemm --m 8192 --n 3072 --k 3072 [--pair 0|1] [--nn] [--cublas]
     python benchmarks/kernel_case.py attention --b 8 --s 1024 --h 24 --d 128
     python benchmarks/kernel_case.py nf4_operand --n 12288 --k 3072 [--transpose]
-    python benchmarks/kernel_case.py rmsnorm --m 8192 --d 3072
+    python benchmarks/kernel_case.py rmsnorm --m 8192 --n 3072
     python benchmarks/kernel_case.py gelu --m 8192 --n 12288
 
-Each case allocates at most a few GB, runs ``--reps`` launches (default 4) and
-prints the mean CUDA-event time of the last ``--reps - 1`` launches.
+Each case allocates at most a few GB and times ``--reps`` launches of the kernel
+itself with CUDA events on the launching stream.  Before every timed launch a
+256 MB buffer (twice the 126 MB L2) is overwritten so each launch starts with a
+cold L2; the flush is outside the events.  The first launch is an untimed warm-up.
+``--profile`` prints the kernels of one extra call (torch profiler) for reading
+only; the reported numbers never come from a profiled run.
 """
 
 from __future__ import annotations
 
 import argparse
+import json
 import os
 import sys
 
@@ -21,27 +26,60 @@ import torch
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
+_FLUSH = None
 
-_PROFILE = False
+
+def _flush_l2():
+    global _FLUSH
+    if _FLUSH is None:
+        _FLUSH = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    _FLUSH.fill_(1)
 
 
-def _time(fn, reps):
+def _time(fn, reps, profile=False):
+    """Mean CUDA-event time (ms) of ``fn`` over ``reps`` cold-L2 launches."""
     fn()
     torch.cuda.synchronize()
-    if _PROFILE:
-        from torch.profiler import ProfilerActivity, profile
+    if profile:
+        from torch.profiler import ProfilerActivity, profile as tprof
 
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        with tprof(activities=[ProfilerActivity.CUDA]) as prof:
             fn()
             torch.cuda.synchronize()
         print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=10))
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(reps - 1):
+    total = 0.0
+    for _ in range(reps):
+        _flush_l2()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
         fn()
-    e.record()
-    torch.cuda.synchronize()
-    return s.elapsed_time(e) / max(1, reps - 1)
+        e.record()
+        torch.cuda.synchronize()
+        total += s.elapsed_time(e)
+    return total / reps
+
+
+def _peaks():
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                        "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def _report(name, ms, byts=None, flops=None, extra=""):
+    hbm, tf, basis = _peaks()
+    parts = [f"{name}: {ms * 1e3:.1f} us"]
+    if byts is not None:
+        gbs = byts / ms / 1e6
+        parts.append(f"{gbs:.0f} GB/s = {gbs / hbm:.2f} of {basis} HBM {hbm:.0f}")
+    if flops is not None:
+        t = flops / ms / 1e9
+        parts.append(f"{t:.0f} TFLOP/s = {t / tf:.2f} of {basis} bf16 {tf:.0f}")
+    print(", ".join(parts) + (f" {extra}" if extra else ""), flush=True)
 
 
 def main():
@@ -51,34 +89,39 @@ def main():
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=3072)
     ap.add_argument("--pair", type=int, default=1)
+    ap.add_argument("--nn", action="store_true", help="gemm: B given as [K, N] (MN-major read)")
+    ap.add_argument("--cublas", action="store_true", help="gemm: also time torch.matmul (cuBLAS)")
     ap.add_argument("--b", type=int, default=8)
     ap.add_argument("--s", type=int, default=1024)
     ap.add_argument("--h", type=int, default=24)
     ap.add_argument("--d", type=int, default=128)
     ap.add_argument("--transpose", action="store_true")
-    ap.add_argument("--nn", action="store_true", help="gemm: B given as [K, N] (MN-major read)")
-    ap.add_argument("--reps", type=int, default=4)
+    ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--profile", action="store_true", help="print one call's kernels (torch profiler)")
     a = ap.parse_args()
-    global _PROFILE
-    _PROFILE = a.profile
 
     from zeroq_b200.ops import _ext
 
     E = _ext.ext()
     dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
     if a.case == "gemm":
         E.set_gemm_pair_mode(a.pair)
         x = torch.randn(a.m, a.k, device=dev, dtype=torch.bfloat16)
         y = torch.empty(a.m, a.n, device=dev, dtype=torch.bfloat16)
+        fl = 2.0 * a.m * a.n * a.k
         if a.nn:
             w = torch.randn(a.k, a.n, device=dev, dtype=torch.bfloat16)
-            ms = _time(lambda: E.gemm_bf16_nn(x, w, y, None, None), a.reps)
+            ms = _time(lambda: E.gemm_bf16_nn(x, w, y, None, None), a.reps, a.profile)
+            ref = lambda: torch.matmul(x, w, out=y)  # noqa: E731
         else:
             w = torch.randn(a.n, a.k, device=dev, dtype=torch.bfloat16)
-            ms = _time(lambda: E.gemm_bf16_tn(x, w, y), a.reps)
-        print(f"gemm {a.m}x{a.n}x{a.k} pair={a.pair} nn={a.nn}: {ms:.4f} ms, "
-              f"{2 * a.m * a.n * a.k / ms / 1e9:.0f} TFLOP/s, status {E.gemm_status(0)}")
+            ms = _time(lambda: E.gemm_bf16_tn(x, w, y), a.reps, a.profile)
+            ref = lambda: torch.matmul(x, w.t(), out=y)  # noqa: E731
+        _report(f"gemm {a.m}x{a.n}x{a.k} pair={a.pair} nn={a.nn}", ms, flops=fl,
+                extra=f"status {E.gemm_status(0)}")
+        if a.cublas:
+            _report(f"cublas {a.m}x{a.n}x{a.k} nn={a.nn}", _time(ref, a.reps), flops=fl)
     elif a.case == "attention":
         from zeroq_b200.ops.attention import flash_attention
 
@@ -86,48 +129,50 @@ def main():
         k = torch.randn_like(q, requires_grad=True)
         v = torch.randn_like(q, requires_grad=True)
         go = torch.randn_like(q)
+        fwd_fl = 4.0 * a.b * a.h * a.s * a.s * a.d / 2  # causal
+        with torch.no_grad():
+            ms_f = _time(lambda: flash_attention(q, k, v, causal=True), a.reps, a.profile)
+        _report(f"attention fwd B={a.b} S={a.s} H={a.h} D={a.d} causal", ms_f, flops=fwd_fl)
 
         def step():
             o = flash_attention(q, k, v, causal=True)
             o.backward(go)
 
         ms = _time(step, a.reps)
-        fl = 4 * a.b * a.h * a.s * a.s * a.d / 2 * 3.5
-        print(f"attention fwd+bwd B={a.b} S={a.s} H={a.h} D={a.d}: {ms:.4f} ms, "
-              f"{fl / ms / 1e9:.0f} TFLOP/s (causal)")
+        _report(f"attention fwd+bwd B={a.b} S={a.s} H={a.h} D={a.d} causal", ms,
+                flops=fwd_fl * 3.5)
     elif a.case == "nf4_operand":
         from zeroq_b200.ops.nf4 import quantize_4bit
 
         w = torch.randn(a.n, a.k, device=dev) * 0.02
         packed, st = quantize_4bit(w, 64, "nf4")
         out = torch.empty(a.n * a.k, device=dev, dtype=torch.bfloat16)
-        ms = _time(lambda: E.nf4_to_bf16(packed, st.absmax, out, a.n, a.k, 64, 0, a.transpose), a.reps)
-        byts = a.n * a.k * (0.5 + 4 / 64 + 2)
-        print(f"nf4_operand {a.n}x{a.k} transpose={a.transpose}: {ms:.4f} ms, {byts / ms / 1e6:.0f} GB/s")
-    elif a.case == "gelu":
-        from zeroq_b200.ops.activations import gelu
-
-        x = torch.randn(a.m, a.n, device=dev, dtype=torch.bfloat16, requires_grad=True)
-        g = torch.randn_like(x)
-
-        def step():
-            gelu(x).backward(g)
-
-        ms = _time(step, a.reps)
-        print(f"gelu fwd+bwd {a.m}x{a.n}: {ms:.4f} ms, {5 * 2 * a.m * a.n / ms / 1e6:.0f} GB/s (5 passes)")
+        ms = _time(lambda: E.nf4_to_bf16(packed, st.absmax, out, a.n, a.k, 64, 0, a.transpose),
+                   a.reps, a.profile)
+        _report(f"nf4_operand {a.n}x{a.k} transpose={a.transpose}", ms,
+                byts=a.n * a.k * (0.5 + 4 / 64 + 2))
     elif a.case == "rmsnorm":
-        from zeroq_b200.ops.norm import add_rmsnorm
-
-        h = torch.randn(a.m, a.d, device=dev, dtype=torch.bfloat16, requires_grad=True)
-        d = torch.randn_like(h, requires_grad=True)
-        w = torch.ones(a.d, device=dev, requires_grad=True)
-
-        def step():
-            hn, y = add_rmsnorm(h, d, w)
-            torch.autograd.backward([hn, y], [torch.ones_like(hn), torch.ones_like(y)])
-
-        ms = _time(step, a.reps)
-        print(f"add_rmsnorm fwd+bwd {a.m}x{a.d}: {ms:.4f} ms")
+        M, D = a.m, a.n
+        h = torch.randn(M, D, device=dev, dtype=torch.bfloat16)
+        d = torch.randn_like(h)
+        w = torch.ones(D, device=dev)
+        hout, y = torch.empty_like(h), torch.empty_like(h)
+        rstd = torch.empty(M, device=dev)
+        ms = _time(lambda: E.add_rmsnorm_fwd(h, d, w, hout, y, rstd, 1e-6), a.reps, a.profile)
+        _report(f"add_rmsnorm fwd {M}x{D}", ms, byts=4 * M * D * 2)
+        gy, gh, dx = torch.randn_like(h), torch.randn_like(h), torch.empty_like(h)
+        part = torch.empty(2 * torch.cuda.get_device_properties(dev).multi_processor_count, D,
+                           device=dev)
+        ms = _time(lambda: E.rmsnorm_bwd(gy, hout, w, rstd, gh, dx, part), a.reps)
+        _report(f"rmsnorm bwd (+residual grad) {M}x{D}", ms, byts=4 * M * D * 2)
+    elif a.case == "gelu":
+        x = torch.randn(a.m, a.n, device=dev, dtype=torch.bfloat16)
+        y = torch.empty_like(x)
+        ms = _time(lambda: E.gelu_fwd(x, y), a.reps, a.profile)
+        _report(f"gelu fwd {a.m}x{a.n}", ms, byts=2 * a.m * a.n * 2)
+        g, dx = torch.randn_like(x), torch.empty_like(x)
+        ms = _time(lambda: E.gelu_bwd(g, x, dx), a.reps)
+        _report(f"gelu bwd {a.m}x{a.n}", ms, byts=3 * a.m * a.n * 2)
 
 
 if __name__ == "__main__":
