@@ -6,6 +6,7 @@
     python benchmarks/kernel_case.py nf4_operand --n 12288 --k 3072 [--transpose]
     python benchmarks/kernel_case.py rmsnorm --m 8192 --n 3072
     python benchmarks/kernel_case.py gelu --m 8192 --n 12288
+    python benchmarks/kernel_case.py q4gemm --m 8192 --n 3072 --k 12288 [--nn]
 
 Each case allocates at most a few GB and times ``--reps`` launches of the kernel
 itself with CUDA events on the launching stream.  Before every timed launch a
@@ -84,7 +85,7 @@ def _report(name, ms, byts=None, flops=None, extra=""):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attention", "nf4_operand", "rmsnorm", "gelu"])
+    ap.add_argument("case", choices=["gemm", "attention", "nf4_operand", "rmsnorm", "gelu", "q4gemm"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=3072)
@@ -122,6 +123,31 @@ def main():
                 extra=f"status {E.gemm_status(0)}")
         if a.cublas:
             _report(f"cublas {a.m}x{a.n}x{a.k} nn={a.nn}", _time(ref, a.reps), flops=fl)
+    elif a.case == "q4gemm":
+        # C[M, N] = X[M, K] · op(W) with W 4-bit: in-kernel decode vs operand kernel + GEMM
+        from zeroq_b200.ops.nf4 import quantize_4bit
+
+        rows, cols = (a.k, a.n) if a.nn else (a.n, a.k)
+        w = torch.randn(rows, cols, device=dev) * 0.02
+        packed, st = quantize_4bit(w, 64, "nf4")
+        del w
+        x = torch.randn(a.m, a.k, device=dev, dtype=torch.bfloat16)
+        y = torch.empty(a.m, a.n, device=dev, dtype=torch.bfloat16)
+        wb = torch.empty(rows * cols, device=dev, dtype=torch.bfloat16)
+        fl = 2.0 * a.m * a.n * a.k
+        ms = _time(lambda: E.gemm_nf4(x, packed, st.absmax, rows, cols, 64, 0, a.nn, y, None, None),
+                   a.reps, a.profile)
+        _report(f"gemm_nf4 (decode in kernel) {a.m}x{a.n}x{a.k} nn={a.nn}", ms, flops=fl,
+                extra=f"status {E.gemm_status(0)}")
+
+        def two_step():
+            E.nf4_to_bf16(packed, st.absmax, wb, rows, cols, 64, 0, False)
+            if a.nn:
+                E.gemm_bf16_nn(x, wb.view(rows, cols), y, None, None)
+            else:
+                E.gemm_bf16_tn(x, wb.view(rows, cols), y)
+
+        _report(f"operand kernel + gemm {a.m}x{a.n}x{a.k} nn={a.nn}", _time(two_step, a.reps), flops=fl)
     elif a.case == "attention":
         from zeroq_b200.ops.attention import flash_attention
 

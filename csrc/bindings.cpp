@@ -9,6 +9,9 @@ void nf4_dequantize(at::Tensor packed, at::Tensor absmax, at::Tensor out, int64_
                     int64_t qtype);
 // gemm_sm100.cu
 void gemm_bf16_tn(at::Tensor a, at::Tensor b, at::Tensor c);
+void gemm_nf4(at::Tensor a, at::Tensor packed, at::Tensor absmax, int64_t rows, int64_t cols,
+              int64_t blocksize, int64_t quant_type, bool w_is_kn, at::Tensor c,
+              c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2);
 void lora_pack(at::Tensor A, at::Tensor B, double scaling, at::Tensor a_pad, at::Tensor b_pad);
 void matmul_accum_f32(at::Tensor A, at::Tensor B, at::Tensor C, double alpha, double beta);
 void gemm_bf16_tn_extra(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor a2, at::Tensor b2);
@@ -73,6 +76,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16_tn", &gemm_bf16_tn);
   m.def("gemm_bf16_tn_extra", &gemm_bf16_tn_extra);
   m.def("gemm_bf16_nn", &gemm_bf16_nn);
+  m.def("gemm_nf4", &gemm_nf4);
   m.def("lora_pack", &lora_pack);
   m.def("matmul_accum_f32", &matmul_accum_f32);
   m.def("gemm_status", &gemm_status);

@@ -46,7 +46,25 @@ struct GemmArgs {
   __nv_bfloat16* C;
   int64_t ldc;
   DeviceStatus* status;
+  // NF4/FP4 B operand decoded in the kernel (Q4 variants only): the weight
+  // W [q_rows, q_cols] in the bitsandbytes layout (flat blocks of q_block along
+  // the row-major order, element 2i in the high nibble, fp32 absmax per block)
+  const uint8_t* q_packed;
+  const float* q_absmax;
+  int q_rows, q_cols, q_block, q_type;  // q_type: 0 = nf4, 1 = fp4
 };
+
+__constant__ float c_code_nf4[16] = {
+    -1.0f, -0.6961928009986877f, -0.5250730514526367f, -0.39491748809814453f,
+    -0.28444138169288635f, -0.18477343022823334f, -0.09105003625154495f, 0.0f,
+    0.07958029955625534f, 0.16093020141124725f, 0.24611230194568634f, 0.33791524171829224f,
+    0.44070982933044434f, 0.5626170039176941f, 0.7229568362236023f, 1.0f};
+__constant__ float c_code_fp4[16] = {0.0f, 0.005208333333f, 0.66666667f, 1.0f, 0.33333333f,
+                                     0.5f, 0.16666667f, 0.25f, -0.0f, -0.005208333333f,
+                                     -0.66666667f, -1.0f, -0.33333333f, -0.5f, -0.16666667f,
+                                     -0.25f};
+
+
 
 template <int BN, int STAGES>
 struct GemmSmem {
@@ -248,11 +266,35 @@ struct PairSmem {
   static constexpr int kEpiOffset = STAGES * kStageBytes;         // 2 x [128 rows][32 cols] bf16
   static constexpr int kEpiBytes = 128 * 32 * 2;
   static constexpr int kBarOffset = kEpiOffset + 2 * kEpiBytes;
+  static constexpr int kLutOffset = kBarOffset + 128;      // 16 fp32 decode values (Q4)
   static constexpr int kBytes = kBarOffset + 256 + 1024;
 };
 
-template <int BN, int STAGES, int KB, bool BMN>
-__global__ void __launch_bounds__(kGemmThreads, 1)
+constexpr int kQ4DecodeWarps = 4;
+constexpr int kGemmQ4Threads = kGemmThreads + 32 * kQ4DecodeWarps;
+
+// 32 consecutive 4-bit codes (16 bytes, element 2i in the high nibble) times
+// their block's absmax -> four 16-byte chunks of bf16, stored at
+// dst + ((chunk0 + i) ^ swz) * 16 for i = 0..3 (the 128-byte swizzle of the
+// tcgen05 operand layout).  The decode is fp32 table lookup x fp32 absmax then
+// one round to bf16 - the same arithmetic as the standalone dequantize kernels.
+__device__ __forceinline__ void q4_decode_store32(const uint4& raw, float am, const float* lut,
+                                                  uint8_t* dst, int chunk0, int swz) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t byte = (w[i] >> (8 * q)) & 0xFFu;
+      o[q] = pack_bf16x2(lut[byte >> 4] * am, lut[byte & 15u] * am);
+    }
+    *reinterpret_cast<uint4*>(dst + (((chunk0 + i) ^ swz) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+template <int BN, int STAGES, int KB, bool BMN, bool Q4 = false>
+__global__ void __launch_bounds__(Q4 ? kGemmQ4Threads : kGemmThreads, 1)
 gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
                     const __grid_constant__ CUtensorMap tmC, GemmArgs args) {
@@ -277,7 +319,8 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full_bar[s], 1);
+      // Q4: the leader's producer arrival plus one per decode warp of both CTAs
+      mbar_init(&full_bar[s], Q4 ? 1 + 2 * kQ4DecodeWarps : 1);
       mbar_init(&empty_bar[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -286,11 +329,15 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     }
     fence_mbar_init();
     prefetch_tmap(&tmA);
-    prefetch_tmap(&tmB);
+    if (!Q4) prefetch_tmap(&tmB);
     if (args.extra_k16 > 0) {
       prefetch_tmap(&tmA2);
       prefetch_tmap(&tmB2);
     }
+  }
+  if (Q4 && threadIdx.x < 16) {
+    reinterpret_cast<float*>(smem + L::kLutOffset)[threadIdx.x] =
+        args.q_type == 1 ? c_code_fp4[threadIdx.x] : c_code_nf4[threadIdx.x];
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, 512);
@@ -318,11 +365,14 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
           uint8_t* sb = sa + L::kABytes;
           const uint32_t leader_full = map_to_cta(smem_u32(&full_bar[stage]), 0);
           if (kt < main_k_tiles) {
-            if (cr == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * L::kStageBytes);
+            if (cr == 0)
+              mbar_arrive_expect_tx(&full_bar[stage], 2 * (Q4 ? L::kABytes : L::kStageBytes));
             for (int kb = 0; kb < KB; ++kb) {
               const int kc = (kt * KB + kb) * kBK;
               tma_load_2d_pair(sa + kb * L::kAAtom, &tmA, leader_full, kc, arow);
-              if (BMN) {
+              if (Q4) {
+                // B is decoded into shared memory by the decode warps
+              } else if (BMN) {
                 // B is [K, N] row-major: boxes of 64 N-columns x 64 K-rows
                 for (int ch = 0; ch < BN / 128; ++ch)
                   tma_load_2d_pair(sb + kb * L::kBAtom + ch * 8192, &tmB, leader_full,
@@ -391,6 +441,81 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         umma_commit_pair(map_to_cta(f, 1));
       }
     }
+  } else if (Q4 && warp >= 6) {
+    // ---------------------------------------------------------------- B decode (both CTAs)
+    // This CTA's B half per stage: 128 rows x 128 K (K-major, BMN = false) or
+    // 128 K-rows x 128 N (MN-major, BMN = true) decoded from 4-bit codes.
+    // Thread mapping per pass p (4 passes): row r = p*32 + dw*8 + lane/4 and a
+    // 32-element chunk kc = lane%4 along the weight's row (16 packed bytes, one
+    // absmax).  Loads for the next stage are issued before waiting for the
+    // current stage's buffer, so global latency overlaps the pipeline wait.
+    static_assert(!Q4 || (BN == 256 && KB == 2), "Q4 decode covers 128 x 128 per CTA and stage");
+    const int dw = warp - 6;
+    const int sub = dw * 8 + (lane >> 2);
+    const int kc = lane & 3;
+    const float* lut = reinterpret_cast<const float*>(smem + L::kLutOffset);
+    const int64_t pitch = (int64_t)args.q_cols >> 1;
+    bool ok = true;
+    int stage = 0;
+    uint32_t phase = 0;
+    // work item w = (tile iteration) * k_tiles + kt for this cluster
+    const int my_tiles = num_tiles > cluster_id ? (num_tiles - cluster_id + num_clusters - 1) / num_clusters : 0;
+    const int total = my_tiles * k_tiles;
+    uint4 raw[4];
+    float am[4];
+    auto load = [&](int w, uint4 (&rr)[4], float (&aa)[4]) {
+      const int ti = w / k_tiles, kt = w - ti * k_tiles;
+      int tm, tn;
+      tile_coords(cluster_id + ti * num_clusters, args.tiles_m, args.tiles_n, tm, tn);
+      const int nb = tn * BN + (int)cr * (BN / 2);   // first output column of this CTA's half
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const int r = p * 32 + sub;
+        int wrow, wcol;
+        if (BMN) { wrow = kt * 128 + r; wcol = nb + kc * 32; }
+        else     { wrow = nb + r;       wcol = kt * 128 + kc * 32; }
+        if (kt < main_k_tiles && wrow < args.q_rows && wcol < args.q_cols) {
+          rr[p] = __ldg(reinterpret_cast<const uint4*>(args.q_packed + (int64_t)wrow * pitch + (wcol >> 1)));
+          aa[p] = __ldg(args.q_absmax + ((int64_t)wrow * args.q_cols + wcol) / args.q_block);
+        } else {
+          rr[p] = make_uint4(0u, 0u, 0u, 0u);
+          aa[p] = 0.0f;
+        }
+      }
+    };
+    if (total > 0) load(0, raw, am);
+    for (int w = 0; w < total && ok; ++w) {
+      uint4 cur[4];
+      float cam[4];
+#pragma unroll
+      for (int p = 0; p < 4; ++p) { cur[p] = raw[p]; cam[p] = am[p]; }
+      if (w + 1 < total) load(w + 1, raw, am);
+      const int kt = w % k_tiles;
+      const bool got = mbar_wait(&empty_bar[stage], phase ^ 1, args.status, kErrProducer);
+      if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+      if (kt < main_k_tiles) {
+        uint8_t* sb = smem + stage * L::kStageBytes + L::kABytes;
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+          const int r = p * 32 + sub;
+          uint8_t* dst;
+          int swz;
+          if (BMN) {  // atom = 64 K-rows; box of 64 N per 8 KB; row kk at kk*128
+            const int kk = r & 63;
+            dst = sb + (r >> 6) * L::kBAtom + (kc >> 1) * 8192 + kk * 128;
+            swz = kk & 7;
+          } else {    // atom = 64 K per row of 128 B; row r at r*128
+            dst = sb + (kc >> 1) * L::kBAtom + r * 128;
+            swz = r & 7;
+          }
+          q4_decode_store32(cur[p], cam[p], lut, dst, (kc & 1) * 4, swz);
+        }
+        fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(map_to_cta(smem_u32(&full_bar[stage]), 0));
+      if (++stage == STAGES) { stage = 0; phase ^= 1; }
+    }
   } else {
     // ---------------------------------------------------------------- epilogue (both CTAs)
     // TMEM -> registers -> bf16 -> 64-byte-swizzled staging tile in shared
@@ -456,16 +581,6 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 // through a 64x64 shared-memory tile so both the packed reads and the bf16
 // writes stay coalesced.
 // ----------------------------------------------------------------------------
-__constant__ float c_code_nf4[16] = {
-    -1.0f, -0.6961928009986877f, -0.5250730514526367f, -0.39491748809814453f,
-    -0.28444138169288635f, -0.18477343022823334f, -0.09105003625154495f, 0.0f,
-    0.07958029955625534f, 0.16093020141124725f, 0.24611230194568634f, 0.33791524171829224f,
-    0.44070982933044434f, 0.5626170039176941f, 0.7229568362236023f, 1.0f};
-__constant__ float c_code_fp4[16] = {0.0f, 0.005208333333f, 0.66666667f, 1.0f, 0.33333333f,
-                                     0.5f, 0.16666667f, 0.25f, -0.0f, -0.005208333333f,
-                                     -0.66666667f, -1.0f, -0.33333333f, -0.5f, -0.16666667f,
-                                     -0.25f};
-
 // 64x64 tile per CTA of 256 threads; each thread expands 16 values (8 bytes).
 __global__ void __launch_bounds__(256) nf4_to_bf16_tile_kernel(
     const uint8_t* __restrict__ packed, const float* __restrict__ absmax,
@@ -636,7 +751,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-template <int BN, int STAGES, int KB, bool BMN>
+template <int BN, int STAGES, int KB, bool BMN, bool Q4 = false>
 static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2,
                              const CUtensorMap& tb2, const CUtensorMap& tc, GemmArgs args,
                              cudaStream_t stream, int sms) {
@@ -645,7 +760,7 @@ static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const
   int dev;
   C10_CUDA_CHECK(cudaGetDevice(&dev));
   if (!configured[dev]) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_tn_pair_kernel<BN, STAGES, KB, BMN>,
+    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_tn_pair_kernel<BN, STAGES, KB, BMN, Q4>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
     configured[dev] = true;
   }
@@ -653,7 +768,7 @@ static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const
   const int clusters = std::max(1, std::min(tiles, sms / 2));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * clusters);
-  cfg.blockDim = dim3(kGemmThreads);
+  cfg.blockDim = dim3(Q4 ? kGemmQ4Threads : kGemmThreads);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -663,7 +778,7 @@ static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tn_pair_kernel<BN, STAGES, KB, BMN>, ta, tb, ta2, tb2, tc, args));
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tn_pair_kernel<BN, STAGES, KB, BMN, Q4>, ta, tb, ta2, tb2, tc, args));
 }
 
 // Pick the N tile that minimises wave quantisation over the SMs.
@@ -728,7 +843,7 @@ static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
   TORCH_CHECK(!b_mn || N % 64 == 0, "gemm: B as [K, N] needs N % 64 == 0");
   const int bn = pair ? choose_bn_pair((int)M, (int)N, sms) : choose_bn((int)M, (int)N, sms);
 
-  GemmArgs args;
+  GemmArgs args{};
   args.M = (int)M;
   args.N = (int)N;
   args.K = (int)K;
@@ -806,7 +921,123 @@ void gemm_bf16_nn(at::Tensor a, at::Tensor b, at::Tensor c, c10::optional<at::Te
   gemm_impl(a, b, c, a2, b2, true);
 }
 
+// GEMM whose B operand is a 4-bit weight W [rows, cols] decoded inside the
+// kernel (no bf16 copy of W exists at any time):
+//   w_is_kn = false:  C[M, rows] = A[M, cols] · Wᵀ   (forward,        K-major B)
+//   w_is_kn = true:   C[M, cols] = A[M, rows] · W    (input gradient, MN-major B)
+// plus the optional extra 64-wide K slab A2 · B2 (same shapes as gemm_bf16_tn_extra /
+// gemm_bf16_nn).  Needs M >= 256, K % 128 == 0, N % 64 == 0, cols % 32 == 0 and a
+// block size that is a multiple of 32.
+void gemm_nf4(at::Tensor a, at::Tensor packed, at::Tensor absmax, int64_t rows, int64_t cols,
+              int64_t blocksize, int64_t quant_type, bool w_is_kn, at::Tensor c,
+              c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2) {
+  TORCH_CHECK(a.is_cuda() && c.is_cuda() && packed.is_cuda() && absmax.is_cuda(), "gemm_nf4: CUDA tensors");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && c.scalar_type() == at::kBFloat16, "gemm_nf4: bf16 A and C");
+  TORCH_CHECK(packed.scalar_type() == at::kByte && packed.is_contiguous() && packed.numel() * 2 == rows * cols,
+              "gemm_nf4: packed must be contiguous uint8 with rows*cols/2 bytes");
+  TORCH_CHECK(absmax.scalar_type() == at::kFloat && absmax.is_contiguous() && blocksize > 0 &&
+                  blocksize % 32 == 0 && absmax.numel() * blocksize >= rows * cols,
+              "gemm_nf4: fp32 absmax per block (block size a multiple of 32)");
+  TORCH_CHECK(quant_type == 0 || quant_type == 1, "gemm_nf4: quant_type 0 (nf4) or 1 (fp4)");
+  TORCH_CHECK(cols % 32 == 0 && (reinterpret_cast<uintptr_t>(packed.data_ptr()) & 15) == 0,
+              "gemm_nf4: cols % 32 == 0 and 16-byte aligned packed data");
+  TORCH_CHECK(a.dim() == 2 && c.dim() == 2 && a.stride(1) == 1 && c.stride(1) == 1, "gemm_nf4: row-major A, C");
+  const int64_t M = a.size(0), K = a.size(1);
+  const int64_t N = w_is_kn ? cols : rows;
+  TORCH_CHECK(K == (w_is_kn ? rows : cols), "gemm_nf4: K mismatch");
+  TORCH_CHECK(c.size(0) == M && c.size(1) == N, "gemm_nf4: C shape");
+  TORCH_CHECK(M >= 2 * kBM && M < (1LL << 31), "gemm_nf4: needs M >= 256");
+  TORCH_CHECK(K % 128 == 0 && N % 64 == 0, "gemm_nf4: needs K % 128 == 0 and N % 64 == 0");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(c.data_ptr()) & 15) == 0 && (c.stride(0) % 8) == 0,
+              "gemm_nf4: C must be 16-byte aligned with a row pitch multiple of 8");
+  TORCH_CHECK(rows < (1LL << 31) && cols < (1LL << 31), "gemm_nf4: weight too large");
+  const at::cuda::CUDAGuard guard(a.device());
+  const int dev = a.get_device();
+  const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  constexpr int bn = 256;
+
+  GemmArgs args{};
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.tiles_m = (int)((M + 2 * kBM - 1) / (2 * kBM));
+  args.tiles_n = (int)((N + bn - 1) / bn);
+  args.C = reinterpret_cast<__nv_bfloat16*>(c.data_ptr<at::BFloat16>());
+  args.ldc = c.stride(0);
+  args.status = status_buffer(dev);
+  args.q_packed = packed.data_ptr<uint8_t>();
+  args.q_absmax = absmax.data_ptr<float>();
+  args.q_rows = (int)rows;
+  args.q_cols = (int)cols;
+  args.q_block = (int)blocksize;
+  args.q_type = (int)quant_type;
+
+  CUtensorMap ta = make_tmap_bf16(a.data_ptr(), M, K, a.stride(0), kBM);
+  CUtensorMap ta2 = ta, tb2 = ta;
+  if (a2.has_value() && a2->defined()) {
+    TORCH_CHECK(b2.has_value() && b2->defined(), "gemm_nf4: extra slab needs both operands");
+    const at::Tensor& x2 = *a2;
+    const at::Tensor& y2 = *b2;
+    TORCH_CHECK(x2.scalar_type() == at::kBFloat16 && y2.scalar_type() == at::kBFloat16, "extra slab bf16");
+    if (w_is_kn) {
+      TORCH_CHECK(x2.size(0) == M && x2.size(1) == 64 && y2.size(0) == 64 && y2.size(1) == N &&
+                      x2.stride(1) == 1 && y2.stride(1) == 1,
+                  "extra slab operands must be [M,64] and [64,N] row-major");
+      tb2 = make_tmap_bf16(y2.data_ptr(), 64, N, y2.stride(0), 64);
+    } else {
+      TORCH_CHECK(x2.size(0) == M && y2.size(0) == N && x2.size(1) == 64 && y2.size(1) == 64 &&
+                      x2.stride(1) == 1 && y2.stride(1) == 1,
+                  "extra slab operands must be [M,64] and [N,64] row-major");
+      tb2 = make_tmap_bf16(y2.data_ptr(), N, 64, y2.stride(0), bn / 2);
+    }
+    ta2 = make_tmap_bf16(x2.data_ptr(), M, 64, x2.stride(0), kBM);
+    args.extra_k16 = 4;
+  }
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const CUtensorMap tc = make_tmap_store_bf16(c.data_ptr(), M, N, c.stride(0));
+  if (w_is_kn) launch_gemm_pair<256, 3, 2, true, true>(ta, ta, ta2, tb2, tc, args, stream, sms);
+  else launch_gemm_pair<256, 3, 2, false, true>(ta, ta, ta2, tb2, tc, args, stream, sms);
+}
+
 // NF4 weight [rows, cols] -> bf16 [rows, cols] (transpose=false) or [cols, rows].
+// Non-transposed expansion is a flat map over the row-major order.  A work unit
+// is 4 packed bytes (8 codes) -> one 16-byte bf16 store; consecutive lanes take
+// consecutive units so every warp load (128 B) and store (512 B) is contiguous.
+// Each thread handles kFlatIlp units 256 apart and issues their loads first.
+constexpr int kFlatIlp = 4;
+
+__global__ void __launch_bounds__(256) nf4_to_bf16_flat_kernel(
+    const uint32_t* __restrict__ packed, const float* __restrict__ absmax, uint4* __restrict__ out,
+    int64_t n8, int blocksize, int qtype) {
+  __shared__ float lut[16];
+  if (threadIdx.x < 16) lut[threadIdx.x] = qtype == 0 ? c_code_nf4[threadIdx.x] : c_code_fp4[threadIdx.x];
+  __syncthreads();
+  const int64_t base = (int64_t)blockIdx.x * blockDim.x * kFlatIlp + threadIdx.x;
+  uint32_t raw[kFlatIlp];
+  float am[kFlatIlp];
+#pragma unroll
+  for (int j = 0; j < kFlatIlp; ++j) {
+    const int64_t i = base + (int64_t)j * blockDim.x;
+    if (i < n8) {
+      raw[j] = __ldg(packed + i);
+      am[j] = __ldg(absmax + (i * 8) / blocksize);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kFlatIlp; ++j) {
+    const int64_t i = base + (int64_t)j * blockDim.x;
+    if (i < n8) {
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t byte = (raw[j] >> (8 * q)) & 0xFFu;
+        o[q] = pack_bf16x2(lut[byte >> 4] * am[j], lut[byte & 15u] * am[j]);
+      }
+      out[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 void nf4_to_bf16(at::Tensor packed, at::Tensor absmax, at::Tensor out, int64_t rows, int64_t cols,
                  int64_t blocksize, int64_t qtype, bool transpose) {
   TORCH_CHECK(packed.is_cuda() && packed.scalar_type() == at::kByte, "nf4_to_bf16: uint8 packed");
@@ -816,6 +1047,19 @@ void nf4_to_bf16(at::Tensor packed, at::Tensor absmax, at::Tensor out, int64_t r
   TORCH_CHECK(cols % 16 == 0 && (!transpose || rows % 16 == 0), "nf4_to_bf16: 16-aligned dims");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(packed.data_ptr()) & 7) == 0, "nf4_to_bf16: packed 8-byte aligned");
   const at::cuda::CUDAGuard guard(out.device());
+  const int64_t total = rows * cols;
+  if (!transpose && total % 8 == 0 && blocksize % 8 == 0 &&
+      (reinterpret_cast<uintptr_t>(packed.data_ptr()) & 3) == 0 &&
+      (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0) {
+    const int64_t n8 = total / 8;
+    const int64_t blocks = (n8 + 256 * kFlatIlp - 1) / (256 * kFlatIlp);
+    if (blocks == 0) return;
+    nf4_to_bf16_flat_kernel<<<(unsigned)blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        reinterpret_cast<const uint32_t*>(packed.data_ptr<uint8_t>()), absmax.data_ptr<float>(),
+        reinterpret_cast<uint4*>(out.data_ptr<at::BFloat16>()), n8, (int)blocksize, (int)qtype);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   dim3 grid((unsigned)((cols + 63) / 64), (unsigned)((rows + 63) / 64));
   nf4_to_bf16_tile_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       packed.data_ptr<uint8_t>(), absmax.data_ptr<float>(),

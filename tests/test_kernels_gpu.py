@@ -85,13 +85,19 @@ def test_gemm_extra_slab(cuda, K):
 
 
 @pytest.mark.parametrize("transpose", [False, True])
-def test_nf4_to_bf16(cuda, transpose):
-    R, C = 384, 1280
+@pytest.mark.parametrize("R,C,bs,qt", [(384, 1280, 64, "nf4"), (33, 48, 64, "nf4"),
+                                       (640, 1024, 128, "fp4"), (1000, 3072, 256, "nf4")])
+def test_nf4_to_bf16(cuda, transpose, R, C, bs, qt):
+    """Flat (non-transposed, 32-aligned) and tiled paths, both code tables."""
+    from zeroq_b200.ops.nf4 import QUANT_TYPE_ID
+
+    if transpose and R % 16:
+        pytest.skip("transposed output needs rows % 16 == 0")
     w = torch.randn(R, C) * 0.02
-    p, a = quantize_4bit_reference(w, 64, "nf4")
-    ref = dequantize_4bit_reference(p, a, R * C, 64, "nf4", torch.bfloat16).view(R, C)
+    p, a = quantize_4bit_reference(w, bs, qt)
+    ref = dequantize_4bit_reference(p, a, R * C, bs, qt, torch.bfloat16).view(R, C)
     out = torch.empty(R * C, dtype=torch.bfloat16, device=cuda)
-    _ext.ext().nf4_to_bf16(p.to(cuda), a.to(cuda), out, R, C, 64, 0, transpose)
+    _ext.ext().nf4_to_bf16(p.to(cuda), a.to(cuda), out, R, C, bs, QUANT_TYPE_ID[qt], transpose)
     got = out.view(C, R).t() if transpose else out.view(R, C)
     assert torch.equal(got.cpu(), ref)
 
@@ -396,3 +402,75 @@ def test_nf4_linear_flat_grads_and_lora_cache(cuda):
     y = lin(x)
     yr, _, _ = ref_grads(x, gy)
     assert (y.float() - yr).abs().max().item() < 2e-2 * yr.abs().max().item()
+
+
+@pytest.mark.parametrize("M,rows,cols", [(256, 256, 128), (300, 320, 384), (1000, 1280, 768),
+                                         (2048, 3072, 3072), (512, 12288, 3072)])
+@pytest.mark.parametrize("w_is_kn", [False, True])
+@pytest.mark.parametrize("extra", [False, True])
+def test_gemm_nf4_in_kernel_decode_matches_operand_path(cuda, M, rows, cols, w_is_kn, extra):
+    """The GEMM that decodes the 4-bit weight inside its B producer gives exactly
+    the result of the standalone operand kernel followed by the bf16 GEMM (same
+    decoded bits, same MMA order), forward (C = A·Wᵀ) and input-gradient (C = A·W)."""
+    from zeroq_b200.ops.nf4 import quantize_4bit
+
+    E = _ext.ext()
+    torch.manual_seed(21)
+    w = torch.randn(rows, cols, device=cuda) * 0.05
+    packed, st = quantize_4bit(w, 64, "nf4")
+    K, N = (rows, cols) if w_is_kn else (cols, rows)
+    if K % 128 or N % 64:
+        pytest.skip("shape outside the in-kernel decode's tiling")
+    a = torch.randn(M, K, device=cuda, dtype=torch.bfloat16)
+    a2 = b2 = None
+    if extra:
+        a2 = torch.randn(M, 64, device=cuda, dtype=torch.bfloat16)
+        b2 = torch.randn(64, N, device=cuda, dtype=torch.bfloat16) if w_is_kn else \
+            torch.randn(N, 64, device=cuda, dtype=torch.bfloat16)
+    c = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+    E.gemm_nf4(a, packed, st.absmax, rows, cols, 64, 0, w_is_kn, c, a2, b2)
+    wb = torch.empty(rows * cols, device=cuda, dtype=torch.bfloat16)
+    E.nf4_to_bf16(packed, st.absmax, wb, rows, cols, 64, 0, False)
+    ref = torch.empty_like(c)
+    if w_is_kn:
+        E.gemm_bf16_nn(a, wb.view(rows, cols), ref, a2, b2)
+    elif extra:
+        E.gemm_bf16_tn_extra(a, wb.view(rows, cols), ref, a2, b2)
+    else:
+        E.set_gemm_pair_mode(1)
+        E.gemm_bf16_tn(a, wb.view(rows, cols), ref)
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    assert torch.equal(c, ref)
+    exact = a.float() @ (wb.view(rows, cols).float() if w_is_kn else wb.view(rows, cols).float().t())
+    if extra:
+        exact = exact + a2.float() @ (b2.float() if w_is_kn else b2.float().t())
+    assert (c.float() - exact).abs().max().item() < 2e-2 * exact.abs().max().item() + 1e-2
+
+
+@pytest.mark.parametrize("quant_type,blocksize", [("fp4", 64), ("nf4", 128), ("nf4", 256)])
+def test_gemm_nf4_fp4_and_block_sizes(cuda, quant_type, blocksize):
+    from zeroq_b200.ops.nf4 import QUANT_TYPE_ID, quantize_4bit
+
+    E = _ext.ext()
+    torch.manual_seed(22)
+    rows, cols, M = 768, 1024, 512
+    w = torch.randn(rows, cols, device=cuda) * 0.05
+    packed, st = quantize_4bit(w, blocksize, quant_type)
+    qt = QUANT_TYPE_ID[quant_type]
+    wb = torch.empty(rows * cols, device=cuda, dtype=torch.bfloat16)
+    E.nf4_to_bf16(packed, st.absmax, wb, rows, cols, blocksize, qt, False)
+    for w_is_kn in (False, True):
+        K, N = (rows, cols) if w_is_kn else (cols, rows)
+        a = torch.randn(M, K, device=cuda, dtype=torch.bfloat16)
+        c = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+        E.gemm_nf4(a, packed, st.absmax, rows, cols, blocksize, qt, w_is_kn, c, None, None)
+        ref = torch.empty_like(c)
+        if w_is_kn:
+            E.gemm_bf16_nn(a, wb.view(rows, cols), ref, None, None)
+        else:
+            E.set_gemm_pair_mode(1)
+            E.gemm_bf16_tn(a, wb.view(rows, cols), ref)
+        torch.cuda.synchronize()
+        _status_ok(cuda)
+        assert torch.equal(c, ref), (quant_type, blocksize, w_is_kn)

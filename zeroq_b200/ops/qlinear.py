@@ -7,9 +7,15 @@ layout); no full-precision copy of it is kept between uses.
 
 CUDA path, per call (``csrc/gemm_sm100.cu``):
 
-* the NF4 operand kernel expands ``W`` to a transient bf16 operand ``[N, K]``
-  that stays L2-resident for the GEMM that follows;
-* the tcgen05/TMEM GEMM computes ``Y = X Wᵀ`` and, in the same MMA chain, the
+* the NF4 operand kernel expands ``W`` once per use into a transient bf16
+  ``[N, K]`` operand (a flat, fully coalesced decode) that stays L2-resident for
+  the GEMM that follows.  The alternative ``gemm_nf4`` decodes ``W`` inside the
+  GEMM (four decode warps per CTA write the bf16 B tile straight into the
+  tensor-core operand layout, no bf16 copy of ``W`` at all) and gives bit-identical
+  results, but it re-decodes every weight tile once per 256 rows of ``X`` and
+  measured 2.4-3.4x slower than decode-once at every M from 256 to 8192 on B200,
+  so it is off by default (``ZEROQ_IN_KERNEL_DECODE=1`` enables it);
+* the tcgen05/TMEM pair GEMM computes ``Y = X Wᵀ`` and, in the same MMA chain, the
   LoRA up-projection as one extra 64-wide K slab (``U = s·X Aᵀ`` against
   ``B``, both zero-padded to rank 64); the input gradient
   ``dX = dY W + (s·dY B) A`` reads the same ``[N, K]`` operand MN-major
@@ -33,6 +39,7 @@ LoRA parameter names follow PEFT (``lora_A [r, in]``, ``lora_B [out, r]``,
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -40,6 +47,14 @@ import torch.nn as nn
 
 from . import _ext
 from .nf4 import QUANT_TYPE_ID, QuantState, dequantize_4bit, quantize_4bit
+
+
+# in-kernel decode of the 4-bit weight inside the GEMM (off by default, see above)
+IN_KERNEL_DECODE = os.environ.get("ZEROQ_IN_KERNEL_DECODE", "0") == "1"
+
+
+def _in_kernel_ok(M: int, K: int, N: int) -> bool:
+    return IN_KERNEL_DECODE and M >= 256 and K % 128 == 0 and N % 64 == 0
 
 
 def _fused_ok(x: torch.Tensor, K: int, N: int, blocksize: int) -> bool:
@@ -104,17 +119,22 @@ class NF4LinearFunction(torch.autograd.Function):
         a_pad = b_pad = None
         if fused:
             E = _ext.ext()
-            w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
             y = torch.empty(M, N, dtype=x2.dtype, device=x2.device)
             if has_lora:
                 if lora_ops is None:
                     lora_ops = _pack_lora(lora_A.detach(), lora_B.detach(), scaling)
                 a_pad, b_pad = lora_ops
                 U = x2 @ a_pad.t()  # [M, 64] skinny product: cuBLAS
-                E.gemm_bf16_tn_extra(x2, w, y, U, b_pad)
+            if _in_kernel_ok(M, K, N):
+                E.gemm_nf4(x2, packed, absmax, N, K, blocksize, QUANT_TYPE_ID[quant_type], False, y,
+                           U, b_pad)
             else:
-                E.gemm_bf16_tn(x2, w, y)
-            del w
+                w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
+                if has_lora:
+                    E.gemm_bf16_tn_extra(x2, w, y, U, b_pad)
+                else:
+                    E.gemm_bf16_tn(x2, w, y)
+                del w
         else:
             w = _dequant_weight(packed, absmax, N, K, blocksize, quant_type, torch.float32)
             y = x2.float() @ w.t()
@@ -146,16 +166,20 @@ class NF4LinearFunction(torch.autograd.Function):
                 V = gy2 @ b_pad  # [M, 64] = dY·B (unscaled), skinny product: cuBLAS
             if ctx.needs_input_grad[0]:
                 gx = torch.empty(M, K, dtype=torch.bfloat16, device=gy2.device)
-                if M >= 256:  # W [N, K] read MN-major: dX = dY·W + V·(s·A)
+                if _in_kernel_ok(M, N, K):  # dX = dY·W + V·(s·A), W decoded in the kernel
+                    E.gemm_nf4(gy2, packed, absmax, N, K, blocksize, QUANT_TYPE_ID[quant_type],
+                               True, gx, V, a_pad)
+                elif M >= 256:  # W [N, K] read MN-major from the operand kernel's copy
                     w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
                     E.gemm_bf16_nn(gy2, w, gx, V, a_pad)
+                    del w
                 else:  # short inputs: single-CTA kernel on the transposed operand
                     w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, True)
                     if has_lora:
                         E.gemm_bf16_tn_extra(gy2, w, gx, V, a_pad.t().contiguous())
                     else:
                         E.gemm_bf16_tn(gy2, w, gx)
-                del w
+                    del w
                 gx = gx.view(*shp[:-1], K)
             if has_lora:
                 # dA = s·Vᵀ·X, dB = dYᵀ·U: bf16 operands, fp32 accumulation
