@@ -663,7 +663,7 @@ using namespace zq;
 // ----------------------------------------------------------------------------
 // host side
 // ----------------------------------------------------------------------------
-static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
   std::call_once(once, [] {
@@ -713,7 +713,7 @@ static CUtensorMap make_tmap_store_bf16(const void* base, int64_t rows, int64_t 
   return map;
 }
 
-static DeviceStatus* status_buffer(int device) {
+DeviceStatus* status_buffer(int device) {
   static DeviceStatus* bufs[64] = {nullptr};
   static std::mutex mu;
   std::lock_guard<std::mutex> g(mu);

@@ -474,3 +474,33 @@ def test_gemm_nf4_fp4_and_block_sizes(cuda, quant_type, blocksize):
         torch.cuda.synchronize()
         _status_ok(cuda)
         assert torch.equal(c, ref), (quant_type, blocksize, w_is_kn)
+
+
+
+@pytest.mark.parametrize("B,S,Hq,Hk", [(2, 256, 4, 4), (1, 1024, 8, 2), (2, 512, 3, 1), (1, 2048, 2, 2)])
+@pytest.mark.parametrize("causal", [True, False])
+def test_attention_forward_tcgen05_vs_fp32(cuda, B, S, Hq, Hk, causal):
+    """tcgen05 forward: output and row log-sum-exp against an fp32 reference."""
+    torch.manual_seed(31)
+    D = 128
+    q = torch.randn(B, S, Hq, D, device=cuda, dtype=torch.bfloat16)
+    k = torch.randn(B, S, Hk, D, device=cuda, dtype=torch.bfloat16)
+    v = torch.randn(B, S, Hk, D, device=cuda, dtype=torch.bfloat16)
+    o = torch.empty_like(q)
+    lse = torch.empty(B, Hq, S, device=cuda)
+    scale = 1.0 / math.sqrt(D)
+    _ext.ext().attn_fwd_tc(q, k, v, o, lse, causal, scale)
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    rep = Hq // Hk
+    qf = q.float().transpose(1, 2)
+    kf = k.float().transpose(1, 2).repeat_interleave(rep, dim=1)
+    vf = v.float().transpose(1, 2).repeat_interleave(rep, dim=1)
+    s = (qf @ kf.transpose(-1, -2)) * scale
+    if causal:
+        mask = torch.ones(S, S, device=cuda, dtype=torch.bool).triu(1)
+        s = s.masked_fill(mask, float("-inf"))
+    ref_lse = torch.logsumexp(s, dim=-1)
+    ref_o = (torch.softmax(s, dim=-1) @ vf).transpose(1, 2)
+    assert (o.float() - ref_o).abs().max().item() < 2e-2
+    assert (lse - ref_lse).abs().max().item() < 1e-3

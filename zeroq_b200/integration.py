@@ -125,8 +125,14 @@ def prepare_model_for_zeroq(model: nn.Module, config: Optional[ZeroQConfig] = No
                             freeze_base: bool = True,
                             trainable_patterns: Iterable[str] = ("lora_",),
                             rank_weights: Optional[Sequence[float]] = None,
-                            process_group=None) -> nn.Module:
-    """Freeze, register, quantise and shard; optionally switch to 4-bit compute."""
+                            process_group=None, checkpoint: Optional[str] = None) -> nn.Module:
+    """Freeze, register, quantise and shard; optionally switch to 4-bit compute.
+
+    With ``checkpoint`` (a safetensors file or directory, Hugging Face
+    Llama/Qwen2 names) the frozen weights are read tensor by tensor and sharded
+    on arrival (:func:`zeroq_b200.utils.loading.stream_load`): register the model
+    with meta-device projection weights (``DecoderLM.init_meta_``) and no rank
+    ever holds the full model in full precision."""
     config = config or B200_CONFIG
     if freeze_base:
         _freeze_base(model, trainable_patterns)
@@ -137,7 +143,12 @@ def prepare_model_for_zeroq(model: nn.Module, config: Optional[ZeroQConfig] = No
     else:
         coordinator = ZeroQCoordinator(config, process_group)
         wrapper = ZeroQModuleWrapper(model, coordinator, trainable_only=False)
-    wrapper.partition()
+    if checkpoint is not None:
+        from .utils.loading import stream_load
+
+        model._zeroq_load_counts = stream_load(model, checkpoint, coordinator)
+    else:
+        wrapper.partition()
     if hetero:
         coordinator.verify_registration_consistency()
     if (config.resolved_backend() == "fused" and coordinator.world_size > 1

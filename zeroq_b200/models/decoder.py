@@ -51,6 +51,7 @@ class DecoderConfig:
     head_dim: int = 64
     ffn_dim: int = 688
     ffn_act: str = "swiglu"  # "swiglu" | "gelu"
+    qkv_bias: bool = False   # Qwen2-family models carry Q/K/V biases
     rope_theta: float = 10000.0
     norm_eps: float = 1e-6
     tie_embeddings: bool = True
@@ -75,6 +76,8 @@ class DecoderConfig:
     def num_params(self) -> int:
         d, L = self.d_model, self.n_layers
         attn = d * self.n_heads * self.head_dim * 2 + d * self.n_kv_heads * self.head_dim * 2
+        if self.qkv_bias:
+            attn += (self.n_heads + 2 * self.n_kv_heads) * self.head_dim
         mlp = d * self.ffn_dim * (3 if self.ffn_act == "swiglu" else 2)
         emb = self.vocab_size * d * (1 if self.tie_embeddings else 2)
         return L * (attn + mlp + 2 * d) + emb + d
@@ -92,11 +95,11 @@ PRESETS = {
                                         "up_proj", "down_proj")),
     "qwen2.5-7b": DecoderConfig(vocab_size=152064, d_model=3584, n_layers=28, n_heads=28,
                                 n_kv_heads=4, head_dim=128, ffn_dim=18944, ffn_act="swiglu",
-                                rope_theta=1e6, tie_embeddings=False,
+                                qkv_bias=True, rope_theta=1e6, tie_embeddings=False,
                                 lora_targets=("q_proj", "k_proj", "v_proj", "o_proj")),
     "qwen2.5-32b": DecoderConfig(vocab_size=152064, d_model=5120, n_layers=64, n_heads=40,
                                  n_kv_heads=8, head_dim=128, ffn_dim=27648, ffn_act="swiglu",
-                                 rope_theta=1e6, tie_embeddings=False,
+                                 qkv_bias=True, rope_theta=1e6, tie_embeddings=False,
                                  activation_checkpointing=True,
                                  lora_targets=("q_proj", "k_proj", "v_proj", "o_proj",
                                                "gate_proj", "up_proj", "down_proj")),
@@ -136,7 +139,8 @@ class DecoderLayer(nn.Module):
 
         def lin(name, i, o):
             r = cfg.lora_r if name in cfg.lora_targets else 0
-            return Linear4bit(i, o, bias=False, blocksize=cfg.blocksize,
+            bias = cfg.qkv_bias and name in ("q_proj", "k_proj", "v_proj")
+            return Linear4bit(i, o, bias=bias, blocksize=cfg.blocksize,
                               quant_type=cfg.quant_type, lora_r=r, lora_alpha=cfg.lora_alpha,
                               device=device, dtype=dtype)
 
@@ -242,6 +246,17 @@ class DecoderLM(nn.Module):
                     m.quantize_from(w)
                     del w
         self._zero_vocab_padding()
+        return self
+
+    def init_meta_(self):
+        """Give every projection a meta-device weight of its full shape: the model
+        can then be registered with a coordinator and filled tensor by tensor
+        from a checkpoint (``zeroq_b200.utils.loading``) without ever holding a
+        full-precision copy."""
+        for layer in self.layers:
+            for _, m in layer.projections():
+                m.weight = nn.Parameter(torch.empty(m.out_features, m.in_features, device="meta",
+                                                    dtype=self.dtype), requires_grad=False)
         return self
 
     def convert_to_4bit_(self):

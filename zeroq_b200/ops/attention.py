@@ -1,11 +1,14 @@
 """Causal (GQA-capable) flash attention, forward and backward.
 
-Tensors keep the projection layout ``[B, S, H, D]`` (``D = 128``) so no
-transposes surround the kernels.  The forward (``csrc/attention.cu``) streams
-K/V tiles with online softmax and writes ``O`` plus the row log-sum-exp ``L``;
-the backward recomputes probabilities from ``L``, accumulates ``dK``/``dV`` per
-key tile in registers and ``dQ`` in fp32 with atomics, after a small kernel that
-forms ``delta = rowsum(dO * O)``.
+Tensors keep the projection layout ``[B, S, H, D]`` so no transposes surround
+the kernels.  For ``D = 128`` the forward runs on the 5th-generation tensor
+cores (``csrc/attention_sm100.cu``: TMA-fed Q/K/V tiles, S and O accumulated in
+tensor memory, softmax in registers, P through shared memory); ``D = 64`` uses
+the ``mma.sync`` kernel in ``csrc/attention.cu``.  Both write ``O`` plus the row
+log-sum-exp ``L``.  The backward (``csrc/attention.cu``) recomputes
+probabilities from ``L``, accumulates ``dK``/``dV`` per key tile in registers and
+``dQ`` in fp32 with atomics, after a small kernel that forms
+``delta = rowsum(dO * O)``.
 
 CPU tensors use PyTorch's SDPA (the oracle).
 """
@@ -43,7 +46,10 @@ class _FlashAttn(torch.autograd.Function):
         B, S, Hq, D = q.shape
         o = torch.empty_like(q)
         lse = torch.empty(B, Hq, S, dtype=torch.float32, device=q.device)
-        _ext.ext().attn_fwd(q, k, v, o, lse, bool(causal), float(scale))
+        if D == 128:
+            _ext.ext().attn_fwd_tc(q, k, v, o, lse, bool(causal), float(scale))
+        else:
+            _ext.ext().attn_fwd(q, k, v, o, lse, bool(causal), float(scale))
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.causal, ctx.scale = causal, scale
         return o

@@ -204,6 +204,14 @@ def load_sharded_checkpoint(path: str, model: nn.Module, optimizer=None,
             name = k[len("nf4/"):-len("/packed")]
             mods[name].set_nf4(v.to(_module_device(mods[name])),
                                tensors[f"nf4/{name}/absmax"].to(_module_device(mods[name])))
+    zcfg = getattr(model, "_zeroq_config", None)
+    if (coord is not None and getattr(model, "_zeroq_wrapper", "hooks") is None
+            and getattr(zcfg, "gather_once", False)):
+        # gather-once mode has no hooks to gather again: rebuild the resident
+        # weights (NF4 for Linear4bit, dequantised for the rest) from the shards
+        from ..integration import convert_to_4bit_compute
+
+        convert_to_4bit_compute(model, coord, None)
     params = dict(model.named_parameters())
     with torch.no_grad():
         for k, v in tensors.items():
