@@ -164,7 +164,7 @@ def main():
             o = flash_attention(q, k, v, causal=True)
             o.backward(go)
 
-        ms = _time(step, a.reps)
+        ms = _time(step, a.reps, a.profile)
         _report(f"attention fwd+bwd B={a.b} S={a.s} H={a.h} D={a.d} causal", ms,
                 flops=fwd_fl * 3.5)
     elif a.case == "nf4_operand":
