@@ -81,3 +81,68 @@ def test_train_qlora_example_cpu_save_resume(tmp_path):
     logs2 = [json.loads(l) for l in r2.stdout.splitlines() if l.startswith("{")]
     assert logs2[0]["resume_step"] == 3
     assert [l["step"] for l in logs2 if "loss" in l] == [4, 5]
+
+
+def _run(args, timeout=600, extra_env=None):
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", PYTHONPATH=ROOT)
+    env.update(extra_env or {})
+    return subprocess.run(args, env=env, capture_output=True, text=True, timeout=timeout)
+
+
+@pytest.mark.parametrize("optimizer", ["adamw", "lion-fused", "adamw-offload"])
+def test_train_from_scratch_example_learns(optimizer):
+    """fp32 master shards (ZeroQTrainConfig): memorising one batch lowers the loss
+    with AdamW, the fused Lion step and the CPU-offload path."""
+    r = _run([sys.executable, os.path.join(ROOT, "examples", "train_from_scratch.py"), "--layers",
+              "2", "--steps", "6", "--seq", "64", "--batch", "2", "--optimizer", optimizer,
+              "--fixed-batch"])
+    assert r.returncode == 0, r.stdout + r.stderr
+    done = [json.loads(l) for l in r.stdout.splitlines() if l.startswith('{"event": "done"')][0]
+    assert done["last_loss"] < done["first_loss"] - 0.5
+
+
+def test_network_test_local_round_trips():
+    r = _run([sys.executable, os.path.join(ROOT, "examples", "network_test.py"), "--role", "local",
+              "--port", "5597", "--reps", "1"], timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    rows = [json.loads(l) for l in r.stdout.splitlines() if l.startswith("{")]
+    assert [row["elements"] for row in rows] == [1 << 10, 1 << 16, 1 << 20, 1 << 24]
+
+
+@pytest.mark.distributed
+def test_smoke_lora_multinode_two_ranks_agree():
+    r = _run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+              "--master-addr", "127.0.0.1", "--master-port", "29563",
+              os.path.join(ROOT, "examples", "smoke_lora_multinode.py")], timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    done = [json.loads(l) for l in r.stdout.splitlines() if l.startswith('{"event": "done"')][0]
+    assert done["ok"] and done["world"] == 2
+
+
+def test_prefetch_tool_help():
+    r = _run([sys.executable, os.path.join(ROOT, "examples", "prefetch_hf_model.py"), "--help"],
+             timeout=120)
+    assert r.returncode == 0 and "--local-dir" in r.stdout
+
+
+def test_launch_script_dry_run_builds_one_torchrun_per_node():
+    env = dict(os.environ, HOSTS="node0 node1 node2", NPROC="8", MASTER_ADDR="10.0.0.1",
+               DRY_RUN="1")
+    r = subprocess.run(["bash", os.path.join(ROOT, "examples", "launch_multinode.sh"), "start",
+                        "examples/train_qlora.py", "--model", "qwen2.5-32b"], env=env,
+                       capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stderr
+    cmds = [l for l in r.stdout.splitlines() if l.startswith("[node")]
+    assert len(cmds) == 3
+    for i, c in enumerate(cmds):
+        assert f"--node-rank {i}" in c and "--nnodes 3" in c and "--master-addr 10.0.0.1" in c
+        assert "setsid" in c and "qwen2.5-32b" in c
+
+
+def test_memory_scaling_benchmark_shards_shrink_with_world():
+    r = _run([sys.executable, os.path.join(ROOT, "benchmarks", "memory_scaling.py"), "--hidden",
+              "256", "--layers", "2", "--world", "1", "2"], timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr
+    rows = {d["world"]: d for d in (json.loads(l) for l in r.stdout.splitlines() if l.startswith("{"))}
+    assert rows[1]["ratio_vs_fp16"] > 3.4   # NF4 + fp32 absmax per 64 vs fp16
+    assert rows[2]["nf4_shard_bytes_per_rank"] <= rows[1]["nf4_shard_bytes_per_rank"] / 2 + 64
