@@ -85,7 +85,8 @@ def _report(name, ms, byts=None, flops=None, extra=""):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attention", "nf4_operand", "rmsnorm", "gelu", "q4gemm"])
+    ap.add_argument("case", choices=["gemm", "attention", "attn_trace", "nf4_operand", "rmsnorm",
+                                     "gelu", "q4gemm"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=3072)
@@ -97,6 +98,7 @@ def main():
     ap.add_argument("--h", type=int, default=24)
     ap.add_argument("--d", type=int, default=128)
     ap.add_argument("--transpose", action="store_true")
+    ap.add_argument("--bhsd", action="store_true", help="attn_trace: K/V as [B, H, S, D]")
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--profile", action="store_true", help="print one call's kernels (torch profiler)")
     a = ap.parse_args()
@@ -148,6 +150,43 @@ def main():
                 E.gemm_bf16_tn(x, wb.view(rows, cols), y)
 
         _report(f"operand kernel + gemm {a.m}x{a.n}x{a.k} nn={a.nn}", _time(two_step, a.reps), flops=fl)
+    elif a.case == "attn_trace":
+        # per-CTA timeline of the tcgen05 forward from its optional timestamp trace
+        q = torch.randn(a.b, a.s, a.h, a.d, device=dev, dtype=torch.bfloat16)
+        k, v = torch.randn_like(q), torch.randn_like(q)
+        o = torch.empty_like(q)
+        lse = torch.empty(a.b, a.h, a.s, device=dev)
+        grid = a.b * a.h * (a.s // 128)
+        tr = torch.zeros(grid, 32, dtype=torch.int64, device=dev)
+        scale = a.d ** -0.5
+        if a.bhsd:  # K/V handed over head-major: every key tile is one contiguous block
+            k, v = k.transpose(1, 2).contiguous(), v.transpose(1, 2).contiguous()
+        for _ in range(3):
+            E.attn_fwd_tc(q, k, v, o, lse, True, scale, None, a.bhsd)
+        torch.cuda.synchronize()
+        ms = _time(lambda: E.attn_fwd_tc(q, k, v, o, lse, True, scale, None, a.bhsd), a.reps)
+        _report(f"attn_fwd_tc kv_bhsd={a.bhsd}", ms, flops=4.0 * a.b * a.h * a.s * a.s * a.d / 2)
+        E.attn_fwd_tc(q, k, v, o, lse, True, scale, tr, a.bhsd)
+        torch.cuda.synchronize()
+        t = tr.cpu().double()
+        n = t[:, 31].long()
+        print(f"attn trace B={a.b} S={a.s} H={a.h}: kernel span "
+              f"{(t[:, 30].max() - t[:, 0].min()) / 1e3:.1f} us over {grid} CTAs")
+        print(f"  CTA start -> first S ready: mean {((t[:, 1] - t[:, 0]) / 1e3).mean():.2f} us")
+        names = ["S ready", "max exchanged", "exps done", "P stored", "p_full arrived",
+                 "MMA: K_next seen", "MMA: S_next issued", "MMA: p_full seen", "MMA: V seen",
+                 "MMA: PV issued", "K_next load issued", "V load issued"]
+        sel = n >= 4  # CTAs that ran tiles 0..3
+        if sel.any():
+            base = t[sel]
+            for j in range(1, 3):
+                s0 = base[:, 2 + 12 * (j - 1)]
+                row = [f"{nm} {((base[:, 2 + 12 * (j - 1) + i] - s0) / 1e3).mean():+.3f}"
+                       for i, nm in enumerate(names) if i > 0]
+                nxt = ((base[:, 2 + 12 * j] - s0) / 1e3).mean() if j < 2 else float("nan")
+                print(f"  tile {j} (us from S ready): " + ", ".join(row) + f"; next S ready +{nxt:.3f}")
+        last_end = t[:, 30]
+        print(f"  CTA duration mean {((last_end - t[:, 0]) / 1e3).mean():.2f} us")
     elif a.case == "attention":
         from zeroq_b200.ops.attention import flash_attention
 

@@ -490,8 +490,14 @@ def test_attention_forward_tcgen05_vs_fp32(cuda, B, S, Hq, Hk, causal):
     lse = torch.empty(B, Hq, S, device=cuda)
     scale = 1.0 / math.sqrt(D)
     _ext.ext().attn_fwd_tc(q, k, v, o, lse, causal, scale)
+    # the same with K/V handed over head-major ([B, Hk, S, D])
+    o2 = torch.empty_like(q)
+    lse2 = torch.empty_like(lse)
+    _ext.ext().attn_fwd_tc(q, k.transpose(1, 2).contiguous(), v.transpose(1, 2).contiguous(), o2,
+                           lse2, causal, scale, None, True)
     torch.cuda.synchronize()
     _status_ok(cuda)
+    assert torch.equal(o, o2) and torch.equal(lse, lse2)
     rep = Hq // Hk
     qf = q.float().transpose(1, 2)
     kf = k.float().transpose(1, 2).repeat_interleave(rep, dim=1)
