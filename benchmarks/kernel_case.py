@@ -85,8 +85,8 @@ def _report(name, ms, byts=None, flops=None, extra=""):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attention", "attn_trace", "nf4_operand", "rmsnorm",
-                                     "gelu", "q4gemm"])
+    ap.add_argument("case", choices=["gemm", "attention", "attn_trace", "attn_bwd_trace",
+                                     "nf4_operand", "rmsnorm", "gelu", "q4gemm"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=3072)
@@ -187,6 +187,39 @@ def main():
                 print(f"  tile {j} (us from S ready): " + ", ".join(row) + f"; next S ready +{nxt:.3f}")
         last_end = t[:, 30]
         print(f"  CTA duration mean {((last_end - t[:, 0]) / 1e3).mean():.2f} us")
+    elif a.case == "attn_bwd_trace":
+        # per-CTA timelines of the tcgen05 backward kernels (dQ, then dK/dV)
+        q = torch.randn(a.b, a.s, a.h, a.d, device=dev, dtype=torch.bfloat16)
+        k, v, do = torch.randn_like(q), torch.randn_like(q), torch.randn_like(q)
+        o = torch.empty_like(q)
+        lse = torch.empty(a.b, a.h, a.s, device=dev)
+        scale = a.d ** -0.5
+        E.attn_fwd_tc(q, k, v, o, lse, True, scale)
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        g = a.b * a.h * (a.s // 128)
+        tr = torch.zeros(2 * g, 32, dtype=torch.int64, device=dev)
+        for _ in range(3):
+            E.attn_bwd_tc(do, q, k, v, o, lse, dq, dk, dv, True, scale)
+        torch.cuda.synchronize()
+        ms = _time(lambda: E.attn_bwd_tc(do, q, k, v, o, lse, dq, dk, dv, True, scale), a.reps)
+        _report("attn_bwd_tc (delta + dQ + dK/dV)", ms,
+                flops=2.5 * 4.0 * a.b * a.h * a.s * a.s * a.d / 2)
+        E.attn_bwd_tc(do, q, k, v, o, lse, dq, dk, dv, True, scale, tr)
+        torch.cuda.synchronize()
+        t = tr.cpu().double()
+        names = ["S/dP seen", "loaded", "computed", "arrived", "MMA: inputs seen", "MMA: S/dP issued",
+                 "MMA: dS seen", "MMA: grads issued"]
+        for label, part in (("dQ", t[:g]), ("dK/dV", t[g:])):
+            sel = (part[:, 1] > 0) & (part[:, 9] > 0) & (part[:, 16] > 0)
+            print(f"{label}: CTA span mean {((part[:, 30] - part[:, 0]) / 1e3).mean():.2f} us")
+            if sel.any():
+                p = part[sel]
+                for j in (1, 2):
+                    s0 = p[:, 1 + 8 * (j - 1)]
+                    row = [f"{nm} {((p[:, 1 + 8 * (j - 1) + i] - s0) / 1e3).mean():+.3f}"
+                           for i, nm in enumerate(names) if i > 0]
+                    print(f"  tile {j}: " + ", ".join(row))
+                print(f"  tile 1 -> tile 2 S/dP seen: {((p[:, 9] - p[:, 1]) / 1e3).mean():.3f} us")
     elif a.case == "attention":
         from zeroq_b200.ops.attention import flash_attention
 

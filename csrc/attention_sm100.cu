@@ -412,6 +412,553 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
   }
 }
 
+// ============================================================================
+// Backward: delta pre-pass, dQ kernel (per query tile) and dK/dV kernel (per
+// key tile), all on the 5th-generation tensor cores.
+//
+//   P  = exp(scale·Q Kᵀ - lse)            (recomputed from the saved lse)
+//   dP = dO Vᵀ,   dS = P ∘ (dP - delta),   delta = rowsum(dO ∘ O)
+//   dQ = scale · dS K,   dK = scale · dSᵀ Q,   dV = Pᵀ dO
+//
+// dQ kernel: one CTA per (128-query tile, head, batch).  Q and dO are copied
+// into tensor memory once; K and V tiles stream through TMA rings.  Per key
+// tile the MMA thread issues S = Q Kᵀ and dP = dO Vᵀ interleaved (two
+// independent accumulation chains), eight compute warps turn them into dS
+// (bf16, written over S's own columns) and the MMA thread adds dS·K into the
+// dQ accumulator (K read MN-major).  dQ is written once, in bf16: no atomics.
+// Tensor memory: S 0-127, dP 128-255, dQ 256-383, Q 384-447, dO 448-511.
+//
+// dK/dV kernel: one CTA per (128-key tile, kv head, batch), looping over the
+// query heads that share the kv head and over the query tiles that see the
+// key tile.  Sᵀ = K Qᵀ and dPᵀ = V dOᵀ (rows = keys) are issued interleaved;
+// the compute warps write Pᵀ and dSᵀ (bf16) over them, and dV += Pᵀ dO and
+// dK += dSᵀ Q read them from tensor memory (dO and Q read MN-major).
+// Tensor memory: dV 0-127, dK 128-255, Sᵀ 256-383, dPᵀ 384-511.
+//
+// In both kernels warps w and w+4 share TMEM lane quadrant w and split the 128
+// columns of a row; every exit from a compute loop is decided by a vote over
+// the pair, and every wait is bounded.
+// ============================================================================
+constexpr int kBwdThreads = 352;   // 8 compute warps, MMA warp, two loader warps
+constexpr int kBwdKStages = 3;     // dQ kernel K ring
+constexpr int kBwdVStages = 2;     // dQ kernel V ring
+constexpr int kBwdQStages = 2;     // dK/dV kernel Q and dO rings
+enum AttBwdErr { kErrBwdLoad = 311, kErrBwdMma = 312, kErrBwdCompute = 313 };
+
+// delta[b, h, s] = sum_d dO[b, s, h, d] * O[b, s, h, d]  (one warp per row, D = 128)
+// and lse2 = lse * log2(e) (the exponent offset in the exp2 form)
+__global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ dout,
+                                  const __nv_bfloat16* __restrict__ o, const float* __restrict__ lse,
+                                  float* __restrict__ delta, float* __restrict__ lse2,
+                                  int64_t rows, int S, int Hq) {
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const uint2 a = *reinterpret_cast<const uint2*>(dout + row * kAttD + lane * 4);
+  const uint2 c = *reinterpret_cast<const uint2*>(o + row * kAttD + lane * 4);
+  const float2 a0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a.x));
+  const float2 a1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a.y));
+  const float2 c0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&c.x));
+  const float2 c1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&c.y));
+  float acc = a0.x * c0.x + a0.y * c0.y + a1.x * c1.x + a1.y * c1.y;
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    const int h = (int)(row % Hq);
+    const int64_t bs = row / Hq;
+    const int s = (int)(bs % S), b = (int)(bs / S);
+    const int64_t li = ((int64_t)b * Hq + h) * S + s;
+    delta[li] = acc;
+    lse2[li] = lse[li] * 1.4426950408889634f;
+  }
+}
+
+// 64 consecutive columns of one TMEM row (this thread's lane) -> registers
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
+  tmem_ld_32x32b_x32(taddr, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+  tmem_ld_32x32b_x32(taddr + 32u, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+}
+
+// one 128-byte row of a 128-byte-swizzled smem atom (64 bf16) -> 32 TMEM columns
+__device__ __forceinline__ void copy_row_to_tmem(const uint8_t* atom_row, int row, uint32_t taddr) {
+  uint32_t v[32];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const uint4 u = *reinterpret_cast<const uint4*>(atom_row + ((c ^ (row & 7)) << 4));
+    v[4 * c + 0] = u.x;
+    v[4 * c + 1] = u.y;
+    v[4 * c + 2] = u.z;
+    v[4 * c + 3] = u.w;
+  }
+  tmem_st_32x32b_x32(taddr, v);
+}
+
+struct BwdDqSmem {
+  static constexpr int kTile = AttSmem::kTile, kAtom = AttSmem::kAtom;
+  static constexpr int kQ = 0, kDO = kTile;
+  static constexpr int kK = 2 * kTile;                        // kBwdKStages stages
+  static constexpr int kV = kK + kBwdKStages * kTile;         // kBwdVStages stages
+  static constexpr int kBar = kV + kBwdVStages * kTile;
+  static constexpr int kBytes = kBar + 256 + 1024;
+};
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                      const float* __restrict__ lse, const float* __restrict__ delta,
+                      __nv_bfloat16* __restrict__ dq, int B, int S, int Hq, int Hk, float scale_log2,
+                      float scale, int causal, DeviceStatus* status,
+                      unsigned long long* __restrict__ trace) {
+  // trace (optional, [grid][32] ns): 0 start; key tiles j = 1, 2 at 1 + 8(j-1) + i:
+  //   compute: i = 0 S/dP seen, 1 loaded, 2 dS computed, 3 arrived;
+  //   MMA: 4 K/V seen, 5 S/dP issued, 6 dS seen, 7 dQ issued;  30 end
+  unsigned long long* tr = trace ? trace + (size_t)blockIdx.x * 32 : nullptr;
+  if (tr && threadIdx.x == 0) tr[0] = globaltimer();
+  using L = BwdDqSmem;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* q_full = bars;                 // Q and dO landed
+  uint64_t* k_full = bars + 1;             // [kBwdKStages]
+  uint64_t* k_empty = bars + 4;            // [kBwdKStages]
+  uint64_t* v_full = bars + 7;             // [kBwdVStages]
+  uint64_t* v_empty = bars + 9;            // [kBwdVStages]
+  uint64_t* s_full = bars + 11;            // S and dP of the current key tile
+  uint64_t* ds_full = bars + 12;           // dS written (one arrival per compute warp)
+  uint64_t* dq_done = bars + 13;
+  uint64_t* in_tmem = bars + 14;           // Q, dO copied into TMEM
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqt = S / kAttRows;
+  const int bh = (int)(blockIdx.x / (unsigned)nqt);
+  const int qt = nqt - 1 - (int)(blockIdx.x % (unsigned)nqt);
+  const int b = bh / Hq, h = bh % Hq;
+  const int hk = h / (Hq / Hk);
+  const int n_kv = causal ? qt + 1 : nqt;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kBwdKStages; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1); }
+    for (int i = 0; i < kBwdVStages; ++i) { mbar_init(&v_full[i], 1); mbar_init(&v_empty[i], 1); }
+    mbar_init(s_full, 1);
+    mbar_init(ds_full, kSoftmaxWarps);
+    mbar_init(dq_done, 1);
+    mbar_init(in_tmem, kSoftmaxWarps);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+    prefetch_tmap(&tmQ); prefetch_tmap(&tmK); prefetch_tmap(&tmV); prefetch_tmap(&tmDO);
+  }
+  if (warp == 8) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp >= 9) {
+    // ------------------------------------------------------------ TMA loaders
+    if (lane == 0) {
+      const bool is_k = warp == 9;
+      if (is_k) {
+        mbar_arrive_expect_tx(q_full, 2 * L::kTile);
+        tma_load_4d(smem + L::kQ, &tmQ, q_full, 0, h, qt * kAttRows, b);
+        tma_load_4d(smem + L::kQ + L::kAtom, &tmQ, q_full, 64, h, qt * kAttRows, b);
+        tma_load_4d(smem + L::kDO, &tmDO, q_full, 0, h, qt * kAttRows, b);
+        tma_load_4d(smem + L::kDO + L::kAtom, &tmDO, q_full, 64, h, qt * kAttRows, b);
+      }
+      const CUtensorMap* map = is_k ? &tmK : &tmV;
+      uint64_t* empty = is_k ? k_empty : v_empty;
+      uint64_t* full = is_k ? k_full : v_full;
+      uint8_t* ring = smem + (is_k ? L::kK : L::kV);
+      const int nst = is_k ? kBwdKStages : kBwdVStages;
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j % nst;
+        if (!mbar_wait(&empty[st], ((j / nst) & 1) ^ 1, status, kErrBwdLoad)) { ok = false; break; }
+        uint8_t* dst = ring + st * L::kTile;
+        mbar_arrive_expect_tx(&full[st], L::kTile);
+        tma_load_4d(dst, map, &full[st], 0, hk, j * kAttKeys, b);
+        tma_load_4d(dst + L::kAtom, map, &full[st], 64, hk, j * kAttKeys, b);
+        issued = j + 1;
+      }
+      if (!ok) {  // let every copy this thread issued land before the CTA can exit
+        if (is_k) mbar_wait(q_full, 0, nullptr, 0);
+        for (int j = (issued > nst ? issued - nst : 0); j < issued; ++j)
+          mbar_wait(&full[j % nst], (j / nst) & 1, nullptr, 0);
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_k = umma_idesc_bf16(kAttRows, kAttKeys);   // S, dP (B K-major)
+      constexpr uint32_t idesc_mn = umma_idesc_bf16_bmn(kAttRows, kAttD); // dQ (K read MN-major)
+      bool ok = mbar_wait(in_tmem, 0, status, kErrBwdMma);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        unsigned long long* tj = (tr && (j == 1 || j == 2)) ? tr + 1 + 8 * (j - 1) : nullptr;
+        const int ks = j % kBwdKStages, vs = j % kBwdVStages;
+        if (!mbar_wait(&k_full[ks], (j / kBwdKStages) & 1, status, kErrBwdMma)) { ok = false; break; }
+        if (!mbar_wait(&v_full[vs], (j / kBwdVStages) & 1, status, kErrBwdMma)) { ok = false; break; }
+        if (tj) tj[4] = globaltimer();
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(smem + L::kK + ks * L::kTile);
+        const uint32_t v_addr = smem_u32(smem + L::kV + vs * L::kTile);
+#pragma unroll
+        for (int kk = 0; kk < kAttD / 16; ++kk) {   // S = Q Kᵀ and dP = dO Vᵀ, interleaved
+          const uint32_t off = (uint32_t)((kk >> 2) * L::kAtom + (kk & 3) * 32);
+          umma_f16_ts(tmem, tmem + 384u + (uint32_t)(kk * 8), umma_desc_sw128_kmajor(k_addr + off),
+                      idesc_k, kk > 0 ? 1u : 0u);
+          umma_f16_ts(tmem + 128u, tmem + 448u + (uint32_t)(kk * 8),
+                      umma_desc_sw128_kmajor(v_addr + off), idesc_k, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full);
+        umma_commit(&v_empty[vs]);   // V_j consumed
+        if (tj) tj[5] = globaltimer();
+        if (!mbar_wait(ds_full, j & 1, status, kErrBwdMma)) { ok = false; break; }
+        if (tj) tj[6] = globaltimer();
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kAttKeys / 16; ++kk)   // dQ += dS K: dS in S's columns, K MN-major
+          umma_f16_ts(tmem + 256u, tmem + (uint32_t)(kk * 8),
+                      umma_desc_sw128_mnmajor(k_addr + (uint32_t)kk * 2048u, (uint32_t)L::kAtom),
+                      idesc_mn, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&k_empty[ks]);   // K_j consumed
+        if (tj) tj[7] = globaltimer();
+      }
+      umma_commit(dq_done);
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ dS + epilogue
+    const int quad = warp & 3, half = warp >> 2;
+    const int row = quad * 32 + lane;                     // query row = TMEM lane
+    const int col0 = half * 64;                           // this half's key (and D) columns
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    const int pair_bar = 1 + quad;
+    const int q = qt * kAttRows + row;
+    const int64_t lrow = ((int64_t)b * Hq + h) * S + q;
+    const float l2 = lse[lrow] * 1.4426950408889634f;      // lse in log2 units
+    const float dl = delta[lrow];
+    bool ok = named_barrier_and(pair_bar, 64, mbar_wait(q_full, 0, status, kErrBwdCompute));
+    if (ok) {  // Q and dO rows into tensor memory (A operands of S and dP)
+      copy_row_to_tmem(smem + L::kQ + half * L::kAtom + row * 128, row,
+                       tmem + lane_base + 384u + (uint32_t)(half * 32));
+      copy_row_to_tmem(smem + L::kDO + half * L::kAtom + row * 128, row,
+                       tmem + lane_base + 448u + (uint32_t)(half * 32));
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(in_tmem);
+    }
+    for (int j = 0; j < n_kv && ok; ++j) {
+      unsigned long long* tj = (tr && threadIdx.x == 0 && (j == 1 || j == 2)) ? tr + 1 + 8 * (j - 1) : nullptr;
+      const bool got = mbar_wait(s_full, j & 1, status, kErrBwdCompute);
+      if (!named_barrier_and(pair_bar, 64, got)) { ok = false; break; }
+      if (tj) tj[0] = globaltimer();
+      tc_fence_after();
+      uint32_t s[64], dp[64];
+      tmem_ld64(tmem + lane_base + (uint32_t)col0, s);
+      tmem_ld64(tmem + lane_base + 128u + (uint32_t)col0, dp);
+      tmem_ld_wait();
+      if (tj) tj[1] = globaltimer();
+      // both halves hold their S columns before either writes dS over them
+      tc_fence_before();
+      named_barrier(pair_bar, 64);
+      tc_fence_after();
+      const bool diag = causal && j == qt;
+      uint32_t pk[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int c = 2 * i;
+        float p0 = fast_exp2(fmaf(__uint_as_float(s[c]), scale_log2, -l2));
+        float p1 = fast_exp2(fmaf(__uint_as_float(s[c + 1]), scale_log2, -l2));
+        if (diag && col0 + c > row) p0 = 0.0f;
+        if (diag && col0 + c + 1 > row) p1 = 0.0f;
+        pk[i] = pack_bf16x2(p0 * (__uint_as_float(dp[c]) - dl), p1 * (__uint_as_float(dp[c + 1]) - dl));
+      }
+      if (tj) tj[2] = globaltimer();
+      tmem_st_32x32b_x32(tmem + lane_base + (uint32_t)(half * 32), pk);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ds_full);
+      if (tj) tj[3] = globaltimer();
+    }
+    if (named_barrier_and(pair_bar, 64, ok)) {
+      const bool done = mbar_wait(dq_done, 0, status, kErrBwdCompute);
+      if (named_barrier_and(pair_bar, 64, done)) {
+        tc_fence_after();
+        __nv_bfloat16* orow = dq + (((int64_t)b * S + q) * Hq + h) * kAttD + col0;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(tmem + lane_base + 256u + (uint32_t)(col0 + c * 32), o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(o[8 * i + 0]) * scale, __uint_as_float(o[8 * i + 1]) * scale);
+            v.y = pack_bf16x2(__uint_as_float(o[8 * i + 2]) * scale, __uint_as_float(o[8 * i + 3]) * scale);
+            v.z = pack_bf16x2(__uint_as_float(o[8 * i + 4]) * scale, __uint_as_float(o[8 * i + 5]) * scale);
+            v.w = pack_bf16x2(__uint_as_float(o[8 * i + 6]) * scale, __uint_as_float(o[8 * i + 7]) * scale);
+            *reinterpret_cast<uint4*>(orow + c * 32 + i * 8) = v;
+          }
+        }
+        if (tr && threadIdx.x == 0) tr[30] = globaltimer();
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) { tc_fence_after(); tmem_dealloc(tmem, 512); }
+}
+
+struct BwdDkvSmem {
+  static constexpr int kTile = AttSmem::kTile, kAtom = AttSmem::kAtom;
+  static constexpr int kK = 0, kV = kTile;
+  static constexpr int kQ = 2 * kTile;                        // kBwdQStages stages
+  static constexpr int kDO = kQ + kBwdQStages * kTile;        // kBwdQStages stages
+  static constexpr int kLD = kDO + kBwdQStages * kTile;        // per stage: lse2[128], delta[128]
+  static constexpr int kBar = kLD + kBwdQStages * 1024;
+  static constexpr int kBytes = kBar + 256 + 1024;
+};
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+attn_bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                       const float* __restrict__ lse2, const float* __restrict__ delta,
+                       __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv, int B, int S,
+                       int Hq, int Hk, float scale_log2, float scale, int causal,
+                       DeviceStatus* status, unsigned long long* __restrict__ trace) {
+  // trace (optional, [grid][32] ns): 0 start; iterations t = 1, 2 at 1 + 8(t-1) + i:
+  //   compute: i = 0 Sᵀ/dPᵀ seen, 1 loaded, 2 Pᵀ/dSᵀ computed, 3 arrived;
+  //   MMA: 4 Q/dO seen, 5 Sᵀ/dPᵀ issued, 6 Pᵀ/dSᵀ seen, 7 dV/dK issued;  30 end
+  unsigned long long* tr = trace ? trace + (size_t)blockIdx.x * 32 : nullptr;
+  if (tr && threadIdx.x == 0) tr[0] = globaltimer();
+  using L = BwdDkvSmem;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* kv_full = bars;                // K_j and V_j landed
+  uint64_t* q_full = bars + 1;             // [kBwdQStages]
+  uint64_t* q_empty = bars + 3;            // [kBwdQStages]
+  uint64_t* o_full = bars + 5;             // [kBwdQStages] dO
+  uint64_t* o_empty = bars + 7;            // [kBwdQStages]
+  uint64_t* s_full = bars + 9;             // Sᵀ and dPᵀ of the current query tile
+  uint64_t* p_full = bars + 10;            // Pᵀ, dSᵀ written (one arrival per compute warp)
+  uint64_t* acc_done = bars + 11;
+  uint64_t* drain = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkt = S / kAttKeys, nqt = S / kAttRows;
+  const int bhk = (int)(blockIdx.x / (unsigned)nkt);
+  const int kt = (int)(blockIdx.x % (unsigned)nkt);        // key tile 0 (most work) first
+  const int b = bhk / Hk, hk = bhk % Hk;
+  const int group = Hq / Hk;
+  const int i0 = causal ? kt : 0;                           // first query tile that sees this key tile
+  const int per_head = nqt - i0;
+  const int n_it = group * per_head;                        // (query head, query tile) iterations
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < kBwdQStages; ++i) {
+      mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], 1);
+      mbar_init(&o_full[i], 1); mbar_init(&o_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, kSoftmaxWarps);
+    mbar_init(acc_done, 1);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+    prefetch_tmap(&tmQ); prefetch_tmap(&tmK); prefetch_tmap(&tmV); prefetch_tmap(&tmDO);
+  }
+  if (warp == 8) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp >= 9) {
+    // ------------------------------------------------------------ TMA loaders
+    if (lane == 0) {
+      const bool is_q = warp == 9;
+      if (is_q) {
+        mbar_arrive_expect_tx(kv_full, 2 * L::kTile);
+        tma_load_4d(smem + L::kK, &tmK, kv_full, 0, hk, kt * kAttKeys, b);
+        tma_load_4d(smem + L::kK + L::kAtom, &tmK, kv_full, 64, hk, kt * kAttKeys, b);
+        tma_load_4d(smem + L::kV, &tmV, kv_full, 0, hk, kt * kAttKeys, b);
+        tma_load_4d(smem + L::kV + L::kAtom, &tmV, kv_full, 64, hk, kt * kAttKeys, b);
+      }
+      const CUtensorMap* map = is_q ? &tmQ : &tmDO;
+      uint64_t* empty = is_q ? q_empty : o_empty;
+      uint64_t* full = is_q ? q_full : o_full;
+      uint8_t* ring = smem + (is_q ? L::kQ : L::kDO);
+      int issued = 0;
+      bool ok = true;
+      for (int t = 0; t < n_it; ++t) {
+        const int st = t % kBwdQStages;
+        const int h = hk * group + t / per_head, it = i0 + t % per_head;
+        if (!mbar_wait(&empty[st], ((t / kBwdQStages) & 1) ^ 1, status, kErrBwdLoad)) { ok = false; break; }
+        uint8_t* dst = ring + st * L::kTile;
+        mbar_arrive_expect_tx(&full[st], L::kTile + (is_q ? 0 : 1024));
+        tma_load_4d(dst, map, &full[st], 0, h, it * kAttRows, b);
+        tma_load_4d(dst + L::kAtom, map, &full[st], 64, h, it * kAttRows, b);
+        if (!is_q) {  // this query tile's lse2 and delta rows (512 B each)
+          const int64_t li = ((int64_t)b * Hq + h) * S + it * kAttRows;
+          bulk_load(smem + L::kLD + st * 1024, lse2 + li, 512, &full[st]);
+          bulk_load(smem + L::kLD + st * 1024 + 512, delta + li, 512, &full[st]);
+        }
+        issued = t + 1;
+      }
+      if (!ok) {  // let every copy this thread issued land before the CTA can exit
+        if (is_q) mbar_wait(kv_full, 0, nullptr, 0);
+        for (int t = (issued > kBwdQStages ? issued - kBwdQStages : 0); t < issued; ++t)
+          mbar_wait(&full[t % kBwdQStages], (t / kBwdQStages) & 1, nullptr, 0);
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_k = umma_idesc_bf16(kAttKeys, kAttRows);   // Sᵀ, dPᵀ
+      constexpr uint32_t idesc_mn = umma_idesc_bf16_bmn(kAttKeys, kAttD); // dV, dK
+      bool ok = mbar_wait(kv_full, 0, status, kErrBwdMma);
+      const uint32_t k_addr = smem_u32(smem + L::kK), v_addr = smem_u32(smem + L::kV);
+      for (int t = 0; t < n_it && ok; ++t) {
+        unsigned long long* tj = (tr && (t == 1 || t == 2)) ? tr + 1 + 8 * (t - 1) : nullptr;
+        const int st = t % kBwdQStages;
+        const uint32_t ph = (t / kBwdQStages) & 1;
+        if (!mbar_wait(&q_full[st], ph, status, kErrBwdMma)) { ok = false; break; }
+        if (!mbar_wait(&o_full[st], ph, status, kErrBwdMma)) { ok = false; break; }
+        if (tj) tj[4] = globaltimer();
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(smem + L::kQ + st * L::kTile);
+        const uint32_t o_addr = smem_u32(smem + L::kDO + st * L::kTile);
+#pragma unroll
+        for (int kk = 0; kk < kAttD / 16; ++kk) {   // Sᵀ = K Qᵀ and dPᵀ = V dOᵀ, interleaved
+          const uint32_t off = (uint32_t)((kk >> 2) * L::kAtom + (kk & 3) * 32);
+          umma_f16_ss(tmem + 256u, umma_desc_sw128_kmajor(k_addr + off),
+                      umma_desc_sw128_kmajor(q_addr + off), idesc_k, kk > 0 ? 1u : 0u);
+          umma_f16_ss(tmem + 384u, umma_desc_sw128_kmajor(v_addr + off),
+                      umma_desc_sw128_kmajor(o_addr + off), idesc_k, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full);
+        if (tj) tj[5] = globaltimer();
+        if (!mbar_wait(p_full, t & 1, status, kErrBwdMma)) { ok = false; break; }
+        if (tj) tj[6] = globaltimer();
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < kAttRows / 16; ++kk) {   // dV += Pᵀ dO and dK += dSᵀ Q, interleaved
+          umma_f16_ts(tmem, tmem + 256u + (uint32_t)(kk * 8),
+                      umma_desc_sw128_mnmajor(o_addr + (uint32_t)kk * 2048u, (uint32_t)L::kAtom),
+                      idesc_mn, (t > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(tmem + 128u, tmem + 384u + (uint32_t)(kk * 8),
+                      umma_desc_sw128_mnmajor(q_addr + (uint32_t)kk * 2048u, (uint32_t)L::kAtom),
+                      idesc_mn, (t > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&q_empty[st]);
+        umma_commit(&o_empty[st]);
+        if (tj) tj[7] = globaltimer();
+      }
+      umma_commit(acc_done);
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ Pᵀ, dSᵀ + epilogue
+    const int quad = warp & 3, half = warp >> 2;
+    const int row = quad * 32 + lane;                     // key row = TMEM lane
+    const int col0 = half * 64;                           // this half's query (and D) columns
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    const int pair_bar = 1 + quad;
+    const int key = kt * kAttKeys + row;
+    bool ok = true;
+    for (int t = 0; t < n_it && ok; ++t) {
+      const int h = hk * group + t / per_head, it = i0 + t % per_head;
+      // lse2 / delta of this query tile, staged with dO (s_full implies they landed)
+      const float* sl = reinterpret_cast<const float*>(smem + L::kLD + (t % kBwdQStages) * 1024) + col0;
+      unsigned long long* tj = (tr && threadIdx.x == 0 && (t == 1 || t == 2)) ? tr + 1 + 8 * (t - 1) : nullptr;
+      // the staged lse2/delta completed o_full; wait on it too so the bulk copy's
+      // data is visible to these threads (it has completed by now)
+      const bool got = mbar_wait(s_full, t & 1, status, kErrBwdCompute) &&
+                       mbar_wait(&o_full[t % kBwdQStages], (t / kBwdQStages) & 1, status, kErrBwdCompute);
+      if (!named_barrier_and(pair_bar, 64, got)) { ok = false; break; }
+      if (tj) tj[0] = globaltimer();
+      tc_fence_after();
+      uint32_t s[64], dp[64];
+      tmem_ld64(tmem + lane_base + 256u + (uint32_t)col0, s);
+      tmem_ld64(tmem + lane_base + 384u + (uint32_t)col0, dp);
+      tmem_ld_wait();
+      if (tj) tj[1] = globaltimer();
+      tc_fence_before();
+      named_barrier(pair_bar, 64);   // both halves hold their columns before either overwrites
+      tc_fence_after();
+      const bool diag = causal && it == kt;
+      uint32_t pp[32], dsp[32];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {   // 4 queries per step: shared-memory broadcasts
+        const float4 l4 = reinterpret_cast<const float4*>(sl)[i];
+        const float4 d4 = reinterpret_cast<const float4*>(sl + 128)[i];
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+        float p[4], ds[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = 4 * i + u;
+          p[u] = fast_exp2(fmaf(__uint_as_float(s[c]), scale_log2, -lv[u]));
+          if (diag && key > it * kAttRows + col0 + c) p[u] = 0.0f;
+          ds[u] = p[u] * (__uint_as_float(dp[c]) - dv4[u]);
+        }
+        pp[2 * i] = pack_bf16x2(p[0], p[1]);
+        pp[2 * i + 1] = pack_bf16x2(p[2], p[3]);
+        dsp[2 * i] = pack_bf16x2(ds[0], ds[1]);
+        dsp[2 * i + 1] = pack_bf16x2(ds[2], ds[3]);
+      }
+      if (tj) tj[2] = globaltimer();
+      tmem_st_32x32b_x32(tmem + lane_base + 256u + (uint32_t)(half * 32), pp);
+      tmem_st_32x32b_x32(tmem + lane_base + 384u + (uint32_t)(half * 32), dsp);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      if (tj) tj[3] = globaltimer();
+    }
+    if (named_barrier_and(pair_bar, 64, ok)) {
+      const bool done = mbar_wait(acc_done, 0, status, kErrBwdCompute);
+      if (named_barrier_and(pair_bar, 64, done)) {
+        tc_fence_after();
+        const int64_t off = (((int64_t)b * S + key) * Hk + hk) * kAttD + col0;
+#pragma unroll 1
+        for (int w = 0; w < 2; ++w) {   // w = 0: dV (scale 1), w = 1: dK (scale)
+          __nv_bfloat16* out = (w == 0 ? dv : dk) + off;
+          const float f = w == 0 ? 1.0f : scale;
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(tmem + lane_base + (uint32_t)(w * 128 + col0 + c * 32), o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint4 v;
+              v.x = pack_bf16x2(__uint_as_float(o[8 * i + 0]) * f, __uint_as_float(o[8 * i + 1]) * f);
+              v.y = pack_bf16x2(__uint_as_float(o[8 * i + 2]) * f, __uint_as_float(o[8 * i + 3]) * f);
+              v.z = pack_bf16x2(__uint_as_float(o[8 * i + 4]) * f, __uint_as_float(o[8 * i + 5]) * f);
+              v.w = pack_bf16x2(__uint_as_float(o[8 * i + 6]) * f, __uint_as_float(o[8 * i + 7]) * f);
+              *reinterpret_cast<uint4*>(out + c * 32 + i * 8) = v;
+            }
+          }
+        }
+        if (tr && threadIdx.x == 0) tr[30] = globaltimer();
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) { tc_fence_after(); tmem_dealloc(tmem, 512); }
+}
+
 }  // namespace zq
 
 using namespace zq;
@@ -481,5 +1028,69 @@ void attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Ten
       tq, tk, tv, reinterpret_cast<__nv_bfloat16*>(o.data_ptr<at::BFloat16>()), lse.data_ptr<float>(),
       (int)B, (int)S, (int)Hq, (int)Hk, (float)(scale * 1.4426950408889634), causal ? 1 : 0,
       status_buffer(dev), trp);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Backward of attn_fwd_tc: dq, dk, dv [B, S, H, D] bf16 from dout, q, k, v, o and
+// the forward's lse.  Three launches: delta, dQ (per query tile), dK/dV (per key tile).
+// trace (optional): int64 [dQ grid + dK/dV grid, 32] per-CTA timestamps.
+void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o,
+                 at::Tensor lse, at::Tensor dq, at::Tensor dk, at::Tensor dv, bool causal,
+                 double scale, c10::optional<at::Tensor> trace) {
+  for (const at::Tensor* t : {&dout, &q, &k, &v, &o, &dq, &dk, &dv}) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->dim() == 4,
+                "attention backward: contiguous bf16 [B, S, H, D] CUDA tensors");
+  }
+  const int64_t B = q.size(0), S = q.size(1), Hq = q.size(2), D = q.size(3), Hk = k.size(2);
+  TORCH_CHECK(D == kAttD, "attention backward (tcgen05): head dim 128");
+  TORCH_CHECK(S % kAttRows == 0 && S > 0, "attention backward: S must be a multiple of 128");
+  TORCH_CHECK(Hk > 0 && Hq % Hk == 0, "attention backward: Hq must be a multiple of Hk");
+  TORCH_CHECK(k.sizes() == v.sizes() && k.size(0) == B && k.size(1) == S && k.size(3) == D &&
+                  dk.sizes() == k.sizes() && dv.sizes() == v.sizes() && dq.sizes() == q.sizes() &&
+                  o.sizes() == q.sizes() && dout.sizes() == q.sizes(),
+              "attention backward: shapes");
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && lse.is_contiguous() && lse.numel() == B * Hq * S,
+              "attention backward: lse [B, Hq, S] fp32");
+  const at::cuda::CUDAGuard guard(q.device());
+  const int dev = q.get_device();
+  auto stream = at::cuda::getCurrentCUDAStream();
+  static bool configured[64] = {false};
+  if (!configured[dev]) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        BwdDqSmem::kBytes));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dkv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        BwdDkvSmem::kBytes));
+    configured[dev] = true;
+  }
+  auto delta = at::empty({B, Hq, S}, q.options().dtype(at::kFloat));
+  auto lse2 = at::empty({B, Hq, S}, q.options().dtype(at::kFloat));
+  const int64_t rows = B * S * Hq;
+  attn_delta_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr<at::BFloat16>()),
+      reinterpret_cast<const __nv_bfloat16*>(o.data_ptr<at::BFloat16>()), lse.data_ptr<float>(),
+      delta.data_ptr<float>(), lse2.data_ptr<float>(), rows, (int)S, (int)Hq);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const CUtensorMap tq = make_tmap_bshd(q), tk = make_tmap_bshd(k), tv = make_tmap_bshd(v),
+                    tdo = make_tmap_bshd(dout);
+  const float sl2 = (float)(scale * 1.4426950408889634);
+  DeviceStatus* st = status_buffer(dev);
+  const int64_t g_dq = B * Hq * (S / kAttRows), g_dkv = B * Hk * (S / kAttKeys);
+  unsigned long long* trp = nullptr;
+  if (trace.has_value() && trace->defined()) {
+    TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->is_contiguous() &&
+                    trace->numel() >= (g_dq + g_dkv) * 32,
+                "attention backward trace: int64 [dQ grid + dK/dV grid, 32]");
+    trp = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+  }
+  attn_bwd_dq_tc_kernel<<<(unsigned)g_dq, kBwdThreads, BwdDqSmem::kBytes, stream>>>(
+      tq, tk, tv, tdo, lse.data_ptr<float>(), delta.data_ptr<float>(),
+      reinterpret_cast<__nv_bfloat16*>(dq.data_ptr<at::BFloat16>()), (int)B, (int)S, (int)Hq, (int)Hk, sl2,
+      (float)scale, causal ? 1 : 0, st, trp);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  attn_bwd_dkv_tc_kernel<<<(unsigned)g_dkv, kBwdThreads, BwdDkvSmem::kBytes, stream>>>(
+      tq, tk, tv, tdo, lse2.data_ptr<float>(), delta.data_ptr<float>(),
+      reinterpret_cast<__nv_bfloat16*>(dk.data_ptr<at::BFloat16>()),
+      reinterpret_cast<__nv_bfloat16*>(dv.data_ptr<at::BFloat16>()), (int)B, (int)S, (int)Hq, (int)Hk, sl2,
+      (float)scale, causal ? 1 : 0, st, trp ? trp + g_dq * 32 : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -11,6 +11,9 @@ void nf4_dequantize(at::Tensor packed, at::Tensor absmax, at::Tensor out, int64_
 void gemm_bf16_tn(at::Tensor a, at::Tensor b, at::Tensor c);
 void attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, bool causal,
                  double scale, c10::optional<at::Tensor> trace, bool kv_bhsd);
+void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o,
+                 at::Tensor lse, at::Tensor dq, at::Tensor dk, at::Tensor dv, bool causal,
+                 double scale, c10::optional<at::Tensor> trace);
 void gemm_nf4(at::Tensor a, at::Tensor packed, at::Tensor absmax, int64_t rows, int64_t cols,
               int64_t blocksize, int64_t quant_type, bool w_is_kn, at::Tensor c,
               c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2);
@@ -79,6 +82,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16_tn_extra", &gemm_bf16_tn_extra);
   m.def("gemm_bf16_nn", &gemm_bf16_nn);
   m.def("gemm_nf4", &gemm_nf4);
+  m.def("attn_bwd_tc", &attn_bwd_tc, "tcgen05 attention backward", pybind11::arg("dout"),
+        pybind11::arg("q"), pybind11::arg("k"), pybind11::arg("v"), pybind11::arg("o"),
+        pybind11::arg("lse"), pybind11::arg("dq"), pybind11::arg("dk"), pybind11::arg("dv"),
+        pybind11::arg("causal"), pybind11::arg("scale"), pybind11::arg("trace") = pybind11::none());
   m.def("attn_fwd_tc", &attn_fwd_tc, "tcgen05 attention forward", pybind11::arg("q"),
         pybind11::arg("k"), pybind11::arg("v"), pybind11::arg("o"), pybind11::arg("lse"),
         pybind11::arg("causal"), pybind11::arg("scale"), pybind11::arg("trace") = pybind11::none(),

@@ -8,7 +8,10 @@ the ``mma.sync`` kernel in ``csrc/attention.cu``.  Both write ``O`` plus the row
 log-sum-exp ``L``.  The backward (``csrc/attention.cu``) recomputes
 probabilities from ``L``, accumulates ``dK``/``dV`` per key tile in registers and
 ``dQ`` in fp32 with atomics, after a small kernel that forms
-``delta = rowsum(dO * O)``.
+``delta = rowsum(dO * O)``; for ``D = 128`` it runs on the tensor cores as well
+(``csrc/attention_sm100.cu``): a dQ kernel per query tile and a dK/dV kernel
+per key tile, both recomputing P from ``L`` with S, dP, P and dS held in
+tensor memory, no atomics.
 
 CPU tensors use PyTorch's SDPA (the oracle).
 """
@@ -61,7 +64,10 @@ class _FlashAttn(torch.autograd.Function):
         dq = torch.empty_like(q)
         dk = torch.empty_like(k)
         dv = torch.empty_like(v)
-        _ext.ext().attn_bwd(do, q, k, v, o, lse, dq, dk, dv, bool(ctx.causal), float(ctx.scale))
+        if q.shape[-1] == 128:
+            _ext.ext().attn_bwd_tc(do, q, k, v, o, lse, dq, dk, dv, bool(ctx.causal), float(ctx.scale))
+        else:
+            _ext.ext().attn_bwd(do, q, k, v, o, lse, dq, dk, dv, bool(ctx.causal), float(ctx.scale))
         return dq, dk, dv, None, None
 
 
