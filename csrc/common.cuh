@@ -128,7 +128,7 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
-// 4-D tiled TMA load into this CTA's shared memory (no multicast)
+// 4-D tiled TMA load into this CTA's own shared memory only
 __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
                                             int32_t c0, int32_t c1, int32_t c2, int32_t c3) {
   asm volatile(
@@ -138,7 +138,13 @@ __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
-// Untiled bulk copy global -> this CTA's shared memory (no multicast); both
+// global fp32 += (x, y, z, w) at a 16-byte-aligned address, no return value
+__device__ __forceinline__ void red_add_v4_f32(float* p, float x, float y, float z, float w) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(x), "f"(y), "f"(z), "f"(w)
+               : "memory");
+}
+
+// Untiled bulk copy global -> this CTA's own shared memory only; both
 // addresses 16-byte aligned, bytes a multiple of 16; completes on `bar` (tx bytes).
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
   asm volatile(

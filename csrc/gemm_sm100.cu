@@ -26,6 +26,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
 
+#include <map>
 #include <mutex>
 
 #include "common.cuh"
@@ -52,7 +53,49 @@ struct GemmArgs {
   const uint8_t* q_packed;
   const float* q_absmax;
   int q_rows, q_cols, q_block, q_type;  // q_type: 0 = nf4, 1 = fp4
+  // stream-K tail (pair kernel): tiles [sk_first, sk_first + sk_tiles) are split
+  // along K into sk_splits parts on different clusters (sk_splits <= 1: off).
+  // Each part adds its fp32 result into the tile's block of sk_ws (zero between
+  // GEMMs); the last part to arrive at the tile's counter in sk_cnt reads the
+  // sum, stores the tile, zeroes the block and resets the counter.
+  int sk_first, sk_tiles, sk_splits;
+  float* sk_ws;
+  int* sk_cnt;
 };
+
+// Work item w of a pair cluster: data-parallel tiles first (whole K), then at
+// most one stream-K part of a tail tile.
+struct PairWork {
+  int tile, k0, k1;   // K range in pipeline stages
+  bool extra;         // this part also runs the extra 64-wide slab
+  int sk, split;      // stream-K tile index and part (sk < 0: whole tile)
+};
+
+__device__ __forceinline__ bool pair_work(const GemmArgs& a, int cluster_id, int num_clusters, int w,
+                                          int main_k, PairWork& out) {
+  const int dp = a.sk_splits > 1 ? a.sk_first : a.tiles_m * a.tiles_n;
+  const int n_dp = dp > cluster_id ? (dp - cluster_id + num_clusters - 1) / num_clusters : 0;
+  if (w < n_dp) {
+    out.tile = cluster_id + w * num_clusters;
+    out.k0 = 0;
+    out.k1 = main_k;
+    out.extra = true;
+    out.sk = -1;
+    out.split = 0;
+    return true;
+  }
+  if (a.sk_splits > 1 && w == n_dp && cluster_id < a.sk_tiles * a.sk_splits) {
+    const int sk = cluster_id / a.sk_splits, sp = cluster_id % a.sk_splits;
+    out.tile = a.sk_first + sk;
+    out.k0 = sp * main_k / a.sk_splits;
+    out.k1 = (sp + 1) * main_k / a.sk_splits;
+    out.extra = sp == a.sk_splits - 1;
+    out.sk = sk;
+    out.split = sp;
+    return true;
+  }
+  return false;
+}
 
 __constant__ float c_code_nf4[16] = {
     -1.0f, -0.6961928009986877f, -0.5250730514526367f, -0.39491748809814453f,
@@ -354,12 +397,14 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       bool ok = true;
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
+      PairWork pw;
+      for (int w = 0; ok && pair_work(args, cluster_id, num_clusters, w, main_k_tiles, pw); ++w) {
         int tm, tn;
-        tile_coords(tile, args.tiles_m, args.tiles_n, tm, tn);
+        tile_coords(pw.tile, args.tiles_m, args.tiles_n, tm, tn);
         const int arow = tm * (2 * kBM) + (int)cr * kBM;
         const int brow = tn * BN + (int)cr * (BN / 2);
-        for (int kt = 0; kt < k_tiles; ++kt) {
+        const int kt_end = pw.k1 + ((pw.extra && args.extra_k16 > 0) ? 1 : 0);
+        for (int kt = pw.k0; kt < kt_end; ++kt) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, args.status, kErrProducer)) { ok = false; break; }
           uint8_t* sa = smem + stage * L::kStageBytes;
           uint8_t* sb = sa + L::kABytes;
@@ -407,12 +452,14 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       uint32_t phase = 0;
       int it = 0;
       constexpr uint32_t idesc = BMN ? umma_idesc_bf16_bmn(2 * kBM, BN) : umma_idesc_bf16(2 * kBM, BN);
-      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters, ++it) {
+      PairWork pw;
+      for (int w = 0; ok && pair_work(args, cluster_id, num_clusters, w, main_k_tiles, pw); ++w, ++it) {
         const int buf = it & 1;
         if (!mbar_wait(&tempty_bar[buf], ((it >> 1) & 1) ^ 1, args.status, kErrMmaAcc)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(buf * 256);
-        for (int kt = 0; kt < k_tiles; ++kt) {
+        const int kt_end = pw.k1 + ((pw.extra && args.extra_k16 > 0) ? 1 : 0);
+        for (int kt = pw.k0; kt < kt_end; ++kt) {
           if (!mbar_wait(&full_bar[stage], phase, args.status, kErrMma)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
@@ -429,7 +476,7 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
               bdesc = umma_desc_sw128_kmajor(b_addr + bo);
             }
             umma_f16_ss_pair(d_tmem, umma_desc_sw128_kmajor(a_addr + ao), bdesc, idesc,
-                             (kt > 0 || kk > 0) ? 1u : 0u);
+                             (kt > pw.k0 || kk > 0) ? 1u : 0u);
           }
           const uint32_t e = smem_u32(&empty_bar[stage]);
           umma_commit_pair(map_to_cta(e, 0));
@@ -526,39 +573,101 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     uint8_t* epi = smem + L::kEpiOffset;
     int it = 0, chunk_no = 0;
     bool ok = true;
-    for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters, ++it) {
+    __shared__ int sk_last;   // stream-K: this CTA arrived last at its tile's counter
+    // bf16 chunk of 32 columns -> 64-byte-swizzled staging tile -> TMA store
+    auto store_chunk = [&](const float (&v)[32], int n_col, int m0) {
+      uint8_t* st = epi + (chunk_no & 1) * L::kEpiBytes;
+      // the store that last used this staging buffer (two chunks ago) must have read it
+      if (leader_thread) bulk_wait_group_read<1>();
+      named_barrier(1, 128);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint4 o;
+        o.x = pack_bf16x2(v[j * 8 + 0], v[j * 8 + 1]);
+        o.y = pack_bf16x2(v[j * 8 + 2], v[j * 8 + 3]);
+        o.z = pack_bf16x2(v[j * 8 + 4], v[j * 8 + 5]);
+        o.w = pack_bf16x2(v[j * 8 + 6], v[j * 8 + 7]);
+        const int pj = j ^ ((row >> 1) & 3);   // 64-byte swizzle
+        *reinterpret_cast<uint4*>(st + row * 64 + pj * 16) = o;
+      }
+      fence_proxy_async_smem();
+      named_barrier(1, 128);
+      if (leader_thread) {
+        tma_store_2d(&tmC, st, n_col, m0);
+        bulk_commit_group();
+      }
+      ++chunk_no;
+    };
+    PairWork pw;
+    for (int w = 0; ok && pair_work(args, cluster_id, num_clusters, w, main_k_tiles, pw); ++w, ++it) {
       int tm, tn;
-      tile_coords(tile, args.tiles_m, args.tiles_n, tm, tn);
+      tile_coords(pw.tile, args.tiles_m, args.tiles_n, tm, tn);
       const int buf = it & 1;
       const bool got = mbar_wait(&tfull_bar[buf], (it >> 1) & 1, args.status, kErrEpi);
       if (!named_barrier_and(1, 128, got)) { ok = false; break; }  // same decision in all 128
       tc_fence_after();
       const int m0 = tm * (2 * kBM) + (int)cr * kBM;
       const int n0 = tn * BN;
+      const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256);
+      if (pw.sk < 0) {
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c, ++chunk_no) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256 + c * 32), r);
-        tmem_ld_wait();
-        uint8_t* st = epi + (chunk_no & 1) * L::kEpiBytes;
-        // the store that last used this staging buffer (two chunks ago) must have read it
-        if (leader_thread) bulk_wait_group_read<1>();
-        named_barrier(1, 128);
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(trow + (uint32_t)(c * 32), r);
+          tmem_ld_wait();
+          float v[32];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4 o;
-          o.x = pack_bf16x2(__uint_as_float(r[j * 8 + 0]), __uint_as_float(r[j * 8 + 1]));
-          o.y = pack_bf16x2(__uint_as_float(r[j * 8 + 2]), __uint_as_float(r[j * 8 + 3]));
-          o.z = pack_bf16x2(__uint_as_float(r[j * 8 + 4]), __uint_as_float(r[j * 8 + 5]));
-          o.w = pack_bf16x2(__uint_as_float(r[j * 8 + 6]), __uint_as_float(r[j * 8 + 7]));
-          const int pj = j ^ ((row >> 1) & 3);   // 64-byte swizzle
-          *reinterpret_cast<uint4*>(st + row * 64 + pj * 16) = o;
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          store_chunk(v, n0 + c * 32, m0);
         }
-        fence_proxy_async_smem();
+      } else {
+        // stream-K part: add this part's fp32 block into the tile's accumulation
+        // buffer (vector reductions, no return), then arrive at the tile's counter
+        const int S = args.sk_splits;
+        float* acc = args.sk_ws + ((size_t)pw.sk * 2 + cr) * ((size_t)128 * BN) + (size_t)row * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(trow + (uint32_t)(c * 32), r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            red_add_v4_f32(acc + c * 32 + 4 * i, __uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                           __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+        }
+        __threadfence();                 // this part's additions done before the arrival below
         named_barrier(1, 128);
         if (leader_thread) {
-          tma_store_2d(&tmC, st, n0 + c * 32, m0);
-          bulk_commit_group();
+          int* cnt = args.sk_cnt + pw.sk * 2 + cr;
+          const int old = atomicAdd(cnt, 1);
+          sk_last = old == S - 1;
+          if (old == S - 1) *cnt = 0;    // every part has arrived: reset for the next GEMM
+        }
+        named_barrier(1, 128);
+        if (sk_last) {
+          __threadfence();               // acquire the other parts' additions
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; c += 2) {   // two chunks per round trip
+            float4 x[16];
+            const float4* src = reinterpret_cast<const float4*>(acc + c * 32);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) x[i] = __ldcg(src + i);
+            float4* z = reinterpret_cast<float4*>(acc + c * 32);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);  // clean for the next GEMM
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+              float v[32];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                v[4 * i] = x[8 * h2 + i].x;
+                v[4 * i + 1] = x[8 * h2 + i].y;
+                v[4 * i + 2] = x[8 * h2 + i].z;
+                v[4 * i + 3] = x[8 * h2 + i].w;
+              }
+              store_chunk(v, n0 + (c + h2) * 32, m0);
+            }
+          }
         }
       }
       tc_fence_before();
@@ -711,6 +820,28 @@ static CUtensorMap make_tmap_store_bf16(const void* base, int64_t rows, int64_t 
                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (store) failed with code ", (int)r);
   return map;
+}
+
+// Stream-K state, one zeroed set per (device, stream): arrival counters and the
+// fp32 accumulation blocks (kSkMaxTiles tiles x 2 CTAs x 128 x 256).  GEMMs on
+// one stream run in order, so no two running GEMMs share them; the last part of
+// a tile resets its counter and zeroes its blocks.
+constexpr int kSkMaxTiles = 64;
+static int* sk_counters(int device, cudaStream_t stream, float** acc) {
+  struct State { int* cnt; float* acc; };
+  static std::map<std::pair<int, cudaStream_t>, State> bufs;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> g(mu);
+  State& st = bufs[{device, stream}];
+  if (st.cnt == nullptr) {
+    const size_t acc_bytes = (size_t)kSkMaxTiles * 2 * 128 * 256 * sizeof(float);
+    C10_CUDA_CHECK(cudaMalloc(&st.cnt, 2 * kSkMaxTiles * sizeof(int)));
+    C10_CUDA_CHECK(cudaMalloc(&st.acc, acc_bytes));
+    C10_CUDA_CHECK(cudaMemsetAsync(st.cnt, 0, 2 * kSkMaxTiles * sizeof(int), stream));
+    C10_CUDA_CHECK(cudaMemsetAsync(st.acc, 0, acc_bytes, stream));
+  }
+  *acc = st.acc;
+  return st.cnt;
 }
 
 DeviceStatus* status_buffer(int device) {
@@ -883,6 +1014,30 @@ static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
   if (pair) {
     const CUtensorMap tc = make_tmap_store_bf16(c.data_ptr(), M, N, c.stride(0));
     const bool k128 = (K % 128) == 0;
+    // stream-K tail: when the last wave of tiles would leave more than half the
+    // clusters idle, split its tiles along K over the clusters (ZEROQ_STREAMK=0: off)
+    static const bool sk_on = [] {
+      const char* e = std::getenv("ZEROQ_STREAMK");
+      return e == nullptr || std::atoi(e) != 0;
+    }();
+    {
+      const int tiles = args.tiles_m * args.tiles_n;
+      const int C = std::max(1, std::min(tiles, sms / 2));
+      const int full = tiles / C, r = tiles % C;
+      const int main_k = (int)(K / (k128 ? 128 : 64));
+      // the split costs ~25 us (fp32 reductions, fence, fix-up): measured on B200 it
+      // pays off from ~48 pipeline stages per tile (8192 x 3072 x 12288: -7%)
+      // and loses below (8192 x 3072 x 3072: +9%)
+      if (sk_on && r > 0 && full >= 1 && 2 * r <= C && r <= kSkMaxTiles && main_k >= 48) {
+        const int S = std::min(C / r, main_k / 2);
+        if (S >= 2) {
+          args.sk_first = full * C;
+          args.sk_tiles = r;
+          args.sk_splits = S;
+          args.sk_cnt = sk_counters(dev, stream, &args.sk_ws);
+        }
+      }
+    }
     if (b_mn) {
       if (bn == 256) {
         if (k128) launch_gemm_pair<256, 3, 2, true>(ta, tb, ta2, tb2, tc, args, stream, sms);

@@ -540,3 +540,38 @@ def test_attention_backward_tcgen05_vs_fp32(cuda, B, S, Hq, Hk, causal):
     for got, ref in ((dq, qr.grad), (dk, kr.grad), (dv, vr.grad)):
         err = (got.float() - ref).abs().max().item()
         assert err < 3e-2 * max(1.0, ref.abs().max().item()), err
+
+
+@pytest.mark.parametrize("M,N,K", [(8192, 3072, 6144), (2048, 3072, 12288), (4096, 1536, 8192)])
+@pytest.mark.parametrize("nn", [False, True])
+@pytest.mark.parametrize("extra", [False, True])
+def test_gemm_stream_k_tail(cuda, M, N, K, nn, extra):
+    """Shapes whose last wave of 256x256 tiles is split along K over the idle
+    clusters (partials in fp32, added by the last part): against fp32, twice in
+    a row (the arrival counters reset themselves)."""
+    torch.manual_seed(51)
+    E = _ext.ext()
+    E.set_gemm_pair_mode(1)
+    a = torch.randn(M, K, device=cuda, dtype=torch.bfloat16)
+    b = torch.randn(K, N, device=cuda, dtype=torch.bfloat16) if nn else \
+        torch.randn(N, K, device=cuda, dtype=torch.bfloat16)
+    a2 = b2 = None
+    if extra:
+        a2 = torch.randn(M, 64, device=cuda, dtype=torch.bfloat16)
+        b2 = torch.randn(64, N, device=cuda, dtype=torch.bfloat16) if nn else \
+            torch.randn(N, 64, device=cuda, dtype=torch.bfloat16)
+    ref = a.float() @ (b.float() if nn else b.float().t())
+    if extra:
+        ref = ref + a2.float() @ (b2.float() if nn else b2.float().t())
+    tol = 2e-2 * math.sqrt(K) + 1e-2 * ref.abs().max().item()
+    for _ in range(2):
+        c = torch.empty(M, N, device=cuda, dtype=torch.bfloat16)
+        if nn:
+            E.gemm_bf16_nn(a, b, c, a2, b2)
+        elif extra:
+            E.gemm_bf16_tn_extra(a, b, c, a2, b2)
+        else:
+            E.gemm_bf16_tn(a, b, c)
+        torch.cuda.synchronize()
+        _status_ok(cuda)
+        assert (c.float() - ref).abs().max().item() < tol
