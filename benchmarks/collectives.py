@@ -6,9 +6,11 @@
 
 ``ag_gemm``: a weight ``W [N, K]`` quantised to NF4 (block 64) and sharded over the
 ranks (uniform split), activations ``X [M, K]`` bf16, output ``Y = X Wᵀ``.
-  * ours: the peer gather+dequantise kernel reads every owner's NF4 bytes over
-    NVLink and writes the bf16 operand in N-chunks on one stream while the
-    tcgen05 GEMM consumes the previous chunk on another;
+  * ours: ONE kernel (gather mode of the tcgen05 pair GEMM): warps of every CTA
+    read the owners' NF4 bytes over NVLink, dequantise them into a local bf16
+    operand and publish per-N-tile counters that the TMA producer waits on, so
+    the transfer overlaps the MMAs tile by tile (each rank starts on its own rows);
+  * two_kernel: the peer gather+dequantise kernel, then the same GEMM;
   * nccl: the reference's path - NCCL all-gather of packed bytes and absmax,
     dequantise, cuBLAS GEMM.
 Roofline = max(2MNK / measured bf16 peak, K·N·0.5625·(W-1)/W / 770 GB/s).
@@ -83,33 +85,17 @@ def ag_gemm(args, rank, world):
         zp = coord._params[0]
         pool = PeerShardPool(coord)
         N = K = KN
-        s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
         for M in args.m:
-            # chunked overlap only pays when the GEMM is long enough to hide a chunk's gather
-            chunks = args.chunks if (args.chunks > 0) else (4 if M >= 8192 else 1)
-            nc = N // chunks
-            bufs = [torch.empty(nc * K, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
             x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
             y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            wb = torch.empty(N, K, device="cuda", dtype=torch.bfloat16)
 
             def ours():
-                cur = torch.cuda.current_stream()
-                start = cur.record_event()
-                s1.wait_event(start)
-                s2.wait_event(start)
-                done = [None, None]
-                for j in range(chunks):
-                    b = j & 1
-                    with torch.cuda.stream(s1):
-                        if done[b] is not None:
-                            s1.wait_event(done[b])
-                        pool.gather_dequant(zp, nc, K, False, bufs[b], row0=j * nc)
-                        ready = s1.record_event()
-                    with torch.cuda.stream(s2):
-                        s2.wait_event(ready)
-                        E.gemm_bf16_tn(x, bufs[b].view(nc, K), y[:, j * nc:(j + 1) * nc])
-                        done[b] = s2.record_event()
-                cur.wait_stream(s2)
+                pool.ag_gemm(zp, x, out=y, wbuf=wb)
+
+            def two_kernel():
+                w = pool.gather_dequant(zp, N, K, out=wb.view(-1))
+                E.gemm_bf16_tn(x, w, y)
 
             packed_full = torch.empty(zp.packed_plan.total, dtype=torch.uint8, device="cuda")
             absmax_full = torch.empty(zp.absmax_plan.total, dtype=torch.float32, device="cuda")
@@ -129,6 +115,10 @@ def ag_gemm(args, rank, world):
 
             t_ours = timed(ours, args.iters, args.warmup)
             y_ours = y.clone()
+            code, detail = E.gemm_status(torch.cuda.current_device())
+            if code:
+                raise RuntimeError(f"ag_gemm kernel reported error {code} (detail {detail})")
+            t_two = timed(two_kernel, args.iters, args.warmup)
             t_nccl = timed(nccl, args.iters, args.warmup)
             err = (y_ours.float() - y.float()).abs().max().item()
             flops = 2.0 * M * N * K
@@ -138,8 +128,8 @@ def ag_gemm(args, rank, world):
             if rank == 0:
                 print(json.dumps({
                     "op": "ag_dequant_gemm", "n_gpus": world, "M": M, "K": K, "N": N,
-                    "chunks": chunks,
-                    "ours_ms": round(t_ours, 4), "nccl_cublas_ms": round(t_nccl, 4),
+                    "ours_ms": round(t_ours, 4), "two_kernel_ms": round(t_two, 4),
+                    "nccl_cublas_ms": round(t_nccl, 4),
                     "speedup": round(t_nccl / t_ours, 3),
                     "ours_tflops": round(flops / t_ours / 1e9, 1),
                     "roofline_ms": round(roof, 4), "bound": "compute" if t_comp >= t_link else "nvlink",
@@ -228,7 +218,6 @@ def main():
     ap.add_argument("--kn", type=int, nargs="+", default=[4096, 8192, 12288])
     ap.add_argument("--m", type=int, nargs="+", default=[1024, 4096, 16384])
     ap.add_argument("--sizes-mb", type=float, nargs="+", default=[1, 16, 256, 1024])
-    ap.add_argument("--chunks", type=int, default=0, help="0 = auto (4 when M >= 8192)")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     args = ap.parse_args()

@@ -62,6 +62,13 @@ void rs_adamw(std::vector<int64_t> grads, std::vector<int64_t> params, std::vect
 void plan_gather(std::vector<int64_t> src, std::vector<int64_t> flags, int64_t rank, int64_t epoch,
                  std::vector<int64_t> offsets, std::vector<int64_t> lengths, at::Tensor out,
                  int64_t timeout_ms);
+void ag_gemm_nf4(at::Tensor a, std::vector<int64_t> psrc, std::vector<int64_t> pstarts,
+                 std::vector<int64_t> asrc, std::vector<int64_t> astarts, int64_t packed_total,
+                 int64_t absmax_total, int64_t rank, int64_t N, int64_t K, int64_t blocksize,
+                 int64_t quant_type, at::Tensor wbuf, at::Tensor c, c10::optional<at::Tensor> a2,
+                 c10::optional<at::Tensor> b2);
+void gemm_gelu(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor aux, bool b_mn,
+               c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2);
 void plan_gather_dequant(std::vector<int64_t> psrc, std::vector<int64_t> pstarts,
                          std::vector<int64_t> asrc, std::vector<int64_t> astarts, int64_t rows,
                          int64_t cols, int64_t row0, int64_t blocksize, int64_t qtype, bool transpose,
@@ -118,6 +125,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rs_adamw", &rs_adamw);
   m.def("plan_gather", &plan_gather);
   m.def("plan_gather_dequant", &plan_gather_dequant);
+  m.def("gemm_gelu", &gemm_gelu, "tcgen05 GEMM with the GELU output / GELU-gradient epilogue",
+        pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("c"), pybind11::arg("aux"),
+        pybind11::arg("b_mn"), pybind11::arg("a2") = pybind11::none(),
+        pybind11::arg("b2") = pybind11::none());
+  m.def("ag_gemm_nf4", &ag_gemm_nf4, "gather + dequantise + tcgen05 GEMM in one kernel",
+        pybind11::arg("a"), pybind11::arg("psrc"), pybind11::arg("pstarts"), pybind11::arg("asrc"),
+        pybind11::arg("astarts"), pybind11::arg("packed_total"), pybind11::arg("absmax_total"),
+        pybind11::arg("rank"), pybind11::arg("N"), pybind11::arg("K"), pybind11::arg("blocksize"),
+        pybind11::arg("quant_type"), pybind11::arg("wbuf"), pybind11::arg("c"),
+        pybind11::arg("a2") = pybind11::none(), pybind11::arg("b2") = pybind11::none());
 #ifdef ZQ_WITH_ATTENTION
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_bwd", &attn_bwd);

@@ -8,6 +8,7 @@
 #include <c10/cuda/CUDAGuard.h>
 
 #include "common.cuh"
+#include "gelu.cuh"
 
 namespace zq {
 
@@ -125,7 +126,7 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_fwd_kernel(
 // Teams walk rows with a grid stride and keep their dw share in registers; the
 // teams of a CTA combine through shared memory into one row of dw_part.
 template <int NC, int TPR>
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
+__global__ void __launch_bounds__(kNormThreads, NC <= 6 ? 2 : 1) rmsnorm_bwd_kernel(
     const __nv_bfloat16* __restrict__ gy, const __nv_bfloat16* __restrict__ x,
     const float* __restrict__ w, const float* __restrict__ rstd,
     const __nv_bfloat16* __restrict__ gh, __nv_bfloat16* __restrict__ dx,
@@ -136,11 +137,10 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
   const int team = threadIdx.x / TPR, tl = threadIdx.x % TPR;
   const int nch = D >> 3;
   for (int i = threadIdx.x; i < D; i += kNormThreads) sdw[i] = 0.0f;
-  float dwacc[NC][8];
-#pragma unroll
-  for (int c = 0; c < NC; ++c)
-#pragma unroll
-    for (int i = 0; i < 8; ++i) dwacc[c][i] = 0.0f;
+  __syncthreads();
+  // the weight gradient accumulates in shared memory (fp32 shared atomics): a
+  // register accumulator per owned column would cost NC*8 registers and halve
+  // the CTAs per SM, and this kernel is bound by how many loads are in flight
   const float4* w4 = reinterpret_cast<const float4*>(w);  // [D/4], L1-resident
   const int64_t groups = (M + R - 1) / R;
   for (int64_t gidx = blockIdx.x; gidx < groups; gidx += gridDim.x) {
@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
         for (int i = 0; i < 8; ++i) {
           const float xh = xf[i] * r;
           dot += gf[i] * ww[i] * xh;
-          dwacc[c][i] += gf[i] * xh;
+          atomicAdd(&sdw[ch * 8 + i], gf[i] * xh);
         }
       }
     }
@@ -198,15 +198,6 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
           *reinterpret_cast<uint4*>(dx + row * D + (int64_t)ch * 8) = f32_to_bf16x8(o);
         }
       }
-    }
-  }
-  __syncthreads();
-#pragma unroll
-  for (int c = 0; c < NC; ++c) {
-    const int ch = c * TPR + tl;
-    if (ch < nch) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) atomicAdd(&sdw[ch * 8 + i], dwacc[c][i]);
     }
   }
   __syncthreads();
@@ -249,33 +240,6 @@ __global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* 
 // ----------------------------------------------------------------------------
 // GELU (erf form) and SwiGLU
 // ----------------------------------------------------------------------------
-// Gaussian CDF and PDF for GELU.  erf uses the rational approximation of
-// Abramowitz & Stegun, Handbook of Mathematical Functions (1964), formula
-// 7.1.26 (Hastings): for a >= 0,
-//   erf(a) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-a^2) + e(a),
-//   t = 1 / (1 + p a),  |e(a)| <= 1.5e-7.
-// With a = |x| / sqrt(2), exp(-a^2) = exp(-x^2 / 2) is also the unnormalised
-// PDF, so one reciprocal and one exponential give both.
-struct GeluCP {
-  float cdf, pdf;
-};
-
-__device__ __forceinline__ GeluCP gelu_cdf_pdf(float x) {
-  constexpr float kP = 0.3275911f;
-  constexpr float kA1 = 0.254829592f, kA2 = -0.284496736f, kA3 = 1.421413741f,
-                  kA4 = -1.453152027f, kA5 = 1.061405429f;
-  constexpr float kInvSqrt2 = 0.70710678118654752f, kInvSqrt2Pi = 0.39894228040143268f;
-  const float a = fabsf(x) * kInvSqrt2;
-  const float t = __fdividef(1.0f, fmaf(kP, a, 1.0f));
-  const float e = __expf(-0.5f * x * x);
-  const float poly = t * fmaf(t, fmaf(t, fmaf(t, fmaf(t, kA5, kA4), kA3), kA2), kA1);
-  const float tail = 0.5f * poly * e;  // = (1 - erf(a)) / 2
-  GeluCP r;
-  r.cdf = x >= 0.0f ? 1.0f - tail : tail;
-  r.pdf = e * kInvSqrt2Pi;
-  return r;
-}
-
 // Each thread handles kEwIlp chunks of 8 elements, kEwIlp * blockDim apart, and
 // issues all loads before computing.
 constexpr int kEwIlp = 4;

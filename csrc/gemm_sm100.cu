@@ -30,6 +30,8 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "peer_gather.cuh"
+#include "gelu.cuh"
 
 namespace zq {
 
@@ -38,7 +40,7 @@ constexpr int kBK = 64;          // one 128-byte swizzle atom of bf16
 constexpr int kGroupM = 8;
 constexpr int kGemmThreads = 192;
 
-enum GemmErr { kErrProducer = 101, kErrMma = 102, kErrMmaAcc = 103, kErrEpi = 104 };
+enum GemmErr { kErrProducer = 101, kErrMma = 102, kErrMmaAcc = 103, kErrEpi = 104, kErrAgWait = 105 };
 
 struct GemmArgs {
   int M, N, K;           // main problem; K % 64 == 0
@@ -61,7 +63,45 @@ struct GemmArgs {
   int sk_first, sk_tiles, sk_splits;
   float* sk_ws;
   int* sk_cnt;
+  // gather mode (AG variants only): B = W [N, K] is assembled inside the kernel
+  // from its owners' 4-bit shards (ag) into the local bf16 buffer ag_w, which the
+  // B tensor map reads.  Gather warps claim items of 8 rows x 1024 columns in
+  // tile order from ag_sync[kAgClaim] and count finished items per N tile in
+  // ag_sync[tn]; the producer loads a tile's B once its counter is full.  N
+  // tiles are visited starting at ag_rot (this rank's own rows first).  The
+  // last CTA to leave resets every counter (ag_sync[kAgExit] counts exits).
+  AgSource ag;
+  __nv_bfloat16* ag_w;
+  int* ag_sync;
+  int ag_rot, ag_kchunks;
+  // epilogue input (kEpiGeluBwd): the pre-activation h [M, N], row pitch epi_ld
+  const __nv_bfloat16* epi_src;
+  int64_t epi_ld;
 };
+
+// Pair-kernel epilogues.  kEpiGeluFwd stores C = bf16(acc) through tmC and
+// gelu(C) through tmC2 (the up-projection writes the pre-activation for the
+// backward and the activation for the next GEMM); kEpiGeluBwd stores
+// bf16(bf16(acc) * gelu'(h)) (the input gradient of the down-projection turned
+// into the gradient of the pre-activation).  Both round the accumulator to bf16
+// first, so they equal a separate GELU kernel applied to the stored GEMM output.
+enum PairEpi { kEpiPlain = 0, kEpiGeluFwd = 1, kEpiGeluBwd = 2 };
+
+constexpr int kAgMaxTilesN = 4096;
+constexpr int kAgClaim = kAgMaxTilesN, kAgExit = kAgMaxTilesN + 1, kAgSyncWords = kAgMaxTilesN + 2;
+
+__device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// generic-proxy global writes <-> async-proxy (TMA) global reads
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
 
 // Work item w of a pair cluster: data-parallel tiles first (whole K), then at
 // most one stream-K part of a tail tile.
@@ -336,11 +376,22 @@ __device__ __forceinline__ void q4_decode_store32(const uint4& raw, float am, co
   }
 }
 
-template <int BN, int STAGES, int KB, bool BMN, bool Q4 = false>
-__global__ void __launch_bounds__(Q4 ? kGemmQ4Threads : kGemmThreads, 1)
+// Output tile (tm, tn) of work tile `tile`: grouped rasterisation, and in
+// gather mode the N tiles rotated to start at this rank's own rows.
+__device__ __forceinline__ void pair_tile_coords(const GemmArgs& a, int tile, bool ag, int& tm, int& tn) {
+  tile_coords(tile, a.tiles_m, a.tiles_n, tm, tn);
+  if (ag) {
+    tn += a.ag_rot;
+    if (tn >= a.tiles_n) tn -= a.tiles_n;
+  }
+}
+
+template <int BN, int STAGES, int KB, bool BMN, bool Q4 = false, bool AG = false, int EPI = kEpiPlain>
+__global__ void __launch_bounds__((Q4 || AG) ? kGemmQ4Threads : kGemmThreads, 1)
 gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2,
-                    const __grid_constant__ CUtensorMap tmC, GemmArgs args) {
+                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2,
+                    GemmArgs args) {
   using L = PairSmem<BN, STAGES, KB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -378,7 +429,7 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       prefetch_tmap(&tmB2);
     }
   }
-  if (Q4 && threadIdx.x < 16) {
+  if ((Q4 || AG) && threadIdx.x < 16) {
     reinterpret_cast<float*>(smem + L::kLutOffset)[threadIdx.x] =
         args.q_type == 1 ? c_code_fp4[threadIdx.x] : c_code_nf4[threadIdx.x];
   }
@@ -400,7 +451,25 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       PairWork pw;
       for (int w = 0; ok && pair_work(args, cluster_id, num_clusters, w, main_k_tiles, pw); ++w) {
         int tm, tn;
-        tile_coords(pw.tile, args.tiles_m, args.tiles_n, tm, tn);
+        pair_tile_coords(args, pw.tile, AG, tm, tn);
+        if (AG) {
+          // this N tile's rows of W must be assembled before its B is loaded
+          const int need = (BN / kAgRows) * args.ag_kchunks;
+          const int* rp = args.ag_sync + tn;
+          if (ld_acquire_gpu_s32(rp) < need) {
+            const unsigned long long t0 = globaltimer();
+            while (ld_acquire_gpu_s32(rp) < need) {
+              if (globaltimer() - t0 > kWaitTimeoutNs) {
+                record_error(args.status, kErrAgWait, tn);
+                ok = false;
+                break;
+              }
+              __nanosleep(64);
+            }
+            if (!ok) break;
+          }
+          fence_proxy_async_global();
+        }
         const int arow = tm * (2 * kBM) + (int)cr * kBM;
         const int brow = tn * BN + (int)cr * (BN / 2);
         const int kt_end = pw.k1 + ((pw.extra && args.extra_k16 > 0) ? 1 : 0);
@@ -488,6 +557,32 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         umma_commit_pair(map_to_cta(f, 1));
       }
     }
+  } else if (AG && warp >= 6) {
+    // ---------------------------------------------------------------- W gather (both CTAs)
+    // Claim items in tile order (the next claim is issued before the current
+    // item is worked on), decode each into ag_w, publish it to the producers.
+    const float* lut = reinterpret_cast<const float*>(smem + L::kLutOffset);
+    const int ipt = (BN / kAgRows) * args.ag_kchunks;
+    const int total = args.tiles_n * ipt;
+    int* claim = args.ag_sync + kAgClaim;
+    int item = 0;
+    if (lane == 0) item = atomicAdd(claim, 1);
+    item = __shfl_sync(0xffffffffu, item, 0);
+    while (item < total) {
+      int next = 0;
+      if (lane == 0) next = atomicAdd(claim, 1);
+      const int p = item / ipt, j = item - p * ipt;
+      int tn = p + args.ag_rot;
+      if (tn >= args.tiles_n) tn -= args.tiles_n;
+      const int rg = j / args.ag_kchunks, kc = j - rg * args.ag_kchunks;
+      ag_item(args.ag, lut, args.N, args.K, args.q_block, tn * BN + rg * kAgRows, kc * kAgCols,
+              args.ag_w, lane);
+      fence_proxy_async_global();
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) red_release_gpu_add(args.ag_sync + tn, 1);
+      item = __shfl_sync(0xffffffffu, next, 0);
+    }
   } else if (Q4 && warp >= 6) {
     // ---------------------------------------------------------------- B decode (both CTAs)
     // This CTA's B half per stage: 128 rows x 128 K (K-major, BMN = false) or
@@ -574,34 +669,68 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     int it = 0, chunk_no = 0;
     bool ok = true;
     __shared__ int sk_last;   // stream-K: this CTA arrived last at its tile's counter
-    // bf16 chunk of 32 columns -> 64-byte-swizzled staging tile -> TMA store
-    auto store_chunk = [&](const float (&v)[32], int n_col, int m0) {
+    // 32 packed bf16 pairs' worth of one row (16 words) -> 64-byte-swizzled
+    // staging tile -> one TMA store of the 128 x 32 chunk through `map`
+    auto stage_store = [&](const uint32_t (&o)[16], const CUtensorMap* map, int n_col, int m0) {
       uint8_t* st = epi + (chunk_no & 1) * L::kEpiBytes;
       // the store that last used this staging buffer (two chunks ago) must have read it
       if (leader_thread) bulk_wait_group_read<1>();
       named_barrier(1, 128);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        uint4 o;
-        o.x = pack_bf16x2(v[j * 8 + 0], v[j * 8 + 1]);
-        o.y = pack_bf16x2(v[j * 8 + 2], v[j * 8 + 3]);
-        o.z = pack_bf16x2(v[j * 8 + 4], v[j * 8 + 5]);
-        o.w = pack_bf16x2(v[j * 8 + 6], v[j * 8 + 7]);
         const int pj = j ^ ((row >> 1) & 3);   // 64-byte swizzle
-        *reinterpret_cast<uint4*>(st + row * 64 + pj * 16) = o;
+        *reinterpret_cast<uint4*>(st + row * 64 + pj * 16) =
+            make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
       }
       fence_proxy_async_smem();
       named_barrier(1, 128);
       if (leader_thread) {
-        tma_store_2d(&tmC, st, n_col, m0);
+        tma_store_2d(map, st, n_col, m0);
         bulk_commit_group();
       }
       ++chunk_no;
     };
+    // pre-activation values of this thread's row for columns n_col .. n_col+31
+    auto load_h = [&](int n_col, int m0, uint4 (&hv)[4]) {
+      const int64_t grow = m0 + row;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c = n_col + 8 * j;
+        hv[j] = (grow < args.M && c < args.N)
+                    ? *reinterpret_cast<const uint4*>(args.epi_src + grow * args.epi_ld + c)
+                    : make_uint4(0u, 0u, 0u, 0u);
+      }
+    };
+    // fp32 chunk of 32 columns -> epilogue -> staging -> TMA store(s)
+    auto store_chunk = [&](const float (&v)[32], int n_col, int m0, const uint4 (&hv)[4]) {
+      uint32_t o[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) o[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+      if constexpr (EPI == kEpiGeluBwd) {
+        const uint32_t hw[16] = {hv[0].x, hv[0].y, hv[0].z, hv[0].w, hv[1].x, hv[1].y, hv[1].z, hv[1].w,
+                                 hv[2].x, hv[2].y, hv[2].z, hv[2].w, hv[3].x, hv[3].y, hv[3].z, hv[3].w};
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 g = bf16x2_to_f2(o[i]);
+          const float2 x = bf16x2_to_f2(hw[i]);
+          const GeluCP c0 = gelu_cdf_pdf(x.x), c1 = gelu_cdf_pdf(x.y);
+          o[i] = pack_bf16x2(g.x * (c0.cdf + x.x * c0.pdf), g.y * (c1.cdf + x.y * c1.pdf));
+        }
+      }
+      stage_store(o, &tmC, n_col, m0);
+      if constexpr (EPI == kEpiGeluFwd) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float2 x = bf16x2_to_f2(o[i]);
+          o[i] = pack_bf16x2(x.x * gelu_cdf_pdf(x.x).cdf, x.y * gelu_cdf_pdf(x.y).cdf);
+        }
+        stage_store(o, &tmC2, n_col, m0);
+      }
+    };
     PairWork pw;
     for (int w = 0; ok && pair_work(args, cluster_id, num_clusters, w, main_k_tiles, pw); ++w, ++it) {
       int tm, tn;
-      tile_coords(pw.tile, args.tiles_m, args.tiles_n, tm, tn);
+      pair_tile_coords(args, pw.tile, AG, tm, tn);
       const int buf = it & 1;
       const bool got = mbar_wait(&tfull_bar[buf], (it >> 1) & 1, args.status, kErrEpi);
       if (!named_barrier_and(1, 128, got)) { ok = false; break; }  // same decision in all 128
@@ -610,15 +739,24 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       const int n0 = tn * BN;
       const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256);
       if (pw.sk < 0) {
+        uint4 hnext[4] = {};
+        if constexpr (EPI == kEpiGeluBwd) load_h(n0, m0, hnext);
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
+          uint4 hv[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) hv[j] = hnext[j];
+          // the next chunk's pre-activation loads overlap this chunk's work
+          if constexpr (EPI == kEpiGeluBwd) {
+            if (c + 1 < BN / 32) load_h(n0 + (c + 1) * 32, m0, hnext);
+          }
           uint32_t r[32];
           tmem_ld_32x32b_x32(trow + (uint32_t)(c * 32), r);
           tmem_ld_wait();
           float v[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          store_chunk(v, n0 + c * 32, m0);
+          store_chunk(v, n0 + c * 32, m0, hv);
         }
       } else {
         // stream-K part: add this part's fp32 block into the tile's accumulation
@@ -657,6 +795,8 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             for (int i = 0; i < 16; ++i) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);  // clean for the next GEMM
 #pragma unroll
             for (int h2 = 0; h2 < 2; ++h2) {
+              uint4 hv[4] = {};
+              if constexpr (EPI == kEpiGeluBwd) load_h(n0 + (c + h2) * 32, m0, hv);
               float v[32];
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
@@ -665,7 +805,7 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 v[4 * i + 2] = x[8 * h2 + i].z;
                 v[4 * i + 3] = x[8 * h2 + i].w;
               }
-              store_chunk(v, n0 + (c + h2) * 32, m0);
+              store_chunk(v, n0 + (c + h2) * 32, m0, hv);
             }
           }
         }
@@ -681,6 +821,16 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, 512);
+  }
+  if (AG && threadIdx.x == 0) {
+    // every warp of this CTA is done with the counters; the last CTA out resets them
+    __threadfence();
+    if (atomicAdd(args.ag_sync + kAgExit, 1) == (int)gridDim.x - 1) {
+      __threadfence();
+      for (int t = 0; t < args.tiles_n; ++t) args.ag_sync[t] = 0;
+      args.ag_sync[kAgClaim] = 0;
+      args.ag_sync[kAgExit] = 0;
+    }
   }
 }
 
@@ -882,16 +1032,16 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUte
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-template <int BN, int STAGES, int KB, bool BMN, bool Q4 = false>
+template <int BN, int STAGES, int KB, bool BMN, bool Q4 = false, bool AG = false, int EPI = kEpiPlain>
 static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2,
                              const CUtensorMap& tb2, const CUtensorMap& tc, GemmArgs args,
-                             cudaStream_t stream, int sms) {
+                             cudaStream_t stream, int sms, const CUtensorMap* tc2 = nullptr) {
   using L = PairSmem<BN, STAGES, KB>;
   static bool configured[64] = {false};
   int dev;
   C10_CUDA_CHECK(cudaGetDevice(&dev));
   if (!configured[dev]) {
-    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_tn_pair_kernel<BN, STAGES, KB, BMN, Q4>,
+    C10_CUDA_CHECK(cudaFuncSetAttribute(gemm_tn_pair_kernel<BN, STAGES, KB, BMN, Q4, AG, EPI>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes));
     configured[dev] = true;
   }
@@ -899,7 +1049,7 @@ static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const
   const int clusters = std::max(1, std::min(tiles, sms / 2));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * clusters);
-  cfg.blockDim = dim3(Q4 ? kGemmQ4Threads : kGemmThreads);
+  cfg.blockDim = dim3((Q4 || AG) ? kGemmQ4Threads : kGemmThreads);
   cfg.dynamicSmemBytes = L::kBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -909,7 +1059,8 @@ static void launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tn_pair_kernel<BN, STAGES, KB, BMN, Q4>, ta, tb, ta2, tb2, tc, args));
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, gemm_tn_pair_kernel<BN, STAGES, KB, BMN, Q4, AG, EPI>, ta, tb, ta2,
+                                    tb2, tc, tc2 != nullptr ? *tc2 : tc, args));
 }
 
 // Pick the N tile that minimises wave quantisation over the SMs.
@@ -926,6 +1077,30 @@ static int choose_bn(int M, int N, int sms) {
     if (cost < best - 1e-9) { best = cost; best_bn = bn; }
   }
   return best_bn;
+}
+
+// Stream-K tail: when the last wave of tiles would leave more than half the
+// clusters idle, split its tiles along K over the clusters (ZEROQ_STREAMK=0: off).
+static void setup_streamk(GemmArgs& args, int main_k, int sms, int dev, cudaStream_t stream) {
+  static const bool sk_on = [] {
+    const char* e = std::getenv("ZEROQ_STREAMK");
+    return e == nullptr || std::atoi(e) != 0;
+  }();
+  const int tiles = args.tiles_m * args.tiles_n;
+  const int C = std::max(1, std::min(tiles, sms / 2));
+  const int full = tiles / C, r = tiles % C;
+  // the split costs ~25 us (fp32 reductions, fence, fix-up): measured on B200 it
+  // pays off from ~48 pipeline stages per tile (8192 x 3072 x 12288: -7%)
+  // and loses below (8192 x 3072 x 3072: +9%)
+  if (sk_on && r > 0 && full >= 1 && 2 * r <= C && r <= kSkMaxTiles && main_k >= 48) {
+    const int S = std::min(C / r, main_k / 2);
+    if (S >= 2) {
+      args.sk_first = full * C;
+      args.sk_tiles = r;
+      args.sk_splits = S;
+      args.sk_cnt = sk_counters(dev, stream, &args.sk_ws);
+    }
+  }
 }
 
 static int g_pair_mode = 1;  // 1: use the CTA-pair kernel when M >= 256 (set_gemm_pair_mode)
@@ -952,7 +1127,7 @@ void set_gemm_pair_mode(int64_t mode) { g_pair_mode = (int)mode; }
 // b_mn = false: B is [N, K] row-major (C = A·Bᵀ); true: B is [K, N] row-major (C = A·B)
 static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
                       const c10::optional<at::Tensor>& a2, const c10::optional<at::Tensor>& b2,
-                      bool b_mn = false) {
+                      bool b_mn = false, int epi = kEpiPlain, const at::Tensor* aux = nullptr) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: CUDA tensors");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 &&
                   c.scalar_type() == at::kBFloat16, "gemm: bf16 operands");
@@ -1011,32 +1186,31 @@ static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
     args.extra_k16 = 4;
   }
   auto stream = at::cuda::getCurrentCUDAStream();
+  TORCH_CHECK(epi == kEpiPlain || (pair && K % 128 == 0 && aux != nullptr),
+              "gemm: fused epilogues need M >= 256, K % 128 == 0 and the auxiliary tensor");
   if (pair) {
     const CUtensorMap tc = make_tmap_store_bf16(c.data_ptr(), M, N, c.stride(0));
     const bool k128 = (K % 128) == 0;
-    // stream-K tail: when the last wave of tiles would leave more than half the
-    // clusters idle, split its tiles along K over the clusters (ZEROQ_STREAMK=0: off)
-    static const bool sk_on = [] {
-      const char* e = std::getenv("ZEROQ_STREAMK");
-      return e == nullptr || std::atoi(e) != 0;
-    }();
-    {
-      const int tiles = args.tiles_m * args.tiles_n;
-      const int C = std::max(1, std::min(tiles, sms / 2));
-      const int full = tiles / C, r = tiles % C;
-      const int main_k = (int)(K / (k128 ? 128 : 64));
-      // the split costs ~25 us (fp32 reductions, fence, fix-up): measured on B200 it
-      // pays off from ~48 pipeline stages per tile (8192 x 3072 x 12288: -7%)
-      // and loses below (8192 x 3072 x 3072: +9%)
-      if (sk_on && r > 0 && full >= 1 && 2 * r <= C && r <= kSkMaxTiles && main_k >= 48) {
-        const int S = std::min(C / r, main_k / 2);
-        if (S >= 2) {
-          args.sk_first = full * C;
-          args.sk_tiles = r;
-          args.sk_splits = S;
-          args.sk_cnt = sk_counters(dev, stream, &args.sk_ws);
-        }
+    setup_streamk(args, (int)(K / (k128 ? 128 : 64)), sms, dev, stream);
+    if (epi != kEpiPlain) {
+      const at::Tensor& x = *aux;
+      TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.size(0) == M &&
+                      x.size(1) == N && x.stride(1) == 1 && (x.stride(0) % 8) == 0 &&
+                      (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0,
+                  "gemm: epilogue tensor must be bf16 [M, N], 16-byte aligned rows");
+      if (epi == kEpiGeluFwd) {
+        TORCH_CHECK(!b_mn, "gemm: the GELU-output epilogue is for the [N, K] weight layout");
+        const CUtensorMap tc2 = make_tmap_store_bf16(x.data_ptr(), M, N, x.stride(0));
+        if (bn == 256) launch_gemm_pair<256, 3, 2, false, false, false, kEpiGeluFwd>(ta, tb, ta2, tb2, tc, args, stream, sms, &tc2);
+        else launch_gemm_pair<128, 4, 2, false, false, false, kEpiGeluFwd>(ta, tb, ta2, tb2, tc, args, stream, sms, &tc2);
+      } else {
+        TORCH_CHECK(b_mn, "gemm: the GELU-gradient epilogue is for the [K, N] weight layout");
+        args.epi_src = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr<at::BFloat16>());
+        args.epi_ld = x.stride(0);
+        if (bn == 256) launch_gemm_pair<256, 3, 2, true, false, false, kEpiGeluBwd>(ta, tb, ta2, tb2, tc, args, stream, sms);
+        else launch_gemm_pair<128, 4, 2, true, false, false, kEpiGeluBwd>(ta, tb, ta2, tb2, tc, args, stream, sms);
       }
+      return;
     }
     if (b_mn) {
       if (bn == 256) {
@@ -1074,6 +1248,14 @@ void gemm_bf16_tn_extra(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor a2,
 void gemm_bf16_nn(at::Tensor a, at::Tensor b, at::Tensor c, c10::optional<at::Tensor> a2,
                   c10::optional<at::Tensor> b2) {
   gemm_impl(a, b, c, a2, b2, true);
+}
+
+// GEMM with the GELU epilogues (needs M >= 256 and K % 128 == 0):
+//   b_mn = false: H = A·Bᵀ (+ A2·B2ᵀ) stored in c and GELU(H) in aux;
+//   b_mn = true:  c = (A·B (+ A2·B2)) * GELU'(aux), aux = the pre-activation.
+void gemm_gelu(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor aux, bool b_mn,
+               c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2) {
+  gemm_impl(a, b, c, a2, b2, b_mn, b_mn ? kEpiGeluBwd : kEpiGeluFwd, &aux);
 }
 
 // GEMM whose B operand is a 4-bit weight W [rows, cols] decoded inside the
@@ -1152,6 +1334,122 @@ void gemm_nf4(at::Tensor a, at::Tensor packed, at::Tensor absmax, int64_t rows, 
   const CUtensorMap tc = make_tmap_store_bf16(c.data_ptr(), M, N, c.stride(0));
   if (w_is_kn) launch_gemm_pair<256, 3, 2, true, true>(ta, ta, ta2, tb2, tc, args, stream, sms);
   else launch_gemm_pair<256, 3, 2, false, true>(ta, ta, ta2, tb2, tc, args, stream, sms);
+}
+
+// Gather-mode counters, one zeroed set per (device, stream); the kernel's last
+// CTA resets them, so consecutive launches on a stream reuse them.
+static int* ag_sync_buffer(int device, cudaStream_t stream) {
+  static std::map<std::pair<int, cudaStream_t>, int*> bufs;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> g(mu);
+  int*& p = bufs[{device, stream}];
+  if (p == nullptr) {
+    C10_CUDA_CHECK(cudaMalloc(&p, kAgSyncWords * sizeof(int)));
+    C10_CUDA_CHECK(cudaMemsetAsync(p, 0, kAgSyncWords * sizeof(int), stream));
+  }
+  return p;
+}
+
+// C[M, N] = A[M, K] · Wᵀ (+ A2[M, 64] · B2[N, 64]) where W [N, K] is a 4-bit
+// weight split over the ranks of the node: rank q holds packed bytes
+// [pstarts[q], pstarts[q+1]) at device address psrc[q] and absmax entries
+// [astarts[q], astarts[q+1]) at asrc[q] (addresses valid in this process: this
+// rank's own memory or CUDA IPC mappings of the peers').  One kernel gathers
+// and dequantises W into wbuf (bf16 [N, K], left assembled for the caller) and
+// multiplies it with tcgen05, each N tile starting as soon as its rows are in.
+void ag_gemm_nf4(at::Tensor a, std::vector<int64_t> psrc, std::vector<int64_t> pstarts,
+                 std::vector<int64_t> asrc, std::vector<int64_t> astarts, int64_t packed_total,
+                 int64_t absmax_total, int64_t rank, int64_t N, int64_t K, int64_t blocksize,
+                 int64_t quant_type, at::Tensor wbuf, at::Tensor c, c10::optional<at::Tensor> a2,
+                 c10::optional<at::Tensor> b2) {
+  const int world = (int)psrc.size();
+  TORCH_CHECK(world >= 1 && world <= kAgMaxRanks && (int)pstarts.size() == world &&
+                  (int)asrc.size() == world && (int)astarts.size() == world,
+              "ag_gemm_nf4: one pointer and start per rank (at most 8 ranks)");
+  TORCH_CHECK(rank >= 0 && rank < world, "ag_gemm_nf4: rank out of range");
+  TORCH_CHECK(a.is_cuda() && c.is_cuda() && wbuf.is_cuda(), "ag_gemm_nf4: CUDA tensors");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && c.scalar_type() == at::kBFloat16 &&
+                  wbuf.scalar_type() == at::kBFloat16, "ag_gemm_nf4: bf16 A, C and W buffer");
+  TORCH_CHECK(a.dim() == 2 && c.dim() == 2 && a.stride(1) == 1 && c.stride(1) == 1,
+              "ag_gemm_nf4: row-major A and C");
+  const int64_t M = a.size(0);
+  TORCH_CHECK(a.size(1) == K && c.size(0) == M && c.size(1) == N, "ag_gemm_nf4: shapes");
+  TORCH_CHECK(M >= 2 * kBM && M < (1LL << 31) && N < (1LL << 31), "ag_gemm_nf4: needs M >= 256");
+  TORCH_CHECK(K % 128 == 0 && N % 8 == 0, "ag_gemm_nf4: needs K % 128 == 0 and N % 8 == 0");
+  TORCH_CHECK(blocksize > 0 && blocksize % 32 == 0, "ag_gemm_nf4: block size a multiple of 32");
+  TORCH_CHECK(quant_type == 0 || quant_type == 1, "ag_gemm_nf4: quant_type 0 (nf4) or 1 (fp4)");
+  TORCH_CHECK(packed_total * 2 == N * K && absmax_total * blocksize >= N * K,
+              "ag_gemm_nf4: packed/absmax totals do not cover W");
+  TORCH_CHECK(wbuf.is_contiguous() && wbuf.numel() == N * K &&
+                  (reinterpret_cast<uintptr_t>(wbuf.data_ptr()) & 15) == 0,
+              "ag_gemm_nf4: W buffer must be contiguous, N*K elements, 16-byte aligned");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(c.data_ptr()) & 15) == 0 && (c.stride(0) % 8) == 0,
+              "ag_gemm_nf4: C must be 16-byte aligned with a row pitch multiple of 8");
+  for (int q = 0; q < world; ++q) {
+    const int64_t pend = q + 1 < world ? pstarts[q + 1] : packed_total;
+    const int64_t aend = q + 1 < world ? astarts[q + 1] : absmax_total;
+    TORCH_CHECK(pstarts[q] >= 0 && pstarts[q] <= pend && astarts[q] >= 0 && astarts[q] <= aend,
+                "ag_gemm_nf4: starts must be non-decreasing");
+    TORCH_CHECK(pend == pstarts[q] || psrc[q] != 0, "ag_gemm_nf4: null shard pointer");
+    TORCH_CHECK(aend == astarts[q] || (asrc[q] != 0 && (asrc[q] & 3) == 0),
+                "ag_gemm_nf4: absmax pointers must be 4-byte aligned");
+  }
+  const at::cuda::CUDAGuard guard(a.device());
+  const int dev = a.get_device();
+  const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+  const int bn = choose_bn_pair((int)M, (int)N, sms);
+
+  GemmArgs args{};
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.tiles_m = (int)((M + 2 * kBM - 1) / (2 * kBM));
+  args.tiles_n = (int)((N + bn - 1) / bn);
+  TORCH_CHECK(args.tiles_n <= kAgMaxTilesN, "ag_gemm_nf4: N too large");
+  args.C = reinterpret_cast<__nv_bfloat16*>(c.data_ptr<at::BFloat16>());
+  args.ldc = c.stride(0);
+  args.status = status_buffer(dev);
+  args.q_block = (int)blocksize;
+  args.q_type = (int)quant_type;
+  args.ag.world = world;
+  for (int q = 0; q < kAgMaxRanks; ++q) {
+    const bool in = q < world;
+    args.ag.packed[q] = in ? reinterpret_cast<const uint8_t*>(psrc[q]) : nullptr;
+    args.ag.absmax[q] = in ? reinterpret_cast<const float*>(asrc[q]) : nullptr;
+    args.ag.pstart[q] = in ? pstarts[q] : packed_total;
+    args.ag.astart[q] = in ? astarts[q] : absmax_total;
+  }
+  args.ag.pstart[kAgMaxRanks] = packed_total;
+  args.ag.astart[kAgMaxRanks] = absmax_total;
+  args.ag_w = reinterpret_cast<__nv_bfloat16*>(wbuf.data_ptr<at::BFloat16>());
+  args.ag_kchunks = (int)((K + kAgCols - 1) / kAgCols);
+  {  // start at the N tile holding this rank's first own row
+    const int64_t pend = rank + 1 < world ? pstarts[rank + 1] : packed_total;
+    const int64_t first_row = pend > pstarts[rank] ? (2 * pstarts[rank]) / K : 0;
+    args.ag_rot = (int)std::min<int64_t>(first_row / bn, args.tiles_n - 1);
+  }
+
+  CUtensorMap ta = make_tmap_bf16(a.data_ptr(), M, K, a.stride(0), kBM);
+  CUtensorMap tb = make_tmap_bf16(wbuf.data_ptr(), N, K, K, bn / 2);
+  CUtensorMap ta2 = ta, tb2 = tb;
+  if (a2.has_value() && a2->defined()) {
+    TORCH_CHECK(b2.has_value() && b2->defined(), "ag_gemm_nf4: extra slab needs both operands");
+    const at::Tensor& x2 = *a2;
+    const at::Tensor& y2 = *b2;
+    TORCH_CHECK(x2.scalar_type() == at::kBFloat16 && y2.scalar_type() == at::kBFloat16 &&
+                    x2.size(0) == M && y2.size(0) == N && x2.size(1) == 64 && y2.size(1) == 64 &&
+                    x2.stride(1) == 1 && y2.stride(1) == 1,
+                "ag_gemm_nf4: extra slab operands must be bf16 [M,64] and [N,64] row-major");
+    ta2 = make_tmap_bf16(x2.data_ptr(), M, 64, x2.stride(0), kBM);
+    tb2 = make_tmap_bf16(y2.data_ptr(), N, 64, y2.stride(0), bn / 2);
+    args.extra_k16 = 4;
+  }
+  auto stream = at::cuda::getCurrentCUDAStream();
+  args.ag_sync = ag_sync_buffer(dev, stream);
+  setup_streamk(args, (int)(K / 128), sms, dev, stream);
+  const CUtensorMap tc = make_tmap_store_bf16(c.data_ptr(), M, N, c.stride(0));
+  if (bn == 256) launch_gemm_pair<256, 3, 2, false, false, true>(ta, tb, ta2, tb2, tc, args, stream, sms);
+  else launch_gemm_pair<128, 4, 2, false, false, true>(ta, tb, ta2, tb2, tc, args, stream, sms);
 }
 
 // NF4 weight [rows, cols] -> bf16 [rows, cols] (transpose=false) or [cols, rows].

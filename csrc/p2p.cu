@@ -25,6 +25,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "peer_gather.cuh"
 
 namespace zq {
 
@@ -342,6 +343,25 @@ __global__ void __launch_bounds__(256) plan_gather_dequant_kernel(
   }
 }
 
+// Non-transposed peer gather + dequantise, one warp per item of 8 rows x 1024
+// columns (16-byte loads, 8 in flight per lane): rows [row0, row0 + rows) of
+// W [*, K] into out_base + r * K (out_base = output - row0 * K).
+__global__ void __launch_bounds__(256) ag_dequant_kernel(AgSource s, int K, int row0, int rows,
+                                                         int blocksize, int qtype,
+                                                         __nv_bfloat16* out_base) {
+  __shared__ float lut[16];
+  if (threadIdx.x < 16) lut[threadIdx.x] = c_p2p_code[qtype][threadIdx.x];
+  __syncthreads();
+  const int kchunks = (K + kAgCols - 1) / kAgCols;
+  const int64_t total = (int64_t)((rows + kAgRows - 1) / kAgRows) * kchunks;
+  const int lane = threadIdx.x & 31;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t it = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; it < total; it += nw) {
+    const int rg = (int)(it / kchunks), kc = (int)(it - (int64_t)rg * kchunks);
+    ag_item(s, lut, row0 + rows, K, blocksize, row0 + rg * kAgRows, kc * kAgCols, out_base, lane);
+  }
+}
+
 }  // namespace zq
 
 using namespace zq;
@@ -474,6 +494,26 @@ void plan_gather_dequant(std::vector<int64_t> psrc, std::vector<int64_t> pstarts
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() == rows * cols,
               "plan_gather_dequant: bf16 output of rows*cols");
   const at::cuda::CUDAGuard guard(out.device());
+  if (!transpose && cols % 32 == 0 && blocksize % 32 == 0 && rows > 0) {
+    AgSource s{};
+    s.world = world;
+    for (int q = 0; q < kAgMaxRanks; ++q) {
+      s.packed[q] = q < world ? reinterpret_cast<const uint8_t*>(psrc[q]) : nullptr;
+      s.absmax[q] = q < world ? reinterpret_cast<const float*>(asrc[q]) : nullptr;
+      // the last rank's piece is unbounded here (the totals are not passed)
+      s.pstart[q] = q < world ? pstarts[q] : INT64_MAX;
+      s.astart[q] = q < world ? astarts[q] : INT64_MAX;
+    }
+    s.pstart[kAgMaxRanks] = s.astart[kAgMaxRanks] = INT64_MAX;
+    const int64_t items = ((rows + kAgRows - 1) / kAgRows) * ((cols + kAgCols - 1) / kAgCols);
+    const int sms = at::cuda::getCurrentDeviceProperties()->multiProcessorCount;
+    const int64_t grid = std::max<int64_t>(1, std::min<int64_t>((items + 7) / 8, (int64_t)sms * 8));
+    ag_dequant_kernel<<<(unsigned)grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        s, (int)cols, (int)row0, (int)rows, (int)blocksize, (int)qtype,
+        reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()) - row0 * cols);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   dim3 grid((unsigned)((cols + 63) / 64), (unsigned)((rows + 63) / 64));
   plan_gather_dequant_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       table_from(psrc), table_from(pstarts), table_from(asrc), table_from(astarts), world, (int)rows,

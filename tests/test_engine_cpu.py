@@ -242,3 +242,81 @@ def test_gather_release_with_frozen_sharded_norms():
     loss.backward()
     assert torch.isfinite(loss)
     assert m.layers[0].q_proj.lora_B.grad is not None
+
+
+def test_linear4bit_peer_source_gathers_when_the_fused_kernel_does_not_apply():
+    """A Linear4bit whose weight stays in its owners' shards (set_peer_source): off
+    the fused path (CPU, torch backend) forward and backward assemble the NF4 data
+    through the pool and match the resident-NF4 module exactly."""
+    from zeroq_b200.ops.qlinear import Linear4bit
+
+    torch.manual_seed(0)
+    lin = Linear4bit(128, 64, lora_r=4, backend="torch", device="cpu")
+    lin.quantize_from(torch.randn(64, 128) * 0.02)
+    with torch.no_grad():
+        lin.lora_B.normal_(0, 0.05)
+    pk, am = lin.weight_packed.clone(), lin.weight_absmax.clone()
+    x = torch.randn(3, 5, 128, requires_grad=True)
+    ref = lin(x)
+    ref.square().sum().backward()
+    gx_ref, gA_ref = x.grad.clone(), lin.lora_A.grad.clone()
+
+    class Pool:
+        calls = 0
+
+        def gather(self, zq):
+            Pool.calls += 1
+
+            class H:
+                def wait(self):
+                    return pk, am
+            return H()
+
+    lin.set_peer_source(Pool(), None)
+    assert lin.has_nf4 and lin.weight_packed is None
+    x.grad = None
+    lin.lora_A.grad = None
+    y = lin(x)
+    y.square().sum().backward()
+    assert torch.equal(y, ref) and torch.equal(x.grad, gx_ref)
+    assert torch.equal(lin.lora_A.grad, gA_ref)
+    assert Pool.calls == 2  # forward and backward each assemble once
+    lin.clear_nf4()
+    assert not lin.has_nf4
+
+
+def test_gelu_mlp_split_form_matches_plain_form_on_cpu():
+    """The split GELU MLP (up returns h and a non-differentiable gelu(h), down takes
+    the gradient through h) gives the plain form's values and gradients off the
+    fused path, including when one layer holds a full-precision weight."""
+    from zeroq_b200.ops.activations import gelu
+    from zeroq_b200.ops.qlinear import Linear4bit
+
+    torch.manual_seed(1)
+    up = Linear4bit(64, 128, lora_r=4, backend="torch", device="cpu")
+    down = Linear4bit(128, 64, lora_r=4, backend="torch", device="cpu")
+    up.quantize_from(torch.randn(128, 64) * 0.05)
+    down.quantize_from(torch.randn(64, 128) * 0.05)
+    with torch.no_grad():
+        up.lora_B.normal_(0, 0.05)
+        down.lora_B.normal_(0, 0.05)
+    x = torch.randn(3, 7, 64, requires_grad=True)
+    for full_precision_down in (False, True):
+        if full_precision_down:
+            w = down.dequantized_weight()
+            down.clear_nf4()
+            down.weight = torch.nn.Parameter(w, requires_grad=False)
+        x.grad = None
+        h, a = up(x, act_out="gelu")
+        assert not a.requires_grad
+        y = down(a, pre=h)
+        y.square().sum().backward()
+        g1, gA1 = x.grad.clone(), up.lora_A.grad.clone()
+        x.grad = None
+        up.lora_A.grad = None
+        y2 = down(gelu(up(x)))
+        y2.square().sum().backward()
+        torch.testing.assert_close(y, y2, rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(g1, x.grad, rtol=1e-4, atol=1e-6)
+        torch.testing.assert_close(gA1, up.lora_A.grad, rtol=1e-4, atol=1e-6)
+        up.lora_A.grad = None

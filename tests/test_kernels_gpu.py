@@ -575,3 +575,175 @@ def test_gemm_stream_k_tail(cuda, M, N, K, nn, extra):
         torch.cuda.synchronize()
         _status_ok(cuda)
         assert (c.float() - ref).abs().max().item() < tol
+
+
+def _split_pieces(t: torch.Tensor, starts):
+    """Copies of t[starts[q]:starts[q+1]] in separate allocations (one per emulated
+    rank, each at a 16-byte-aligned base), plus their device addresses."""
+    bounds = list(starts) + [t.numel()]
+    pieces = [t[bounds[q]:bounds[q + 1]].clone() for q in range(len(starts))]
+    # an empty piece still needs an address; the kernel never reads it
+    ptrs = [p.data_ptr() if p.numel() else t.data_ptr() for p in pieces]
+    return pieces, ptrs
+
+
+@pytest.mark.parametrize("M,N,K,starts_frac", [
+    (512, 384, 512, [0.0, 0.5]),                 # two even pieces
+    (1024, 4096, 4096, [0.0, 0.25, 0.5, 0.75]),  # four ranks, several N tiles each
+    (768, 1000, 1536, [0.0, 0.3, 0.31, 0.8]),    # uneven pieces, N and K not tile multiples
+    (300, 520, 384, [0.0, 0.0, 0.6]),            # an empty piece, ragged M
+    (2048, 3072, 12288, [0.0, 0.5]),             # stream-K tail active
+])
+@pytest.mark.parametrize("extra", [False, True])
+def test_ag_gemm_one_kernel_matches_dequant_then_gemm(cuda, M, N, K, starts_frac, extra):
+    """The gather + dequantise + GEMM kernel over per-rank pieces (emulated on one
+    GPU as separate allocations) against the standalone dequantise and the same
+    GEMM: the assembled operand is bit-identical, the product too (up to the
+    stream-K reduction order), for every rank's tile rotation, launched twice in a
+    row (the counters reset themselves)."""
+    from zeroq_b200.parallel.peer import ag_gemm_pieces
+
+    torch.manual_seed(3)
+    W = torch.randn(N, K, device=cuda) * 0.02
+    packed, st = quantize_4bit(W, 64, "nf4")
+    packed, absmax = packed.reshape(-1), st.absmax.reshape(-1)
+    # packed starts at odd byte offsets exercise the byte-wise path at boundaries
+    pst = [int(f * packed.numel()) | (1 if 0 < f < 0.5 else 0) for f in starts_frac]
+    pst[0] = 0
+    ast = [int(f * absmax.numel()) for f in starts_frac]
+    ppieces, pptrs = _split_pieces(packed, pst)
+    apieces, aptrs = _split_pieces(absmax, ast)
+    full = torch.empty(N * K, dtype=torch.bfloat16, device=cuda)
+    _ext.ext().nf4_to_bf16(packed, absmax, full, N, K, 64, 0, False)
+    x = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    ex = None
+    ref = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    if extra:
+        ex = ((torch.randn(M, 64, device=cuda) * 0.1).to(torch.bfloat16),
+              (torch.randn(N, 64, device=cuda) * 0.1).to(torch.bfloat16))
+        _ext.ext().gemm_bf16_tn_extra(x, full.view(N, K), ref, ex[0], ex[1])
+    else:
+        _ext.ext().gemm_bf16_tn(x, full.view(N, K), ref)
+    streamk = K >= 128 * 48
+    for rank in range(len(pst)):
+        for _ in range(2):
+            y, wbuf = ag_gemm_pieces(x, pptrs, pst, aptrs, ast, N, K, 64, "nf4", rank=rank,
+                                     extra=ex)
+            torch.cuda.synchronize()
+            _status_ok(cuda)
+            assert torch.equal(wbuf.reshape(-1), full)
+            if streamk:
+                torch.testing.assert_close(y.float(), ref.float(), rtol=1e-2, atol=1e-2)
+            else:
+                assert torch.equal(y, ref), (rank, (y.float() - ref.float()).abs().max().item())
+    # sanity against fp32
+    want = x.float() @ full.view(N, K).float().t()
+    if extra:
+        want += ex[0].float() @ ex[1].float().t()
+    assert (y.float() - want).abs().max().item() < 2e-2 * want.abs().max().item() + 1e-2
+
+
+def test_gather_dequant_fast_path_matches_full(cuda):
+    """The warp-per-item peer gather + dequantise (standalone kernel) over uneven
+    pieces equals the full dequantise, for a row window too."""
+    N, K = 1000, 1536
+    torch.manual_seed(4)
+    packed, st = quantize_4bit(torch.randn(N, K, device=cuda) * 0.02, 64, "nf4")
+    packed, absmax = packed.reshape(-1), st.absmax.reshape(-1)
+    pst = [0, 100003, 400000]
+    ast = [0, 3125, 12500]
+    ppieces, pptrs = _split_pieces(packed, pst)
+    apieces, aptrs = _split_pieces(absmax, ast)
+    full = torch.empty(N * K, dtype=torch.bfloat16, device=cuda)
+    _ext.ext().nf4_to_bf16(packed, absmax, full, N, K, 64, 0, False)
+    for row0, rows in ((0, N), (136, 264)):
+        out = torch.empty(rows * K, dtype=torch.bfloat16, device=cuda)
+        _ext.ext().plan_gather_dequant(pptrs, pst, aptrs, ast, rows, K, row0, 64, 0, False, out)
+        torch.cuda.synchronize()
+        assert torch.equal(out, full[row0 * K:(row0 + rows) * K])
+
+
+@pytest.mark.parametrize("M,K,N", [(512, 384, 1024), (300, 1536, 640), (2048, 3072, 12288)])
+@pytest.mark.parametrize("extra", [False, True])
+def test_gemm_gelu_epilogues_match_separate_kernels(cuda, M, K, N, extra):
+    """GELU-output epilogue (H and gelu(H) from one GEMM) and GELU-gradient
+    epilogue ((dY·W) * gelu'(H)) against the plain GEMM followed by the GELU
+    kernels: bit-identical (the epilogues round the accumulator to bf16 first)."""
+    E = _ext.ext()
+    torch.manual_seed(5)
+    x = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=cuda) * 0.05).to(torch.bfloat16)
+    a2 = b2 = None
+    if extra:
+        a2 = (torch.randn(M, 64, device=cuda) * 0.1).to(torch.bfloat16)
+        b2 = (torch.randn(N, 64, device=cuda) * 0.1).to(torch.bfloat16)
+    h = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    act = torch.empty_like(h)
+    E.gemm_gelu(x, w, h, act, False, a2, b2)
+    h_ref = torch.empty_like(h)
+    if extra:
+        E.gemm_bf16_tn_extra(x, w, h_ref, a2, b2)
+    else:
+        E.gemm_bf16_tn(x, w, h_ref)
+    act_ref = torch.empty_like(h)
+    E.gelu_fwd(h_ref, act_ref)
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    streamk = K >= 128 * 48
+    if streamk:
+        torch.testing.assert_close(h.float(), h_ref.float(), rtol=1e-2, atol=1e-2)
+    else:
+        assert torch.equal(h, h_ref) and torch.equal(act, act_ref)
+    # backward: dH = (dY [M, N] · W [N, K]... here the GEMM is dY [M, K'] x Wd [K', N])
+    gy = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    wd = (torch.randn(K, N, device=cuda) * 0.05).to(torch.bfloat16)  # [K', N] read MN-major
+    a3 = b3 = None
+    if extra:
+        a3 = (torch.randn(M, 64, device=cuda) * 0.1).to(torch.bfloat16)
+        b3 = (torch.randn(64, N, device=cuda) * 0.1).to(torch.bfloat16)
+    dh = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    E.gemm_gelu(gy, wd, dh, h_ref, True, a3, b3)
+    da = torch.empty_like(dh)
+    E.gemm_bf16_nn(gy, wd, da, a3, b3)
+    dh_ref = torch.empty_like(dh)
+    E.gelu_bwd(da, h_ref, dh_ref)
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    assert torch.equal(dh, dh_ref), (dh.float() - dh_ref.float()).abs().max().item()
+
+
+@pytest.mark.parametrize("lora_r", [0, 16])
+def test_fused_gelu_mlp_matches_unfused(cuda, lora_r):
+    """up_proj(x, act_out='gelu') + down_proj(f, pre=h) equals gelu between two
+    plain NF4 layers, values and gradients (input and LoRA)."""
+    from zeroq_b200.ops.activations import gelu
+    from zeroq_b200.ops.qlinear import Linear4bit
+
+    torch.manual_seed(6)
+    d, f = 512, 1536
+    up = Linear4bit(d, f, lora_r=lora_r, device=cuda)
+    down = Linear4bit(f, d, lora_r=lora_r, device=cuda)
+    up.quantize_from(torch.randn(f, d, device=cuda) * 0.03)
+    down.quantize_from(torch.randn(d, f, device=cuda) * 0.03)
+    if lora_r:
+        with torch.no_grad():
+            up.lora_B.normal_(0, 0.02)
+            down.lora_B.normal_(0, 0.02)
+    x = (torch.randn(2, 200, d, device=cuda)).to(torch.bfloat16).requires_grad_(True)
+    hpre, a = up(x, act_out="gelu")
+    y = down(a, pre=hpre)
+    (y.float() ** 2).sum().backward()
+    grads = [x.grad.clone()] + ([up.lora_A.grad.clone(), up.lora_B.grad.clone(),
+                                 down.lora_A.grad.clone(), down.lora_B.grad.clone()] if lora_r else [])
+    for p in [x] + ([up.lora_A, up.lora_B, down.lora_A, down.lora_B] if lora_r else []):
+        p.grad = None
+    y2 = down(gelu(up(x)))
+    (y2.float() ** 2).sum().backward()
+    grads2 = [x.grad] + ([up.lora_A.grad, up.lora_B.grad, down.lora_A.grad, down.lora_B.grad]
+                         if lora_r else [])
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    assert torch.equal(y, y2)
+    assert torch.equal(grads[0], grads2[0])
+    for g1, g2 in zip(grads[1:], grads2[1:]):
+        torch.testing.assert_close(g1, g2, rtol=1e-5, atol=1e-6)

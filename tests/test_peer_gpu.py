@@ -121,12 +121,85 @@ def w_peer_gather(rank, world):
         pool.close()
 
 
+def w_peer_ag_gemm(rank, world):
+    """One-kernel gather + dequantise + GEMM from the owners' shards against the
+    assembled weight, standalone and as the forward of a peer-sourced Linear4bit
+    (whose backward reads the operand straight from the shards too)."""
+    import zeroq_b200 as zq
+    from zeroq_b200.ops import _ext
+    from zeroq_b200.ops.qlinear import Linear4bit
+    from zeroq_b200.parallel.peer import PeerShardPool
+
+    E = _ext.ext()
+    for hetero in (False, True):
+        torch.manual_seed(2)
+        m = torch.nn.Sequential(Linear4bit(512, 384, device="cuda", lora_r=8),
+                                Linear4bit(384, 320, device="cuda"))
+        for lin in m:
+            lin.weight = torch.nn.Parameter(torch.randn(lin.out_features, lin.in_features,
+                                                        device="cuda") * 0.02, requires_grad=False)
+        with torch.no_grad():
+            m[0].lora_B.normal_(0, 0.02)
+        cfg = zq.ZeroQConfig(exclude_modules=[], backend="fused", compute_in_4bit=True)
+        if hetero:
+            coord = zq.HeteroZeroQCoordinator(cfg, rank_weights=[3.0, 1.0])
+            zq.HeteroZeroQModuleWrapper(m, coord).partition()
+        else:
+            coord = zq.ZeroQCoordinator(cfg)
+            zq.ZeroQModuleWrapper(m, coord).partition()
+        pool = PeerShardPool(coord)
+        for p in coord._params.values():
+            N, K = p.original_shape
+            pk, am = pool.gather(p).wait()
+            full = torch.empty(N * K, dtype=torch.bfloat16, device="cuda")
+            E.nf4_to_bf16(pk, am, full, N, K, 64, 0, False)
+            x = (torch.randn(300, K, device="cuda") * 0.5).to(torch.bfloat16)
+            ref = torch.empty(300, N, dtype=torch.bfloat16, device="cuda")
+            E.gemm_bf16_tn(x, full.view(N, K), ref)
+            for _ in range(2):
+                y, wbuf = pool.ag_gemm(p, x)
+                torch.cuda.synchronize()
+                assert torch.equal(wbuf.reshape(-1), full)
+                assert torch.equal(y, ref)
+        # module path: the pre-forward hook hands each Linear4bit its peer source
+        lin = m[0]
+        calls = []
+        fused_call = pool.ag_gemm
+        pool.ag_gemm = lambda *a, **k: (calls.append(1), fused_call(*a, **k))[1]
+        x = (torch.randn(2, 160, 512, device="cuda") * 0.5).to(torch.bfloat16).requires_grad_(True)
+        y = m(x)
+        assert len(calls) == 2  # both layers ran the one-kernel path
+        y.float().square().sum().backward()
+        gx, gA = x.grad.clone(), lin.lora_A.grad.clone()
+        # the same through assembled NF4 (set_nf4) with the hooks removed
+        ref_m = torch.nn.Sequential(*[Linear4bit(l.in_features, l.out_features, device="cuda",
+                                                 lora_r=l.lora_r) for l in m])
+        for src, dst, p in zip(m, ref_m, coord._params.values()):
+            pk, am = pool.gather(p).wait()
+            dst.set_nf4(pk, am)
+            if src.lora_r:
+                dst.lora_A.data.copy_(src.lora_A.data)
+                dst.lora_B.data.copy_(src.lora_B.data)
+        x2 = x.detach().clone().requires_grad_(True)
+        y2 = ref_m(x2)
+        y2.float().square().sum().backward()
+        assert torch.equal(y, y2)
+        assert torch.equal(gx, x2.grad)
+        torch.testing.assert_close(gA, ref_m[0].lora_A.grad, rtol=1e-4, atol=1e-5)
+        torch.cuda.synchronize()
+        pool.close()
+
+
 def test_fused_reduce_scatter_adamw_matches_nccl():
     _run("w_fused_adamw", 2)
 
 
 def test_peer_gather_and_gather_dequant_match_nccl():
     _run("w_peer_gather", 2)
+
+
+def test_peer_ag_gemm_one_kernel_matches_assembled():
+    _run("w_peer_ag_gemm", 2)
 
 
 def test_peer_wait_times_out_with_error_status(cuda):

@@ -183,9 +183,22 @@ class DecoderLayer(nn.Module):
         h, x = self.mlp_norm(h, a)
         if self.gate_proj is not None:
             f = swiglu(self.gate_proj(x), self.up_proj(x))
+        elif self._fused_gelu_mlp():
+            # up-projection epilogue writes h and gelu(h); the down-projection's
+            # input-gradient epilogue applies gelu'(h): no GELU kernels
+            pre, f = self.up_proj(x, act_out="gelu")
+            return h, self.down_proj(f, pre=pre)
         else:
             f = gelu(self.up_proj(x))
         return h, self.down_proj(f)
+
+    def _fused_gelu_mlp(self) -> bool:
+        from ..ops.qlinear import Linear4bit
+
+        mods = (self.up_proj, self.down_proj)
+        return (all(isinstance(m, Linear4bit) for m in mods)
+                and not any(m._forward_hooks or m._forward_pre_hooks or m._backward_hooks
+                            or m._backward_pre_hooks for m in mods))
 
 
 class DecoderLM(nn.Module):

@@ -102,11 +102,21 @@ class NF4LinearFunction(torch.autograd.Function):
     LoRA up-projection rides as the extra 64-wide K slab of the same GEMM
     (``U = x·(s·A)ᵀ`` against ``B``, zero-padded to rank 64).  ``lora_ops`` is
     the cached pair ``(s·A padded [64, K], B padded [N, 64])`` in bf16.
+
+    GELU MLP fusion (``act_out`` / ``pre``):
+
+    * ``act_out="gelu"``: returns ``(h, gelu(h))`` with ``h`` the layer output; the
+      GEMM epilogue writes both (no separate GELU kernel), ``gelu(h)`` is
+      non-differentiable and the gradient flows through ``h``;
+    * ``pre=h``: ``x`` is ``gelu(h)`` (no gradient of its own) and the gradient is
+      returned for ``h`` - the input-gradient GEMM's epilogue multiplies by
+      ``gelu'(h)``, so the gradient of ``gelu(h)`` is never stored.
+    Off the fused path both fall back to the GELU kernels with the same results.
     """
 
     @staticmethod
     def forward(ctx, x, packed, absmax, lora_A, lora_B, bias, N, K, blocksize, quant_type,
-                scaling, backend, lora_ops=None):
+                scaling, backend, lora_ops=None, peer=None, act_out=None, pre=None):
         shp = x.shape
         x2 = x.reshape(-1, K)
         if not x2.is_contiguous():
@@ -115,8 +125,16 @@ class NF4LinearFunction(torch.autograd.Function):
         has_lora = lora_A is not None and lora_B is not None
         r = lora_A.shape[0] if has_lora else 0
         fused = backend != "torch" and _fused_ok(x2, K, N, blocksize) and r <= 64
+        # peer = (PeerShardPool, ZeroQParameter): W stays in its owners' shards and
+        # the fused gather + dequantise + GEMM kernel reads it there
+        peer_fused = peer is not None and fused and _peer_ag_ok(M, N, K, blocksize)
+        if peer is not None and not peer_fused:
+            packed, absmax = peer[0].gather(peer[1]).wait()
         U = None
         a_pad = b_pad = None
+        act = None
+        if act_out not in (None, "gelu"):
+            raise ValueError(f"unsupported fused activation {act_out!r}")
         if fused:
             E = _ext.ext()
             y = torch.empty(M, N, dtype=x2.dtype, device=x2.device)
@@ -125,7 +143,16 @@ class NF4LinearFunction(torch.autograd.Function):
                     lora_ops = _pack_lora(lora_A.detach(), lora_B.detach(), scaling)
                 a_pad, b_pad = lora_ops
                 U = x2 @ a_pad.t()  # [M, 64] skinny product: cuBLAS
-            if _in_kernel_ok(M, K, N):
+            if peer_fused:
+                _, wbuf = peer[0].ag_gemm(peer[1], x2, out=y,
+                                          extra=(U, b_pad) if has_lora else None)
+                del wbuf
+            elif act_out == "gelu" and bias is None and _epi_ok(M, K) and not _in_kernel_ok(M, K, N):
+                w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
+                act = torch.empty_like(y)
+                E.gemm_gelu(x2, w, y, act, False, U, b_pad)
+                del w
+            elif _in_kernel_ok(M, K, N):
                 E.gemm_nf4(x2, packed, absmax, N, K, blocksize, QUANT_TYPE_ID[quant_type], False, y,
                            U, b_pad)
             else:
@@ -144,33 +171,68 @@ class NF4LinearFunction(torch.autograd.Function):
             y = y.to(x2.dtype)
         if bias is not None:
             y = y + bias.to(y.dtype)
+        if peer is not None:
+            packed = absmax = None  # re-read from the owners in backward
+        pre2 = None
+        if pre is not None:
+            pre2 = pre.reshape(-1, K)
+            if not pre2.is_contiguous():
+                pre2 = pre2.contiguous()
         ctx.save_for_backward(x2 if has_lora else None, packed, absmax, lora_A, lora_B, U,
-                              a_pad, b_pad)
+                              a_pad, b_pad, pre2)
         ctx.meta = (shp, N, K, blocksize, quant_type, scaling, fused, bias is not None, has_lora, r)
-        return y.view(*shp[:-1], N)
+        ctx.peer = peer
+        y = y.view(*shp[:-1], N)
+        if act_out == "gelu":
+            if act is None:
+                act = _gelu_kernel(y)
+            act = act.view(*shp[:-1], N)
+            ctx.mark_non_differentiable(act)
+            return y, act
+        return y
 
     @staticmethod
-    def backward(ctx, gy):
-        x2, packed, absmax, lora_A, lora_B, U, a_pad, b_pad = ctx.saved_tensors
+    def backward(ctx, gy, g_act=None):
+        x2, packed, absmax, lora_A, lora_B, U, a_pad, b_pad, pre2 = ctx.saved_tensors
         shp, N, K, blocksize, quant_type, scaling, fused, has_bias, has_lora, r = ctx.meta
         gy2 = gy.reshape(-1, N)
         if not gy2.is_contiguous():
             gy2 = gy2.contiguous()
         M = gy2.shape[0]
         gx = gA = gB = gbias = None
+        # with pre=h the input gradient is taken for h (through gelu'(h))
+        want_gx = ctx.needs_input_grad[15] if pre2 is not None else ctx.needs_input_grad[0]
+        peer = ctx.peer
+        peer_operand = (peer is not None and fused and M >= 256 and want_gx
+                        and not _in_kernel_ok(M, N, K))
+        if peer is not None and not peer_operand and want_gx:
+            packed, absmax = peer[0].gather(peer[1]).wait()
+        gelu_done = False
         if fused:
             E = _ext.ext()
             gy2 = gy2.to(torch.bfloat16)
             V = None
             if has_lora:
                 V = gy2 @ b_pad  # [M, 64] = dY·B (unscaled), skinny product: cuBLAS
-            if ctx.needs_input_grad[0]:
+            if want_gx:
                 gx = torch.empty(M, K, dtype=torch.bfloat16, device=gy2.device)
-                if _in_kernel_ok(M, N, K):  # dX = dY·W + V·(s·A), W decoded in the kernel
+                if pre2 is not None and _epi_ok(M, N) and not _in_kernel_ok(M, N, K):
+                    # dH = (dY·W + V·(s·A)) * gelu'(H) in the GEMM epilogue
+                    if peer_operand:
+                        w = peer[0].gather_dequant(peer[1], N, K)
+                    else:
+                        w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
+                    E.gemm_gelu(gy2, w, gx, pre2, True, V, a_pad)
+                    gelu_done = True
+                    del w
+                elif _in_kernel_ok(M, N, K):  # dX = dY·W + V·(s·A), W decoded in the kernel
                     E.gemm_nf4(gy2, packed, absmax, N, K, blocksize, QUANT_TYPE_ID[quant_type],
                                True, gx, V, a_pad)
                 elif M >= 256:  # W [N, K] read MN-major from the operand kernel's copy
-                    w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
+                    if peer_operand:  # straight from the owners' shards (one kernel)
+                        w = peer[0].gather_dequant(peer[1], N, K)
+                    else:
+                        w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
                     E.gemm_bf16_nn(gy2, w, gx, V, a_pad)
                     del w
                 else:  # short inputs: single-CTA kernel on the transposed operand
@@ -201,7 +263,7 @@ class NF4LinearFunction(torch.autograd.Function):
             Vf = None
             if has_lora:
                 Vf = (gy2.float() @ lora_B.float()) * scaling
-            if ctx.needs_input_grad[0]:
+            if want_gx:
                 w = _dequant_weight(packed, absmax, N, K, blocksize, quant_type, torch.float32)
                 g = gy2.float() @ w
                 if has_lora:
@@ -214,7 +276,43 @@ class NF4LinearFunction(torch.autograd.Function):
                     gB = (gy2.float().t() @ U.float()).to(lora_B.dtype)
         if has_bias and ctx.needs_input_grad[5]:
             gbias = gy2.float().sum(0)
-        return gx, None, None, gA, gB, gbias, None, None, None, None, None, None, None
+        if pre2 is not None:
+            g_pre = None
+            if gx is not None:
+                g_pre = gx if gelu_done else _gelu_grad_kernel(gx, pre2.view(gx.shape))
+            return (None, None, None, gA, gB, gbias, None, None, None, None, None, None, None,
+                    None, None, g_pre)
+        return (gx, None, None, gA, gB, gbias, None, None, None, None, None, None, None, None,
+                None, None)
+
+
+def _epi_ok(M: int, K: int) -> bool:
+    """Shapes the GELU-epilogue GEMMs take (pair kernel, 128-wide K stages)."""
+    return M >= 256 and K % 128 == 0
+
+
+def _gelu_kernel(h: torch.Tensor) -> torch.Tensor:
+    from .activations import gelu
+
+    with torch.no_grad():
+        return gelu(h)
+
+
+def _gelu_grad_kernel(g: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
+    if g.is_cuda and g.dtype == torch.bfloat16:
+        out = torch.empty_like(g)
+        _ext.ext().gelu_bwd(g.contiguous(), h.contiguous(), out)
+        return out
+    hf = h.float()
+    cdf = 0.5 * (1.0 + torch.erf(hf * 0.7071067811865476))
+    pdf = torch.exp(-0.5 * hf * hf) * 0.3989422804014327
+    return (g.float() * (cdf + hf * pdf)).to(g.dtype)
+
+
+def _peer_ag_ok(M: int, N: int, K: int, blocksize: int) -> bool:
+    from ..parallel.peer import ag_gemm_ok
+
+    return ag_gemm_ok(M, N, K, blocksize)
 
 
 def _pack_lora(A: torch.Tensor, B: torch.Tensor, scaling: float, out=None):
@@ -236,11 +334,13 @@ def _pack_lora(A: torch.Tensor, B: torch.Tensor, scaling: float, out=None):
 
 def nf4_linear(x, packed, absmax, out_features: int, in_features: int, bias=None,
                lora_A=None, lora_B=None, scaling: float = 1.0, blocksize: int = 64,
-               quant_type: str = "nf4", backend: str = "auto", lora_ops=None):
+               quant_type: str = "nf4", backend: str = "auto", lora_ops=None, peer=None,
+               act_out=None, pre=None):
     if backend == "auto":
         backend = "fused" if x.is_cuda else "torch"
     return NF4LinearFunction.apply(x, packed, absmax, lora_A, lora_B, bias, out_features,
-                                   in_features, blocksize, quant_type, scaling, backend, lora_ops)
+                                   in_features, blocksize, quant_type, scaling, backend, lora_ops,
+                                   peer, act_out, pre)
 
 
 class Linear4bit(nn.Module):
@@ -281,6 +381,7 @@ class Linear4bit(nn.Module):
             self.lora_B = None
         self._lora_ops = None
         self._lora_key = None
+        self._peer = None
 
     # -- weight management ---------------------------------------------------
     @classmethod
@@ -310,16 +411,30 @@ class Linear4bit(nn.Module):
     def set_nf4(self, packed: torch.Tensor, absmax: torch.Tensor, meta: Optional[dict] = None):
         self.weight_packed = packed.reshape(-1)
         self.weight_absmax = absmax.reshape(-1).float()
+        self._peer = None
+
+    def set_peer_source(self, pool, zq):
+        """Use the NF4 shards of ``zq`` where they live (every rank's piece in
+        ``pool``'s peer memory) instead of an assembled copy: the forward GEMM
+        gathers and dequantises them itself (one kernel)."""
+        self.weight_packed = None
+        self.weight_absmax = None
+        self._peer = (pool, zq)
 
     def clear_nf4(self):
         self.weight_packed = None
         self.weight_absmax = None
+        self._peer = None
 
     @property
     def has_nf4(self) -> bool:
-        return self.weight_packed is not None
+        return self.weight_packed is not None or getattr(self, "_peer", None) is not None
 
     def dequantized_weight(self, dtype=torch.float32) -> torch.Tensor:
+        if getattr(self, "_peer", None) is not None:
+            packed, absmax = self._peer[0].gather(self._peer[1]).wait()
+            return _dequant_weight(packed, absmax, self.out_features, self.in_features,
+                                   self.blocksize, self.quant_type, dtype)
         return _dequant_weight(self.weight_packed, self.weight_absmax, self.out_features,
                                self.in_features, self.blocksize, self.quant_type, dtype)
 
@@ -346,20 +461,37 @@ class Linear4bit(nn.Module):
         return self._lora_ops
 
     # -- forward -------------------------------------------------------------
-    def forward(self, x: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, act_out: Optional[str] = None,
+                pre: Optional[torch.Tensor] = None):
+        """``act_out="gelu"``: return ``(y, gelu(y))`` with ``gelu(y)`` carrying no
+        gradient of its own; ``pre=h``: ``x`` is ``gelu(h)`` and the gradient goes to
+        ``h`` (the two halves of a GELU MLP; see :class:`NF4LinearFunction`)."""
+        peer = getattr(self, "_peer", None)
+        if peer is not None:
+            ops = self._lora_operands() if (self.lora_r and x.is_cuda) else None
+            return nf4_linear(x, None, None, self.out_features, self.in_features, self.bias,
+                              self.lora_A, self.lora_B, self.scaling, self.blocksize,
+                              self.quant_type, self.backend, ops, peer, act_out, pre)
         if self.weight_packed is None:
             if self.weight.numel() == 0:
                 raise RuntimeError("Linear4bit has no weight: neither NF4 data nor a "
                                    "gathered full-precision weight is present")
+            if pre is not None:  # same gradient path as the fused form: through h
+                from .activations import gelu
+
+                x = gelu(pre)
             y = torch.nn.functional.linear(x, self.weight.to(x.dtype),
                                            None if self.bias is None else self.bias.to(x.dtype))
             if self.lora_r:
                 y = y + (x @ self.lora_A.t().to(x.dtype)) @ self.lora_B.t().to(x.dtype) * self.scaling
+            if act_out == "gelu":
+                return y, _gelu_kernel(y.detach())
             return y
         ops = self._lora_operands() if (self.lora_r and x.is_cuda) else None
         return nf4_linear(x, self.weight_packed, self.weight_absmax, self.out_features,
                           self.in_features, self.bias, self.lora_A, self.lora_B,
-                          self.scaling, self.blocksize, self.quant_type, self.backend, ops)
+                          self.scaling, self.blocksize, self.quant_type, self.backend, ops,
+                          None, act_out, pre)
 
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, "

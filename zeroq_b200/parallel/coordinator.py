@@ -253,12 +253,27 @@ class ZeroQParameter:
             return self._start_gather_fp32(group, async_op)
         if self.local_packed is None:
             raise RuntimeError(f"param_id={self.param_id} is not partitioned")
+        if self._use_peer_source():
+            # fused backend, 4-bit compute: nothing is gathered here; the module's
+            # GEMM reads every owner's shard itself (gather + dequant + GEMM kernel)
+            self.module.set_peer_source(self._peer_pool, self)
+            self.status = ZeroQParamStatus.AVAILABLE
+            return None
         self._pending = comm.gather_nf4(self, group=group, async_op=async_op)
         self.status = ZeroQParamStatus.INFLIGHT
         if not async_op:
             self.wait_gather()
             return None
         return self._pending
+
+    def _use_peer_source(self) -> bool:
+        if (getattr(self, "_peer_pool", None) is None or not self.compute_in_4bit
+                or self.param_name != "weight" or self.world_size == 1
+                or comm._backend(self) != "fused"):
+            return False
+        from ..ops.qlinear import Linear4bit
+
+        return isinstance(self.module, Linear4bit)
 
     def wait_gather(self):
         if self.status != ZeroQParamStatus.INFLIGHT:

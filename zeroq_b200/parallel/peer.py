@@ -18,7 +18,8 @@ buffers with ordinary loads and stores.
   with no padding, staging or unpad copies (reference
   ``src/coordinator.py:385-533``, ``src/hetero/zeroq_hetero.py:312-452``), and
   ``gather_dequant(zq)`` additionally expands to the bf16 GEMM operand in the
-  same kernel.
+  same kernel, and ``ag_gemm(zq, x)`` runs gather, dequantise and the tcgen05
+  GEMM ``x Wᵀ`` as ONE kernel (:func:`ag_gemm_pieces`).
 
 Cross-rank synchronisation is by epoch flags with bounded waits; a timeout
 leaves an error code that :meth:`PeerFlags.check` raises on the host.
@@ -148,6 +149,46 @@ def peer_flat_allocator(group):
     return alloc
 
 
+def ag_gemm_ok(M: int, N: int, K: int, blocksize: int) -> bool:
+    """Shapes the fused gather + dequantise + GEMM kernel takes."""
+    return M >= 256 and K % 128 == 0 and N % 8 == 0 and blocksize % 32 == 0
+
+
+def ag_gemm_pieces(x: torch.Tensor, packed_ptrs: List[int], packed_starts: List[int],
+                   absmax_ptrs: List[int], absmax_starts: List[int], N: int, K: int,
+                   blocksize: int, quant_type: str = "nf4", rank: int = 0,
+                   out: Optional[torch.Tensor] = None, wbuf: Optional[torch.Tensor] = None,
+                   extra: Optional[tuple] = None):
+    """``y [M, N] = x [M, K] · Wᵀ`` for a 4-bit ``W [N, K]`` whose flat packed
+    bytes and absmax are split into per-rank pieces (piece ``q`` starts at flat
+    index ``*_starts[q]`` and lives at device address ``*_ptrs[q]``: local memory
+    or a peer's through CUDA IPC).
+
+    One kernel (``csrc/gemm_sm100.cu``, gather mode of the pair GEMM): warps of
+    every CTA pull 8 x 1024 pieces of ``W`` over NVLink, dequantise them into
+    ``wbuf`` (bf16 ``[N, K]``) and publish a per-N-tile counter; the TMA producer
+    loads an N tile's B once its counter is full, and each rank starts on the N
+    tiles of its own rows.  ``extra = (x2 [M, 64], w2 [N, 64])`` adds the 64-wide
+    K slab of the LoRA up-projection.  Returns ``(y, wbuf)``; ``wbuf`` holds the
+    assembled bf16 weight afterwards.  Needs :func:`ag_gemm_ok`.
+    """
+    from ..ops.nf4 import QUANT_TYPE_ID
+
+    M = x.shape[0]
+    if not ag_gemm_ok(M, N, K, blocksize):
+        raise ValueError(f"ag_gemm: unsupported shape M={M} N={N} K={K} blocksize={blocksize}")
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    if wbuf is None:
+        wbuf = torch.empty(N, K, dtype=torch.bfloat16, device=x.device)
+    a2, b2 = extra if extra is not None else (None, None)
+    _ext.ext().ag_gemm_nf4(x, [int(p) for p in packed_ptrs], [int(v) for v in packed_starts],
+                           [int(p) for p in absmax_ptrs], [int(v) for v in absmax_starts],
+                           N * K // 2, -(-N * K // blocksize), int(rank), int(N), int(K),
+                           int(blocksize), QUANT_TYPE_ID[quant_type], wbuf, out, a2, b2)
+    return out, wbuf
+
+
 class PeerShardPool:
     """Every NF4 shard of a coordinator, in one peer buffer per rank.
 
@@ -224,6 +265,18 @@ class PeerShardPool:
                                        int(m["blocksize"]), QUANT_TYPE_ID[m["quant_type"]],
                                        bool(transpose), out)
         return out.view(cols, rows) if transpose else out.view(rows, cols)
+
+    def ag_gemm(self, zq, x: torch.Tensor, out: Optional[torch.Tensor] = None,
+                wbuf: Optional[torch.Tensor] = None, extra: Optional[tuple] = None):
+        """``x Wᵀ`` with ``W`` read from the owners' NF4 shards inside the GEMM
+        kernel (:func:`ag_gemm_pieces`); returns ``(y, wbuf)``."""
+        psrc, _, _ = self._segments(zq, 0)
+        asrc, _, _ = self._segments(zq, 1)
+        N, K = zq.original_shape
+        m = zq._quant_meta
+        return ag_gemm_pieces(x, psrc, list(zq.packed_plan.offsets), asrc,
+                              list(zq.absmax_plan.offsets), N, K, int(m["blocksize"]),
+                              m["quant_type"], self.rank, out, wbuf, extra)
 
     def sync_after_update(self):
         """Barrier after shards were re-quantised in place (training mode)."""
