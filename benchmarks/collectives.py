@@ -15,6 +15,13 @@ ranks (uniform split), activations ``X [M, K]`` bf16, output ``Y = X Wᵀ``.
     dequantise, cuBLAS GEMM.
 Roofline = max(2MNK / measured bf16 peak, K·N·0.5625·(W-1)/W / 770 GB/s).
 
+``master_gemm``: an fp32 weight ``W [N, K]`` sharded over the ranks as
+train-from-scratch masters (ceil split), activations ``X [M, K]`` bf16, ``Y = X bf16(W)ᵀ``.
+  * ours: ONE kernel gathers the fp32 master pieces over NVLink, casts them to bf16
+    into a local operand and runs the GEMM as each N tile's rows arrive;
+  * nccl: NCCL all-gather of the fp32 shards, cast, cuBLAS GEMM.
+Roofline = max(2MNK / measured bf16 peak, 4·K·N·(W-1)/W / 770 GB/s).
+
 ``rs_adamw``: a flat bf16 gradient of S bytes per rank, fp32 parameters and AdamW
 moments sharded 1/W.
   * ours: one peer kernel per rank sums its shard's slices from every peer, scales
@@ -142,6 +149,60 @@ def ag_gemm(args, rank, world):
         torch.cuda.empty_cache()
 
 
+def master_gemm(args, rank, world):
+    from zeroq_b200.parallel.peer import PeerBuffer, ag_gemm_f32_pieces
+
+    pk = peaks()
+    for KN in args.kn:
+        N = K = KN
+        chunk = (N * K + world - 1) // world
+        buf = PeerBuffer(chunk * 4, None)
+        g = torch.Generator(device="cuda").manual_seed(0)
+        full = torch.randn(N * K, device="cuda", generator=g) * 0.02
+        mine = buf.tensor(chunk, torch.float32)
+        mine.zero_()
+        lo, hi = rank * chunk, min((rank + 1) * chunk, N * K)
+        mine[: hi - lo].copy_(full[lo:hi])
+        torch.cuda.synchronize()
+        dist.barrier()
+        starts = [q * chunk for q in range(world)]
+        gathered = torch.empty(chunk * world, device="cuda")
+        wb = torch.empty(N, K, device="cuda", dtype=torch.bfloat16)
+        for M in args.m:
+            x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+            y = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+
+            def ours():
+                ag_gemm_f32_pieces(x, buf.ptrs, starts, chunk * world, N, K, rank, out=y, wbuf=wb)
+
+            def nccl():
+                dist.all_gather_into_tensor(gathered, mine)
+                w = gathered[: N * K].view(N, K).to(torch.bfloat16)
+                torch.matmul(x, w.t(), out=y)
+
+            t_ours = timed(ours, args.iters, args.warmup)
+            y_ours = y.clone()
+            t_nccl = timed(nccl, args.iters, args.warmup)
+            err = (y_ours.float() - y.float()).abs().max().item()
+            flops = 2.0 * M * N * K
+            t_comp = flops / (pk["bf16_tflops"] * 1e12) * 1e3
+            t_link = K * N * 4.0 * (world - 1) / world / (LINK_GBS * 1e9) * 1e3
+            roof = max(t_comp, t_link)
+            if rank == 0:
+                print(json.dumps({
+                    "op": "master_gather_cast_gemm", "n_gpus": world, "M": M, "K": K, "N": N,
+                    "ours_ms": round(t_ours, 4), "nccl_cublas_ms": round(t_nccl, 4),
+                    "speedup": round(t_nccl / t_ours, 3),
+                    "roofline_ms": round(roof, 4), "bound": "compute" if t_comp >= t_link else "nvlink",
+                    "frac_of_roofline": round(roof / t_ours, 3),
+                    "max_abs_diff_vs_nccl": round(err, 4)}), flush=True)
+            del x, y
+        torch.cuda.synchronize()
+        dist.barrier()
+        buf.close()
+        torch.cuda.empty_cache()
+
+
 def rs_adamw(args, rank, world):
     from zeroq_b200.ops.optim import adamw_step
     from zeroq_b200.parallel.peer import PeerBuffer, PeerFlags, PeerReduceScatterAdamW
@@ -214,7 +275,7 @@ def rs_adamw(args, rank, world):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["ag_gemm", "rs_adamw"], required=True)
+    ap.add_argument("--op", choices=["ag_gemm", "master_gemm", "rs_adamw"], required=True)
     ap.add_argument("--kn", type=int, nargs="+", default=[4096, 8192, 12288])
     ap.add_argument("--m", type=int, nargs="+", default=[1024, 4096, 16384])
     ap.add_argument("--sizes-mb", type=float, nargs="+", default=[1, 16, 256, 1024])
@@ -229,6 +290,8 @@ def main():
     try:
         if args.op == "ag_gemm":
             ag_gemm(args, rank, world)
+        elif args.op == "master_gemm":
+            master_gemm(args, rank, world)
         else:
             rs_adamw(args, rank, world)
     finally:

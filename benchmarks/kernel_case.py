@@ -86,7 +86,7 @@ def _report(name, ms, byts=None, flops=None, extra=""):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["gemm", "attention", "attn_trace", "attn_bwd_trace",
-                                     "nf4_operand", "rmsnorm", "gelu", "q4gemm"])
+                                     "nf4_operand", "rmsnorm", "gelu", "q4gemm", "gelu_gemm"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=3072)
@@ -125,6 +125,30 @@ def main():
                 extra=f"status {E.gemm_status(0)}")
         if a.cublas:
             _report(f"cublas {a.m}x{a.n}x{a.k} nn={a.nn}", _time(ref, a.reps), flops=fl)
+    elif a.case == "gelu_gemm":
+        # GELU MLP halves: up-projection with the GELU-output epilogue vs GEMM + GELU
+        # kernel, and the down-projection input gradient with the GELU-gradient
+        # epilogue vs GEMM + GELU-backward kernel (M x N output, K reduction)
+        x = torch.randn(a.m, a.k, device=dev, dtype=torch.bfloat16)
+        w = (torch.randn(a.n, a.k, device=dev) * 0.05).to(torch.bfloat16)
+        wd = (torch.randn(a.k, a.n, device=dev) * 0.05).to(torch.bfloat16)
+        h = torch.empty(a.m, a.n, device=dev, dtype=torch.bfloat16)
+        act = torch.empty_like(h)
+        dh = torch.empty_like(h)
+        fl = 2.0 * a.m * a.n * a.k
+        _report("gemm tn", _time(lambda: E.gemm_bf16_tn(x, w, h), a.reps), flops=fl)
+        _report("gemm tn + gelu_fwd kernel",
+                _time(lambda: (E.gemm_bf16_tn(x, w, h), E.gelu_fwd(h, act)), a.reps), flops=fl)
+        _report("gemm tn, GELU-output epilogue",
+                _time(lambda: E.gemm_gelu(x, w, h, act, False, None, None), a.reps, a.profile),
+                flops=fl)
+        _report("gemm nn", _time(lambda: E.gemm_bf16_nn(x, wd, dh, None, None), a.reps), flops=fl)
+        _report("gemm nn + gelu_bwd kernel",
+                _time(lambda: (E.gemm_bf16_nn(x, wd, act, None, None), E.gelu_bwd(act, h, dh)),
+                      a.reps), flops=fl)
+        _report("gemm nn, GELU-gradient epilogue",
+                _time(lambda: E.gemm_gelu(x, wd, dh, h, True, None, None), a.reps, a.profile),
+                flops=fl, extra=f"status {E.gemm_status(0)}")
     elif a.case == "q4gemm":
         # C[M, N] = X[M, K] · op(W) with W 4-bit: in-kernel decode vs operand kernel + GEMM
         from zeroq_b200.ops.nf4 import quantize_4bit

@@ -67,6 +67,9 @@ void ag_gemm_nf4(at::Tensor a, std::vector<int64_t> psrc, std::vector<int64_t> p
                  int64_t absmax_total, int64_t rank, int64_t N, int64_t K, int64_t blocksize,
                  int64_t quant_type, at::Tensor wbuf, at::Tensor c, c10::optional<at::Tensor> a2,
                  c10::optional<at::Tensor> b2);
+void ag_gemm_f32(at::Tensor a, std::vector<int64_t> src, std::vector<int64_t> starts, int64_t total,
+                 int64_t rank, int64_t N, int64_t K, at::Tensor wbuf, at::Tensor c,
+                 c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2);
 void gemm_gelu(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor aux, bool b_mn,
                c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2);
 void plan_gather_dequant(std::vector<int64_t> psrc, std::vector<int64_t> pstarts,
@@ -125,6 +128,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rs_adamw", &rs_adamw);
   m.def("plan_gather", &plan_gather);
   m.def("plan_gather_dequant", &plan_gather_dequant);
+  m.def("ag_gemm_f32", &ag_gemm_f32, "gather of fp32 pieces + bf16 cast + tcgen05 GEMM in one kernel",
+        pybind11::arg("a"), pybind11::arg("src"), pybind11::arg("starts"), pybind11::arg("total"),
+        pybind11::arg("rank"), pybind11::arg("N"), pybind11::arg("K"), pybind11::arg("wbuf"),
+        pybind11::arg("c"), pybind11::arg("a2") = pybind11::none(), pybind11::arg("b2") = pybind11::none());
   m.def("gemm_gelu", &gemm_gelu, "tcgen05 GEMM with the GELU output / GELU-gradient epilogue",
         pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("c"), pybind11::arg("aux"),
         pybind11::arg("b_mn"), pybind11::arg("a2") = pybind11::none(),

@@ -73,7 +73,7 @@ struct GemmArgs {
   AgSource ag;
   __nv_bfloat16* ag_w;
   int* ag_sync;
-  int ag_rot, ag_kchunks;
+  int ag_rot, ag_kchunks, ag_cols;  // ag_cols: columns per gather item
   // epilogue input (kEpiGeluBwd): the pre-activation h [M, N], row pitch epi_ld
   const __nv_bfloat16* epi_src;
   int64_t epi_ld;
@@ -575,8 +575,11 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       int tn = p + args.ag_rot;
       if (tn >= args.tiles_n) tn -= args.tiles_n;
       const int rg = j / args.ag_kchunks, kc = j - rg * args.ag_kchunks;
-      ag_item(args.ag, lut, args.N, args.K, args.q_block, tn * BN + rg * kAgRows, kc * kAgCols,
-              args.ag_w, lane);
+      if (args.ag.kind == kAgF32)
+        ag_item_f32(args.ag, args.N, args.K, tn * BN + rg * kAgRows, kc * args.ag_cols, args.ag_w, lane);
+      else
+        ag_item(args.ag, lut, args.N, args.K, args.q_block, tn * BN + rg * kAgRows, kc * args.ag_cols,
+                args.ag_w, lane);
       fence_proxy_async_global();
       __threadfence();
       __syncwarp();
@@ -1357,11 +1360,11 @@ static int* ag_sync_buffer(int device, cudaStream_t stream) {
 // rank's own memory or CUDA IPC mappings of the peers').  One kernel gathers
 // and dequantises W into wbuf (bf16 [N, K], left assembled for the caller) and
 // multiplies it with tcgen05, each N tile starting as soon as its rows are in.
-void ag_gemm_nf4(at::Tensor a, std::vector<int64_t> psrc, std::vector<int64_t> pstarts,
-                 std::vector<int64_t> asrc, std::vector<int64_t> astarts, int64_t packed_total,
-                 int64_t absmax_total, int64_t rank, int64_t N, int64_t K, int64_t blocksize,
-                 int64_t quant_type, at::Tensor wbuf, at::Tensor c, c10::optional<at::Tensor> a2,
-                 c10::optional<at::Tensor> b2) {
+static void ag_gemm_impl(int kind, at::Tensor a, std::vector<int64_t> psrc, std::vector<int64_t> pstarts,
+                         std::vector<int64_t> asrc, std::vector<int64_t> astarts, int64_t packed_total,
+                         int64_t absmax_total, int64_t rank, int64_t N, int64_t K, int64_t blocksize,
+                         int64_t quant_type, at::Tensor wbuf, at::Tensor c, c10::optional<at::Tensor> a2,
+                         c10::optional<at::Tensor> b2) {
   const int world = (int)psrc.size();
   TORCH_CHECK(world >= 1 && world <= kAgMaxRanks && (int)pstarts.size() == world &&
                   (int)asrc.size() == world && (int)astarts.size() == world,
@@ -1376,10 +1379,14 @@ void ag_gemm_nf4(at::Tensor a, std::vector<int64_t> psrc, std::vector<int64_t> p
   TORCH_CHECK(a.size(1) == K && c.size(0) == M && c.size(1) == N, "ag_gemm_nf4: shapes");
   TORCH_CHECK(M >= 2 * kBM && M < (1LL << 31) && N < (1LL << 31), "ag_gemm_nf4: needs M >= 256");
   TORCH_CHECK(K % 128 == 0 && N % 8 == 0, "ag_gemm_nf4: needs K % 128 == 0 and N % 8 == 0");
-  TORCH_CHECK(blocksize > 0 && blocksize % 32 == 0, "ag_gemm_nf4: block size a multiple of 32");
-  TORCH_CHECK(quant_type == 0 || quant_type == 1, "ag_gemm_nf4: quant_type 0 (nf4) or 1 (fp4)");
-  TORCH_CHECK(packed_total * 2 == N * K && absmax_total * blocksize >= N * K,
-              "ag_gemm_nf4: packed/absmax totals do not cover W");
+  if (kind == kAgNf4) {
+    TORCH_CHECK(blocksize > 0 && blocksize % 32 == 0, "ag_gemm_nf4: block size a multiple of 32");
+    TORCH_CHECK(quant_type == 0 || quant_type == 1, "ag_gemm_nf4: quant_type 0 (nf4) or 1 (fp4)");
+    TORCH_CHECK(packed_total * 2 == N * K && absmax_total * blocksize >= N * K,
+                "ag_gemm_nf4: packed/absmax totals do not cover W");
+  } else {
+    TORCH_CHECK(packed_total >= N * K, "ag_gemm_f32: the pieces do not cover W");
+  }
   TORCH_CHECK(wbuf.is_contiguous() && wbuf.numel() == N * K &&
                   (reinterpret_cast<uintptr_t>(wbuf.data_ptr()) & 15) == 0,
               "ag_gemm_nf4: W buffer must be contiguous, N*K elements, 16-byte aligned");
@@ -1391,8 +1398,10 @@ void ag_gemm_nf4(at::Tensor a, std::vector<int64_t> psrc, std::vector<int64_t> p
     TORCH_CHECK(pstarts[q] >= 0 && pstarts[q] <= pend && astarts[q] >= 0 && astarts[q] <= aend,
                 "ag_gemm_nf4: starts must be non-decreasing");
     TORCH_CHECK(pend == pstarts[q] || psrc[q] != 0, "ag_gemm_nf4: null shard pointer");
-    TORCH_CHECK(aend == astarts[q] || (asrc[q] != 0 && (asrc[q] & 3) == 0),
+    TORCH_CHECK(kind == kAgF32 || aend == astarts[q] || (asrc[q] != 0 && (asrc[q] & 3) == 0),
                 "ag_gemm_nf4: absmax pointers must be 4-byte aligned");
+    TORCH_CHECK(kind == kAgNf4 || pend == pstarts[q] || (psrc[q] & 3) == 0,
+                "ag_gemm_f32: fp32 pieces must be 4-byte aligned");
   }
   const at::cuda::CUDAGuard guard(a.device());
   const int dev = a.get_device();
@@ -1412,6 +1421,7 @@ void ag_gemm_nf4(at::Tensor a, std::vector<int64_t> psrc, std::vector<int64_t> p
   args.q_block = (int)blocksize;
   args.q_type = (int)quant_type;
   args.ag.world = world;
+  args.ag.kind = kind;
   for (int q = 0; q < kAgMaxRanks; ++q) {
     const bool in = q < world;
     args.ag.packed[q] = in ? reinterpret_cast<const uint8_t*>(psrc[q]) : nullptr;
@@ -1422,10 +1432,12 @@ void ag_gemm_nf4(at::Tensor a, std::vector<int64_t> psrc, std::vector<int64_t> p
   args.ag.pstart[kAgMaxRanks] = packed_total;
   args.ag.astart[kAgMaxRanks] = absmax_total;
   args.ag_w = reinterpret_cast<__nv_bfloat16*>(wbuf.data_ptr<at::BFloat16>());
-  args.ag_kchunks = (int)((K + kAgCols - 1) / kAgCols);
+  args.ag_cols = kind == kAgF32 ? kAgColsF32 : kAgCols;
+  args.ag_kchunks = (int)((K + args.ag_cols - 1) / args.ag_cols);
   {  // start at the N tile holding this rank's first own row
     const int64_t pend = rank + 1 < world ? pstarts[rank + 1] : packed_total;
-    const int64_t first_row = pend > pstarts[rank] ? (2 * pstarts[rank]) / K : 0;
+    const int64_t first_elem = kind == kAgF32 ? pstarts[rank] : 2 * pstarts[rank];
+    const int64_t first_row = pend > pstarts[rank] ? std::min<int64_t>(first_elem / K, N - 1) : 0;
     args.ag_rot = (int)std::min<int64_t>(first_row / bn, args.tiles_n - 1);
   }
 
@@ -1450,6 +1462,25 @@ void ag_gemm_nf4(at::Tensor a, std::vector<int64_t> psrc, std::vector<int64_t> p
   const CUtensorMap tc = make_tmap_store_bf16(c.data_ptr(), M, N, c.stride(0));
   if (bn == 256) launch_gemm_pair<256, 3, 2, false, false, true>(ta, tb, ta2, tb2, tc, args, stream, sms);
   else launch_gemm_pair<128, 4, 2, false, false, true>(ta, tb, ta2, tb2, tc, args, stream, sms);
+}
+
+void ag_gemm_nf4(at::Tensor a, std::vector<int64_t> psrc, std::vector<int64_t> pstarts,
+                 std::vector<int64_t> asrc, std::vector<int64_t> astarts, int64_t packed_total,
+                 int64_t absmax_total, int64_t rank, int64_t N, int64_t K, int64_t blocksize,
+                 int64_t quant_type, at::Tensor wbuf, at::Tensor c, c10::optional<at::Tensor> a2,
+                 c10::optional<at::Tensor> b2) {
+  ag_gemm_impl(kAgNf4, a, psrc, pstarts, asrc, astarts, packed_total, absmax_total, rank, N, K,
+               blocksize, quant_type, wbuf, c, a2, b2);
+}
+
+// The same with W [N, K] held as fp32 pieces (flat elements [starts[q],
+// starts[q+1]) at src[q]; total >= N*K, a zero-padded tail allowed): gather,
+// cast to bf16 into wbuf and multiply in one kernel.
+void ag_gemm_f32(at::Tensor a, std::vector<int64_t> src, std::vector<int64_t> starts, int64_t total,
+                 int64_t rank, int64_t N, int64_t K, at::Tensor wbuf, at::Tensor c,
+                 c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2) {
+  std::vector<int64_t> none(src.size(), 0);
+  ag_gemm_impl(kAgF32, a, src, starts, none, none, total, 0, rank, N, K, 64, 0, wbuf, c, a2, b2);
 }
 
 // NF4 weight [rows, cols] -> bf16 [rows, cols] (transpose=false) or [cols, rows].

@@ -15,6 +15,12 @@
 // owns 32 consecutive columns (16 packed bytes, inside one absmax block when
 // blocksize % 32 == 0) of each of the 8 rows, issues all 8 row loads before
 // decoding any, and writes 8 x 64 contiguous bytes of bf16.
+//
+// The same machinery gathers fp32 master weights split over the ranks (the
+// train-from-scratch layout: rank q holds flat elements [pstart[q],
+// pstart[q+1]), reference src/coordinator.py:606-611 all-gathers them) and
+// casts them to bf16: items of 8 rows x 256 columns, 8 consecutive fp32 per
+// lane and row (two 16-byte loads), one 16-byte bf16 store.
 #pragma once
 
 #include "common.cuh"
@@ -23,14 +29,18 @@ namespace zq {
 
 constexpr int kAgMaxRanks = 8;
 constexpr int kAgRows = 8;          // rows of W per gather item
-constexpr int kAgCols = 1024;       // columns of W per gather item (32 per lane)
+constexpr int kAgCols = 1024;       // columns of W per 4-bit gather item (32 per lane)
+constexpr int kAgColsF32 = 256;     // columns of W per fp32 gather item (8 per lane)
+
+enum AgKind { kAgNf4 = 0, kAgF32 = 1 };
 
 struct AgSource {
-  const uint8_t* packed[kAgMaxRanks];
+  const uint8_t* packed[kAgMaxRanks];  // kAgF32: the fp32 pieces
   const float* absmax[kAgMaxRanks];
-  int64_t pstart[kAgMaxRanks + 1];  // pstart[world] = total packed bytes
+  int64_t pstart[kAgMaxRanks + 1];  // pstart[world] = total packed bytes (kAgF32: elements)
   int64_t astart[kAgMaxRanks + 1];  // astart[world] = total absmax entries
   int world;
+  int kind;                         // AgKind
 };
 
 // Piece of flat index idx: the last rank whose start is <= idx (ranks with an
@@ -141,6 +151,62 @@ __device__ __forceinline__ void ag_item(const AgSource& s, const float* lut, int
     if (i < rows_here)
       ag_decode_store32(raw[i], am[i], lut,
                         reinterpret_cast<uint4*>(w_out + (int64_t)(r0 + i) * K + k));
+  }
+}
+
+// Rows [r0, r0 + 8) x columns [k0, k0 + 256) of the fp32 W (clipped to N and
+// K) cast to bf16 into w_out [N, K].  Needs K % 8 == 0.
+__device__ __forceinline__ void ag_item_f32(const AgSource& s, int N, int K, int r0, int k0,
+                                            __nv_bfloat16* w_out, int lane) {
+  const int rows_here = min(kAgRows, N - r0);
+  const int cols_here = min(kAgColsF32, K - k0);
+  const int64_t e_first = (int64_t)r0 * K + k0;
+  const int64_t e_end = (int64_t)(r0 + rows_here - 1) * K + k0 + cols_here;  // exclusive
+  const AgPiece pp = ag_packed_piece(s, e_first);
+  const bool fast = e_end <= pp.end &&
+                    ((reinterpret_cast<uintptr_t>(pp.base) - (uintptr_t)(pp.start * 4)) & 15) == 0;
+  const int k = k0 + lane * 8;
+  if (k >= K) return;
+  if (!fast) {
+#pragma unroll 1
+    for (int i = 0; i < rows_here; ++i) {
+      const int64_t e = (int64_t)(r0 + i) * K + k;
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const AgPiece a = ag_packed_piece(s, e + 2 * j);
+        const AgPiece b = ag_packed_piece(s, e + 2 * j + 1);
+        o[j] = pack_bf16x2(reinterpret_cast<const float*>(a.base)[e + 2 * j - a.start],
+                           reinterpret_cast<const float*>(b.base)[e + 2 * j + 1 - b.start]);
+      }
+      *reinterpret_cast<uint4*>(w_out + (int64_t)(r0 + i) * K + k) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    return;
+  }
+  const float* fbase = reinterpret_cast<const float*>(pp.base) - pp.start;
+  // two passes of 4 rows: 8 loads (4 KB per warp) in flight per pass
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    uint4 lo[4], hi[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (half * 4 + i < rows_here) {
+        const float* src = fbase + (int64_t)(r0 + half * 4 + i) * K + k;
+        lo[i] = ld_v4_no_l1(src);
+        hi[i] = ld_v4_no_l1(src + 4);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (half * 4 + i < rows_here) {
+        const uint4 o = make_uint4(
+            pack_bf16x2(__uint_as_float(lo[i].x), __uint_as_float(lo[i].y)),
+            pack_bf16x2(__uint_as_float(lo[i].z), __uint_as_float(lo[i].w)),
+            pack_bf16x2(__uint_as_float(hi[i].x), __uint_as_float(hi[i].y)),
+            pack_bf16x2(__uint_as_float(hi[i].z), __uint_as_float(hi[i].w)));
+        *reinterpret_cast<uint4*>(w_out + (int64_t)(r0 + half * 4 + i) * K + k) = o;
+      }
+    }
   }
 }
 

@@ -747,3 +747,32 @@ def test_fused_gelu_mlp_matches_unfused(cuda, lora_r):
     assert torch.equal(grads[0], grads2[0])
     for g1, g2 in zip(grads[1:], grads2[1:]):
         torch.testing.assert_close(g1, g2, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("M,N,K,starts_frac", [
+    (512, 384, 512, [0.0, 0.5]),
+    (768, 1000, 1536, [0.0, 0.3, 0.31, 0.8]),   # uneven pieces, odd element starts
+    (300, 520, 384, [0.0, 0.0, 0.6]),           # an empty piece, ragged M
+])
+def test_ag_gemm_f32_master_pieces_match_cast_then_gemm(cuda, M, N, K, starts_frac):
+    """Gather of fp32 master pieces + bf16 cast + GEMM in one kernel against the
+    cast weight and the same GEMM (bit-identical), for every rank's rotation, with
+    a zero-padded tail on the last piece."""
+    from zeroq_b200.parallel.peer import ag_gemm_f32_pieces
+
+    torch.manual_seed(8)
+    W = torch.randn(N, K, device=cuda) * 0.05
+    flat = torch.cat([W.reshape(-1), torch.zeros(37, device=cuda)])   # padded tail
+    starts = [int(f * N * K) | (1 if 0 < f < 0.5 else 0) for f in starts_frac]
+    starts[0] = 0
+    pieces, ptrs = _split_pieces(flat, starts)
+    x = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    wb = W.to(torch.bfloat16)
+    ref = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    _ext.ext().gemm_bf16_tn(x, wb, ref)
+    for rank in range(len(starts)):
+        y, wbuf = ag_gemm_f32_pieces(x, ptrs, starts, flat.numel(), N, K, rank)
+        torch.cuda.synchronize()
+        _status_ok(cuda)
+        assert torch.equal(wbuf, wb)
+        assert torch.equal(y, ref)

@@ -190,6 +190,56 @@ def w_peer_ag_gemm(rank, world):
         pool.close()
 
 
+def w_peer_master_gemm(rank, world):
+    """Train-from-scratch: a Linear4bit whose fp32 masters sit in peer memory runs
+    its forward as the one-kernel gather + cast + GEMM and reduce-scatters dW into
+    the master shard; against the NCCL all-gather path of an identical model."""
+    import zeroq_b200 as zq
+    from zeroq_b200.ops.qlinear import Linear4bit
+    from zeroq_b200.parallel.peer import PeerMasterPool
+
+    def build():
+        torch.manual_seed(3)
+        m = torch.nn.Sequential(Linear4bit(512, 384, device="cuda"), Linear4bit(384, 256, device="cuda"))
+        for lin in m:
+            lin.weight = torch.nn.Parameter(torch.randn(lin.out_features, lin.in_features,
+                                                        device="cuda") * 0.05)
+        coord = zq.ZeroQCoordinator(zq.ZeroQTrainConfig(exclude_modules=[]))
+        zq.ZeroQModuleWrapper(m, coord).partition()
+        return m, coord
+
+    m1, c1 = build()
+    pool = PeerMasterPool(c1)
+    m2, c2 = build()
+    torch.manual_seed(10 + rank)
+    x = torch.randn(300, 512, device="cuda").to(torch.bfloat16)
+    outs = []
+    for m in (m1, m2):
+        xi = x.clone().requires_grad_(True)
+        y = m(xi)
+        y.float().square().sum().backward()
+        outs.append((y.detach(), xi.grad))
+    torch.testing.assert_close(outs[0][0].float(), outs[1][0].float(), rtol=2e-2, atol=2e-2)
+    torch.testing.assert_close(outs[0][1].float(), outs[1][1].float(), rtol=2e-2, atol=2e-2)
+    for p1, p2 in zip(c1._params.values(), c2._params.values()):
+        if p1.param_name != "weight":
+            continue
+        g1, g2 = p1.master_shard.grad, p2.master_shard.grad
+        assert g1 is not None and g2 is not None
+        torch.testing.assert_close(g1, g2, rtol=2e-2, atol=2e-3 * g2.abs().max().item())
+    # an in-place optimizer update of the peer-resident masters is seen by the next forward
+    with torch.no_grad():
+        for p1 in c1._params.values():
+            if p1.param_name == "weight":
+                p1.master_shard.mul_(0.5)
+    pool.sync_after_update()
+    y_half = m1(x)
+    assert (y_half.float() - 0.25 * outs[0][0].float()).abs().max().item() < \
+        2e-2 * outs[0][0].float().abs().max().item() + 1e-2
+    torch.cuda.synchronize()
+    pool.close()
+
+
 def test_fused_reduce_scatter_adamw_matches_nccl():
     _run("w_fused_adamw", 2)
 
@@ -200,6 +250,10 @@ def test_peer_gather_and_gather_dequant_match_nccl():
 
 def test_peer_ag_gemm_one_kernel_matches_assembled():
     _run("w_peer_ag_gemm", 2)
+
+
+def test_peer_master_gather_gemm_matches_nccl_path():
+    _run("w_peer_master_gemm", 2)
 
 
 def test_peer_wait_times_out_with_error_status(cuda):

@@ -315,6 +315,67 @@ def _peer_ag_ok(M: int, N: int, K: int, blocksize: int) -> bool:
     return ag_gemm_ok(M, N, K, blocksize)
 
 
+class MasterGatherLinearFunction(torch.autograd.Function):
+    """``y = x · bf16(W)ᵀ (+ bias)`` for a trainable weight whose fp32 masters are
+    sharded over the ranks (train-from-scratch): the forward gathers every rank's
+    master shard over NVLink, casts it to bf16 and multiplies in one kernel
+    (:meth:`~zeroq_b200.parallel.peer.PeerMasterPool.ag_gemm`); the backward
+    reuses the assembled bf16 weight for ``dX``, forms ``dW = dYᵀ X`` in fp32 and
+    reduce-scatters it straight into the master shard's gradient (the reference
+    all-gathers the fp32 masters and reduce-scatters the gradient in a tensor
+    hook, ``src/coordinator.py:606-611`` and ``:349-359``).
+    """
+
+    @staticmethod
+    def forward(ctx, x, master_shard, bias, pool, zq):
+        N, K = zq.original_shape
+        x2 = x.reshape(-1, K)
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        y, wbuf = pool.ag_gemm(zq, x2)
+        if bias is not None:
+            y = y + bias.to(y.dtype)
+        ctx.save_for_backward(x2, wbuf)
+        ctx.meta = (x.shape, N, K, bias is not None)
+        ctx.zq = zq
+        return y.view(*x.shape[:-1], N)
+
+    @staticmethod
+    def backward(ctx, gy):
+        from ..parallel.gradient_sync import reduce_scatter_grads
+
+        x2, wbuf = ctx.saved_tensors
+        shp, N, K, has_bias = ctx.meta
+        zq = ctx.zq
+        gy2 = gy.reshape(-1, N).to(torch.bfloat16).contiguous()
+        M = gy2.shape[0]
+        E = _ext.ext()
+        gx = gshard = gbias = None
+        if ctx.needs_input_grad[0]:
+            if M >= 256 and N % 64 == 0 and K % 64 == 0:
+                gx = torch.empty(M, K, dtype=torch.bfloat16, device=gy2.device)
+                E.gemm_bf16_nn(gy2, wbuf, gx, None, None)
+            else:
+                gx = gy2 @ wbuf
+            gx = gx.view(*shp[:-1], K)
+        if ctx.needs_input_grad[1]:
+            gW = torch.empty(N, K, dtype=torch.float32, device=gy2.device)
+            E.matmul_accum_f32(gy2.t(), x2, gW, 1.0, 0.0)
+            gshard = reduce_scatter_grads(gW, zq.world_size, zq.rank, group=zq.process_group)
+            gshard = gshard[: zq.master_shard.numel()].to(zq.master_shard.dtype)
+        if has_bias and ctx.needs_input_grad[2]:
+            gbias = gy2.float().sum(0)
+        return gx, gshard, gbias, None, None
+
+
+def _master_fused_ok(x: torch.Tensor, N: int, K: int) -> bool:
+    from ..parallel.peer import ag_gemm_ok
+
+    M = x.numel() // K if x.numel() else 0
+    return (x.is_cuda and x.dtype == torch.bfloat16 and ag_gemm_ok(M, N, K, 32)
+            and N % 64 == 0 and K % 64 == 0)
+
+
 def _pack_lora(A: torch.Tensor, B: torch.Tensor, scaling: float, out=None):
     """``(s·A padded to [64, K], B padded to [N, 64])`` in bf16; ``out`` reuses buffers
     whose padding is already zero."""
@@ -382,6 +443,7 @@ class Linear4bit(nn.Module):
         self._lora_ops = None
         self._lora_key = None
         self._peer = None
+        self._master = None
 
     # -- weight management ---------------------------------------------------
     @classmethod
@@ -426,6 +488,15 @@ class Linear4bit(nn.Module):
         self.weight_absmax = None
         self._peer = None
 
+    def set_master_source(self, pool, zq):
+        """Train-from-scratch: read the weight from every rank's fp32 master shard
+        inside the forward GEMM (:class:`MasterGatherLinearFunction`) instead of an
+        all-gathered full-precision copy."""
+        self._master = (pool, zq)
+
+    def clear_master_source(self):
+        self._master = None
+
     @property
     def has_nf4(self) -> bool:
         return self.weight_packed is not None or getattr(self, "_peer", None) is not None
@@ -466,6 +537,15 @@ class Linear4bit(nn.Module):
         """``act_out="gelu"``: return ``(y, gelu(y))`` with ``gelu(y)`` carrying no
         gradient of its own; ``pre=h``: ``x`` is ``gelu(h)`` and the gradient goes to
         ``h`` (the two halves of a GELU MLP; see :class:`NF4LinearFunction`)."""
+        master = getattr(self, "_master", None)
+        if master is not None:
+            pool, zq = master
+            if (act_out is None and pre is None and not self.lora_r
+                    and _master_fused_ok(x, self.out_features, self.in_features)):
+                return MasterGatherLinearFunction.apply(x, zq.master_shard, self.bias, pool, zq)
+            # off the fused path: the regular fp32 all-gather into self.weight
+            self._master = None
+            zq._start_gather_fp32(zq.process_group, async_op=False)
         peer = getattr(self, "_peer", None)
         if peer is not None:
             ops = self._lora_operands() if (self.lora_r and x.is_cuda) else None

@@ -250,6 +250,11 @@ class ZeroQParameter:
             return self._pending
         group = group if group is not None else self.process_group
         if self._is_fp32_mode():
+            if self._use_master_source():
+                # the module's GEMM gathers and casts the fp32 masters itself
+                self.module.set_master_source(self._peer_master_pool, self)
+                self.status = ZeroQParamStatus.AVAILABLE
+                return None
             return self._start_gather_fp32(group, async_op)
         if self.local_packed is None:
             raise RuntimeError(f"param_id={self.param_id} is not partitioned")
@@ -265,6 +270,14 @@ class ZeroQParameter:
             self.wait_gather()
             return None
         return self._pending
+
+    def _use_master_source(self) -> bool:
+        if (getattr(self, "_peer_master_pool", None) is None or self.param_name != "weight"
+                or self.world_size == 1):
+            return False
+        from ..ops.qlinear import Linear4bit
+
+        return isinstance(self.module, Linear4bit)
 
     def _use_peer_source(self) -> bool:
         if (getattr(self, "_peer_pool", None) is None or not self.compute_in_4bit
@@ -368,6 +381,8 @@ class ZeroQParameter:
             dtype, rg = torch.float32, True
         else:
             device, dtype, rg = self.param.device, self.original_dtype, self.param.requires_grad
+        if isinstance(self.module, Linear4bit) and self.param_name == "weight":
+            self.module.clear_master_source()
         if (self.compute_in_4bit and isinstance(self.module, Linear4bit)
                 and self.param_name == "weight" and not self._is_fp32_mode()):
             self.module.clear_nf4()

@@ -20,6 +20,11 @@ buffers with ordinary loads and stores.
   ``gather_dequant(zq)`` additionally expands to the bf16 GEMM operand in the
   same kernel, and ``ag_gemm(zq, x)`` runs gather, dequantise and the tcgen05
   GEMM ``x Wᵀ`` as ONE kernel (:func:`ag_gemm_pieces`).
+* :class:`PeerMasterPool` - the fp32 master shards of a train-from-scratch
+  coordinator in one peer buffer per rank (the optimizer updates them in place);
+  ``ag_gemm(zq, x)`` gathers the masters, casts them to bf16 and multiplies in
+  one kernel, replacing the reference's fp32 all-gather before the layer
+  (``src/coordinator.py:606-611``).
 
 Cross-rank synchronisation is by epoch flags with bounded waits; a timeout
 leaves an error code that :meth:`PeerFlags.check` raises on the host.
@@ -189,6 +194,26 @@ def ag_gemm_pieces(x: torch.Tensor, packed_ptrs: List[int], packed_starts: List[
     return out, wbuf
 
 
+def ag_gemm_f32_pieces(x: torch.Tensor, ptrs: List[int], starts: List[int], total: int, N: int,
+                       K: int, rank: int = 0, out: Optional[torch.Tensor] = None,
+                       wbuf: Optional[torch.Tensor] = None, extra: Optional[tuple] = None):
+    """``y = x · bf16(W)ᵀ`` for an fp32 ``W [N, K]`` split into per-rank pieces
+    (flat elements ``[starts[q], starts[q+1])`` at ``ptrs[q]``; ``total`` >= N*K
+    counts a zero-padded tail): gather, cast and GEMM in one kernel, like
+    :func:`ag_gemm_pieces`.  Returns ``(y, wbuf)`` with ``wbuf`` = bf16 ``W``."""
+    M = x.shape[0]
+    if not ag_gemm_ok(M, N, K, 32):
+        raise ValueError(f"ag_gemm_f32: unsupported shape M={M} N={N} K={K}")
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    if wbuf is None:
+        wbuf = torch.empty(N, K, dtype=torch.bfloat16, device=x.device)
+    a2, b2 = extra if extra is not None else (None, None)
+    _ext.ext().ag_gemm_f32(x, [int(p) for p in ptrs], [int(v) for v in starts], int(total),
+                           int(rank), int(N), int(K), wbuf, out, a2, b2)
+    return out, wbuf
+
+
 class PeerShardPool:
     """Every NF4 shard of a coordinator, in one peer buffer per rank.
 
@@ -286,3 +311,58 @@ class PeerShardPool:
     def close(self):
         self.buf.close()
         self.flags.close()
+
+
+class PeerMasterPool:
+    """The fp32 master shards of every training-mode parameter of a coordinator,
+    moved into one peer buffer per rank.
+
+    Each parameter's shard is ``ceil(n / W)`` elements on every rank (zero-padded
+    on the last), so its offset in the buffer is the same everywhere.  The
+    shards' ``master_shard`` parameters keep their identity (the optimizer's
+    state stays valid); only their storage moves.  After an optimizer step every
+    rank must call :meth:`sync_after_update` before the next forward reads a
+    peer's masters.
+    """
+
+    ALIGN = 16
+
+    def __init__(self, coordinator, group=None):
+        self.group = group if group is not None else coordinator.process_group
+        self.rank, self.world = _group_info(self.group)
+        params = [p for p in coordinator._params.values()
+                  if getattr(p, "master_shard", None) is not None
+                  and p.master_shard.dtype == torch.float32 and p.master_shard.is_cuda]
+        self.offsets: Dict[int, int] = {}
+        end = 0
+        for zq in params:
+            self.offsets[zq.param_id] = end
+            end = (end + 4 * zq.master_shard.numel() + self.ALIGN - 1) // self.ALIGN * self.ALIGN
+        self.buf = PeerBuffer(max(end, 16), self.group)
+        for zq in params:
+            view = self.buf.tensor(zq.master_shard.numel(), torch.float32, self.offsets[zq.param_id])
+            view.copy_(zq.master_shard.data)
+            zq.master_shard.data = view
+            zq._peer_master_pool = self
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+
+    def ag_gemm(self, zq, x: torch.Tensor, out: Optional[torch.Tensor] = None,
+                wbuf: Optional[torch.Tensor] = None, extra: Optional[tuple] = None):
+        """``x · bf16(W)ᵀ`` with ``W`` gathered from every rank's master shard inside
+        the GEMM kernel; returns ``(y, wbuf)``."""
+        chunk = zq.master_shard.numel()
+        off = self.offsets[zq.param_id]
+        ptrs = [self.buf.ptrs[q] + off for q in range(self.world)]
+        starts = [q * chunk for q in range(self.world)]
+        N, K = zq.original_shape
+        return ag_gemm_f32_pieces(x, ptrs, starts, chunk * self.world, N, K, self.rank, out,
+                                  wbuf, extra)
+
+    def sync_after_update(self):
+        """Barrier after the masters were updated in place."""
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+
+    def close(self):
+        self.buf.close()
