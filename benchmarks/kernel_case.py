@@ -86,7 +86,8 @@ def _report(name, ms, byts=None, flops=None, extra=""):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["gemm", "attention", "attn_trace", "attn_bwd_trace",
-                                     "nf4_operand", "rmsnorm", "gelu", "q4gemm", "gelu_gemm"])
+                                     "nf4_operand", "rmsnorm", "gelu", "q4gemm", "gelu_gemm",
+                                     "ag_gemm"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=3072)
@@ -100,6 +101,7 @@ def main():
     ap.add_argument("--transpose", action="store_true")
     ap.add_argument("--bhsd", action="store_true", help="attn_trace: K/V as [B, H, S, D]")
     ap.add_argument("--reps", type=int, default=5)
+    ap.add_argument("--world", type=int, default=4, help="ag_gemm: emulated ranks (pieces)")
     ap.add_argument("--profile", action="store_true", help="print one call's kernels (torch profiler)")
     a = ap.parse_args()
 
@@ -149,6 +151,35 @@ def main():
         _report("gemm nn, GELU-gradient epilogue",
                 _time(lambda: E.gemm_gelu(x, wd, dh, h, True, None, None), a.reps, a.profile),
                 flops=fl, extra=f"status {E.gemm_status(0)}")
+    elif a.case == "ag_gemm":
+        # one-kernel gather + dequantise + GEMM over `world` pieces held in separate
+        # allocations of this GPU (the kernel sees only pointers, as with peers),
+        # against the standalone dequantise followed by the same GEMM
+        from zeroq_b200.ops.nf4 import quantize_4bit
+        from zeroq_b200.parallel.peer import ag_gemm_pieces
+
+        N, K = a.n, a.k
+        packed, st = quantize_4bit(torch.randn(N, K, device=dev) * 0.02, 64, "nf4")
+        packed, absmax = packed.reshape(-1), st.absmax.reshape(-1)
+        pp = [packed.numel() * q // a.world // 16 * 16 for q in range(a.world)]
+        ap_ = [absmax.numel() * q // a.world for q in range(a.world)]
+        pk = [packed[pp[q]:(pp[q + 1] if q + 1 < a.world else None)].clone() for q in range(a.world)]
+        am = [absmax[ap_[q]:(ap_[q + 1] if q + 1 < a.world else None)].clone() for q in range(a.world)]
+        x = torch.randn(a.m, K, device=dev, dtype=torch.bfloat16)
+        y = torch.empty(a.m, N, device=dev, dtype=torch.bfloat16)
+        wb = torch.empty(N, K, device=dev, dtype=torch.bfloat16)
+        fl = 2.0 * a.m * N * K
+        ms = _time(lambda: ag_gemm_pieces(x, [t.data_ptr() for t in pk], pp,
+                                          [t.data_ptr() for t in am], ap_, N, K, 64, "nf4", 0,
+                                          out=y, wbuf=wb), a.reps, a.profile)
+        _report(f"ag_gemm one kernel {a.m}x{N}x{K} pieces={a.world}", ms, flops=fl,
+                extra=f"status {E.gemm_status(0)}")
+
+        def two():
+            E.nf4_to_bf16(packed, absmax, wb.view(-1), N, K, 64, 0, False)
+            E.gemm_bf16_tn(x, wb, y)
+        _report(f"dequantise + gemm {a.m}x{N}x{K}", _time(two, a.reps), flops=fl)
+        _report(f"gemm only {a.m}x{N}x{K}", _time(lambda: E.gemm_bf16_tn(x, wb, y), a.reps), flops=fl)
     elif a.case == "q4gemm":
         # C[M, N] = X[M, K] · op(W) with W 4-bit: in-kernel decode vs operand kernel + GEMM
         from zeroq_b200.ops.nf4 import quantize_4bit

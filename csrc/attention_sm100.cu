@@ -501,12 +501,65 @@ struct BwdDqSmem {
   static constexpr int kBytes = kBar + 256 + 1024;
 };
 
+// One thread's half row (columns col0 .. col0 + 63 of a 128-wide head) of an fp32
+// accumulator block in TMEM (tblk: this lane's column 0 of the block), times f,
+// rounded to bf16 and stored.  With cs (the row position's (cos, sin) of the 64
+// rotary pairs) the gradient is rotated back by the inverse RoPE first - the
+// pair partners (i, i + 64) sit in the two halves, so both are read; the result
+// equals the standalone RoPE kernel with sign -1 applied to the bf16 gradient.
+__device__ __forceinline__ void bwd_store_half_row(uint32_t tblk, int col0, float f, const float2* cs,
+                                                   __nv_bfloat16* out) {
+#pragma unroll 1
+  for (int c = 0; c < 2; ++c) {
+    uint32_t o[32];
+    tmem_ld_32x32b_x32(tblk + (uint32_t)(col0 + c * 32), o);
+    if (cs == nullptr) {
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 v;
+        v.x = pack_bf16x2(__uint_as_float(o[8 * i + 0]) * f, __uint_as_float(o[8 * i + 1]) * f);
+        v.y = pack_bf16x2(__uint_as_float(o[8 * i + 2]) * f, __uint_as_float(o[8 * i + 3]) * f);
+        v.z = pack_bf16x2(__uint_as_float(o[8 * i + 4]) * f, __uint_as_float(o[8 * i + 5]) * f);
+        v.w = pack_bf16x2(__uint_as_float(o[8 * i + 6]) * f, __uint_as_float(o[8 * i + 7]) * f);
+        *reinterpret_cast<uint4*>(out + c * 32 + i * 8) = v;
+      }
+      continue;
+    }
+    uint32_t p[32];
+    tmem_ld_32x32b_x32(tblk + (uint32_t)(64 - col0 + c * 32), p);
+    const float4* cs4 = reinterpret_cast<const float4*>(cs + c * 32);
+    tmem_ld_wait();
+    uint32_t w[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      // bf16-rounded gradient of columns 2i, 2i + 1 in this half (m) and the partner's (q)
+      const float2 m = bf16x2_to_f2(pack_bf16x2(__uint_as_float(o[2 * i]) * f, __uint_as_float(o[2 * i + 1]) * f));
+      const float2 q = bf16x2_to_f2(pack_bf16x2(__uint_as_float(p[2 * i]) * f, __uint_as_float(p[2 * i + 1]) * f));
+      const float4 t = __ldg(cs4 + i);   // (cos, sin) of pairs 2i and 2i + 1 of this chunk
+      const float c0 = t.x, s0 = t.y * -1.0f, c1 = t.z, s1 = t.w * -1.0f;
+      float r0, r1;
+      if (col0 == 0) {   // this half holds x1, the partner x2
+        r0 = rope_lo(m.x, q.x, c0, s0);
+        r1 = rope_lo(m.y, q.y, c1, s1);
+      } else {           // this half holds x2, the partner x1
+        r0 = rope_hi(q.x, m.x, c0, s0);
+        r1 = rope_hi(q.y, m.y, c1, s1);
+      }
+      w[i] = pack_bf16x2(r0, r1);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      *reinterpret_cast<uint4*>(out + c * 32 + i * 8) = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+  }
+}
+
 __global__ void __launch_bounds__(kBwdThreads, 1)
 attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                       const float* __restrict__ lse, const float* __restrict__ delta,
                       __nv_bfloat16* __restrict__ dq, int B, int S, int Hq, int Hk, float scale_log2,
-                      float scale, int causal, DeviceStatus* status,
+                      float scale, int causal, const float2* __restrict__ rope_cs, DeviceStatus* status,
                       unsigned long long* __restrict__ trace) {
   // trace (optional, [grid][32] ns): 0 start; key tiles j = 1, 2 at 1 + 8(j-1) + i:
   //   compute: i = 0 S/dP seen, 1 loaded, 2 dS computed, 3 arrived;
@@ -690,21 +743,8 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_cons
       if (named_barrier_and(pair_bar, 64, done)) {
         tc_fence_after();
         __nv_bfloat16* orow = dq + (((int64_t)b * S + q) * Hq + h) * kAttD + col0;
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          uint32_t o[32];
-          tmem_ld_32x32b_x32(tmem + lane_base + 256u + (uint32_t)(col0 + c * 32), o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint4 v;
-            v.x = pack_bf16x2(__uint_as_float(o[8 * i + 0]) * scale, __uint_as_float(o[8 * i + 1]) * scale);
-            v.y = pack_bf16x2(__uint_as_float(o[8 * i + 2]) * scale, __uint_as_float(o[8 * i + 3]) * scale);
-            v.z = pack_bf16x2(__uint_as_float(o[8 * i + 4]) * scale, __uint_as_float(o[8 * i + 5]) * scale);
-            v.w = pack_bf16x2(__uint_as_float(o[8 * i + 6]) * scale, __uint_as_float(o[8 * i + 7]) * scale);
-            *reinterpret_cast<uint4*>(orow + c * 32 + i * 8) = v;
-          }
-        }
+        bwd_store_half_row(tmem + lane_base + 256u, col0, scale,
+                           rope_cs != nullptr ? rope_cs + (int64_t)q * 64 : nullptr, orow);
         if (tr && threadIdx.x == 0) tr[30] = globaltimer();
       }
     }
@@ -731,7 +771,8 @@ attn_bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_con
                        const float* __restrict__ lse2, const float* __restrict__ delta,
                        __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv, int B, int S,
                        int Hq, int Hk, float scale_log2, float scale, int causal,
-                       DeviceStatus* status, unsigned long long* __restrict__ trace) {
+                       const float2* __restrict__ rope_cs, DeviceStatus* status,
+                       unsigned long long* __restrict__ trace) {
   // trace (optional, [grid][32] ns): 0 start; iterations t = 1, 2 at 1 + 8(t-1) + i:
   //   compute: i = 0 Sᵀ/dPᵀ seen, 1 loaded, 2 Pᵀ/dSᵀ computed, 3 arrived;
   //   MMA: 4 Q/dO seen, 5 Sᵀ/dPᵀ issued, 6 Pᵀ/dSᵀ seen, 7 dV/dK issued;  30 end
@@ -933,21 +974,9 @@ attn_bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_con
         for (int w = 0; w < 2; ++w) {   // w = 0: dV (scale 1), w = 1: dK (scale)
           __nv_bfloat16* out = (w == 0 ? dv : dk) + off;
           const float f = w == 0 ? 1.0f : scale;
-#pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
-            uint32_t o[32];
-            tmem_ld_32x32b_x32(tmem + lane_base + (uint32_t)(w * 128 + col0 + c * 32), o);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint4 v;
-              v.x = pack_bf16x2(__uint_as_float(o[8 * i + 0]) * f, __uint_as_float(o[8 * i + 1]) * f);
-              v.y = pack_bf16x2(__uint_as_float(o[8 * i + 2]) * f, __uint_as_float(o[8 * i + 3]) * f);
-              v.z = pack_bf16x2(__uint_as_float(o[8 * i + 4]) * f, __uint_as_float(o[8 * i + 5]) * f);
-              v.w = pack_bf16x2(__uint_as_float(o[8 * i + 6]) * f, __uint_as_float(o[8 * i + 7]) * f);
-              *reinterpret_cast<uint4*>(out + c * 32 + i * 8) = v;
-            }
-          }
+          // dK of rotary-embedded keys: rotated back (dV never is)
+          bwd_store_half_row(tmem + lane_base + (uint32_t)(w * 128), col0, f,
+                             (w == 1 && rope_cs != nullptr) ? rope_cs + (int64_t)key * 64 : nullptr, out);
         }
         if (tr && threadIdx.x == 0) tr[30] = globaltimer();
       }
@@ -1036,7 +1065,7 @@ void attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Ten
 // trace (optional): int64 [dQ grid + dK/dV grid, 32] per-CTA timestamps.
 void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o,
                  at::Tensor lse, at::Tensor dq, at::Tensor dk, at::Tensor dv, bool causal,
-                 double scale, c10::optional<at::Tensor> trace) {
+                 double scale, c10::optional<at::Tensor> trace, c10::optional<at::Tensor> rope_cs) {
   for (const at::Tensor* t : {&dout, &q, &k, &v, &o, &dq, &dk, &dv}) {
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->dim() == 4,
                 "attention backward: contiguous bf16 [B, S, H, D] CUDA tensors");
@@ -1062,6 +1091,14 @@ void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::
                                         BwdDkvSmem::kBytes));
     configured[dev] = true;
   }
+  const float2* rcs = nullptr;
+  if (rope_cs.has_value() && rope_cs->defined()) {
+    const at::Tensor& t = *rope_cs;
+    TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous() && t.dim() == 3 &&
+                    t.size(0) == S && t.size(1) == 64 && t.size(2) == 2,
+                "attention backward: rope table must be fp32 [S, 64, 2]");
+    rcs = reinterpret_cast<const float2*>(t.data_ptr<float>());
+  }
   auto delta = at::empty({B, Hq, S}, q.options().dtype(at::kFloat));
   auto lse2 = at::empty({B, Hq, S}, q.options().dtype(at::kFloat));
   const int64_t rows = B * S * Hq;
@@ -1085,12 +1122,12 @@ void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::
   attn_bwd_dq_tc_kernel<<<(unsigned)g_dq, kBwdThreads, BwdDqSmem::kBytes, stream>>>(
       tq, tk, tv, tdo, lse.data_ptr<float>(), delta.data_ptr<float>(),
       reinterpret_cast<__nv_bfloat16*>(dq.data_ptr<at::BFloat16>()), (int)B, (int)S, (int)Hq, (int)Hk, sl2,
-      (float)scale, causal ? 1 : 0, st, trp);
+      (float)scale, causal ? 1 : 0, rcs, st, trp);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   attn_bwd_dkv_tc_kernel<<<(unsigned)g_dkv, kBwdThreads, BwdDkvSmem::kBytes, stream>>>(
       tq, tk, tv, tdo, lse2.data_ptr<float>(), delta.data_ptr<float>(),
       reinterpret_cast<__nv_bfloat16*>(dk.data_ptr<at::BFloat16>()),
       reinterpret_cast<__nv_bfloat16*>(dv.data_ptr<at::BFloat16>()), (int)B, (int)S, (int)Hq, (int)Hk, sl2,
-      (float)scale, causal ? 1 : 0, st, trp ? trp + g_dq * 32 : nullptr);
+      (float)scale, causal ? 1 : 0, rcs, st, trp ? trp + g_dq * 32 : nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

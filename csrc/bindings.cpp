@@ -13,7 +13,7 @@ void attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Ten
                  double scale, c10::optional<at::Tensor> trace, bool kv_bhsd);
 void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o,
                  at::Tensor lse, at::Tensor dq, at::Tensor dk, at::Tensor dv, bool causal,
-                 double scale, c10::optional<at::Tensor> trace);
+                 double scale, c10::optional<at::Tensor> trace, c10::optional<at::Tensor> rope_cs);
 void gemm_nf4(at::Tensor a, at::Tensor packed, at::Tensor absmax, int64_t rows, int64_t cols,
               int64_t blocksize, int64_t quant_type, bool w_is_kn, at::Tensor c,
               c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2);
@@ -70,6 +70,8 @@ void ag_gemm_nf4(at::Tensor a, std::vector<int64_t> psrc, std::vector<int64_t> p
 void ag_gemm_f32(at::Tensor a, std::vector<int64_t> src, std::vector<int64_t> starts, int64_t total,
                  int64_t rank, int64_t N, int64_t K, at::Tensor wbuf, at::Tensor c,
                  c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2);
+void gemm_rope(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor cs,
+               c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2);
 void gemm_gelu(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor aux, bool b_mn,
                c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2);
 void plan_gather_dequant(std::vector<int64_t> psrc, std::vector<int64_t> pstarts,
@@ -95,7 +97,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd_tc", &attn_bwd_tc, "tcgen05 attention backward", pybind11::arg("dout"),
         pybind11::arg("q"), pybind11::arg("k"), pybind11::arg("v"), pybind11::arg("o"),
         pybind11::arg("lse"), pybind11::arg("dq"), pybind11::arg("dk"), pybind11::arg("dv"),
-        pybind11::arg("causal"), pybind11::arg("scale"), pybind11::arg("trace") = pybind11::none());
+        pybind11::arg("causal"), pybind11::arg("scale"), pybind11::arg("trace") = pybind11::none(),
+        pybind11::arg("rope_cs") = pybind11::none());
   m.def("attn_fwd_tc", &attn_fwd_tc, "tcgen05 attention forward", pybind11::arg("q"),
         pybind11::arg("k"), pybind11::arg("v"), pybind11::arg("o"), pybind11::arg("lse"),
         pybind11::arg("causal"), pybind11::arg("scale"), pybind11::arg("trace") = pybind11::none(),
@@ -132,6 +135,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("a"), pybind11::arg("src"), pybind11::arg("starts"), pybind11::arg("total"),
         pybind11::arg("rank"), pybind11::arg("N"), pybind11::arg("K"), pybind11::arg("wbuf"),
         pybind11::arg("c"), pybind11::arg("a2") = pybind11::none(), pybind11::arg("b2") = pybind11::none());
+  m.def("gemm_rope", &gemm_rope, "tcgen05 GEMM with the rotary-embedding epilogue",
+        pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("c"), pybind11::arg("cs"),
+        pybind11::arg("a2") = pybind11::none(), pybind11::arg("b2") = pybind11::none());
   m.def("gemm_gelu", &gemm_gelu, "tcgen05 GEMM with the GELU output / GELU-gradient epilogue",
         pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("c"), pybind11::arg("aux"),
         pybind11::arg("b_mn"), pybind11::arg("a2") = pybind11::none(),

@@ -418,6 +418,16 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Rotary embedding of one pair (x1, x2) by (c, s): x1*c - x2*s and x2*c + x1*s,
+// with one rounding order in every kernel that applies it (so the GEMM and
+// attention epilogues equal the standalone RoPE kernel bit for bit).
+__device__ __forceinline__ float rope_lo(float x1, float x2, float c, float s) {
+  return __fmaf_rn(x1, c, -__fmul_rn(x2, s));
+}
+__device__ __forceinline__ float rope_hi(float x1, float x2, float c, float s) {
+  return __fmaf_rn(x2, c, __fmul_rn(x1, s));
+}
+
 // two bf16 packed in one word (low half first) -> float2
 __device__ __forceinline__ float2 bf16x2_to_f2(uint32_t w) {
   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));

@@ -228,10 +228,10 @@ __global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* 
   for (int j = 0; j < 4; ++j) {
     const float4 v = c4[j];  // (cos, sin) of pairs 2j and 2j+1
     const float c0 = v.x, s0 = v.y * sign, c1 = v.z, s1 = v.w * sign;
-    oa[2 * j] = a[2 * j] * c0 - b[2 * j] * s0;
-    ob[2 * j] = b[2 * j] * c0 + a[2 * j] * s0;
-    oa[2 * j + 1] = a[2 * j + 1] * c1 - b[2 * j + 1] * s1;
-    ob[2 * j + 1] = b[2 * j + 1] * c1 + a[2 * j + 1] * s1;
+    oa[2 * j] = rope_lo(a[2 * j], b[2 * j], c0, s0);
+    ob[2 * j] = rope_hi(a[2 * j], b[2 * j], c0, s0);
+    oa[2 * j + 1] = rope_lo(a[2 * j + 1], b[2 * j + 1], c1, s1);
+    ob[2 * j + 1] = rope_hi(a[2 * j + 1], b[2 * j + 1], c1, s1);
   }
   *reinterpret_cast<uint4*>(out + row * D + i0) = f32_to_bf16x8(oa);
   *reinterpret_cast<uint4*>(out + row * D + half + i0) = f32_to_bf16x8(ob);

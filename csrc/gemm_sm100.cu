@@ -77,6 +77,9 @@ struct GemmArgs {
   // epilogue input (kEpiGeluBwd): the pre-activation h [M, N], row pitch epi_ld
   const __nv_bfloat16* epi_src;
   int64_t epi_ld;
+  // epilogue input (kEpiRope): (cos, sin) table [epi_S, 64] of float2
+  const float2* epi_cs;
+  int epi_S;
 };
 
 // Pair-kernel epilogues.  kEpiGeluFwd stores C = bf16(acc) through tmC and
@@ -85,7 +88,12 @@ struct GemmArgs {
 // bf16(bf16(acc) * gelu'(h)) (the input gradient of the down-projection turned
 // into the gradient of the pre-activation).  Both round the accumulator to bf16
 // first, so they equal a separate GELU kernel applied to the stored GEMM output.
-enum PairEpi { kEpiPlain = 0, kEpiGeluFwd = 1, kEpiGeluBwd = 2 };
+//
+// kEpiRope applies rotary position embedding (rotate-half pairs (i, i + 64) of
+// every 128-wide head) to the bf16-rounded output: row m is position m % S and
+// epi_cs holds (cos, sin) of each position and pair (fp32, [S, 64, 2]) - the
+// arithmetic of the standalone RoPE kernel, so q/k projections need no RoPE pass.
+enum PairEpi { kEpiPlain = 0, kEpiGeluFwd = 1, kEpiGeluBwd = 2, kEpiRope = 3 };
 
 constexpr int kAgMaxTilesN = 4096;
 constexpr int kAgClaim = kAgMaxTilesN, kAgExit = kAgMaxTilesN + 1, kAgSyncWords = kAgMaxTilesN + 2;
@@ -741,7 +749,36 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       const int m0 = tm * (2 * kBM) + (int)cr * kBM;
       const int n0 = tn * BN;
       const uint32_t trow = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * 256);
-      if (pw.sk < 0) {
+      if (EPI == kEpiRope && pw.sk < 0) {
+        // pairs of chunks (c, c + 2) of each 128-wide head: x1 = cols i, x2 = i + 64
+        const float2* cs = args.epi_cs + (int64_t)((m0 + row) % args.epi_S) * 64;
+        const uint4 none[4] = {};
+#pragma unroll 1
+        for (int hp = 0; hp < BN / 64; ++hp) {
+          const int c0 = (hp >> 1) * 4 + (hp & 1), c1 = c0 + 2;
+          float4 t[16];   // (cos, sin) of pairs (hp & 1) * 32 + 0..31
+          const float4* cs4 = reinterpret_cast<const float4*>(cs + (hp & 1) * 32);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) t[i] = __ldg(cs4 + i);
+          uint32_t ra[32], rb[32];
+          tmem_ld_32x32b_x32(trow + (uint32_t)(c0 * 32), ra);
+          tmem_ld_32x32b_x32(trow + (uint32_t)(c1 * 32), rb);
+          tmem_ld_wait();
+          float oa[32], ob[32];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const float2 a = bf16x2_to_f2(pack_bf16x2(__uint_as_float(ra[i]), __uint_as_float(ra[i + 1])));
+            const float2 b = bf16x2_to_f2(pack_bf16x2(__uint_as_float(rb[i]), __uint_as_float(rb[i + 1])));
+            const float4 v = t[i >> 1];  // (cos, sin) of pairs i and i + 1
+            oa[i] = rope_lo(a.x, b.x, v.x, v.y);
+            ob[i] = rope_hi(a.x, b.x, v.x, v.y);
+            oa[i + 1] = rope_lo(a.y, b.y, v.z, v.w);
+            ob[i + 1] = rope_hi(a.y, b.y, v.z, v.w);
+          }
+          store_chunk(oa, n0 + c0 * 32, m0, none);
+          store_chunk(ob, n0 + c1 * 32, m0, none);
+        }
+      } else if (pw.sk < 0) {
         uint4 hnext[4] = {};
         if constexpr (EPI == kEpiGeluBwd) load_h(n0, m0, hnext);
 #pragma unroll 1
@@ -1194,7 +1231,19 @@ static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
   if (pair) {
     const CUtensorMap tc = make_tmap_store_bf16(c.data_ptr(), M, N, c.stride(0));
     const bool k128 = (K % 128) == 0;
-    setup_streamk(args, (int)(K / (k128 ? 128 : 64)), sms, dev, stream);
+    if (epi != kEpiRope) setup_streamk(args, (int)(K / (k128 ? 128 : 64)), sms, dev, stream);
+    if (epi == kEpiRope) {
+      const at::Tensor& t = *aux;
+      TORCH_CHECK(!b_mn && N % 128 == 0, "gemm: the RoPE epilogue needs [N, K] weights and 128-wide heads");
+      TORCH_CHECK(t.scalar_type() == at::kFloat && t.is_contiguous() && t.dim() == 3 && t.size(1) == 64 &&
+                      t.size(2) == 2 && M % t.size(0) == 0,
+                  "gemm: RoPE table must be fp32 [S, 64, 2] with M a multiple of S");
+      args.epi_cs = reinterpret_cast<const float2*>(t.data_ptr<float>());
+      args.epi_S = (int)t.size(0);
+      if (bn == 256) launch_gemm_pair<256, 3, 2, false, false, false, kEpiRope>(ta, tb, ta2, tb2, tc, args, stream, sms);
+      else launch_gemm_pair<128, 4, 2, false, false, false, kEpiRope>(ta, tb, ta2, tb2, tc, args, stream, sms);
+      return;
+    }
     if (epi != kEpiPlain) {
       const at::Tensor& x = *aux;
       TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.size(0) == M &&
@@ -1259,6 +1308,13 @@ void gemm_bf16_nn(at::Tensor a, at::Tensor b, at::Tensor c, c10::optional<at::Te
 void gemm_gelu(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor aux, bool b_mn,
                c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2) {
   gemm_impl(a, b, c, a2, b2, b_mn, b_mn ? kEpiGeluBwd : kEpiGeluFwd, &aux);
+}
+
+// C = rope(A·Bᵀ (+ A2·B2ᵀ)) for 128-wide heads; cs: fp32 [S, 64, 2] (cos, sin) per
+// position and pair, row m of C at position m % S.  Needs M >= 256, K % 128 == 0.
+void gemm_rope(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor cs,
+               c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2) {
+  gemm_impl(a, b, c, a2, b2, false, kEpiRope, &cs);
 }
 
 // GEMM whose B operand is a 4-bit weight W [rows, cols] decoded inside the

@@ -320,3 +320,26 @@ def test_gelu_mlp_split_form_matches_plain_form_on_cpu():
         torch.testing.assert_close(g1, x.grad, rtol=1e-4, atol=1e-6)
         torch.testing.assert_close(gA1, up.lora_A.grad, rtol=1e-4, atol=1e-6)
         up.lora_A.grad = None
+
+
+def test_linear4bit_rope_argument_matches_apply_rope_on_cpu():
+    """Off the fused path (CPU) the rope= argument rotates the projection's output
+    like apply_rope, values and input gradients."""
+    from zeroq_b200.ops.qlinear import Linear4bit
+    from zeroq_b200.ops.rope import apply_rope, rope_table
+
+    torch.manual_seed(2)
+    B, S, d, H = 2, 6, 64, 2
+    lin = Linear4bit(d, H * 128, lora_r=4, backend="torch", device="cpu")
+    lin.quantize_from(torch.randn(H * 128, d) * 0.05)
+    x = torch.randn(B, S, d, requires_grad=True)
+    cs = rope_table(S, 128, 10000.0, "cpu")
+    y = lin(x, rope=cs)
+    y.square().sum().backward()
+    g1 = x.grad.clone()
+    x.grad = None
+    y0 = lin(x).view(B, S, H, 128)
+    y2, _ = apply_rope(y0, y0, 10000.0)
+    y2.square().sum().backward()
+    torch.testing.assert_close(y.view(B, S, H, 128), y2, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(g1, x.grad, rtol=1e-4, atol=1e-6)

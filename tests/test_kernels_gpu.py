@@ -776,3 +776,143 @@ def test_ag_gemm_f32_master_pieces_match_cast_then_gemm(cuda, M, N, K, starts_fr
         _status_ok(cuda)
         assert torch.equal(wbuf, wb)
         assert torch.equal(y, ref)
+
+
+@pytest.mark.parametrize("B,S,H,K", [(2, 512, 8, 1024), (1, 384, 3, 512), (4, 1024, 24, 3072)])
+@pytest.mark.parametrize("extra", [False, True])
+def test_gemm_rope_epilogue_matches_rope_kernel(cuda, B, S, H, K, extra):
+    """RoPE applied in the GEMM epilogue equals the GEMM followed by the RoPE
+    kernel, bit for bit (both rotate the bf16-rounded output in fp32)."""
+    from zeroq_b200.ops.rope import rope_table
+
+    E = _ext.ext()
+    torch.manual_seed(9)
+    M, N = B * S, H * 128
+    x = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=cuda) * 0.05).to(torch.bfloat16)
+    a2 = b2 = None
+    if extra:
+        a2 = (torch.randn(M, 64, device=cuda) * 0.1).to(torch.bfloat16)
+        b2 = (torch.randn(N, 64, device=cuda) * 0.1).to(torch.bfloat16)
+    cs = rope_table(S, 128, 10000.0, cuda)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    E.gemm_rope(x, w, y, cs, a2, b2)
+    h = torch.empty_like(y)
+    if extra:
+        E.gemm_bf16_tn_extra(x, w, h, a2, b2)
+    else:
+        E.gemm_bf16_tn(x, w, h)
+    ref = torch.empty_like(h)
+    E.rope(h.view(B, S, H, 128), ref.view(B, S, H, 128), cs, 1.0)
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    assert torch.equal(y, ref), (y.float() - ref.float()).abs().max().item()
+
+
+@pytest.mark.parametrize("lora_r", [0, 16])
+def test_linear4bit_rope_output_matches_apply_rope(cuda, lora_r):
+    """q/k projections with the rotary embedding in the GEMM epilogue give the
+    same values and gradients as the projection followed by apply_rope."""
+    from zeroq_b200.ops.qlinear import Linear4bit
+    from zeroq_b200.ops.rope import apply_rope, rope_table
+
+    torch.manual_seed(10)
+    B, S, d, Hq, Hk = 2, 256, 512, 4, 2
+    q_proj = Linear4bit(d, Hq * 128, lora_r=lora_r, device=cuda)
+    k_proj = Linear4bit(d, Hk * 128, lora_r=lora_r, device=cuda)
+    for m in (q_proj, k_proj):
+        m.quantize_from(torch.randn(m.out_features, d, device=cuda) * 0.05)
+        if lora_r:
+            with torch.no_grad():
+                m.lora_B.normal_(0, 0.02)
+    x = torch.randn(B, S, d, device=cuda).to(torch.bfloat16).requires_grad_(True)
+    cs = rope_table(S, 128, 10000.0, cuda)
+    q = q_proj(x, rope=cs).view(B, S, Hq, 128)
+    k = k_proj(x, rope=cs).view(B, S, Hk, 128)
+    (q.float().square().sum() + (k.float() * 0.5).sum()).backward()
+    gx = x.grad.clone()
+    gA = q_proj.lora_A.grad.clone() if lora_r else None
+    x.grad = None
+    if lora_r:
+        q_proj.lora_A.grad = None
+        k_proj.lora_A.grad = None
+        q_proj.lora_B.grad = None
+        k_proj.lora_B.grad = None
+    q2, k2 = apply_rope(q_proj(x).view(B, S, Hq, 128), k_proj(x).view(B, S, Hk, 128), 10000.0)
+    (q2.float().square().sum() + (k2.float() * 0.5).sum()).backward()
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    assert torch.equal(q, q2) and torch.equal(k, k2)
+    assert torch.equal(gx, x.grad)
+    if lora_r:
+        torch.testing.assert_close(gA, q_proj.lora_A.grad, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("B,S,Hq,Hk", [(2, 256, 4, 4), (1, 512, 8, 2)])
+def test_attention_backward_inverse_rope_epilogue(cuda, B, S, Hq, Hk):
+    """dQ/dK written rotated back by the attention backward (rope table given)
+    equal the plain backward followed by the inverse RoPE kernel, bit for bit."""
+    from zeroq_b200.ops.rope import rope_table
+
+    E = _ext.ext()
+    torch.manual_seed(11)
+    q = torch.randn(B, S, Hq, 128, device=cuda).to(torch.bfloat16)
+    k = torch.randn(B, S, Hk, 128, device=cuda).to(torch.bfloat16)
+    v = torch.randn(B, S, Hk, 128, device=cuda).to(torch.bfloat16)
+    do = torch.randn(B, S, Hq, 128, device=cuda).to(torch.bfloat16)
+    o = torch.empty_like(q)
+    lse = torch.empty(B, Hq, S, device=cuda)
+    scale = 128 ** -0.5
+    E.attn_fwd_tc(q, k, v, o, lse, True, scale)
+    cs = rope_table(S, 128, 10000.0, cuda)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    E.attn_bwd_tc(do, q, k, v, o, lse, dq, dk, dv, True, scale)
+    dq_r, dk_r, dv_r = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    E.attn_bwd_tc(do, q, k, v, o, lse, dq_r, dk_r, dv_r, True, scale, None, cs)
+    ref_q, ref_k = torch.empty_like(dq), torch.empty_like(dk)
+    E.rope(dq, ref_q, cs, -1.0)
+    E.rope(dk, ref_k, cs, -1.0)
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    assert torch.equal(dv_r, dv)
+    assert torch.equal(dq_r, ref_q), (dq_r.float() - ref_q.float()).abs().max().item()
+    assert torch.equal(dk_r, ref_k), (dk_r.float() - ref_k.float()).abs().max().item()
+
+
+def test_rope_spec_projection_attention_chain_matches_apply_rope(cuda):
+    """q/k projections rotating in their epilogue + attention rotating dQ/dK back
+    (shared RopeSpec) against projections, apply_rope and plain attention."""
+    from zeroq_b200.ops.attention import flash_attention
+    from zeroq_b200.ops.qlinear import Linear4bit
+    from zeroq_b200.ops.rope import RopeSpec, apply_rope, rope_table
+
+    torch.manual_seed(12)
+    B, S, d, Hq, Hk = 2, 256, 512, 4, 2
+    qp = Linear4bit(d, Hq * 128, lora_r=8, device=cuda)
+    kp = Linear4bit(d, Hk * 128, lora_r=8, device=cuda)
+    vp = Linear4bit(d, Hk * 128, device=cuda)
+    for m in (qp, kp, vp):
+        m.quantize_from(torch.randn(m.out_features, d, device=cuda) * 0.05)
+    with torch.no_grad():
+        qp.lora_B.normal_(0, 0.02)
+        kp.lora_B.normal_(0, 0.02)
+    x = torch.randn(B, S, d, device=cuda).to(torch.bfloat16).requires_grad_(True)
+    spec = RopeSpec(rope_table(S, 128, 10000.0, cuda))
+    o = flash_attention(qp(x, rope=spec).view(B, S, Hq, 128), kp(x, rope=spec).view(B, S, Hk, 128),
+                        vp(x).view(B, S, Hk, 128), causal=True, rope=spec)
+    o.float().square().sum().backward()
+    assert spec.grads_unrotated
+    g1, gA1 = x.grad.clone(), qp.lora_A.grad.clone()
+    x.grad = None
+    qp.lora_A.grad = None
+    kp.lora_A.grad = None
+    qp.lora_B.grad = None
+    kp.lora_B.grad = None
+    q2, k2 = apply_rope(qp(x).view(B, S, Hq, 128), kp(x).view(B, S, Hk, 128), 10000.0)
+    o2 = flash_attention(q2, k2, vp(x).view(B, S, Hk, 128), causal=True)
+    o2.float().square().sum().backward()
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    assert torch.equal(o, o2)
+    assert torch.equal(g1, x.grad)
+    torch.testing.assert_close(gA1, qp.lora_A.grad, rtol=1e-5, atol=1e-6)

@@ -38,7 +38,7 @@ from ..ops.cross_entropy import cross_entropy
 from ..ops.gemm import LMHeadFunction
 from ..ops.norm import add_rmsnorm
 from ..ops.qlinear import Linear4bit
-from ..ops.rope import apply_rope
+from ..ops.rope import RopeSpec, apply_rope, rope_table
 
 
 @dataclass
@@ -174,11 +174,20 @@ class DecoderLayer(nn.Module):
             x = self.attn_norm(h)
         else:
             h, x = self.attn_norm(h, delta)
-        q = self.q_proj(x).view(B, S, cfg.n_heads, cfg.head_dim)
-        k = self.k_proj(x).view(B, S, cfg.n_kv_heads, cfg.head_dim)
-        v = self.v_proj(x).view(B, S, cfg.n_kv_heads, cfg.head_dim)
-        q, k = apply_rope(q, k, cfg.rope_theta)
-        o = flash_attention(q, k, v, causal=True)
+        if self._fused_rope(x):
+            # the q/k projection GEMMs apply the rotary embedding in their epilogue
+            # and the attention backward rotates dQ/dK back (shared RopeSpec)
+            spec = RopeSpec(rope_table(S, cfg.head_dim, cfg.rope_theta, x.device))
+            q = self.q_proj(x, rope=spec).view(B, S, cfg.n_heads, cfg.head_dim)
+            k = self.k_proj(x, rope=spec).view(B, S, cfg.n_kv_heads, cfg.head_dim)
+            v = self.v_proj(x).view(B, S, cfg.n_kv_heads, cfg.head_dim)
+            o = flash_attention(q, k, v, causal=True, rope=spec)
+        else:
+            q = self.q_proj(x).view(B, S, cfg.n_heads, cfg.head_dim)
+            k = self.k_proj(x).view(B, S, cfg.n_kv_heads, cfg.head_dim)
+            v = self.v_proj(x).view(B, S, cfg.n_kv_heads, cfg.head_dim)
+            q, k = apply_rope(q, k, cfg.rope_theta)
+            o = flash_attention(q, k, v, causal=True)
         a = self.o_proj(o.view(B, S, cfg.n_heads * cfg.head_dim))
         h, x = self.mlp_norm(h, a)
         if self.gate_proj is not None:
@@ -191,6 +200,15 @@ class DecoderLayer(nn.Module):
         else:
             f = gelu(self.up_proj(x))
         return h, self.down_proj(f)
+
+    def _fused_rope(self, x: torch.Tensor) -> bool:
+        from ..ops.qlinear import Linear4bit
+
+        mods = (self.q_proj, self.k_proj)
+        return (x.is_cuda and self.cfg.head_dim == 128
+                and all(isinstance(m, Linear4bit) for m in mods)
+                and not any(m._forward_hooks or m._forward_pre_hooks or m._backward_hooks
+                            or m._backward_pre_hooks for m in mods))
 
     def _fused_gelu_mlp(self) -> bool:
         from ..ops.qlinear import Linear4bit

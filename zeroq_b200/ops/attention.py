@@ -44,7 +44,7 @@ def attention_reference(q, k, v, causal: bool = True, scale=None):
 
 class _FlashAttn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, causal, scale):
+    def forward(ctx, q, k, v, causal, scale, rope=None):
         q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
         B, S, Hq, D = q.shape
         o = torch.empty_like(q)
@@ -55,6 +55,7 @@ class _FlashAttn(torch.autograd.Function):
             _ext.ext().attn_fwd(q, k, v, o, lse, bool(causal), float(scale))
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.causal, ctx.scale = causal, scale
+        ctx.rope = rope if (rope is not None and hasattr(rope, "grads_unrotated")) else None
         return o
 
     @staticmethod
@@ -65,15 +66,23 @@ class _FlashAttn(torch.autograd.Function):
         dk = torch.empty_like(k)
         dv = torch.empty_like(v)
         if q.shape[-1] == 128:
-            _ext.ext().attn_bwd_tc(do, q, k, v, o, lse, dq, dk, dv, bool(ctx.causal), float(ctx.scale))
+            rope = ctx.rope
+            cs = rope.cs if rope is not None and rope.cs.shape[0] == q.shape[1] else None
+            _ext.ext().attn_bwd_tc(do, q, k, v, o, lse, dq, dk, dv, bool(ctx.causal), float(ctx.scale),
+                                   None, cs)
+            if cs is not None:
+                rope.grads_unrotated = True  # dQ/dK are gradients of the pre-rotation q/k
         else:
             _ext.ext().attn_bwd(do, q, k, v, o, lse, dq, dk, dv, bool(ctx.causal), float(ctx.scale))
-        return dq, dk, dv, None, None
+        return dq, dk, dv, None, None, None
 
 
-def flash_attention(q, k, v, causal: bool = True, scale=None):
+def flash_attention(q, k, v, causal: bool = True, scale=None, rope=None):
+    """``rope``: the :class:`~zeroq_b200.ops.rope.RopeSpec` with which q and k were
+    rotated by their projections; the backward then writes dQ/dK rotated back
+    (tcgen05 path) and marks the spec so the projections do not rotate again."""
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
     if q.is_cuda and q.dtype == torch.bfloat16:
-        return _FlashAttn.apply(q, k, v, causal, scale)
+        return _FlashAttn.apply(q, k, v, causal, scale, rope)
     return attention_reference(q, k, v, causal, scale)

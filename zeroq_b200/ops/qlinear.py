@@ -112,11 +112,15 @@ class NF4LinearFunction(torch.autograd.Function):
       returned for ``h`` - the input-gradient GEMM's epilogue multiplies by
       ``gelu'(h)``, so the gradient of ``gelu(h)`` is never stored.
     Off the fused path both fall back to the GELU kernels with the same results.
+
+    ``rope=cs`` (a ``[S, D/2, 2]`` cos/sin table, D = 128): the output is returned
+    rotary-embedded (row m at position m % S); the GEMM epilogue applies the
+    rotation, and the backward un-rotates the incoming gradient first.
     """
 
     @staticmethod
     def forward(ctx, x, packed, absmax, lora_A, lora_B, bias, N, K, blocksize, quant_type,
-                scaling, backend, lora_ops=None, peer=None, act_out=None, pre=None):
+                scaling, backend, lora_ops=None, peer=None, act_out=None, pre=None, rope=None):
         shp = x.shape
         x2 = x.reshape(-1, K)
         if not x2.is_contiguous():
@@ -133,6 +137,12 @@ class NF4LinearFunction(torch.autograd.Function):
         U = None
         a_pad = b_pad = None
         act = None
+        rope_done = False
+        rope_cs = None
+        if rope is not None:
+            from .rope import rope_table_of
+
+            rope_cs = rope_table_of(rope)
         if act_out not in (None, "gelu"):
             raise ValueError(f"unsupported fused activation {act_out!r}")
         if fused:
@@ -147,6 +157,13 @@ class NF4LinearFunction(torch.autograd.Function):
                 _, wbuf = peer[0].ag_gemm(peer[1], x2, out=y,
                                           extra=(U, b_pad) if has_lora else None)
                 del wbuf
+            elif (rope is not None and bias is None and _epi_ok(M, K) and N % 128 == 0
+                  and rope_cs.shape[1] == 64 and M % rope_cs.shape[0] == 0
+                  and not _in_kernel_ok(M, K, N)):
+                w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
+                E.gemm_rope(x2, w, y, rope_cs, U, b_pad)
+                rope_done = True
+                del w
             elif act_out == "gelu" and bias is None and _epi_ok(M, K) and not _in_kernel_ok(M, K, N):
                 w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
                 act = torch.empty_like(y)
@@ -171,6 +188,11 @@ class NF4LinearFunction(torch.autograd.Function):
             y = y.to(x2.dtype)
         if bias is not None:
             y = y + bias.to(y.dtype)
+        if rope is not None and not rope_done:
+            from .rope import rope_rows
+
+            y = rope_rows(y, rope_cs, 1.0)
+        ctx.rope = rope
         if peer is not None:
             packed = absmax = None  # re-read from the owners in backward
         pre2 = None
@@ -198,6 +220,11 @@ class NF4LinearFunction(torch.autograd.Function):
         gy2 = gy.reshape(-1, N)
         if not gy2.is_contiguous():
             gy2 = gy2.contiguous()
+        if ctx.rope is not None:  # gradient of the pre-rotation output
+            from .rope import rope_grad_done, rope_rows, rope_table_of
+
+            if not rope_grad_done(ctx.rope):  # (else the attention backward did it)
+                gy2 = rope_rows(gy2, rope_table_of(ctx.rope), -1.0)
         M = gy2.shape[0]
         gx = gA = gB = gbias = None
         # with pre=h the input gradient is taken for h (through gelu'(h))
@@ -281,9 +308,9 @@ class NF4LinearFunction(torch.autograd.Function):
             if gx is not None:
                 g_pre = gx if gelu_done else _gelu_grad_kernel(gx, pre2.view(gx.shape))
             return (None, None, None, gA, gB, gbias, None, None, None, None, None, None, None,
-                    None, None, g_pre)
+                    None, None, g_pre, None)
         return (gx, None, None, gA, gB, gbias, None, None, None, None, None, None, None, None,
-                None, None)
+                None, None, None)
 
 
 def _epi_ok(M: int, K: int) -> bool:
@@ -396,12 +423,12 @@ def _pack_lora(A: torch.Tensor, B: torch.Tensor, scaling: float, out=None):
 def nf4_linear(x, packed, absmax, out_features: int, in_features: int, bias=None,
                lora_A=None, lora_B=None, scaling: float = 1.0, blocksize: int = 64,
                quant_type: str = "nf4", backend: str = "auto", lora_ops=None, peer=None,
-               act_out=None, pre=None):
+               act_out=None, pre=None, rope=None):
     if backend == "auto":
         backend = "fused" if x.is_cuda else "torch"
     return NF4LinearFunction.apply(x, packed, absmax, lora_A, lora_B, bias, out_features,
                                    in_features, blocksize, quant_type, scaling, backend, lora_ops,
-                                   peer, act_out, pre)
+                                   peer, act_out, pre, rope)
 
 
 class Linear4bit(nn.Module):
@@ -533,14 +560,16 @@ class Linear4bit(nn.Module):
 
     # -- forward -------------------------------------------------------------
     def forward(self, x: torch.Tensor, act_out: Optional[str] = None,
-                pre: Optional[torch.Tensor] = None):
+                pre: Optional[torch.Tensor] = None, rope=None):
         """``act_out="gelu"``: return ``(y, gelu(y))`` with ``gelu(y)`` carrying no
         gradient of its own; ``pre=h``: ``x`` is ``gelu(h)`` and the gradient goes to
-        ``h`` (the two halves of a GELU MLP; see :class:`NF4LinearFunction`)."""
+        ``h`` (the two halves of a GELU MLP; see :class:`NF4LinearFunction`);
+        ``rope``: a cos/sin table or a :class:`~zeroq_b200.ops.rope.RopeSpec` - return
+        the output rotary-embedded."""
         master = getattr(self, "_master", None)
         if master is not None:
             pool, zq = master
-            if (act_out is None and pre is None and not self.lora_r
+            if (act_out is None and pre is None and rope is None and not self.lora_r
                     and _master_fused_ok(x, self.out_features, self.in_features)):
                 return MasterGatherLinearFunction.apply(x, zq.master_shard, self.bias, pool, zq)
             # off the fused path: the regular fp32 all-gather into self.weight
@@ -551,7 +580,7 @@ class Linear4bit(nn.Module):
             ops = self._lora_operands() if (self.lora_r and x.is_cuda) else None
             return nf4_linear(x, None, None, self.out_features, self.in_features, self.bias,
                               self.lora_A, self.lora_B, self.scaling, self.blocksize,
-                              self.quant_type, self.backend, ops, peer, act_out, pre)
+                              self.quant_type, self.backend, ops, peer, act_out, pre, rope)
         if self.weight_packed is None:
             if self.weight.numel() == 0:
                 raise RuntimeError("Linear4bit has no weight: neither NF4 data nor a "
@@ -564,6 +593,10 @@ class Linear4bit(nn.Module):
                                            None if self.bias is None else self.bias.to(x.dtype))
             if self.lora_r:
                 y = y + (x @ self.lora_A.t().to(x.dtype)) @ self.lora_B.t().to(x.dtype) * self.scaling
+            if rope is not None:
+                from .rope import rope_rows_autograd
+
+                y = rope_rows_autograd(y.reshape(-1, y.shape[-1]), rope).view(y.shape)
             if act_out == "gelu":
                 return y, _gelu_kernel(y.detach())
             return y
@@ -571,7 +604,7 @@ class Linear4bit(nn.Module):
         return nf4_linear(x, self.weight_packed, self.weight_absmax, self.out_features,
                           self.in_features, self.bias, self.lora_A, self.lora_B,
                           self.scaling, self.blocksize, self.quant_type, self.backend, ops,
-                          None, act_out, pre)
+                          None, act_out, pre, rope)
 
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, "

@@ -69,3 +69,59 @@ def apply_rope(q: torch.Tensor, k: torch.Tensor, theta: float = 10000.0):
     if q.is_cuda and q.dtype == torch.bfloat16:
         return _Rope.apply(q, k, theta)
     return rope_reference(q, theta), rope_reference(k, theta)
+
+
+def rope_rows(x: torch.Tensor, cs: torch.Tensor, sign: float = 1.0) -> torch.Tensor:
+    """Rotate the rows of ``x [M, H*D]`` (row m at position m % S, heads of
+    ``D = 2 * cs.shape[1]``) by the table ``cs [S, D/2, 2]`` (``sign=-1``: the
+    inverse rotation, i.e. the backward).  No autograd."""
+    S, half = cs.shape[0], cs.shape[1]
+    D = 2 * half
+    M, N = x.shape
+    x4 = x.reshape(M // S, S, N // D, D)
+    if x.is_cuda and x.dtype == torch.bfloat16:
+        out = torch.empty_like(x4)
+        _ext.ext().rope(x4.contiguous(), out, cs, float(sign))
+        return out.view(M, N)
+    xf = x4.float()
+    c = cs[..., 0][None, :, None, :].float()
+    s_ = cs[..., 1][None, :, None, :].float() * sign
+    x1, x2 = xf[..., :half], xf[..., half:]
+    return torch.cat([x1 * c - x2 * s_, x2 * c + x1 * s_], dim=-1).to(x.dtype).view(M, N)
+
+
+class RopeSpec:
+    """The rotary table ``cs`` of one layer's q/k projections, shared with the
+    attention that consumes their outputs.  A projection given a spec returns its
+    output rotated (in the GEMM epilogue where it can); when the attention backward
+    writes dQ/dK already rotated back it sets ``grads_unrotated``, and the
+    projections then skip their own inverse rotation."""
+
+    def __init__(self, cs: torch.Tensor):
+        self.cs = cs
+        self.grads_unrotated = False
+
+
+def rope_table_of(rope) -> torch.Tensor:
+    return rope.cs if isinstance(rope, RopeSpec) else rope
+
+
+def rope_grad_done(rope) -> bool:
+    return isinstance(rope, RopeSpec) and rope.grads_unrotated
+
+
+class _RopeRows(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, rope):
+        ctx.rope = rope
+        return rope_rows(x, rope_table_of(rope), 1.0)
+
+    @staticmethod
+    def backward(ctx, g):
+        if rope_grad_done(ctx.rope):
+            return g, None
+        return rope_rows(g.contiguous(), rope_table_of(ctx.rope), -1.0), None
+
+
+def rope_rows_autograd(x: torch.Tensor, rope) -> torch.Tensor:
+    return _RopeRows.apply(x, rope)
