@@ -294,6 +294,20 @@ def main():
         ms = _time(step, a.reps, a.profile)
         _report(f"attention fwd+bwd B={a.b} S={a.s} H={a.h} D={a.d} causal", ms,
                 flops=fwd_fl * 3.5)
+        if a.d == 128:
+            # backward kernels alone, plain and with the inverse-RoPE dQ/dK epilogue
+            from zeroq_b200.ops.rope import rope_table
+
+            qd, kd, vd = q.detach(), k.detach(), v.detach()
+            o = torch.empty_like(qd)
+            lse = torch.empty(a.b, a.h, a.s, device=dev)
+            E.attn_fwd_tc(qd, kd, vd, o, lse, True, a.d ** -0.5)
+            dq, dk, dv = torch.empty_like(qd), torch.empty_like(kd), torch.empty_like(vd)
+            cs = rope_table(a.s, a.d, 10000.0, dev)
+            for name, t in (("plain", None), ("inverse-RoPE epilogue", cs)):
+                ms_b = _time(lambda: E.attn_bwd_tc(go, qd, kd, vd, o, lse, dq, dk, dv, True,
+                                                   a.d ** -0.5, None, t), a.reps)
+                _report(f"attention bwd kernels ({name})", ms_b, flops=fwd_fl * 2.5)
     elif a.case == "nf4_operand":
         from zeroq_b200.ops.nf4 import quantize_4bit
 

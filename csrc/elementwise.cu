@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_fwd_kernel(
 // Teams walk rows with a grid stride and keep their dw share in registers; the
 // teams of a CTA combine through shared memory into one row of dw_part.
 template <int NC, int TPR>
-__global__ void __launch_bounds__(kNormThreads, NC <= 6 ? 2 : 1) rmsnorm_bwd_kernel(
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
     const __nv_bfloat16* __restrict__ gy, const __nv_bfloat16* __restrict__ x,
     const float* __restrict__ w, const float* __restrict__ rstd,
     const __nv_bfloat16* __restrict__ gh, __nv_bfloat16* __restrict__ dx,
@@ -137,10 +137,11 @@ __global__ void __launch_bounds__(kNormThreads, NC <= 6 ? 2 : 1) rmsnorm_bwd_ker
   const int team = threadIdx.x / TPR, tl = threadIdx.x % TPR;
   const int nch = D >> 3;
   for (int i = threadIdx.x; i < D; i += kNormThreads) sdw[i] = 0.0f;
-  __syncthreads();
-  // the weight gradient accumulates in shared memory (fp32 shared atomics): a
-  // register accumulator per owned column would cost NC*8 registers and halve
-  // the CTAs per SM, and this kernel is bound by how many loads are in flight
+  float dwacc[NC][8];
+#pragma unroll
+  for (int c = 0; c < NC; ++c)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dwacc[c][i] = 0.0f;
   const float4* w4 = reinterpret_cast<const float4*>(w);  // [D/4], L1-resident
   const int64_t groups = (M + R - 1) / R;
   for (int64_t gidx = blockIdx.x; gidx < groups; gidx += gridDim.x) {
@@ -172,7 +173,7 @@ __global__ void __launch_bounds__(kNormThreads, NC <= 6 ? 2 : 1) rmsnorm_bwd_ker
         for (int i = 0; i < 8; ++i) {
           const float xh = xf[i] * r;
           dot += gf[i] * ww[i] * xh;
-          atomicAdd(&sdw[ch * 8 + i], gf[i] * xh);
+          dwacc[c][i] += gf[i] * xh;
         }
       }
     }
@@ -198,6 +199,15 @@ __global__ void __launch_bounds__(kNormThreads, NC <= 6 ? 2 : 1) rmsnorm_bwd_ker
           *reinterpret_cast<uint4*>(dx + row * D + (int64_t)ch * 8) = f32_to_bf16x8(o);
         }
       }
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    const int ch = c * TPR + tl;
+    if (ch < nch) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) atomicAdd(&sdw[ch * 8 + i], dwacc[c][i]);
     }
   }
   __syncthreads();

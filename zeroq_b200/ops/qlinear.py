@@ -210,11 +210,16 @@ class NF4LinearFunction(torch.autograd.Function):
                 act = _gelu_kernel(y)
             act = act.view(*shp[:-1], N)
             ctx.mark_non_differentiable(act)
+            # no zero-filled gradient for gelu(h) (it never has one): saves a
+            # full-size fill per layer
+            ctx.set_materialize_grads(False)
             return y, act
         return y
 
     @staticmethod
     def backward(ctx, gy, g_act=None):
+        if gy is None:  # (grads are not materialised for the act_out form)
+            return (None,) * 17
         x2, packed, absmax, lora_A, lora_B, U, a_pad, b_pad, pre2 = ctx.saved_tensors
         shp, N, K, blocksize, quant_type, scaling, fused, has_bias, has_lora, r = ctx.meta
         gy2 = gy.reshape(-1, N)
