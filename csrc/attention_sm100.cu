@@ -1002,10 +1002,15 @@ static CUtensorMap make_tmap_bshd(const at::Tensor& t, bool bhsd = false) {
   const int64_t B = t.size(0), S = bhsd ? t.size(2) : t.size(1), H = bhsd ? t.size(1) : t.size(2),
                 D = t.size(3);
   TORCH_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0, "attention: 16-byte aligned tensors");
+  // any strides with unit D stride and 16-byte multiples (e.g. q/k/v as column
+  // slices of one fused projection output)
+  const int64_t sH = bhsd ? t.stride(1) : t.stride(2), sS = bhsd ? t.stride(2) : t.stride(1),
+                sB = t.stride(0);
+  TORCH_CHECK(t.stride(3) == 1 && sH % 8 == 0 && sS % 8 == 0 && sB % 8 == 0,
+              "attention: unit head-dim stride and 16-byte multiple strides");
   CUtensorMap map;
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
-  cuuint64_t strides[3] = {(cuuint64_t)(bhsd ? S * D * 2 : D * 2), (cuuint64_t)(bhsd ? D * 2 : H * D * 2),
-                           (cuuint64_t)(S * H * D * 2)};
+  cuuint64_t strides[3] = {(cuuint64_t)(sH * 2), (cuuint64_t)(sS * 2), (cuuint64_t)(sB * 2)};
   cuuint32_t box[4] = {64u, 1u, (cuuint32_t)kAttRows, 1u};
   cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
   CUresult r = get_encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, t.data_ptr(), dims, strides,
@@ -1020,9 +1025,10 @@ static CUtensorMap make_tmap_bshd(const at::Tensor& t, bool bhsd = false) {
 void attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, bool causal,
                  double scale, c10::optional<at::Tensor> trace, bool kv_bhsd) {
   for (const at::Tensor* t : {&q, &k, &v, &o}) {
-    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->dim() == 4,
-                "attention: contiguous bf16 [B, S, H, D] CUDA tensors");
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 4,
+                "attention: bf16 [B, S, H, D] CUDA tensors");
   }
+  TORCH_CHECK(o.is_contiguous(), "attention: o must be contiguous (q/k/v may be strided)");
   const int64_t B = q.size(0), S = q.size(1), Hq = q.size(2), D = q.size(3),
                 Hk = kv_bhsd ? k.size(1) : k.size(2);
   TORCH_CHECK(D == kAttD, "attention (tcgen05): head dim 128");
@@ -1067,9 +1073,11 @@ void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::
                  at::Tensor lse, at::Tensor dq, at::Tensor dk, at::Tensor dv, bool causal,
                  double scale, c10::optional<at::Tensor> trace, c10::optional<at::Tensor> rope_cs) {
   for (const at::Tensor* t : {&dout, &q, &k, &v, &o, &dq, &dk, &dv}) {
-    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->dim() == 4,
-                "attention backward: contiguous bf16 [B, S, H, D] CUDA tensors");
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 4,
+                "attention backward: bf16 [B, S, H, D] CUDA tensors");
   }
+  for (const at::Tensor* t : {&dout, &o, &dq, &dk, &dv})
+    TORCH_CHECK(t->is_contiguous(), "attention backward: dout, o, dq, dk, dv must be contiguous");
   const int64_t B = q.size(0), S = q.size(1), Hq = q.size(2), D = q.size(3), Hk = k.size(2);
   TORCH_CHECK(D == kAttD, "attention backward (tcgen05): head dim 128");
   TORCH_CHECK(S % kAttRows == 0 && S > 0, "attention backward: S must be a multiple of 128");

@@ -32,6 +32,7 @@ void add_rmsnorm_fwd(at::Tensor h, c10::optional<at::Tensor> d, at::Tensor w, at
 void rmsnorm_bwd(at::Tensor gy, at::Tensor x, at::Tensor w, at::Tensor rstd,
                  c10::optional<at::Tensor> gh, at::Tensor dx, at::Tensor dw_part);
 void rope(at::Tensor x, at::Tensor out, at::Tensor cs, double sign);
+void rope_into(at::Tensor x, at::Tensor out, at::Tensor cs, double sign);
 void gelu_fwd(at::Tensor x, at::Tensor y);
 void gelu_cdf_pdf(at::Tensor x, at::Tensor cdf, at::Tensor pdf);
 void gelu_bwd(at::Tensor g, at::Tensor x, at::Tensor dx);
@@ -71,7 +72,7 @@ void ag_gemm_f32(at::Tensor a, std::vector<int64_t> src, std::vector<int64_t> st
                  int64_t rank, int64_t N, int64_t K, at::Tensor wbuf, at::Tensor c,
                  c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2);
 void gemm_rope(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor cs,
-               c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2);
+               c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2, int64_t ncols);
 void gemm_gelu(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor aux, bool b_mn,
                c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2);
 void plan_gather_dequant(std::vector<int64_t> psrc, std::vector<int64_t> pstarts,
@@ -111,6 +112,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("rope", &rope);
+  m.def("rope_into", &rope_into);
   m.def("gelu_fwd", &gelu_fwd);
   m.def("gelu_bwd", &gelu_bwd);
   m.def("gelu_cdf_pdf", &gelu_cdf_pdf);
@@ -137,7 +139,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("c"), pybind11::arg("a2") = pybind11::none(), pybind11::arg("b2") = pybind11::none());
   m.def("gemm_rope", &gemm_rope, "tcgen05 GEMM with the rotary-embedding epilogue",
         pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("c"), pybind11::arg("cs"),
-        pybind11::arg("a2") = pybind11::none(), pybind11::arg("b2") = pybind11::none());
+        pybind11::arg("a2") = pybind11::none(), pybind11::arg("b2") = pybind11::none(),
+        pybind11::arg("ncols") = -1);
   m.def("gemm_gelu", &gemm_gelu, "tcgen05 GEMM with the GELU output / GELU-gradient epilogue",
         pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("c"), pybind11::arg("aux"),
         pybind11::arg("b_mn"), pybind11::arg("a2") = pybind11::none(),

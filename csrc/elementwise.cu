@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
 // ----------------------------------------------------------------------------
 __global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ out,
                             const float2* __restrict__ cs, int64_t rows, int S, int H, int D,
-                            float sign) {
+                            float sign, int64_t out_ld) {
   const int half = D >> 1;
   const int groups = half >> 3;
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -243,8 +243,10 @@ __global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* 
     oa[2 * j + 1] = rope_lo(a[2 * j + 1], b[2 * j + 1], c1, s1);
     ob[2 * j + 1] = rope_hi(a[2 * j + 1], b[2 * j + 1], c1, s1);
   }
-  *reinterpret_cast<uint4*>(out + row * D + i0) = f32_to_bf16x8(oa);
-  *reinterpret_cast<uint4*>(out + row * D + half + i0) = f32_to_bf16x8(ob);
+  // output row of token row / H has pitch out_ld (H * D when contiguous)
+  __nv_bfloat16* orow = out + (row / H) * out_ld + (row % H) * D;
+  *reinterpret_cast<uint4*>(orow + i0) = f32_to_bf16x8(oa);
+  *reinterpret_cast<uint4*>(orow + half + i0) = f32_to_bf16x8(ob);
 }
 
 // ----------------------------------------------------------------------------
@@ -646,7 +648,30 @@ void rope(at::Tensor x, at::Tensor out, at::Tensor cs, double sign) {
   const int bs = 256;
   rope_kernel<<<(unsigned)((total + bs - 1) / bs), bs, 0, at::cuda::getCurrentCUDAStream()>>>(
       cbf(x), bf(out), reinterpret_cast<const float2*>(cs.data_ptr<float>()), rows, (int)S,
-      (int)H, (int)D, (float)sign);
+      (int)H, (int)D, (float)sign, H * D);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// RoPE of x [B, S, H, D] written into the first H*D columns of the rows of
+// out [B*S, >= H*D] (row pitch out.stride(0)): a slice of a wider buffer.
+void rope_into(at::Tensor x, at::Tensor out, at::Tensor cs, double sign) {
+  check_bf16(x, "x");
+  TORCH_CHECK(x.dim() == 4, "rope_into: x must be [B, S, H, D]");
+  const int64_t B = x.size(0), S = x.size(1), H = x.size(2), D = x.size(3);
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.dim() == 2 &&
+                  out.size(0) == B * S && out.size(1) >= H * D && out.stride(1) == 1 &&
+                  out.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0,
+              "rope_into: out must be bf16 [B*S, >= H*D] with 16-byte aligned rows");
+  TORCH_CHECK(D % 16 == 0, "rope_into: head dim must be a multiple of 16");
+  TORCH_CHECK(cs.scalar_type() == at::kFloat && cs.is_contiguous() && cs.numel() >= S * D,
+              "rope_into: cos/sin table must be fp32 [S, D/2, 2]");
+  const at::cuda::CUDAGuard guard(x.device());
+  const int64_t rows = B * S * H;
+  const int64_t total = rows * (D / 16);
+  rope_kernel<<<(unsigned)((total + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      cbf(x), reinterpret_cast<__nv_bfloat16*>(out.data_ptr<at::BFloat16>()),
+      reinterpret_cast<const float2*>(cs.data_ptr<float>()), rows, (int)S, (int)H, (int)D,
+      (float)sign, out.stride(0));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

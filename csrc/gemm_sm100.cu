@@ -44,7 +44,8 @@ enum GemmErr { kErrProducer = 101, kErrMma = 102, kErrMmaAcc = 103, kErrEpi = 10
 
 struct GemmArgs {
   int M, N, K;           // main problem; K % 64 == 0
-  int extra_k16;         // number of K=16 MMA steps in the extra slab (0 = none)
+  int extra_k16;         // K=16 MMA steps in the extra slab (0 = none); the pair kernel
+                         // takes 4, 8, 12 or 16 (one pipeline stage per 64 columns)
   int tiles_m, tiles_n;
   __nv_bfloat16* C;
   int64_t ldc;
@@ -80,6 +81,7 @@ struct GemmArgs {
   // epilogue input (kEpiRope): (cos, sin) table [epi_S, 64] of float2
   const float2* epi_cs;
   int epi_S;
+  int epi_ncols;   // kEpiRope: only heads in columns [0, epi_ncols) are rotated
 };
 
 // Pair-kernel epilogues.  kEpiGeluFwd stores C = bf16(acc) through tmC and
@@ -417,7 +419,7 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
   const int num_clusters = gridDim.x >> 1;
   const int num_tiles = args.tiles_m * args.tiles_n;  // tiles of 256 x BN
   const int main_k_tiles = args.K / (kBK * KB);
-  const int k_tiles = main_k_tiles + (args.extra_k16 > 0 ? 1 : 0);
+  const int k_tiles = main_k_tiles + args.extra_k16 / 4;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -480,7 +482,7 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         }
         const int arow = tm * (2 * kBM) + (int)cr * kBM;
         const int brow = tn * BN + (int)cr * (BN / 2);
-        const int kt_end = pw.k1 + ((pw.extra && args.extra_k16 > 0) ? 1 : 0);
+        const int kt_end = pw.k1 + (pw.extra ? args.extra_k16 / 4 : 0);
         for (int kt = pw.k0; kt < kt_end; ++kt) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, args.status, kErrProducer)) { ok = false; break; }
           uint8_t* sa = smem + stage * L::kStageBytes;
@@ -503,14 +505,15 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 tma_load_2d_pair(sb + kb * L::kBAtom, &tmB, leader_full, kc, brow);
               }
             }
-          } else {  // extra 64-wide slab: first atom of the stage only
+          } else {  // extra slab: one 64-wide atom per stage, first atom of the stage only
+            const int ec = (kt - main_k_tiles) * kBK;
             if (cr == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * (L::kAAtom + L::kBAtom));
-            tma_load_2d_pair(sa, &tmA2, leader_full, 0, arow);
+            tma_load_2d_pair(sa, &tmA2, leader_full, ec, arow);
             if (BMN) {
               for (int ch = 0; ch < BN / 128; ++ch)
-                tma_load_2d_pair(sb + ch * 8192, &tmB2, leader_full, brow + ch * 64, 0);
+                tma_load_2d_pair(sb + ch * 8192, &tmB2, leader_full, brow + ch * 64, ec);
             } else {
-              tma_load_2d_pair(sb, &tmB2, leader_full, 0, brow);
+              tma_load_2d_pair(sb, &tmB2, leader_full, ec, brow);
             }
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -535,13 +538,13 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         if (!mbar_wait(&tempty_bar[buf], ((it >> 1) & 1) ^ 1, args.status, kErrMmaAcc)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(buf * 256);
-        const int kt_end = pw.k1 + ((pw.extra && args.extra_k16 > 0) ? 1 : 0);
+        const int kt_end = pw.k1 + (pw.extra ? args.extra_k16 / 4 : 0);
         for (int kt = pw.k0; kt < kt_end; ++kt) {
           if (!mbar_wait(&full_bar[stage], phase, args.status, kErrMma)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * L::kStageBytes);
           const uint32_t b_addr = a_addr + L::kABytes;
-          const int nk = kt < main_k_tiles ? KB * (kBK / 16) : args.extra_k16;
+          const int nk = kt < main_k_tiles ? KB * (kBK / 16) : 4;
           for (int kk = 0; kk < nk; ++kk) {
             const uint32_t ao = (uint32_t)((kk >> 2) * L::kAAtom + (kk & 3) * 32);
             uint64_t bdesc;
@@ -775,8 +778,18 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             oa[i + 1] = rope_lo(a.y, b.y, v.z, v.w);
             ob[i + 1] = rope_hi(a.y, b.y, v.z, v.w);
           }
-          store_chunk(oa, n0 + c0 * 32, m0, none);
-          store_chunk(ob, n0 + c1 * 32, m0, none);
+          if (n0 + c0 * 32 < args.epi_ncols) {
+            store_chunk(oa, n0 + c0 * 32, m0, none);
+            store_chunk(ob, n0 + c1 * 32, m0, none);
+          } else {  // a head past the rotated columns (v of a fused q/k/v GEMM): as is
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              oa[i] = __uint_as_float(ra[i]);
+              ob[i] = __uint_as_float(rb[i]);
+            }
+            store_chunk(oa, n0 + c0 * 32, m0, none);
+            store_chunk(ob, n0 + c1 * 32, m0, none);
+          }
         }
       } else if (pw.sk < 0) {
         uint4 hnext[4] = {};
@@ -1167,7 +1180,8 @@ void set_gemm_pair_mode(int64_t mode) { g_pair_mode = (int)mode; }
 // b_mn = false: B is [N, K] row-major (C = A·Bᵀ); true: B is [K, N] row-major (C = A·B)
 static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
                       const c10::optional<at::Tensor>& a2, const c10::optional<at::Tensor>& b2,
-                      bool b_mn = false, int epi = kEpiPlain, const at::Tensor* aux = nullptr) {
+                      bool b_mn = false, int epi = kEpiPlain, const at::Tensor* aux = nullptr,
+                      int64_t rope_ncols = -1) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: CUDA tensors");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 &&
                   c.scalar_type() == at::kBFloat16, "gemm: bf16 operands");
@@ -1211,19 +1225,23 @@ static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
     const at::Tensor& x2 = *a2;
     const at::Tensor& y2 = *b2;
     TORCH_CHECK(x2.scalar_type() == at::kBFloat16 && y2.scalar_type() == at::kBFloat16, "extra slab bf16");
+    // width 64 everywhere; 128, 192 or 256 (one stage per 64 columns) on the pair kernel
+    const int64_t E = x2.size(1);
+    TORCH_CHECK(E == 64 || (E % 64 == 0 && E <= 256 && pair),
+                "extra slab width must be 64 (or 128/192/256 on the CTA-pair kernel, M >= 256)");
     if (b_mn) {
-      TORCH_CHECK(x2.size(0) == M && x2.size(1) == 64 && y2.size(0) == 64 && y2.size(1) == N &&
+      TORCH_CHECK(x2.size(0) == M && y2.size(0) == E && y2.size(1) == N &&
                       x2.stride(1) == 1 && y2.stride(1) == 1,
-                  "extra slab operands must be [M,64] and [64,N] row-major");
+                  "extra slab operands must be [M,E] and [E,N] row-major");
     } else {
-      TORCH_CHECK(x2.size(0) == M && y2.size(0) == N && x2.size(1) == 64 && y2.size(1) == 64 &&
+      TORCH_CHECK(x2.size(0) == M && y2.size(0) == N && y2.size(1) == E &&
                       x2.stride(1) == 1 && y2.stride(1) == 1,
-                  "extra slab operands must be [M,64] and [N,64] row-major");
+                  "extra slab operands must be [M,E] and [N,E] row-major");
     }
-    ta2 = make_tmap_bf16(x2.data_ptr(), M, 64, x2.stride(0), kBM);
-    tb2 = b_mn ? make_tmap_bf16(y2.data_ptr(), 64, N, y2.stride(0), 64)
-               : make_tmap_bf16(y2.data_ptr(), N, 64, y2.stride(0), b_box);
-    args.extra_k16 = 4;
+    ta2 = make_tmap_bf16(x2.data_ptr(), M, E, x2.stride(0), kBM);
+    tb2 = b_mn ? make_tmap_bf16(y2.data_ptr(), E, N, y2.stride(0), 64)
+               : make_tmap_bf16(y2.data_ptr(), N, E, y2.stride(0), b_box);
+    args.extra_k16 = (int)(E / 16);
   }
   auto stream = at::cuda::getCurrentCUDAStream();
   TORCH_CHECK(epi == kEpiPlain || (pair && K % 128 == 0 && aux != nullptr),
@@ -1240,6 +1258,8 @@ static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
                   "gemm: RoPE table must be fp32 [S, 64, 2] with M a multiple of S");
       args.epi_cs = reinterpret_cast<const float2*>(t.data_ptr<float>());
       args.epi_S = (int)t.size(0);
+      args.epi_ncols = rope_ncols < 0 ? (int)N : (int)rope_ncols;
+      TORCH_CHECK(args.epi_ncols % 128 == 0, "gemm: rotated columns must be whole 128-wide heads");
       if (bn == 256) launch_gemm_pair<256, 3, 2, false, false, false, kEpiRope>(ta, tb, ta2, tb2, tc, args, stream, sms);
       else launch_gemm_pair<128, 4, 2, false, false, false, kEpiRope>(ta, tb, ta2, tb2, tc, args, stream, sms);
       return;
@@ -1311,10 +1331,11 @@ void gemm_gelu(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor aux, bool b_
 }
 
 // C = rope(A·Bᵀ (+ A2·B2ᵀ)) for 128-wide heads; cs: fp32 [S, 64, 2] (cos, sin) per
-// position and pair, row m of C at position m % S.  Needs M >= 256, K % 128 == 0.
+// position and pair, row m of C at position m % S; only columns [0, ncols) are
+// rotated (ncols < 0: all).  Needs M >= 256, K % 128 == 0.
 void gemm_rope(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor cs,
-               c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2) {
-  gemm_impl(a, b, c, a2, b2, false, kEpiRope, &cs);
+               c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2, int64_t ncols) {
+  gemm_impl(a, b, c, a2, b2, false, kEpiRope, &cs, ncols);
 }
 
 // GEMM whose B operand is a 4-bit weight W [rows, cols] decoded inside the

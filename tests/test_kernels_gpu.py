@@ -916,3 +916,79 @@ def test_rope_spec_projection_attention_chain_matches_apply_rope(cuda):
     assert torch.equal(o, o2)
     assert torch.equal(g1, x.grad)
     torch.testing.assert_close(gA1, qp.lora_A.grad, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("lora_r", [0, 16])
+def test_fused_qkv_projection_matches_separate_projections(cuda, lora_r):
+    """One GEMM for q, k, v (RoPE on the q/k columns, three LoRA slabs) and its
+    backward (one input-gradient GEMM over the concatenated gradient) against the
+    three projections + apply_rope, through the attention."""
+    from zeroq_b200.ops.attention import flash_attention
+    from zeroq_b200.ops.qkv import qkv_fusable, qkv_projection
+    from zeroq_b200.ops.qlinear import Linear4bit
+    from zeroq_b200.ops.rope import apply_rope, rope_table
+
+    torch.manual_seed(13)
+    B, S, d, Hq, Hk = 2, 256, 512, 4, 2
+    mods = [Linear4bit(d, h * 128, lora_r=lora_r, device=cuda) for h in (Hq, Hk, Hk)]
+    for m in mods:
+        m.quantize_from(torch.randn(m.out_features, d, device=cuda) * 0.05)
+        if lora_r:
+            with torch.no_grad():
+                m.lora_B.normal_(0, 0.05)
+    x = torch.randn(B, S, d, device=cuda).to(torch.bfloat16).requires_grad_(True)
+    cs = rope_table(S, 128, 10000.0, cuda)
+    assert qkv_fusable(mods, x, S)
+    go = torch.randn(B, S, Hq, 128, device=cuda).to(torch.bfloat16)
+    results = []
+    cache = {}
+    for fused in (True, False, True):   # fused twice: the LoRA block cache is reused
+        x.grad = None
+        for m in mods:
+            if lora_r:
+                m.lora_A.grad = None
+                m.lora_B.grad = None
+        if fused:
+            q, k, v = qkv_projection(x, mods, cs, cache)
+        else:
+            q, k = apply_rope(mods[0](x).view(B, S, Hq, 128), mods[1](x).view(B, S, Hk, 128), 10000.0)
+            v = mods[2](x).view(B, S, Hk, 128)
+        o = flash_attention(q, k, v, causal=True)
+        o.backward(go)
+        results.append([o.detach().clone(), x.grad.clone()] +
+                       ([g for m in mods for g in (m.lora_A.grad.clone(), m.lora_B.grad.clone())]
+                        if lora_r else []))
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    for a, b in zip(results[0], results[1]):
+        scale = b.float().abs().max().item() + 1e-6
+        assert (a.float() - b.float()).abs().max().item() <= 2e-2 * scale, (a.shape,)
+    for a, b in zip(results[0], results[2]):
+        assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("E", [128, 192, 256])
+@pytest.mark.parametrize("nn", [False, True])
+def test_gemm_wide_extra_slab_matches_concatenated_k(cuda, E, nn):
+    """An extra K slab of 2-4 x 64 columns (one pipeline stage each) equals the
+    GEMM over the concatenated K dimension."""
+    Ex = _ext.ext()
+    torch.manual_seed(14)
+    M, N, K = 512, 768, 1024
+    x = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    a2 = (torch.randn(M, E, device=cuda) * 0.1).to(torch.bfloat16)
+    y = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    ref = torch.empty_like(y)
+    if nn:
+        w = (torch.randn(K, N, device=cuda) * 0.05).to(torch.bfloat16)
+        b2 = (torch.randn(E, N, device=cuda) * 0.1).to(torch.bfloat16)
+        Ex.gemm_bf16_nn(x, w, y, a2, b2)
+        Ex.gemm_bf16_nn(torch.cat([x, a2], 1), torch.cat([w, b2], 0), ref, None, None)
+    else:
+        w = (torch.randn(N, K, device=cuda) * 0.05).to(torch.bfloat16)
+        b2 = (torch.randn(N, E, device=cuda) * 0.1).to(torch.bfloat16)
+        Ex.gemm_bf16_tn_extra(x, w, y, a2, b2)
+        Ex.gemm_bf16_tn(torch.cat([x, a2], 1), torch.cat([w, b2], 1), ref)
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    torch.testing.assert_close(y.float(), ref.float(), rtol=1e-2, atol=1e-2)

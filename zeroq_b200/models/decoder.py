@@ -38,6 +38,7 @@ from ..ops.cross_entropy import cross_entropy
 from ..ops.gemm import LMHeadFunction
 from ..ops.norm import add_rmsnorm
 from ..ops.qlinear import Linear4bit
+from ..ops.qkv import qkv_fusable, qkv_projection
 from ..ops.rope import RopeSpec, apply_rope, rope_table
 
 
@@ -131,6 +132,11 @@ class RMSNorm(nn.Module):
         return add_rmsnorm(h, delta, self.weight, self.eps)
 
 
+def _hooked(m: nn.Module) -> bool:
+    return bool(m._forward_hooks or m._forward_pre_hooks or m._backward_hooks
+                or m._backward_pre_hooks)
+
+
 class DecoderLayer(nn.Module):
     def __init__(self, cfg: DecoderConfig, device=None, dtype=torch.bfloat16):
         super().__init__()
@@ -180,10 +186,18 @@ class DecoderLayer(nn.Module):
             # rope=spec) but measured slower than the RoPE kernel it replaces
             # (B=8 S=1024 H=24: +97 us against 2 x 25 us), so the projections'
             # backward un-rotates
-            spec = RopeSpec(rope_table(S, cfg.head_dim, cfg.rope_theta, x.device))
-            q = self.q_proj(x, rope=spec).view(B, S, cfg.n_heads, cfg.head_dim)
-            k = self.k_proj(x, rope=spec).view(B, S, cfg.n_kv_heads, cfg.head_dim)
-            v = self.v_proj(x).view(B, S, cfg.n_kv_heads, cfg.head_dim)
+            cs = rope_table(S, cfg.head_dim, cfg.rope_theta, x.device)
+            mods = (self.q_proj, self.k_proj, self.v_proj)
+            if not any(_hooked(m) for m in mods) and qkv_fusable(mods, x, S):
+                # one GEMM for q, k and v (column slices of one output)
+                if not hasattr(self, "_qkv_cache"):
+                    self._qkv_cache = {}
+                q, k, v = qkv_projection(x, mods, cs, self._qkv_cache)
+            else:
+                spec = RopeSpec(cs)
+                q = self.q_proj(x, rope=spec).view(B, S, cfg.n_heads, cfg.head_dim)
+                k = self.k_proj(x, rope=spec).view(B, S, cfg.n_kv_heads, cfg.head_dim)
+                v = self.v_proj(x).view(B, S, cfg.n_kv_heads, cfg.head_dim)
             o = flash_attention(q, k, v, causal=True)
         else:
             q = self.q_proj(x).view(B, S, cfg.n_heads, cfg.head_dim)
@@ -210,8 +224,7 @@ class DecoderLayer(nn.Module):
         mods = (self.q_proj, self.k_proj)
         return (x.is_cuda and self.cfg.head_dim == 128
                 and all(isinstance(m, Linear4bit) for m in mods)
-                and not any(m._forward_hooks or m._forward_pre_hooks or m._backward_hooks
-                            or m._backward_pre_hooks for m in mods))
+                and not any(_hooked(m) for m in mods))
 
     def _fused_gelu_mlp(self) -> bool:
         from ..ops.qlinear import Linear4bit

@@ -42,12 +42,20 @@ def attention_reference(q, k, v, causal: bool = True, scale=None):
     return o.transpose(1, 2).to(q.dtype)
 
 
+def _tma_ok(t: torch.Tensor) -> bool:
+    return (t.stride(-1) == 1 and all(st % 8 == 0 for st in t.stride()[:-1])
+            and t.data_ptr() % 16 == 0)
+
+
 class _FlashAttn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, causal, scale, rope=None):
-        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        D = q.shape[-1]
+        # the tcgen05 kernels read q/k/v through TMA maps and take strided views
+        # (column slices of a fused q/k/v projection) as they are
+        q, k, v = (t if (D == 128 and _tma_ok(t)) else t.contiguous() for t in (q, k, v))
         B, S, Hq, D = q.shape
-        o = torch.empty_like(q)
+        o = torch.empty(q.shape, dtype=q.dtype, device=q.device)
         lse = torch.empty(B, Hq, S, dtype=torch.float32, device=q.device)
         if D == 128:
             _ext.ext().attn_fwd_tc(q, k, v, o, lse, bool(causal), float(scale))
@@ -62,9 +70,7 @@ class _FlashAttn(torch.autograd.Function):
     def backward(ctx, do):
         q, k, v, o, lse = ctx.saved_tensors
         do = do.contiguous()
-        dq = torch.empty_like(q)
-        dk = torch.empty_like(k)
-        dv = torch.empty_like(v)
+        dq, dk, dv = (torch.empty(t.shape, dtype=t.dtype, device=t.device) for t in (q, k, v))
         if q.shape[-1] == 128:
             rope = ctx.rope
             cs = rope.cs if rope is not None and rope.cs.shape[0] == q.shape[1] else None
