@@ -19,7 +19,10 @@ Reported (rank 0, one JSON line):
   steps (barrier + synchronize on both sides, max over ranks); inputs resident.
 * ``e2e``: the same through ``Trainer.step`` - pinned host -> device copy of the
   batch and a device -> host read of the loss every step.
-* ``gpu_launches``: this framework's kernel launches inside the timed region.
+* ``gpu_launches``: this framework's kernel launches inside the timed region
+  (with ``cuda_graph``, the kernels captured in one step times the steps).
+* ``cuda_graph``: each step ran as one CUDA graph replay (the default for the
+  resident-weight configs; ``--no-graph`` runs eagerly).
 * ``clocks``: nvidia-smi SM clock median and throttle reasons sampled during it.
 The step's working set (NF4 weights, activations, logits) is tens of GB, far
 larger than the 126 MB L2, so no explicit L2 flush is needed between steps.
@@ -101,6 +104,8 @@ def main():
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--seq", type=int, default=None)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="run the steps eagerly instead of as one CUDA graph replay each")
     ap.add_argument("--torch-profile", default=None,
                     help="after timing, profile one more step and write a per-kernel table here")
     args = ap.parse_args()
@@ -154,10 +159,16 @@ def main():
     x_host, y_host = synthetic_batch(B, S, cfg.vocab_size, seed=1000 + rank)
     x_dev, y_dev = x_host.to(device), y_host.to(device)
 
+    # CUDA graph (weights resident, fixed shapes): warm-up step 0 runs eagerly,
+    # step 1 runs eagerly on the capture stream and captures, later steps replay
+    use_graph = not args.no_graph and mode == "4bit-once"
     losses = []
-    for _ in range(args.warmup):
+    for i in range(args.warmup):
+        if use_graph and i == 1:
+            trainer.enable_cuda_graph()
         losses.append(trainer.step_device(x_dev, y_dev))
     torch.cuda.synchronize()
+    graphed = trainer._graph is not None
 
     with ClockSampler(local) as clk, _ext.LaunchCounter() as lc:
         ms = device_time_ms(lambda: trainer.step_device(x_dev, y_dev), args.steps)
@@ -215,7 +226,8 @@ def main():
                                       + y_host.numel() * y_host.element_size()),
             "d2h_bytes_per_step": 4,
         },
-        "gpu_launches": lc.count,
+        "gpu_launches": trainer.graph_launches * args.steps if graphed else lc.count,
+        "cuda_graph": graphed,
         "clocks": clk.summary(),
         "achieved_tflops_per_gpu": round(tflops_per_gpu, 1),
         "frac_of_measured_bf16_sustained": round(tflops_per_gpu / peaks["bf16_tflops_sustained"], 3),

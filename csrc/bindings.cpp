@@ -44,7 +44,8 @@ void ce_bwd(at::Tensor logits, at::Tensor targets, at::Tensor lse, at::Tensor sc
             int64_t ignore_index);
 void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> pbf16,
                 double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
-                double gscale);
+                double gscale, c10::optional<at::Tensor> bc);
+void opt_tick(at::Tensor clk, at::Tensor bc, double b1, double b2, bool bump_epoch);
 void lion_step(at::Tensor master, at::Tensor grad, at::Tensor mom, double lr, double b1, double b2,
                double wd, int64_t seed);
 // p2p.cu
@@ -59,7 +60,8 @@ int64_t peer_flag_words();
 void rs_adamw(std::vector<int64_t> grads, std::vector<int64_t> params, std::vector<int64_t> flags,
               int64_t rank, int64_t epoch, int64_t lo, int64_t n, at::Tensor m, at::Tensor v,
               int64_t grad_is_bf16, double lr, double b1, double b2, double eps, double wd,
-              double bc1, double bc2, double gscale, bool push, int64_t timeout_ms);
+              double bc1, double bc2, double gscale, bool push, int64_t timeout_ms,
+              c10::optional<at::Tensor> clk, c10::optional<at::Tensor> bc);
 void plan_gather(std::vector<int64_t> src, std::vector<int64_t> flags, int64_t rank, int64_t epoch,
                  std::vector<int64_t> offsets, std::vector<int64_t> lengths, at::Tensor out,
                  int64_t timeout_ms);
@@ -120,7 +122,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("ce_fwd", &ce_fwd);
   m.def("ce_bwd", &ce_bwd);
-  m.def("adamw_step", &adamw_step);
+  m.def("adamw_step", [](at::Tensor p, at::Tensor g, at::Tensor m_, at::Tensor v,
+                         c10::optional<at::Tensor> pbf16, double lr, double b1, double b2, double eps,
+                         double wd, double bc1, double bc2, double gscale) {
+    adamw_step(p, g, m_, v, pbf16, lr, b1, b2, eps, wd, bc1, bc2, gscale, c10::nullopt);
+  });
+  // bias corrections read from the device-side optimizer clock (bc, see opt_tick)
+  m.def("adamw_step_dev", &adamw_step);
+  m.def("opt_tick", &opt_tick, "advance the device-side optimizer clock");
   m.def("lion_step", &lion_step);
   m.def("peer_alloc", &peer_alloc);
   m.def("peer_handle", &peer_handle);
@@ -130,7 +139,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("peer_status_read", &peer_status_read);
   m.def("peer_flag_words", &peer_flag_words);
-  m.def("rs_adamw", &rs_adamw);
+  m.def("rs_adamw", [](std::vector<int64_t> grads, std::vector<int64_t> params, std::vector<int64_t> flags,
+                       int64_t rank, int64_t epoch, int64_t lo, int64_t n, at::Tensor m_, at::Tensor v,
+                       int64_t grad_is_bf16, double lr, double b1, double b2, double eps, double wd,
+                       double bc1, double bc2, double gscale, bool push, int64_t timeout_ms) {
+    rs_adamw(grads, params, flags, rank, epoch, lo, n, m_, v, grad_is_bf16, lr, b1, b2, eps, wd, bc1,
+             bc2, gscale, push, timeout_ms, c10::nullopt, c10::nullopt);
+  });
+  // epoch and bias corrections from the device-side optimizer clock
+  m.def("rs_adamw_dev", &rs_adamw);
   m.def("plan_gather", &plan_gather);
   m.def("plan_gather_dequant", &plan_gather_dequant);
   m.def("ag_gemm_f32", &ag_gemm_f32, "gather of fp32 pieces + bf16 cast + tcgen05 GEMM in one kernel",

@@ -443,7 +443,11 @@ template <typename G>
 __global__ void adamw_kernel(float* __restrict__ p, const G* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ pbf, int64_t n,
                              float lr, float b1, float b2, float eps, float wd, float bc1,
-                             float bc2, float gscale) {
+                             float bc2, float gscale, const float* __restrict__ bcp) {
+  if (bcp != nullptr) {  // bias corrections from the device-side optimizer clock
+    bc1 = bcp[0];
+    bc2 = bcp[1];
+  }
   const float step_size = lr / bc1;
   const float inv_sqrt_bc2 = rsqrtf(bc2);
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -773,7 +777,12 @@ void ce_bwd(at::Tensor logits, at::Tensor targets, at::Tensor lse, at::Tensor sc
 
 void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v,
                 c10::optional<at::Tensor> pbf16, double lr, double b1, double b2, double eps,
-                double wd, double bc1, double bc2, double gscale) {
+                double wd, double bc1, double bc2, double gscale, c10::optional<at::Tensor> bc) {
+  const float* bcp = nullptr;
+  if (bc.has_value() && bc->defined()) {
+    TORCH_CHECK(bc->is_cuda() && bc->scalar_type() == at::kFloat && bc->numel() >= 2, "adamw: bc fp32[2]");
+    bcp = bc->data_ptr<float>();
+  }
   TORCH_CHECK(p.is_cuda() && p.scalar_type() == at::kFloat && p.is_contiguous(), "adamw: fp32 param");
   TORCH_CHECK(m.scalar_type() == at::kFloat && v.scalar_type() == at::kFloat, "adamw: fp32 moments");
   const int64_t n = p.numel();
@@ -787,13 +796,36 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v,
   if (g.scalar_type() == at::kFloat) {
     adamw_kernel<float><<<grid, 256, 0, stream>>>(p.data_ptr<float>(), g.data_ptr<float>(),
         m.data_ptr<float>(), v.data_ptr<float>(), pb, n, (float)lr, (float)b1, (float)b2,
-        (float)eps, (float)wd, (float)bc1, (float)bc2, (float)gscale);
+        (float)eps, (float)wd, (float)bc1, (float)bc2, (float)gscale, bcp);
   } else {
     TORCH_CHECK(g.scalar_type() == at::kBFloat16, "adamw: grad fp32 or bf16");
     adamw_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(p.data_ptr<float>(), cbf(g),
         m.data_ptr<float>(), v.data_ptr<float>(), pb, n, (float)lr, (float)b1, (float)b2,
-        (float)eps, (float)wd, (float)bc1, (float)bc2, (float)gscale);
+        (float)eps, (float)wd, (float)bc1, (float)bc2, (float)gscale, bcp);
   }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Device-side optimizer clock: clk = int64 [step, epoch], bc = fp32 [1 - b1^step,
+// 1 - b2^step].  One thread advances the step (and the cross-rank epoch when
+// bump_epoch) and recomputes the bias corrections in double precision, as the
+// host does; kernels later on the stream read them, so a CUDA graph that
+// captured this launch advances the optimizer on every replay.
+__global__ void opt_tick_kernel(int64_t* clk, float* bc, double b1, double b2, int bump_epoch) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    const int64_t step = ++clk[0];
+    if (bump_epoch) ++clk[1];
+    bc[0] = (float)(1.0 - pow(b1, (double)step));
+    bc[1] = (float)(1.0 - pow(b2, (double)step));
+  }
+}
+
+void opt_tick(at::Tensor clk, at::Tensor bc, double b1, double b2, bool bump_epoch) {
+  TORCH_CHECK(clk.is_cuda() && clk.scalar_type() == at::kLong && clk.numel() >= 2, "opt_tick: clk int64[2]");
+  TORCH_CHECK(bc.is_cuda() && bc.scalar_type() == at::kFloat && bc.numel() >= 2, "opt_tick: bc fp32[2]");
+  const at::cuda::CUDAGuard guard(clk.device());
+  opt_tick_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(clk.data_ptr<int64_t>(), bc.data_ptr<float>(),
+                                                                 b1, b2, bump_epoch ? 1 : 0);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

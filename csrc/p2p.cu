@@ -162,7 +162,16 @@ __global__ void __launch_bounds__(256) rs_adamw_kernel(PeerTable grads, PeerTabl
                                                        float* __restrict__ v, float lr, float b1,
                                                        float b2, float eps, float wd, float bc1,
                                                        float bc2, float gscale, int push,
-                                                       unsigned long long wait_ns) {
+                                                       unsigned long long wait_ns,
+                                                       const int64_t* __restrict__ clk,
+                                                       const float* __restrict__ bcp) {
+  // device-side optimizer clock (CUDA-graph replays): epoch and bias corrections
+  // written by opt_tick earlier on this stream instead of launch arguments
+  if (clk != nullptr) epoch = (int)clk[1];
+  if (bcp != nullptr) {
+    bc1 = bcp[0];
+    bc2 = bcp[1];
+  }
   const bool ok = grid_start(flags, rank, world, epoch, wait_ns);
   if (ok) {
     const float step_size = lr / bc1;
@@ -436,7 +445,8 @@ static int resident_grid(K kernel, int threads) {
 void rs_adamw(std::vector<int64_t> grads, std::vector<int64_t> params, std::vector<int64_t> flags,
               int64_t rank, int64_t epoch, int64_t lo, int64_t n, at::Tensor m, at::Tensor v,
               int64_t grad_is_bf16, double lr, double b1, double b2, double eps, double wd,
-              double bc1, double bc2, double gscale, bool push, int64_t timeout_ms) {
+              double bc1, double bc2, double gscale, bool push, int64_t timeout_ms,
+              c10::optional<at::Tensor> clk, c10::optional<at::Tensor> bc) {
   const int world = (int)grads.size();
   TORCH_CHECK(world >= 1 && world <= kMaxRanks && (int)params.size() == world &&
                   (int)flags.size() == world, "rs_adamw: one pointer per rank");
@@ -444,18 +454,27 @@ void rs_adamw(std::vector<int64_t> grads, std::vector<int64_t> params, std::vect
   TORCH_CHECK(m.numel() >= n && v.numel() >= n, "rs_adamw: moments too small");
   const at::cuda::CUDAGuard guard(m.device());
   auto stream = at::cuda::getCurrentCUDAStream();
+  const int64_t* clkp = nullptr;
+  const float* bcp = nullptr;
+  if (clk.has_value() && clk->defined()) {
+    TORCH_CHECK(clk->scalar_type() == at::kLong && clk->numel() >= 2 && clk->is_cuda(), "rs_adamw: clk int64[2]");
+    TORCH_CHECK(bc.has_value() && bc->defined() && bc->scalar_type() == at::kFloat && bc->numel() >= 2,
+                "rs_adamw: bc fp32[2] with clk");
+    clkp = clk->data_ptr<int64_t>();
+    bcp = bc->data_ptr<float>();
+  }
   const int grid = grad_is_bf16 ? resident_grid(rs_adamw_kernel<__nv_bfloat16>, 256)
                                 : resident_grid(rs_adamw_kernel<float>, 256);
   if (grad_is_bf16) {
     rs_adamw_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
         table_from(grads), table_from(params), table_from(flags), (int)rank, world, (int)epoch, lo, n,
         m.data_ptr<float>(), v.data_ptr<float>(), (float)lr, (float)b1, (float)b2, (float)eps,
-        (float)wd, (float)bc1, (float)bc2, (float)gscale, push ? 1 : 0, wait_ns(timeout_ms));
+        (float)wd, (float)bc1, (float)bc2, (float)gscale, push ? 1 : 0, wait_ns(timeout_ms), clkp, bcp);
   } else {
     rs_adamw_kernel<float><<<grid, 256, 0, stream>>>(
         table_from(grads), table_from(params), table_from(flags), (int)rank, world, (int)epoch, lo, n,
         m.data_ptr<float>(), v.data_ptr<float>(), (float)lr, (float)b1, (float)b2, (float)eps,
-        (float)wd, (float)bc1, (float)bc2, (float)gscale, push ? 1 : 0, wait_ns(timeout_ms));
+        (float)wd, (float)bc1, (float)bc2, (float)gscale, push ? 1 : 0, wait_ns(timeout_ms), clkp, bcp);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

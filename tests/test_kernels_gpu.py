@@ -992,3 +992,46 @@ def test_gemm_wide_extra_slab_matches_concatenated_k(cuda, E, nn):
     torch.cuda.synchronize()
     _status_ok(cuda)
     torch.testing.assert_close(y.float(), ref.float(), rtol=1e-2, atol=1e-2)
+
+
+def test_cuda_graph_training_steps_match_eager(cuda):
+    """Trainer steps replayed from one captured CUDA graph (device-side optimizer
+    clock) track the same steps run eagerly.  Eager steps are not bitwise
+    reproducible (floating-point atomics, and Adam's first updates are close to
+    sign(grad), which amplifies last-bit differences), so the graph run must stay
+    within a few times the spread between two eager runs."""
+    from zeroq_b200 import ShardedAdamW, ZeroQConfig, initialize
+    from zeroq_b200.models import DecoderLM, get_config
+    from zeroq_b200.train import Trainer
+
+    def run(graph: bool):
+        cfg = get_config("4.7b", n_layers=2, lora_r=8, lora_alpha=16.0)
+        model = DecoderLM(cfg, device=cuda)
+        model.init_dense_(std=0.02, seed=7)
+        zq = ZeroQConfig(compute_dtype=torch.bfloat16, compute_in_4bit=True, gather_once=True,
+                         exclude_modules=["lm_head", "embed_tokens"], backend="auto")
+        initialize(model, zq, trainable_patterns=("lora_", "norm"))
+        opt = ShardedAdamW(model.trainable_parameters(), lr=1e-3)
+        tr = Trainer(model, opt, cuda)
+        g = torch.Generator().manual_seed(3)
+        x = torch.randint(0, cfg.vocab_size, (2, 256), generator=g).to(cuda)
+        y = torch.randint(0, cfg.vocab_size, (2, 256), generator=g).to(cuda)
+        losses = [float(tr.step_device(x, y))]
+        if graph:
+            tr.enable_cuda_graph()
+        for _ in range(5):
+            losses.append(float(tr.step_device(x, y)))
+        torch.cuda.synchronize()
+        assert (tr._graph is not None) == graph
+        assert opt.state_dict()["step"] == 6   # the device clock advanced on every replay
+        return torch.tensor(losses), torch.cat([p.detach().float().reshape(-1) for p in opt.params])
+
+    la, pa = run(False)
+    lb, pb = run(False)
+    lg, pg = run(True)
+    _status_ok(cuda)
+    assert lg[-1] < lg[0] - 1.0 and la[-1] < la[0] - 1.0
+    spread_l = (lb - la).abs().max().item()
+    spread_p = (pb - pa).abs().max().item()
+    assert (lg - la).abs().max().item() <= 3 * spread_l + 2e-3, (lg, la, lb)
+    assert (pg - pa).abs().max().item() <= 3 * spread_p + 1e-4

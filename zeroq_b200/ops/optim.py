@@ -24,10 +24,18 @@ from . import _ext
 def adamw_step(param: torch.Tensor, grad: torch.Tensor, exp_avg: torch.Tensor,
                exp_avg_sq: torch.Tensor, *, lr: float, beta1: float = 0.9,
                beta2: float = 0.999, eps: float = 1e-8, weight_decay: float = 0.0,
-               step: int = 1, grad_scale: float = 1.0, param_bf16: torch.Tensor = None):
-    """In-place AdamW on flat fp32 tensors (``grad`` may be fp32 or bf16)."""
+               step: int = 1, grad_scale: float = 1.0, param_bf16: torch.Tensor = None,
+               bc_dev: torch.Tensor = None):
+    """In-place AdamW on flat fp32 tensors (``grad`` may be fp32 or bf16).
+    ``bc_dev``: fp32 [2] bias corrections on the device (device-side optimizer
+    clock), used instead of ``step``."""
     bc1 = 1.0 - beta1 ** step
     bc2 = 1.0 - beta2 ** step
+    if param.is_cuda and bc_dev is not None:
+        _ext.ext().adamw_step_dev(param, grad, exp_avg, exp_avg_sq, param_bf16, float(lr),
+                                  float(beta1), float(beta2), float(eps), float(weight_decay),
+                                  1.0, 1.0, float(grad_scale), bc_dev)
+        return
     if param.is_cuda:
         _ext.ext().adamw_step(param, grad, exp_avg, exp_avg_sq, param_bf16, float(lr),
                               float(beta1), float(beta2), float(eps), float(weight_decay),

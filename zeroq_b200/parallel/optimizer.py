@@ -124,6 +124,26 @@ class ShardedAdamW:
         if backend == "fused" and self._peer is None:
             self.backend = "nccl"
         self.last_grad_norm: Optional[torch.Tensor] = None
+        self.device_clock = None   # (clk int64 [step, epoch], bc fp32 [2]) once enabled
+
+    def use_device_clock(self):
+        """Keep the step count, the bias corrections and (fused backend) the
+        cross-rank barrier epoch on the device, advanced by a kernel at the start of
+        every step, so a CUDA graph that captured a step replays it correctly."""
+        if self.device_clock is not None:
+            return
+        dev = self.flat.data.device
+        epoch = self._peer.flags.epoch if self._peer is not None else 0
+        clk = torch.tensor([self.step_count, epoch], dtype=torch.int64, device=dev)
+        bc = torch.ones(2, dtype=torch.float32, device=dev)
+        self.device_clock = (clk, bc)
+
+    def _tick(self):
+        from ..ops import _ext
+
+        b1, b2 = self.betas
+        clk, bc = self.device_clock
+        _ext.ext().opt_tick(clk, bc, float(b1), float(b2), self._peer is not None)
 
     @property
     def params(self):
@@ -151,11 +171,17 @@ class ShardedAdamW:
     def _step(self):
         self.step_count += 1
         b1, b2 = self.betas
+        bc_dev = None
+        if self.device_clock is not None:
+            if self.max_grad_norm is not None:
+                raise NotImplementedError("gradient clipping syncs with the host; not with the device clock")
+            self._tick()
+            bc_dev = self.device_clock[1]
         if self.world == 1:
             scale = self._clip_scale(self.flat.grad, 1.0)
             adamw_step(self.flat.data, self.flat.grad, self.exp_avg, self.exp_avg_sq, lr=self.lr,
                        beta1=b1, beta2=b2, eps=self.eps, weight_decay=self.wd,
-                       step=self.step_count, grad_scale=scale)
+                       step=self.step_count, grad_scale=scale, bc_dev=bc_dev)
             return
         lo = self.rank * self.shard
         mine = self.flat.data[lo:lo + self.shard]
@@ -171,13 +197,15 @@ class ShardedAdamW:
         scale = self._clip_scale(self.grad_shard, 1.0 / self.world) / self.world
         adamw_step(mine, self.grad_shard, self.exp_avg, self.exp_avg_sq, lr=self.lr,
                    beta1=b1, beta2=b2, eps=self.eps, weight_decay=self.wd,
-                   step=self.step_count, grad_scale=scale)
+                   step=self.step_count, grad_scale=scale, bc_dev=bc_dev)
         # NCCL gathers in place when the input is this rank's slice of the output;
         # other backends get a private copy of the shard.
         src = mine if self.flat.data.is_cuda else mine.clone()
         dist.all_gather_into_tensor(self.flat.data, src, group=self.pg)
 
     def state_dict(self) -> dict:
+        if self.device_clock is not None:   # replays advance only the device clock
+            self.step_count = int(self.device_clock[0][0])
         return {"step": self.step_count, "exp_avg": self.exp_avg.detach().cpu(),
                 "exp_avg_sq": self.exp_avg_sq.detach().cpu(), "lr": self.lr,
                 "betas": self.betas, "eps": self.eps, "weight_decay": self.wd,
@@ -187,5 +215,7 @@ class ShardedAdamW:
         if st["shard"] != self.shard:
             raise ValueError("optimizer shard size differs (different world size or params)")
         self.step_count = int(st["step"])
+        if self.device_clock is not None:
+            self.device_clock[0][0] = self.step_count
         self.exp_avg.copy_(st["exp_avg"])
         self.exp_avg_sq.copy_(st["exp_avg_sq"])

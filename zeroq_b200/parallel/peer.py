@@ -119,9 +119,20 @@ class PeerReduceScatterAdamW:
         return owner
 
     def run(self, lo: int, n: int, m: torch.Tensor, v: torch.Tensor, *, lr, beta1, beta2, eps,
-            weight_decay, step, grad_scale, push: bool = True, timeout_ms: int = 0):
+            weight_decay, step, grad_scale, push: bool = True, timeout_ms: int = 0,
+            clock=None):
+        """``clock = (clk, bc)``: take the barrier epoch and the bias corrections from
+        the device-side optimizer clock (see :meth:`ShardedAdamW.use_device_clock`)
+        instead of launch arguments."""
         bc1 = 1.0 - beta1 ** step
         bc2 = 1.0 - beta2 ** step
+        if clock is not None:
+            _ext.ext().rs_adamw_dev(self.grad_buf.ptrs, self.param_buf.ptrs, self.flags.ptrs,
+                                    self.flags.rank, 0, int(lo), int(n), m, v,
+                                    1 if self.grad_is_bf16 else 0, float(lr), float(beta1),
+                                    float(beta2), float(eps), float(weight_decay), 1.0, 1.0,
+                                    float(grad_scale), bool(push), int(timeout_ms), clock[0], clock[1])
+            return
         _ext.ext().rs_adamw(self.grad_buf.ptrs, self.param_buf.ptrs, self.flags.ptrs,
                             self.flags.rank, self.flags.next_epoch(), int(lo), int(n), m, v,
                             1 if self.grad_is_bf16 else 0, float(lr), float(beta1), float(beta2),
@@ -133,7 +144,7 @@ class PeerReduceScatterAdamW:
         lo = opt.rank * opt.shard
         self.run(lo, opt.shard, opt.exp_avg, opt.exp_avg_sq, lr=opt.lr, beta1=b1, beta2=b2,
                  eps=opt.eps, weight_decay=opt.wd, step=opt.step_count,
-                 grad_scale=1.0 / opt.world, push=True)
+                 grad_scale=1.0 / opt.world, push=True, clock=opt.device_clock)
 
 
 def peer_flat_allocator(group):

@@ -36,6 +36,47 @@ class Trainer:
         self.pg = process_group
         self._in = None
         self._tg = None
+        self._graph_on = False
+        self._graph = None
+        self.graph_launches = 0   # this framework's kernels in one captured step
+
+    def enable_cuda_graph(self):
+        """Run every later step as one CUDA graph replay (the whole forward,
+        backward and optimizer step: no per-kernel launch gaps).  The first step
+        after this call runs eagerly on the capture stream (allocating per-stream
+        state) and then captures the step; it counts as one training step.  Needs
+        fixed input shapes and an optimizer with a device-side clock
+        (:meth:`~zeroq_b200.parallel.optimizer.ShardedAdamW.use_device_clock`)."""
+        if not hasattr(self.opt, "use_device_clock"):
+            raise RuntimeError("CUDA-graph steps need ShardedAdamW (device-side optimizer clock)")
+        self.opt.use_device_clock()
+        self._graph_on = True
+
+    def _eager(self, input_ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        loss = self.model(input_ids, targets)
+        loss.backward()
+        self.opt.step()
+        self.opt.zero_grad()
+        return loss.detach()
+
+    def _capture(self, input_ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        from .ops._ext import LaunchCounter
+
+        self._gin = input_ids.clone()
+        self._gtg = targets.clone()
+        stream = torch.cuda.Stream(device=self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(stream):
+            loss = self._eager(self._gin, self._gtg)   # this call's step
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        torch.cuda.synchronize(self.device)
+        graph = torch.cuda.CUDAGraph()
+        with LaunchCounter() as lc:
+            with torch.cuda.graph(graph, stream=stream):
+                self._gloss = self._eager(self._gin, self._gtg)
+        self.graph_launches = lc.count
+        self._graph = graph
+        return loss
 
     def _buffers(self, shape):
         if self._in is None or self._in.shape != shape:
@@ -44,13 +85,21 @@ class Trainer:
         return self._in, self._tg
 
     def step_device(self, input_ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
-        loss = self.model(input_ids, targets)
-        loss.backward()
-        self.opt.step()
-        self.opt.zero_grad()
-        return loss.detach()
+        if not self._graph_on:
+            return self._eager(input_ids, targets)
+        if self._graph is None:
+            return self._capture(input_ids, targets)
+        if input_ids.data_ptr() != self._gin.data_ptr():
+            self._gin.copy_(input_ids, non_blocking=True)
+            self._gtg.copy_(targets, non_blocking=True)
+        self._graph.replay()
+        return self._gloss
 
     def step(self, input_ids_host: torch.Tensor, targets_host: torch.Tensor) -> float:
+        if self._graph is not None:  # straight into the graph's static inputs
+            self._gin.copy_(input_ids_host, non_blocking=True)
+            self._gtg.copy_(targets_host, non_blocking=True)
+            return float(self.step_device(self._gin, self._gtg).item())
         dev_in, dev_tg = self._buffers(input_ids_host.shape)
         dev_in.copy_(input_ids_host, non_blocking=True)
         dev_tg.copy_(targets_host, non_blocking=True)
