@@ -447,28 +447,56 @@ enum AttBwdErr { kErrBwdLoad = 311, kErrBwdMma = 312, kErrBwdCompute = 313 };
 
 // delta[b, h, s] = sum_d dO[b, s, h, d] * O[b, s, h, d]  (one warp per row, D = 128)
 // and lse2 = lse * log2(e) (the exponent offset in the exp2 form)
-__global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ dout,
+// delta = rowsum(dO * O) per (b, h, s) and lse2 = lse * log2(e), in [B, H, S]
+// order.  Grid-stride: 16 lanes x 16-byte loads per 128-wide row, two rows per
+// warp, two row pairs per iteration in flight (a warp per row with 8-byte loads
+// and a block per 8 rows was bound by block scheduling).
+__global__ void __launch_bounds__(256) attn_delta_kernel(const __nv_bfloat16* __restrict__ dout,
                                   const __nv_bfloat16* __restrict__ o, const float* __restrict__ lse,
                                   float* __restrict__ delta, float* __restrict__ lse2,
                                   int64_t rows, int S, int Hq) {
-  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const uint2 a = *reinterpret_cast<const uint2*>(dout + row * kAttD + lane * 4);
-  const uint2 c = *reinterpret_cast<const uint2*>(o + row * kAttD + lane * 4);
-  const float2 a0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a.x));
-  const float2 a1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&a.y));
-  const float2 c0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&c.x));
-  const float2 c1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&c.y));
-  float acc = a0.x * c0.x + a0.y * c0.y + a1.x * c1.x + a1.y * c1.y;
-  acc = warp_sum(acc);
-  if (lane == 0) {
-    const int h = (int)(row % Hq);
-    const int64_t bs = row / Hq;
-    const int s = (int)(bs % S), b = (int)(bs / S);
-    const int64_t li = ((int64_t)b * Hq + h) * S + s;
-    delta[li] = acc;
-    lse2[li] = lse[li] * 1.4426950408889634f;
+  const int half = lane >> 4, l16 = lane & 15;
+  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t pairs = (rows + 1) >> 1;
+  for (int64_t p0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p0 < pairs; p0 += 2 * nw) {
+    float acc[2] = {0.0f, 0.0f};
+    uint4 a[2], c[2];
+    int64_t row[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      row[u] = (p0 + u * nw) * 2 + half;
+      if (p0 + u * nw < pairs && row[u] < rows) {
+        a[u] = *reinterpret_cast<const uint4*>(dout + row[u] * kAttD + l16 * 8);
+        c[u] = *reinterpret_cast<const uint4*>(o + row[u] * kAttD + l16 * 8);
+      } else {
+        a[u] = c[u] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const uint32_t aw[4] = {a[u].x, a[u].y, a[u].z, a[u].w};
+      const uint32_t cw[4] = {c[u].x, c[u].y, c[u].z, c[u].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 x = bf16x2_to_f2(aw[j]), y = bf16x2_to_f2(cw[j]);
+        acc[u] = fmaf(x.x, y.x, acc[u]);
+        acc[u] = fmaf(x.y, y.y, acc[u]);
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], off);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      if (l16 == 0 && p0 + u * nw < pairs && row[u] < rows) {
+        const int h = (int)(row[u] % Hq);
+        const int64_t bs = row[u] / Hq;
+        const int s = (int)(bs % S), b = (int)(bs / S);
+        const int64_t li = ((int64_t)b * Hq + h) * S + s;
+        delta[li] = acc[u];
+        lse2[li] = lse[li] * 1.4426950408889634f;
+      }
+    }
   }
 }
 
@@ -1110,7 +1138,9 @@ void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::
   auto delta = at::empty({B, Hq, S}, q.options().dtype(at::kFloat));
   auto lse2 = at::empty({B, Hq, S}, q.options().dtype(at::kFloat));
   const int64_t rows = B * S * Hq;
-  attn_delta_kernel<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, stream>>>(
+  const int64_t delta_blocks = std::max<int64_t>(
+      1, std::min<int64_t>((rows / 2 + 7) / 8, (int64_t)at::cuda::getCurrentDeviceProperties()->multiProcessorCount * 8));
+  attn_delta_kernel<<<(unsigned)delta_blocks, 256, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr<at::BFloat16>()),
       reinterpret_cast<const __nv_bfloat16*>(o.data_ptr<at::BFloat16>()), lse.data_ptr<float>(),
       delta.data_ptr<float>(), lse2.data_ptr<float>(), rows, (int)S, (int)Hq);
