@@ -106,8 +106,6 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true",
                     help="run the steps eagerly instead of as one CUDA graph replay each")
-    ap.add_argument("--graph-multi", action="store_true",
-                    help="also replay CUDA graphs with more than one rank")
     ap.add_argument("--torch-profile", default=None,
                     help="after timing, profile one more step and write a per-kernel table here")
     args = ap.parse_args()
@@ -163,7 +161,7 @@ def main():
 
     # CUDA graph (weights resident, fixed shapes): warm-up step 0 runs eagerly,
     # step 1 runs eagerly on the capture stream and captures, later steps replay
-    use_graph = not args.no_graph and mode == "4bit-once" and (world == 1 or args.graph_multi)
+    use_graph = not args.no_graph and mode == "4bit-once"
     losses = []
     for i in range(args.warmup):
         if use_graph and i == 1:
