@@ -41,8 +41,10 @@ __device__ __forceinline__ uint4 f32_to_bf16x8(const float (&f)[8]) {
   return u;
 }
 
-// Sum of v over the TPR lanes of this thread's team.  Every thread of the CTA
-// must call it (it contains __syncthreads when TPR > 32).
+// Sum of v over the TPR lanes of this thread's team.  Every thread of the team
+// must call it.  Teams wider than a warp exchange through shared memory under a
+// named barrier of their own (id 1 + team, TPR threads), so the teams of a CTA
+// never wait for one another and one team's loads overlap another's arithmetic.
 template <int TPR>
 __device__ __forceinline__ float team_sum(float v, float* red) {
   v = warp_sum(v);
@@ -51,13 +53,14 @@ __device__ __forceinline__ float team_sum(float v, float* red) {
   } else {
     constexpr int W = TPR / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bar = 1 + (int)threadIdx.x / TPR;
     if (lane == 0) red[warp] = v;
-    __syncthreads();
+    asm volatile("bar.sync %0, %1;" ::"r"(bar), "n"(TPR) : "memory");
     const int base = (warp / W) * W;
     float r = 0.0f;
 #pragma unroll
     for (int i = 0; i < W; ++i) r += red[base + i];
-    __syncthreads();
+    asm volatile("bar.sync %0, %1;" ::"r"(bar), "n"(TPR) : "memory");
     return r;
   }
 }
@@ -124,9 +127,12 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_fwd_kernel(
 
 // dx = r * (g*w - xhat * mean(g*w*xhat)) [+ gh];  dw += sum_rows g * xhat.
 // Teams walk rows with a grid stride and keep their dw share in registers; the
-// teams of a CTA combine through shared memory into one row of dw_part.
-template <int NC, int TPR>
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
+// teams of a CTA combine through shared memory into one row of dw_part.  With
+// PF the next row group's x, dy and rstd are loaded before this group's
+// arithmetic (two groups in flight per team); the residual gradient gh is loaded
+// at the top of its own group and first used after the row reduction.
+template <int NC, int TPR, bool PF>
+__global__ void __launch_bounds__(kNormThreads, (PF && NC <= 3) ? 2 : 1) rmsnorm_bwd_kernel(
     const __nv_bfloat16* __restrict__ gy, const __nv_bfloat16* __restrict__ x,
     const float* __restrict__ w, const float* __restrict__ rstd,
     const __nv_bfloat16* __restrict__ gh, __nv_bfloat16* __restrict__ dx,
@@ -144,21 +150,43 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
     for (int i = 0; i < 8; ++i) dwacc[c][i] = 0.0f;
   const float4* w4 = reinterpret_cast<const float4*>(w);  // [D/4], L1-resident
   const int64_t groups = (M + R - 1) / R;
-  for (int64_t gidx = blockIdx.x; gidx < groups; gidx += gridDim.x) {
-    const int64_t row = gidx * R + team;
-    const bool live = row < M;
-    uint4 xv[NC], gv[NC], hv[NC];
+  uint4 xv[NC], gv[NC];
+  float r = 0.0f;
+  auto load_xg = [&](int64_t row, uint4 (&xo)[NC], uint4 (&go)[NC], float& ro) {
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
       const int ch = c * TPR + tl;
-      if (live && ch < nch) {
+      if (ch < nch) {
         const int64_t off = row * D + (int64_t)ch * 8;
-        xv[c] = *reinterpret_cast<const uint4*>(x + off);
-        gv[c] = *reinterpret_cast<const uint4*>(gy + off);
-        if (gh != nullptr) hv[c] = *reinterpret_cast<const uint4*>(gh + off);
+        xo[c] = *reinterpret_cast<const uint4*>(x + off);
+        go[c] = *reinterpret_cast<const uint4*>(gy + off);
       }
     }
-    const float r = live ? rstd[row] : 0.0f;
+    ro = rstd[row];
+  };
+  if constexpr (PF) {
+    const int64_t row0 = (int64_t)blockIdx.x * R + team;
+    if (row0 < M) load_xg(row0, xv, gv, r);
+  }
+  for (int64_t gidx = blockIdx.x; gidx < groups; gidx += gridDim.x) {
+    const int64_t row = gidx * R + team;
+    const bool live = row < M;
+    uint4 hv[NC];
+    if (live && gh != nullptr) {
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        const int ch = c * TPR + tl;
+        if (ch < nch) hv[c] = *reinterpret_cast<const uint4*>(gh + row * D + (int64_t)ch * 8);
+      }
+    }
+    uint4 xn[NC], gn[NC];
+    float rn = 0.0f;
+    if constexpr (PF) {
+      const int64_t nrow = (gidx + gridDim.x) * R + team;  // >= M once past the last group
+      if (nrow < M) load_xg(nrow, xn, gn, rn);
+    } else {
+      if (live) load_xg(row, xv, gv, r);
+    }
     float dot = 0.0f;
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
@@ -199,6 +227,14 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
           *reinterpret_cast<uint4*>(dx + row * D + (int64_t)ch * 8) = f32_to_bf16x8(o);
         }
       }
+    }
+    if constexpr (PF) {
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
+        xv[c] = xn[c];
+        gv[c] = gn[c];
+      }
+      r = rn;
     }
   }
   __syncthreads();
@@ -525,6 +561,40 @@ static void check_bf16(const at::Tensor& t, const char* name) {
 
 // Team width and chunks per lane for a row of D bf16: the narrowest team whose
 // lanes need at most 8 chunks, then the smallest instantiated chunk count.
+// Backward team shape: at most 4 chunks per lane up to D = 2048, then 128-lane
+// teams (D = 3072: 3 chunks).  Up to 5 chunks per lane the kernel keeps two row
+// groups in flight per team (with up to 3 chunks in 128 registers, so two CTAs
+// per SM); wider rows load one group at a time.
+static void norm_bwd_shape(int64_t D, int* tpr, int* nc) {
+  const int64_t chunks = D / 8;
+  if (chunks <= 32) { *tpr = 32; *nc = 1; }
+  else if (chunks <= 64) { *tpr = 32; *nc = 2; }
+  else if (chunks <= 128) { *tpr = 32; *nc = 4; }
+  else if (chunks <= 256) { *tpr = 64; *nc = 4; }
+  else {
+    *tpr = 128;
+    const int64_t need = (chunks + 127) / 128;
+    *nc = need <= 3 ? 3 : need <= 5 ? (int)need : need <= 6 ? 6 : 8;
+  }
+}
+
+#define ZQ_NORM_BWD_DISPATCH(TPR, NC, ...)                                        \
+  do {                                                                            \
+    if (TPR == 32) {                                                              \
+      if (NC == 1) rmsnorm_bwd_kernel<1, 32, true>__VA_ARGS__;                    \
+      else if (NC == 2) rmsnorm_bwd_kernel<2, 32, true>__VA_ARGS__;               \
+      else rmsnorm_bwd_kernel<4, 32, true>__VA_ARGS__;                            \
+    } else if (TPR == 64) {                                                       \
+      rmsnorm_bwd_kernel<4, 64, true>__VA_ARGS__;                                 \
+    } else {                                                                      \
+      if (NC == 3) rmsnorm_bwd_kernel<3, 128, true>__VA_ARGS__;                   \
+      else if (NC == 4) rmsnorm_bwd_kernel<4, 128, true>__VA_ARGS__;              \
+      else if (NC == 5) rmsnorm_bwd_kernel<5, 128, true>__VA_ARGS__;              \
+      else if (NC == 6) rmsnorm_bwd_kernel<6, 128, false>__VA_ARGS__;             \
+      else rmsnorm_bwd_kernel<8, 128, false>__VA_ARGS__;                          \
+    }                                                                             \
+  } while (0)
+
 static void norm_shape(int64_t D, int* tpr, int* nc) {
   const int64_t chunks = D / 8;
   *tpr = chunks <= 32 * 8 ? 32 : (chunks <= 64 * 8 ? 64 : 128);
@@ -591,12 +661,12 @@ cudaError_t launch_rmsnorm_bwd(const __nv_bfloat16* gy, const __nv_bfloat16* x, 
                                cudaStream_t stream, int64_t* grid_out) {
   if (M < 1 || D < 8 || D % 8 != 0 || D > kNormMaxD || max_grid < 1) return cudaErrorInvalidValue;
   int tpr, nc;
-  norm_shape(D, &tpr, &nc);
+  norm_bwd_shape(D, &tpr, &nc);
   const int rows_per_cta = kNormThreads / tpr;
   const int64_t groups = (M + rows_per_cta - 1) / rows_per_cta;
   const int64_t grid = std::min<int64_t>(groups, max_grid);
   const size_t smem = (size_t)D * sizeof(float);
-  ZQ_NORM_DISPATCH(tpr, nc, rmsnorm_bwd_kernel, <<<(unsigned)grid, kNormThreads, smem, stream>>>(
+  ZQ_NORM_BWD_DISPATCH(tpr, nc, <<<(unsigned)grid, kNormThreads, smem, stream>>>(
       gy, x, w, rstd, gh, dx, dw_part, M, D));
   *grid_out = grid;
   return cudaGetLastError();

@@ -103,7 +103,8 @@ def test_nf4_to_bf16(cuda, transpose, R, C, bs, qt):
 
 
 @pytest.mark.parametrize("M,D", [(300, 3072), (1001, 256), (77, 2056), (513, 3584), (130, 5120),
-                                 (64, 8192), (4099, 3072)])
+                                 (64, 8192), (4099, 3072), (20001, 512), (333, 1024), (1500, 2048),
+                                 (200, 6144)])
 def test_add_rmsnorm_fwd_bwd(cuda, M, D):
     """Every team width (32/64/128 lanes) and chunk count, ragged row counts."""
     from zeroq_b200.ops.norm import add_rmsnorm
