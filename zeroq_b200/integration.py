@@ -102,7 +102,16 @@ def convert_to_4bit_compute(model: nn.Module, coordinator: ZeroQCoordinator,
     for zq in coordinator._params.values():
         if zq.local_packed is None:
             continue
-        zq.start_gather(group=coordinator.process_group, async_op=False)
+        # Resident means a local copy: without the peer pool the gather assembles
+        # the whole NF4 weight here once (a peer source would re-read every
+        # owner's shard over NVLink on every use and rule out the fused q/k/v
+        # GEMM and its epilogues).
+        pool = getattr(zq, "_peer_pool", None)
+        zq._peer_pool = None
+        try:
+            zq.start_gather(group=coordinator.process_group, async_op=False)
+        finally:
+            zq._peer_pool = pool
         if zq.status == ZeroQParamStatus.INFLIGHT:
             zq.wait_gather()
         if isinstance(zq.module, Linear4bit) and zq.param_name == "weight":
