@@ -67,7 +67,15 @@ CONFIGS = {
                        "prefetch and released after use, activation checkpointing, LoRA r=64 "
                        "on all linears, AdamW"),
 }
-HETERO_WEIGHTS = [2.0, 2.0, 1.0, 1.0, 1.0, 1.0, 1.0, 1.0]
+
+
+def hetero_weights(world: int):
+    """Rank weights of the hetero config: the 8-rank plan [2,2,1,1,1,1,1,1] and, at
+    fewer ranks, the same 2:1 split with a quarter of the ranks (at least one)
+    holding double shares - [2,1] at 2 ranks, [2,1,1,1] at 4 - so every rank
+    count measures a genuinely uneven plan."""
+    heavy = max(1, world // 4)
+    return [2.0] * heavy + [1.0] * (world - heavy)
 
 
 def run_reference(args):
@@ -146,7 +154,7 @@ def main():
     zq = ZeroQConfig(compute_dtype=torch.bfloat16, compute_in_4bit=True, double_quant=False,
                      gather_once=(mode == "4bit-once"), prefetch_count=1, async_gather=True,
                      exclude_modules=["lm_head", "embed_tokens"], backend="auto")
-    rank_weights = HETERO_WEIGHTS[:world] if mode == "hetero" else None
+    rank_weights = hetero_weights(world) if mode == "hetero" else None
     trainable = ("lora_", "norm") if mode == "4bit-once" else ("lora_",)
     initialize(model, zq, trainable_patterns=trainable, rank_weights=rank_weights)
     torch.cuda.empty_cache()

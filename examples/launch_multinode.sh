@@ -89,9 +89,9 @@ cmd_sync() {
     local host=${HOST_LIST[$i]}
     [[ "$host" == "localhost" || "$host" == "127.0.0.1" ]] && continue
     if [[ "$DRY_RUN" == "1" ]]; then
-      echo "[$host] rsync -az --exclude .git --exclude gpurun_out $REMOTE_DIR/ $host:$REMOTE_DIR/"
+      echo "[$host] rsync -az --exclude .git $REMOTE_DIR/ $host:$REMOTE_DIR/"
     else
-      rsync -az --exclude .git --exclude gpurun_out "$REMOTE_DIR/" "$host:$REMOTE_DIR/"
+      rsync -az --exclude .git "$REMOTE_DIR/" "$host:$REMOTE_DIR/"
     fi
   done
 }

@@ -102,19 +102,21 @@ def convert_to_4bit_compute(model: nn.Module, coordinator: ZeroQCoordinator,
     for zq in coordinator._params.values():
         if zq.local_packed is None:
             continue
-        # Resident means a local copy: without the peer pool the gather assembles
-        # the whole NF4 weight here once (a peer source would re-read every
-        # owner's shard over NVLink on every use and rule out the fused q/k/v
-        # GEMM and its epilogues).
-        pool = getattr(zq, "_peer_pool", None)
-        zq._peer_pool = None
-        try:
-            zq.start_gather(group=coordinator.process_group, async_op=False)
-        finally:
-            zq._peer_pool = pool
+        # Resident means a local copy: the gather assembles the whole NF4 weight
+        # here once (with a peer pool registered, through the peer plan-gather
+        # kernel).  A peer source would re-read every owner's shard over NVLink on
+        # every use and rule out the fused q/k/v GEMM and its epilogues, so a
+        # parameter that a forward hook already attached to its peer source is
+        # released first.
+        if zq.status == ZeroQParamStatus.AVAILABLE and getattr(zq.module, "_peer", None) is not None:
+            zq.release()
+        zq.start_gather(group=coordinator.process_group, async_op=False, force_local=True)
         if zq.status == ZeroQParamStatus.INFLIGHT:
             zq.wait_gather()
         if isinstance(zq.module, Linear4bit) and zq.param_name == "weight":
+            if zq.module._peer is not None:
+                raise RuntimeError(f"convert_to_4bit_compute: param_id={zq.param_id} is still "
+                                   "attached to its peer shards after the local gather")
             if not zq.compute_in_4bit:
                 # dequantised during the gather; quantised again for NF4 compute
                 zq.module.quantize_from(zq.module.weight.data)

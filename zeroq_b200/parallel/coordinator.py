@@ -240,7 +240,13 @@ class ZeroQParameter:
             _cfg(self.config, "cpu_offload", False)) and not bool(
             _cfg(self.config, "fused_shard_step", False))
 
-    def start_gather(self, group: Optional[dist.ProcessGroup] = None, async_op: bool = True):
+    def start_gather(self, group: Optional[dist.ProcessGroup] = None, async_op: bool = True,
+                     force_local: bool = False):
+        """Start gathering this parameter.
+
+        ``force_local=True`` always assembles the whole NF4 weight on this rank
+        (through the peer plan-gather kernel when a peer pool is registered, NCCL
+        otherwise) instead of attaching the module to its owners' shards."""
         if self.status == ZeroQParamStatus.AVAILABLE:
             return None
         if self.status == ZeroQParamStatus.INFLIGHT:
@@ -258,7 +264,7 @@ class ZeroQParameter:
             return self._start_gather_fp32(group, async_op)
         if self.local_packed is None:
             raise RuntimeError(f"param_id={self.param_id} is not partitioned")
-        if self._use_peer_source():
+        if not force_local and self._use_peer_source():
             # fused backend, 4-bit compute: nothing is gathered here; the module's
             # GEMM reads every owner's shard itself (gather + dequant + GEMM kernel)
             self.module.set_peer_source(self._peer_pool, self)

@@ -89,9 +89,6 @@ class HeteroZeroQParameter(ZeroQParameter):
     def _make_plans(self, packed_total: int, absmax_total: int):
         return make_plan(packed_total, self.rank_weights), make_plan(absmax_total, self.rank_weights)
 
-    def start_gather(self, group=None, *, async_op: bool = True):
-        return super().start_gather(group=group, async_op=async_op)
-
 
 class HeteroZeroQCoordinator(ZeroQCoordinator):
     param_cls = HeteroZeroQParameter
