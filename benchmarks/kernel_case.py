@@ -7,6 +7,7 @@
     python benchmarks/kernel_case.py rmsnorm --m 8192 --n 3072
     python benchmarks/kernel_case.py gelu --m 8192 --n 12288
     python benchmarks/kernel_case.py q4gemm --m 8192 --n 3072 --k 12288 [--nn]
+    python benchmarks/kernel_case.py lora --m 8192 --k 3072 --n 3072 --r 16 [--cublas]
 
 Each case allocates at most a few GB and times ``--reps`` launches of the kernel
 itself with CUDA events on the launching stream.  Before every timed launch a
@@ -87,7 +88,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["gemm", "attention", "attn_trace", "attn_bwd_trace",
                                      "nf4_operand", "rmsnorm", "gelu", "q4gemm", "gelu_gemm",
-                                     "ag_gemm"])
+                                     "ag_gemm", "lora"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=3072)
@@ -101,6 +102,7 @@ def main():
     ap.add_argument("--transpose", action="store_true")
     ap.add_argument("--bhsd", action="store_true", help="attn_trace: K/V as [B, H, S, D]")
     ap.add_argument("--reps", type=int, default=5)
+    ap.add_argument("--r", type=int, default=16, help="lora: adapter rank (packed width)")
     ap.add_argument("--world", type=int, default=4, help="ag_gemm: emulated ranks (pieces)")
     ap.add_argument("--profile", action="store_true", help="print one call's kernels (torch profiler)")
     a = ap.parse_args()
@@ -332,6 +334,39 @@ def main():
                            device=dev)
         ms = _time(lambda: E.rmsnorm_bwd(gy, hout, w, rstd, gh, dx, part), a.reps)
         _report(f"rmsnorm bwd (+residual grad) {M}x{D}", ms, byts=4 * M * D * 2)
+    elif a.case == "lora":
+        # the four rank-space products of one adapter on x [M, K] -> y [M, N]
+        from zeroq_b200.ops import lora as L
+
+        M, K, N, r = a.m, a.k, a.n, a.r
+        r16 = L.round16(r)
+        x = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+        gy = torch.randn(M, N, device=dev, dtype=torch.bfloat16)
+        sa = (0.02 * torch.randn(r16, K, device=dev)).bfloat16()
+        bt = (0.02 * torch.randn(r16, N, device=dev)).bfloat16()
+        u, ut = L.down(x, sa)
+        v, vt = L.down(gy, bt)
+        gA = torch.zeros(r, K, device=dev)
+        gB = torch.zeros(N, r, device=dev)
+        ms = _time(lambda: L.down(x, sa), a.reps, a.profile)
+        _report(f"lora_down U=x·Aᵀ {M}x{K} r={r}", ms, byts=M * K * 2 + M * (64 + r16) * 2)
+        ms = _time(lambda: L.down(gy, bt), a.reps)
+        _report(f"lora_down V=dY·B {M}x{N} r={r}", ms, byts=M * N * 2 + M * (64 + r16) * 2)
+        ms = _time(lambda: L.wgrad(x, vt, r16, [(0, K, 0, 1.0)], [gA], r16, r, True), a.reps)
+        _report(f"lora_wgrad dA=Vᵀ·x {M}x{K} r={r}", ms, byts=M * K * 2 + M * r16 * 2)
+        ms = _time(lambda: L.wgrad(gy, ut, r16, [(0, N, 0, 1.0)], [gB], r16, r, False), a.reps)
+        _report(f"lora_wgrad dB=dYᵀ·U {M}x{N} r={r}", ms, byts=M * N * 2 + M * r16 * 2)
+        if L.vdb(gy, bt, ut, 64, [(0, N, 0)], [gB], r16, r) is not None:
+            ms = _time(lambda: L.vdb(gy, bt, ut, 64, [(0, N, 0)], [gB], r16, r), a.reps)
+            _report(f"lora_vdb V and dB {M}x{N} r={r}", ms, byts=M * N * 2 + M * (64 + 2 * r16) * 2)
+        if a.cublas:
+            ap_, bp_ = torch.zeros(64, K, device=dev, dtype=torch.bfloat16), torch.zeros(
+                N, 64, device=dev, dtype=torch.bfloat16)
+            _report(f"cublas x·A_padᵀ {M}x{K}x64", _time(lambda: x @ ap_.t(), a.reps),
+                    byts=M * K * 2 + M * 64 * 2)
+            _report(f"cublas dY·B_pad {M}x{N}x64", _time(lambda: gy @ bp_, a.reps),
+                    byts=M * N * 2 + M * 64 * 2)
+        print(f"status {E.gemm_status(0)}", flush=True)
     elif a.case == "gelu":
         x = torch.randn(a.m, a.n, device=dev, dtype=torch.bfloat16)
         y = torch.empty_like(x)

@@ -800,7 +800,9 @@ attn_bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_con
                        __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv, int B, int S,
                        int Hq, int Hk, float scale_log2, float scale, int causal,
                        const float2* __restrict__ rope_cs, DeviceStatus* status,
-                       unsigned long long* __restrict__ trace) {
+                       unsigned long long* __restrict__ trace, int64_t ld_dk, int64_t ld_dv) {
+  // ld_dk / ld_dv: elements between consecutive tokens of dK / dV (Hk * 128 when
+  // contiguous; wider when the output is a column slice of a fused gradient)
   // trace (optional, [grid][32] ns): 0 start; iterations t = 1, 2 at 1 + 8(t-1) + i:
   //   compute: i = 0 Sᵀ/dPᵀ seen, 1 loaded, 2 Pᵀ/dSᵀ computed, 3 arrived;
   //   MMA: 4 Q/dO seen, 5 Sᵀ/dPᵀ issued, 6 Pᵀ/dSᵀ seen, 7 dV/dK issued;  30 end
@@ -997,10 +999,10 @@ attn_bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_con
       const bool done = mbar_wait(acc_done, 0, status, kErrBwdCompute);
       if (named_barrier_and(pair_bar, 64, done)) {
         tc_fence_after();
-        const int64_t off = (((int64_t)b * S + key) * Hk + hk) * kAttD + col0;
+        const int64_t tok = (int64_t)b * S + key, hoff = (int64_t)hk * kAttD + col0;
 #pragma unroll 1
         for (int w = 0; w < 2; ++w) {   // w = 0: dV (scale 1), w = 1: dK (scale)
-          __nv_bfloat16* out = (w == 0 ? dv : dk) + off;
+          __nv_bfloat16* out = w == 0 ? dv + tok * ld_dv + hoff : dk + tok * ld_dk + hoff;
           const float f = w == 0 ? 1.0f : scale;
           // dK of rotary-embedded keys: rotated back (dV never is)
           bwd_store_half_row(tmem + lane_base + (uint32_t)(w * 128), col0, f,
@@ -1104,8 +1106,15 @@ void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::
     TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 4,
                 "attention backward: bf16 [B, S, H, D] CUDA tensors");
   }
-  for (const at::Tensor* t : {&dout, &o, &dq, &dk, &dv})
-    TORCH_CHECK(t->is_contiguous(), "attention backward: dout, o, dq, dk, dv must be contiguous");
+  for (const at::Tensor* t : {&dout, &o, &dq})
+    TORCH_CHECK(t->is_contiguous(), "attention backward: dout, o, dq must be contiguous");
+  // dK / dV: [B, S, H, D] with unit head-dim stride, D between heads and any
+  // 16-byte-multiple token pitch (a column slice of a wider gradient buffer)
+  for (const at::Tensor* t : {&dk, &dv})
+    TORCH_CHECK(t->stride(3) == 1 && t->stride(2) == t->size(3) && t->stride(1) >= t->size(2) * t->size(3) &&
+                    t->stride(1) % 8 == 0 && t->stride(0) == t->size(1) * t->stride(1) &&
+                    (reinterpret_cast<uintptr_t>(t->data_ptr()) & 15) == 0,
+                "attention backward: dk / dv must be [B, S, H, D] rows of a token-pitched buffer");
   const int64_t B = q.size(0), S = q.size(1), Hq = q.size(2), D = q.size(3), Hk = k.size(2);
   TORCH_CHECK(D == kAttD, "attention backward (tcgen05): head dim 128");
   TORCH_CHECK(S % kAttRows == 0 && S > 0, "attention backward: S must be a multiple of 128");
@@ -1166,6 +1175,6 @@ void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::
       tq, tk, tv, tdo, lse2.data_ptr<float>(), delta.data_ptr<float>(),
       reinterpret_cast<__nv_bfloat16*>(dk.data_ptr<at::BFloat16>()),
       reinterpret_cast<__nv_bfloat16*>(dv.data_ptr<at::BFloat16>()), (int)B, (int)S, (int)Hq, (int)Hk, sl2,
-      (float)scale, causal ? 1 : 0, rcs, st, trp ? trp + g_dq * 32 : nullptr);
+      (float)scale, causal ? 1 : 0, rcs, st, trp ? trp + g_dq * 32 : nullptr, dk.stride(1), dv.stride(1));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

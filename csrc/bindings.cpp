@@ -17,7 +17,18 @@ void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::
 void gemm_nf4(at::Tensor a, at::Tensor packed, at::Tensor absmax, int64_t rows, int64_t cols,
               int64_t blocksize, int64_t quant_type, bool w_is_kn, at::Tensor c,
               c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2);
-void lora_pack(at::Tensor A, at::Tensor B, double scaling, at::Tensor a_pad, at::Tensor b_pad);
+void lora_pack(at::Tensor A, at::Tensor B, double scaling, at::Tensor a_pad, at::Tensor b_pad,
+               c10::optional<at::Tensor> b_t);
+// lora_sm100.cu
+void lora_down(at::Tensor p, at::Tensor w, at::Tensor u, c10::optional<at::Tensor> ut, int64_t cs,
+               int64_t stages, int64_t kb);
+void lora_wgrad(at::Tensor p, at::Tensor qt, int64_t nq, std::vector<int64_t> i_begin,
+                std::vector<int64_t> i_count, std::vector<int64_t> q_row, std::vector<double> alpha,
+                std::vector<at::Tensor> outs, int64_t gsz, int64_t rvalid, bool transposed,
+                int64_t splits, int64_t stages, int64_t kb);
+bool lora_vdb(at::Tensor g, at::Tensor bt, at::Tensor ut, at::Tensor v, at::Tensor vt, int64_t nqb,
+              std::vector<int64_t> n_begin, std::vector<int64_t> n_count, std::vector<int64_t> q_row,
+              std::vector<at::Tensor> outs, int64_t rvalid, int64_t cs, int64_t stages);
 void matmul_accum_f32(at::Tensor A, at::Tensor B, at::Tensor C, double alpha, double beta);
 void gemm_bf16_tn_extra(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor a2, at::Tensor b2);
 void gemm_bf16_nn(at::Tensor a, at::Tensor b, at::Tensor c, c10::optional<at::Tensor> a2,
@@ -31,6 +42,7 @@ void add_rmsnorm_fwd(at::Tensor h, c10::optional<at::Tensor> d, at::Tensor w, at
                      at::Tensor y, at::Tensor rstd, double eps);
 void rmsnorm_bwd(at::Tensor gy, at::Tensor x, at::Tensor w, at::Tensor rstd,
                  c10::optional<at::Tensor> gh, at::Tensor dx, at::Tensor dw_part);
+void colsum_accum(at::Tensor part, at::Tensor out);
 void rope(at::Tensor x, at::Tensor out, at::Tensor cs, double sign);
 void rope_into(at::Tensor x, at::Tensor out, at::Tensor cs, double sign);
 void gelu_fwd(at::Tensor x, at::Tensor y);
@@ -106,13 +118,24 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("k"), pybind11::arg("v"), pybind11::arg("o"), pybind11::arg("lse"),
         pybind11::arg("causal"), pybind11::arg("scale"), pybind11::arg("trace") = pybind11::none(),
         pybind11::arg("kv_bhsd") = false);
-  m.def("lora_pack", &lora_pack);
+  m.def("lora_pack", &lora_pack, py::arg("A"), py::arg("B"), py::arg("scaling"), py::arg("a_pad"),
+        py::arg("b_pad"), py::arg("b_t") = py::none());
+  m.def("lora_down", &lora_down, py::arg("p"), py::arg("w"), py::arg("u"), py::arg("ut") = py::none(),
+        py::arg("cs") = 0, py::arg("stages") = 0, py::arg("kb") = 0);
+  m.def("lora_wgrad", &lora_wgrad, py::arg("p"), py::arg("qt"), py::arg("nq"), py::arg("i_begin"),
+        py::arg("i_count"), py::arg("q_row"), py::arg("alpha"), py::arg("outs"), py::arg("gsz"),
+        py::arg("rvalid"), py::arg("transposed"), py::arg("splits") = 0, py::arg("stages") = 0,
+        py::arg("kb") = 0);
+  m.def("lora_vdb", &lora_vdb, py::arg("g"), py::arg("bt"), py::arg("ut"), py::arg("v"), py::arg("vt"),
+        py::arg("nqb"), py::arg("n_begin"), py::arg("n_count"), py::arg("q_row"), py::arg("outs"),
+        py::arg("rvalid"), py::arg("cs") = 0, py::arg("stages") = 0);
   m.def("matmul_accum_f32", &matmul_accum_f32);
   m.def("gemm_status", &gemm_status);
   m.def("set_gemm_pair_mode", &set_gemm_pair_mode);
   m.def("nf4_to_bf16", &nf4_to_bf16);
   m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("colsum_accum", &colsum_accum);
   m.def("rope", &rope);
   m.def("rope_into", &rope_into);
   m.def("gelu_fwd", &gelu_fwd);

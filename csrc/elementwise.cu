@@ -707,6 +707,42 @@ void rmsnorm_bwd(at::Tensor gy, at::Tensor x, at::Tensor w, at::Tensor rstd,
   if (grid < dw_part.size(0)) dw_part.narrow(0, grid, dw_part.size(0) - grid).zero_();
 }
 
+namespace zq {
+// out[c] += sum over rows r of part[r, c] (fp32, D % 4 == 0): each block sums
+// 16 rows x 256 columns and adds them with one vector reduction per thread, so
+// the partial rows of a norm backward fold into the gradient in one pass.
+__global__ void __launch_bounds__(64) colsum_accum_kernel(const float4* __restrict__ part, int64_t rows,
+                                                          int64_t d4, float* __restrict__ out) {
+  const int64_t c = (int64_t)blockIdx.x * 64 + threadIdx.x;
+  if (c >= d4) return;
+  const int64_t r0 = (int64_t)blockIdx.y * 16;
+  const int64_t r1 = r0 + 16 < rows ? r0 + 16 : rows;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 16
+  for (int64_t r = r0; r < r1; ++r) {
+    const float4 v = __ldg(part + r * d4 + c);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  red_add_v4_f32(out + 4 * c, acc.x, acc.y, acc.z, acc.w);
+}
+}  // namespace zq
+
+// out [D] fp32 += column sums of part [G, D] fp32 (both contiguous, D % 4 == 0).
+void colsum_accum(at::Tensor part, at::Tensor out) {
+  TORCH_CHECK(part.is_cuda() && part.scalar_type() == at::kFloat && part.dim() == 2 && part.is_contiguous(),
+              "colsum_accum: part must be contiguous fp32 [G, D]");
+  const int64_t G = part.size(0), D = part.size(1);
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous() && out.numel() == D &&
+                  D % 4 == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0,
+              "colsum_accum: out must be 16-byte aligned contiguous fp32 [D], D % 4 == 0");
+  if (G == 0 || D == 0) return;
+  const at::cuda::CUDAGuard guard(part.device());
+  const dim3 grid((unsigned)((D / 4 + 63) / 64), (unsigned)((G + 15) / 16));
+  zq::colsum_accum_kernel<<<grid, 64, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const float4*>(part.data_ptr<float>()), G, D / 4, out.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void rope(at::Tensor x, at::Tensor out, at::Tensor cs, double sign) {
   check_bf16(x, "x");
   check_bf16(out, "out");

@@ -1,11 +1,12 @@
 // LoRA support for the NF4 linear layer:
 //  * lora_pack: the padded, pre-scaled bf16 operands that ride as the extra
-//    64-wide K slab of the tcgen05 GEMM (one launch per module per optimizer
-//    step, rows/columns past the rank stay zero);
-//  * matmul_accum_f32: C (fp32) = beta * C + alpha * A @ B for bf16 A, B, so the
-//    LoRA weight gradients accumulate straight into the fp32 .grad buffers with
-//    no cast or add kernel.  This is a plain library GEMM (cuBLAS, bf16 inputs,
-//    fp32 accumulate and output).
+//    64-wide K slab of the tcgen05 GEMM, plus the transposed B that the
+//    rank-space product V = dY·B reads (one launch per module per optimizer
+//    step, rows/columns past the rank stay zero); the LoRA products themselves
+//    are the tcgen05 kernels of lora_sm100.cu;
+//  * matmul_accum_f32: C (fp32) = beta * C + alpha * A @ B for bf16 A, B - a
+//    plain library GEMM (cuBLAS, bf16 inputs, fp32 accumulate and output) kept
+//    for the full-size weight gradient of train-from-scratch layers.
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -15,20 +16,26 @@
 
 namespace zq {
 
-// a_pad[i, k] = s * A[i, k] for i < r; b_pad[n, j] = B[n, j] for j < r.
+// a_pad[i, k] = s * A[i, k] for i < r; b_pad[n, j] = B[n, j] for j < r; and,
+// when b_t is given, b_t[j, n] = B[n, j] (the K-major operand of V = dY·B),
+// each output written in its own index order so every store is coalesced.
 __global__ void lora_pack_kernel(const float* __restrict__ A, const float* __restrict__ B,
                                  __nv_bfloat16* __restrict__ a_pad, int64_t a_ld,
-                                 __nv_bfloat16* __restrict__ b_pad, int64_t b_ld, int r, int64_t K,
+                                 __nv_bfloat16* __restrict__ b_pad, int64_t b_ld,
+                                 __nv_bfloat16* __restrict__ b_t, int64_t t_ld, int r, int64_t K,
                                  int64_t N, float s) {
-  const int64_t na = (int64_t)r * K, nb = N * r;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < na + nb;
+  const int64_t na = (int64_t)r * K, nb = N * r, nt = b_t != nullptr ? N * r : 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < na + nb + nt;
        i += (int64_t)gridDim.x * blockDim.x) {
     if (i < na) {
       const int64_t row = i / K, col = i % K;
       a_pad[row * a_ld + col] = __float2bfloat16_rn(s * A[i]);
-    } else {
+    } else if (i < na + nb) {
       const int64_t j = i - na, row = j / r, col = j % r;
       b_pad[row * b_ld + col] = __float2bfloat16_rn(B[j]);
+    } else {
+      const int64_t j = i - na - nb, row = j / N, col = j % N;  // b_t[row, col] = B[col, row]
+      b_t[row * t_ld + col] = __float2bfloat16_rn(B[col * r + row]);
     }
   }
 }
@@ -37,7 +44,8 @@ __global__ void lora_pack_kernel(const float* __restrict__ A, const float* __res
 
 using namespace zq;
 
-void lora_pack(at::Tensor A, at::Tensor B, double scaling, at::Tensor a_pad, at::Tensor b_pad) {
+void lora_pack(at::Tensor A, at::Tensor B, double scaling, at::Tensor a_pad, at::Tensor b_pad,
+               c10::optional<at::Tensor> b_t) {
   TORCH_CHECK(A.is_cuda() && A.scalar_type() == at::kFloat && A.is_contiguous() && A.dim() == 2,
               "lora_pack: A must be contiguous fp32 [r, K]");
   TORCH_CHECK(B.is_cuda() && B.scalar_type() == at::kFloat && B.is_contiguous() && B.dim() == 2,
@@ -50,14 +58,23 @@ void lora_pack(at::Tensor A, at::Tensor B, double scaling, at::Tensor a_pad, at:
   TORCH_CHECK(b_pad.scalar_type() == at::kBFloat16 && b_pad.dim() == 2 && b_pad.size(0) == N &&
                   b_pad.size(1) >= r && b_pad.stride(1) == 1,
               "lora_pack: b_pad must be bf16 [N, >= r] with unit column stride");
+  __nv_bfloat16* btp = nullptr;
+  int64_t t_ld = 0;
+  if (b_t.has_value() && b_t->defined()) {
+    TORCH_CHECK(b_t->scalar_type() == at::kBFloat16 && b_t->dim() == 2 && b_t->size(0) >= r &&
+                    b_t->size(1) == N && b_t->stride(1) == 1,
+                "lora_pack: b_t must be bf16 [>= r, N] with unit column stride");
+    btp = reinterpret_cast<__nv_bfloat16*>(b_t->data_ptr());
+    t_ld = b_t->stride(0);
+  }
   const at::cuda::CUDAGuard guard(A.device());
-  const int64_t total = r * K + N * r;
+  const int64_t total = r * K + N * r + (btp != nullptr ? N * r : 0);
   if (total == 0) return;
   const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 8);
   lora_pack_kernel<<<(unsigned)blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       A.data_ptr<float>(), B.data_ptr<float>(),
       reinterpret_cast<__nv_bfloat16*>(a_pad.data_ptr()), a_pad.stride(0),
-      reinterpret_cast<__nv_bfloat16*>(b_pad.data_ptr()), b_pad.stride(0), (int)r, K, N,
+      reinterpret_cast<__nv_bfloat16*>(b_pad.data_ptr()), b_pad.stride(0), btp, t_ld, (int)r, K, N,
       (float)scaling);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -746,8 +746,8 @@ def test_fused_gelu_mlp_matches_unfused(cuda, lora_r):
     _status_ok(cuda)
     assert torch.equal(y, y2)
     assert torch.equal(grads[0], grads2[0])
-    for g1, g2 in zip(grads[1:], grads2[1:]):
-        torch.testing.assert_close(g1, g2, rtol=1e-5, atol=1e-6)
+    for g1, g2 in zip(grads[1:], grads2[1:]):  # LoRA grads: atomic fp32 sums, no fixed order
+        torch.testing.assert_close(g1, g2, rtol=1e-4, atol=1e-5)
 
 
 @pytest.mark.parametrize("M,N,K,starts_frac", [
@@ -846,7 +846,9 @@ def test_linear4bit_rope_output_matches_apply_rope(cuda, lora_r):
     assert torch.equal(q, q2) and torch.equal(k, k2)
     assert torch.equal(gx, x.grad)
     if lora_r:
-        torch.testing.assert_close(gA, q_proj.lora_A.grad, rtol=1e-5, atol=1e-6)
+        # the LoRA weight-gradient kernel adds fp32 partial sums over token ranges
+        # with atomics, in no fixed order: two runs agree to fp32 rounding only
+        torch.testing.assert_close(gA, q_proj.lora_A.grad, rtol=1e-4, atol=1e-5)
 
 
 @pytest.mark.parametrize("B,S,Hq,Hk", [(2, 256, 4, 4), (1, 512, 8, 2)])
@@ -916,7 +918,7 @@ def test_rope_spec_projection_attention_chain_matches_apply_rope(cuda):
     _status_ok(cuda)
     assert torch.equal(o, o2)
     assert torch.equal(g1, x.grad)
-    torch.testing.assert_close(gA1, qp.lora_A.grad, rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(gA1, qp.lora_A.grad, rtol=1e-4, atol=1e-5)  # atomic fp32 sums
 
 
 @pytest.mark.parametrize("lora_r", [0, 16])
@@ -964,8 +966,11 @@ def test_fused_qkv_projection_matches_separate_projections(cuda, lora_r):
     for a, b in zip(results[0], results[1]):
         scale = b.float().abs().max().item() + 1e-6
         assert (a.float() - b.float()).abs().max().item() <= 2e-2 * scale, (a.shape,)
-    for a, b in zip(results[0], results[2]):
-        assert torch.equal(a, b)
+    for i, (a, b) in enumerate(zip(results[0], results[2])):
+        if i < 2:
+            assert torch.equal(a, b)
+        else:  # LoRA grads: atomic fp32 sums over token ranges, no fixed order
+            torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-5)
 
 
 @pytest.mark.parametrize("E", [128, 192, 256])

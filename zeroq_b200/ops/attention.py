@@ -70,7 +70,10 @@ class _FlashAttn(torch.autograd.Function):
     def backward(ctx, do):
         q, k, v, o, lse = ctx.saved_tensors
         do = do.contiguous()
-        dq, dk, dv = (torch.empty(t.shape, dtype=t.dtype, device=t.device) for t in (q, k, v))
+        dq, dk = (torch.empty(t.shape, dtype=t.dtype, device=t.device) for t in (q, k))
+        dv = _like_token_pitched(v) if q.shape[-1] == 128 else None
+        if dv is None:
+            dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
         if q.shape[-1] == 128:
             rope = ctx.rope
             cs = rope.cs if rope is not None and rope.cs.shape[0] == q.shape[1] else None
@@ -81,6 +84,20 @@ class _FlashAttn(torch.autograd.Function):
         else:
             _ext.ext().attn_bwd(do, q, k, v, o, lse, dq, dk, dv, bool(ctx.causal), float(ctx.scale))
         return dq, dk, dv, None, None, None
+
+
+def _like_token_pitched(v: torch.Tensor):
+    """For ``v`` a column slice of a token-pitched 2-D buffer (the fused q/k/v
+    projection's output ``[B*S, Nq+Nk+Nv]``), a gradient with the same layout in a
+    fresh buffer of that width: the backward writes dV straight into the slice
+    the fused projection's backward reads, so no copy assembles its gradient."""
+    B, S, H, D = v.shape
+    P = v.stride(1)
+    if (v.stride(3) != 1 or v.stride(2) != D or P <= H * D or v.stride(0) != S * P
+            or P % 8 or v.storage_offset() + H * D > P):
+        return None
+    buf = torch.empty(B * S * P, dtype=v.dtype, device=v.device)
+    return buf.as_strided(v.shape, v.stride(), v.storage_offset())
 
 
 def flash_attention(q, k, v, causal: bool = True, scale=None, rope=None):

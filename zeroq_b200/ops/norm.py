@@ -42,9 +42,9 @@ class _AddRMSNorm(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g_h, g_y):
         hout, w, rstd = ctx.saved_tensors
-        dx, dw = _norm_bwd(g_y, g_h, hout, w, rstd)
+        dx, dw = _norm_bwd(g_y, g_h, hout, w, rstd, ctx.needs_input_grad[2])
         dx = dx.view(ctx.shape)
-        return dx, dx, dw.to(w.dtype), None
+        return dx, dx, None if dw is None else dw.to(w.dtype), None
 
 
 class _RMSNorm(torch.autograd.Function):
@@ -62,19 +62,36 @@ class _RMSNorm(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g_y):
         x2, w, rstd = ctx.saved_tensors
-        dx, dw = _norm_bwd(g_y, None, x2, w, rstd)
-        return dx.view(ctx.shape), dw.to(w.dtype), None
+        dx, dw = _norm_bwd(g_y, None, x2, w, rstd, ctx.needs_input_grad[1])
+        return dx.view(ctx.shape), None if dw is None else dw.to(w.dtype), None
 
 
-def _norm_bwd(g_y, g_h, x2, w, rstd):
+def _norm_bwd(g_y, g_h, x2, w, rstd, want_dw: bool = True):
+    """``(dx, dw)``; ``dw`` is None when not wanted or when it was added straight
+    into ``w``'s bound fp32 gradient (a parameter bound by ``FlatParams``)."""
     D = x2.shape[-1]
     gy2 = g_y.reshape(-1, D).contiguous() if g_y is not None else torch.zeros_like(x2)
     gh2 = g_h.reshape(-1, D).contiguous() if g_h is not None else None
     dx = torch.empty_like(x2)
     grid = min(x2.shape[0], _num_sms(x2.device) * 2)
     dw_part = torch.empty(grid, D, dtype=torch.float32, device=x2.device)
-    _ext.ext().rmsnorm_bwd(gy2, x2, w, rstd, gh2, dx, dw_part)
-    return dx, dw_part.sum(0)
+    E = _ext.ext()
+    E.rmsnorm_bwd(gy2, x2, w, rstd, gh2, dx, dw_part)
+    if not want_dw:
+        return dx, None
+    # the per-CTA partial rows fold into the gradient in one column-sum kernel
+    direct = (getattr(w, "_zq_flat_grad", False) and w.grad is not None
+              and w.grad.dtype == torch.float32 and w.grad.is_contiguous() and D % 4 == 0
+              and w.grad.data_ptr() % 16 == 0)
+    if direct:
+        E.colsum_accum(dw_part, w.grad)
+        return dx, None
+    dw = torch.zeros(D, dtype=torch.float32, device=x2.device)
+    if D % 4 == 0:
+        E.colsum_accum(dw_part, dw)
+    else:
+        dw = dw_part.sum(0)
+    return dx, dw
 
 
 _SMS = {}

@@ -2,9 +2,12 @@
 
 The three frozen NF4 weights are decoded into one bf16 operand ``[Nq+Nk+Nv, d]``
 and multiplied in ONE tcgen05 GEMM (one wave-quantised grid instead of three).
-The three LoRA up-projections ride in the same MMA chain as three 64-wide extra
-K slabs: ``U = x·[sA_q; sA_k; sA_v]ᵀ`` (one skinny GEMM reading ``x`` once)
-against a block-diagonal ``[B_q, B_k, B_v]``.  The GEMM epilogue applies the
+The three LoRA up-projections ride in the same MMA chain as extra K slabs:
+``U = x·[sA_q; sA_k; sA_v]ᵀ`` (one rank-space kernel reading ``x`` once, from
+``csrc/lora_sm100.cu``) against a block-diagonal ``[B_q, B_k, B_v]``.  With
+ranks up to 21 the three adapters pack side by side into ONE 64-wide slab
+(columns ``[g·i, g·i + r)`` of adapter ``i``, ``g`` = rank rounded up to 16);
+larger ranks take one 64-wide slab each.  The GEMM epilogue applies the
 rotary embedding to the q and k columns (``csrc/gemm_sm100.cu`` ``kEpiRope``).
 q, k and v are returned as column slices of the one output, which the tcgen05
 attention reads through strided TMA maps.
@@ -12,8 +15,8 @@ attention reads through strided TMA maps.
 Backward: dQ and dK are rotated back straight into the column slices of one
 ``[M, Nq+Nk+Nv]`` gradient and dV is copied into the third, so the input
 gradient is one MN-major GEMM (no residual-gradient adds) with the LoRA term
-``V·[sA]`` folded in the same way (``V = dY·B_blk``, one skinny GEMM), and the
-three ``dA`` products are one skinny GEMM.  The reference runs three separate
+``V·[sA]`` folded in the same way (``V = dY·B_blk``, one rank-space kernel), the
+three ``dA`` products are one pass over ``x`` and the three ``dB`` one launch.  The reference runs three separate
 projections (``transformers`` q_proj/k_proj/v_proj modules around
 ``bnb.matmul_4bit``, see ``src/hetero/zeroq_hetero.py:477-500``).
 """
@@ -25,6 +28,7 @@ from typing import Optional, Sequence
 import torch
 
 from . import _ext
+from . import lora as lora_k
 from .nf4 import QUANT_TYPE_ID
 
 
@@ -39,21 +43,33 @@ def _decode_into(mods, w: torch.Tensor):
 
 
 def _lora_blocks(mods, cache: dict):
-    """``A_cat [64·3, d]`` (the modules' cached scaled, padded A operands stacked)
-    and the block-diagonal ``B_blk [Nq+Nk+Nv, 64·3]``, rebuilt only when a
-    module's LoRA operands change."""
+    """``(g, A_cat [W, d], B_blk [Nq+Nk+Nv, W], B_catT [3g, Nq+Nk+Nv])`` with ``g`` the
+    per-adapter column stride in rank space and ``W`` the slab width (64 when the
+    three ranks pack into one slab, else 3 x 64), rebuilt only when a module's
+    LoRA operands change."""
     ops = [m._lora_operands() for m in mods]
     key = tuple(m._lora_key for m in mods)
     if cache.get("key") != key:
+        r = mods[0].lora_r
+        g = lora_k.round16(r)
+        if 3 * g > 64:
+            g = 64
+        W = 64 if 3 * g <= 64 else 3 * 64
         Nt = sum(m.out_features for m in mods)
-        A_cat = torch.cat([o[0] for o in ops], 0)
-        B_blk = torch.zeros(Nt, 64 * len(mods), dtype=torch.bfloat16, device=A_cat.device)
+        d = mods[0].in_features
+        dev = ops[0][0].device
+        A_cat = torch.zeros(W, d, dtype=torch.bfloat16, device=dev)
+        B_blk = torch.zeros(Nt, W, dtype=torch.bfloat16, device=dev)
+        B_catT = torch.zeros(3 * g, Nt, dtype=torch.bfloat16, device=dev)
         off = 0
         for i, (m, o) in enumerate(zip(mods, ops)):
-            B_blk[off:off + m.out_features, 64 * i:64 * (i + 1)] = o[1]
-            off += m.out_features
-        cache.update(key=key, A_cat=A_cat, B_blk=B_blk)
-    return cache["A_cat"], cache["B_blk"]
+            n = m.out_features
+            A_cat[g * i:g * i + r] = o[0][:r]
+            B_blk[off:off + n, g * i:g * i + r] = o[1][:, :r]
+            B_catT[g * i:g * i + r, off:off + n] = o[2][:r]
+            off += n
+        cache.update(key=key, g=g, A_cat=A_cat, B_blk=B_blk, B_catT=B_catT)
+    return cache["g"], cache["A_cat"], cache["B_blk"], cache["B_catT"]
 
 
 def _direct(p) -> bool:
@@ -75,14 +91,17 @@ class QKVFunction(torch.autograd.Function):
         w = torch.empty(Nt, d, dtype=torch.bfloat16, device=x2.device)
         _decode_into(mods, w)
         lora = mods[0].lora_r > 0
-        U = A_cat = B_blk = None
+        U = Ut = A_cat = B_blk = B_catT = None
+        g = 0
         if lora:
-            A_cat, B_blk = _lora_blocks(mods, cache)
-            U = x2 @ A_cat.t()                      # [M, 192]: x read once for all three
+            g, A_cat, B_blk, B_catT = _lora_blocks(mods, cache)
+            # x read once for all three adapters: U [M, slab width] and Ut [3g, M]
+            U, Ut = lora_k.down(x2, A_cat[:3 * g], upad=A_cat.shape[0])
         y = torch.empty(M, Nt, dtype=torch.bfloat16, device=x2.device)
         E.gemm_rope(x2, w, y, cs, U, B_blk, Ns[0] + Ns[1])
-        del w
-        ctx.save_for_backward(x2 if lora else None, U, A_cat, B_blk)
+        del w, U
+        ctx.save_for_backward(x2 if lora else None, Ut, A_cat, B_blk, B_catT)
+        ctx.g = g
         ctx.mods, ctx.cs, ctx.meta = mods, cs, (x.shape, Ns, lora)
         S = cs.shape[0]
         B = M // S
@@ -94,7 +113,8 @@ class QKVFunction(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dq, dk, dv):
-        x2, U, A_cat, B_blk = ctx.saved_tensors
+        x2, Ut, A_cat, B_blk, B_catT = ctx.saved_tensors
+        gw = ctx.g
         shp, Ns, lora = ctx.meta
         mods, cs = ctx.mods, ctx.cs
         E = _ext.ext()
@@ -103,19 +123,44 @@ class QKVFunction(torch.autograd.Function):
         ref = dq if dq is not None else (dk if dk is not None else dv)
         M = ref.shape[0] * ref.shape[1]
         dev = ref.device
-        g = torch.empty(M, Nt, dtype=torch.bfloat16, device=dev)
+        # the attention backward writes dV in the layout of the fused output (a
+        # column slice of a [M, Nt] buffer): that buffer becomes the gradient
+        in_place = (dv is not None and dv.dtype == torch.bfloat16 and dv.dim() == 4
+                    and dv.stride(3) == 1 and dv.stride(2) == dv.shape[3] and dv.stride(1) == Nt
+                    and dv.stride(0) == dv.shape[1] * Nt and dv.storage_offset() == o2
+                    and dv.untyped_storage().nbytes() == M * Nt * 2)
+        if in_place:
+            g = torch.empty(0, dtype=torch.bfloat16, device=dev).set_(
+                dv.untyped_storage(), 0, (M, Nt), (Nt, 1))
+        else:
+            g = torch.empty(M, Nt, dtype=torch.bfloat16, device=dev)
         for grad, lo, hi, rot in ((dq, 0, o1, True), (dk, o1, o2, True), (dv, o2, Nt, False)):
             if grad is None:
                 g[:, lo:hi].zero_()
             elif rot:   # gradient of the pre-rotation columns, straight into its slice
                 E.rope_into(grad.contiguous(), g[:, lo:hi], cs, -1.0)
-            else:
+            elif not in_place:
                 g[:, lo:hi].copy_(grad.reshape(M, hi - lo))
         d = mods[0].in_features
         gx = None
-        V = None
+        V = Vt = None
+        b_outs = None
         if lora:
-            V = g @ B_blk                          # [M, 192], unscaled dY·B per projection
+            # unscaled dY·B per projection: V [M, slab width] and Vt [3g, M]; with
+            # the three dB (each from its column slice of dY) in the same pass
+            r = mods[0].lora_r
+            res = None
+            if any(ctx.needs_input_grad[2 + 2 * i] for i in range(3)):
+                b_outs = [m.lora_B.grad if _direct(m.lora_B) else
+                          torch.zeros(m.out_features, r, dtype=torch.float32, device=dev)
+                          for m in mods]
+                segs = [(0, Ns[0], 0), (o1, Ns[1], gw), (o2, Ns[2], 2 * gw)]
+                # (None: nothing launched, the outputs are untouched)
+                res = lora_k.vdb(g, B_catT, Ut, A_cat.shape[0], segs, b_outs, gw, r)
+            vdb_done = res is not None
+            if res is None:
+                res = lora_k.down(g, B_catT, upad=A_cat.shape[0])
+            V, Vt = res
         if ctx.needs_input_grad[0]:
             w = torch.empty(Nt, d, dtype=torch.bfloat16, device=dev)
             _decode_into(mods, w)
@@ -125,27 +170,36 @@ class QKVFunction(torch.autograd.Function):
             gx = gx.view(*shp[:-1], d)
         grads = [None] * 6
         if lora:
-            dA_cat = torch.empty(A_cat.shape[0], d, dtype=torch.float32, device=dev)
-            E.matmul_accum_f32(V.t(), x2, dA_cat, 1.0, 0.0)   # all three dA in one product
-            off = 0
-            for i, m in enumerate(mods):
-                r = m.lora_r
-                A, Bm = m.lora_A, m.lora_B
-                if ctx.needs_input_grad[1 + 2 * i]:
-                    gA = dA_cat[64 * i:64 * i + r] * m.scaling
-                    if _direct(A):
-                        A.grad.add_(gA)
-                    else:
-                        grads[2 * i] = gA.to(A.dtype)
-                if ctx.needs_input_grad[2 + 2 * i]:
-                    gy_i = g[:, off:off + m.out_features]
-                    if _direct(Bm):
-                        E.matmul_accum_f32(gy_i.t(), U[:, 64 * i:64 * i + r], Bm.grad, 1.0, 1.0)
-                    else:
-                        gB = torch.empty(m.out_features, r, dtype=torch.float32, device=dev)
-                        E.matmul_accum_f32(gy_i.t(), U[:, 64 * i:64 * i + r], gB, 1.0, 0.0)
-                        grads[2 * i + 1] = gB.to(Bm.dtype)
-                off += m.out_features
+            r = mods[0].lora_r
+            scal = {m.scaling for m in mods}
+            want_a = [ctx.needs_input_grad[1 + 2 * i] for i in range(3)]
+            want_b = [ctx.needs_input_grad[2 + 2 * i] for i in range(3)]
+            # dA of all three adapters: one pass over x (groups of gw rank columns)
+            if any(want_a):
+                one = len(scal) == 1
+                outs = [m.lora_A.grad if (one and _direct(m.lora_A)) else
+                        torch.zeros(r, d, dtype=torch.float32, device=dev) for m in mods]
+                alpha = next(iter(scal)) if one else 1.0
+                lora_k.wgrad(x2, Vt, 3 * gw, [(0, d, 0, alpha)], outs, gw, r, True)
+                for i, m in enumerate(mods):
+                    if want_a[i] and outs[i] is not m.lora_A.grad:
+                        gA = outs[i] if one else outs[i] * m.scaling
+                        if _direct(m.lora_A):
+                            m.lora_A.grad.add_(gA)
+                        else:
+                            grads[2 * i] = gA.to(m.lora_A.dtype)
+            # dB of each adapter from its own column slice of dY: three jobs, one
+            # launch (unless the fused pass above already added them)
+            if any(want_b):
+                if not vdb_done:
+                    jobs, off = [], 0
+                    for i, m in enumerate(mods):
+                        jobs.append((off, m.out_features, gw * i, 1.0))
+                        off += m.out_features
+                    lora_k.wgrad(g, Ut, gw, jobs, b_outs, gw, r, False)
+                for i, m in enumerate(mods):
+                    if want_b[i] and b_outs[i] is not m.lora_B.grad:
+                        grads[2 * i + 1] = b_outs[i].to(m.lora_B.dtype)
         return (gx, *grads, None, None, None)
 
 

@@ -20,12 +20,15 @@ CUDA path, per call (``csrc/gemm_sm100.cu``):
   ``B``, both zero-padded to rank 64); the input gradient
   ``dX = dY W + (s·dY B) A`` reads the same ``[N, K]`` operand MN-major
   (``gemm_bf16_nn``), so no transposed operand is produced;
-* ``U``/``V`` (rank-64 padded, skinny) and the ``A``/``B`` weight gradients
-  (contractions over tokens) are small cuBLAS GEMMs; the weight gradients
-  accumulate straight into fp32 ``.grad`` buffers bound by ``FlatParams``.
+* the rank-space products ``U = x·(sA)ᵀ``, ``V = dY·B`` and the ``A``/``B`` weight
+  gradients (contractions over tokens) are the tcgen05 kernels of
+  ``csrc/lora_sm100.cu`` (:mod:`zeroq_b200.ops.lora`): ``U``/``V`` are computed at
+  the rank rounded up to 16 and written zero-padded to the 64-wide slab plus a
+  transposed copy, and the weight gradients accumulate in fp32 straight into the
+  ``.grad`` buffers bound by ``FlatParams``.
 
-The padded bf16 LoRA operands (``s·A`` as ``[64, in]`` and ``B`` as
-``[out, 64]``) are cached per module and rebuilt by one kernel when the
+The padded bf16 LoRA operands (``s·A`` as ``[64, in]``, ``B`` as ``[out, 64]``
+and ``Bᵀ`` as ``[r16, out]``) are cached per module and rebuilt by one kernel when the
 parameters' version counters change (every in-place update by an optimizer
 bumps them; ``ShardedAdamW`` bumps them after its kernels).  Writes through
 ``.data`` bypass the counters: call :meth:`Linear4bit.refresh_lora_cache`
@@ -46,6 +49,7 @@ import torch
 import torch.nn as nn
 
 from . import _ext
+from . import lora as lora_k
 from .nf4 import QUANT_TYPE_ID, QuantState, dequantize_4bit, quantize_4bit
 
 
@@ -101,7 +105,8 @@ class NF4LinearFunction(torch.autograd.Function):
     CUDA path: the NF4 operand is produced in the tcgen05 operand layout and the
     LoRA up-projection rides as the extra 64-wide K slab of the same GEMM
     (``U = x·(s·A)ᵀ`` against ``B``, zero-padded to rank 64).  ``lora_ops`` is
-    the cached pair ``(s·A padded [64, K], B padded [N, 64])`` in bf16.
+    the cached triple ``(s·A padded [64, K], B padded [N, 64], Bᵀ [r16, N])`` in
+    bf16.
 
     GELU MLP fusion (``act_out`` / ``pre``):
 
@@ -135,7 +140,8 @@ class NF4LinearFunction(torch.autograd.Function):
         if peer is not None and not peer_fused:
             packed, absmax = peer[0].gather(peer[1]).wait()
         U = None
-        a_pad = b_pad = None
+        Ut = None
+        a_pad = b_pad = b_t = None
         act = None
         rope_done = False
         rope_cs = None
@@ -151,8 +157,9 @@ class NF4LinearFunction(torch.autograd.Function):
             if has_lora:
                 if lora_ops is None:
                     lora_ops = _pack_lora(lora_A.detach(), lora_B.detach(), scaling)
-                a_pad, b_pad = lora_ops
-                U = x2 @ a_pad.t()  # [M, 64] skinny product: cuBLAS
+                a_pad, b_pad, b_t = lora_ops
+                # U [M, 64] (zero past the rank) for the GEMM slab, Ut [r16, M] for dB
+                U, Ut = lora_k.down(x2, a_pad[:lora_k.round16(r)])
             if peer_fused:
                 _, wbuf = peer[0].ag_gemm(peer[1], x2, out=y,
                                           extra=(U, b_pad) if has_lora else None)
@@ -200,8 +207,9 @@ class NF4LinearFunction(torch.autograd.Function):
             pre2 = pre.reshape(-1, K)
             if not pre2.is_contiguous():
                 pre2 = pre2.contiguous()
-        ctx.save_for_backward(x2 if has_lora else None, packed, absmax, lora_A, lora_B, U,
-                              a_pad, b_pad, pre2)
+        # fused path: the transposed rank-space product is what the backward reads
+        ctx.save_for_backward(x2 if has_lora else None, packed, absmax, lora_A, lora_B,
+                              Ut if fused else U, a_pad, b_pad, b_t, pre2)
         ctx.meta = (shp, N, K, blocksize, quant_type, scaling, fused, bias is not None, has_lora, r)
         ctx.peer = peer
         y = y.view(*shp[:-1], N)
@@ -220,7 +228,7 @@ class NF4LinearFunction(torch.autograd.Function):
     def backward(ctx, gy, g_act=None):
         if gy is None:  # (grads are not materialised for the act_out form)
             return (None,) * 17
-        x2, packed, absmax, lora_A, lora_B, U, a_pad, b_pad, pre2 = ctx.saved_tensors
+        x2, packed, absmax, lora_A, lora_B, U, a_pad, b_pad, b_t, pre2 = ctx.saved_tensors
         shp, N, K, blocksize, quant_type, scaling, fused, has_bias, has_lora, r = ctx.meta
         gy2 = gy.reshape(-1, N)
         if not gy2.is_contiguous():
@@ -243,9 +251,24 @@ class NF4LinearFunction(torch.autograd.Function):
         if fused:
             E = _ext.ext()
             gy2 = gy2.to(torch.bfloat16)
-            V = None
+            V = Vt = None
+            b_done = False
             if has_lora:
-                V = gy2 @ b_pad  # [M, 64] = dY·B (unscaled), skinny product: cuBLAS
+                r16 = lora_k.round16(r)
+                res = None
+                if ctx.needs_input_grad[4]:
+                    # V = dY·B and dB += dYᵀ·U in one pass over dY
+                    direct_b = _direct_grad(lora_B)
+                    out_b = lora_B.grad if direct_b else torch.zeros(N, r, dtype=torch.float32,
+                                                                     device=gy2.device)
+                    res = lora_k.vdb(gy2, b_t, U, 64, [(0, N, 0)], [out_b], r16, r)
+                    if res is not None:
+                        b_done = True
+                        if not direct_b:
+                            gB = out_b.to(lora_B.dtype)
+                if res is None:
+                    res = lora_k.down(gy2, b_t)  # [M, 64] = dY·B (unscaled), and Vᵀ
+                V, Vt = res
             if want_gx:
                 gx = torch.empty(M, K, dtype=torch.bfloat16, device=gy2.device)
                 if pre2 is not None and _epi_ok(M, N) and not _in_kernel_ok(M, N, K):
@@ -276,21 +299,22 @@ class NF4LinearFunction(torch.autograd.Function):
                     del w
                 gx = gx.view(*shp[:-1], K)
             if has_lora:
-                # dA = s·Vᵀ·X, dB = dYᵀ·U: bf16 operands, fp32 accumulation
+                # dA += s·Vᵀ·X, dB += dYᵀ·U: bf16 operands, fp32 accumulation straight
+                # into the bound gradient (or a zeroed buffer), U read as Ut [r16, M]
                 if ctx.needs_input_grad[3]:
-                    if _direct_grad(lora_A):
-                        E.matmul_accum_f32(V[:, :r].t(), x2, lora_A.grad, scaling, 1.0)
-                    else:
-                        gA = torch.empty(r, K, dtype=torch.float32, device=gy2.device)
-                        E.matmul_accum_f32(V[:, :r].t(), x2, gA, scaling, 0.0)
-                        gA = gA.to(lora_A.dtype)
-                if ctx.needs_input_grad[4]:
-                    if _direct_grad(lora_B):
-                        E.matmul_accum_f32(gy2.t(), U[:, :r], lora_B.grad, 1.0, 1.0)
-                    else:
-                        gB = torch.empty(N, r, dtype=torch.float32, device=gy2.device)
-                        E.matmul_accum_f32(gy2.t(), U[:, :r], gB, 1.0, 0.0)
-                        gB = gB.to(lora_B.dtype)
+                    direct = _direct_grad(lora_A)
+                    out = lora_A.grad if direct else torch.zeros(r, K, dtype=torch.float32,
+                                                                 device=gy2.device)
+                    lora_k.wgrad(x2, Vt, r16, [(0, K, 0, scaling)], [out], r16, r, True)
+                    if not direct:
+                        gA = out.to(lora_A.dtype)
+                if ctx.needs_input_grad[4] and not b_done:
+                    direct = _direct_grad(lora_B)
+                    out = lora_B.grad if direct else torch.zeros(N, r, dtype=torch.float32,
+                                                                 device=gy2.device)
+                    lora_k.wgrad(gy2, U, r16, [(0, N, 0, 1.0)], [out], r16, r, False)
+                    if not direct:
+                        gB = out.to(lora_B.dtype)
         else:
             Vf = None
             if has_lora:
@@ -409,20 +433,22 @@ def _master_fused_ok(x: torch.Tensor, N: int, K: int) -> bool:
 
 
 def _pack_lora(A: torch.Tensor, B: torch.Tensor, scaling: float, out=None):
-    """``(s·A padded to [64, K], B padded to [N, 64])`` in bf16; ``out`` reuses buffers
-    whose padding is already zero."""
+    """``(s·A padded to [64, K], B padded to [N, 64], Bᵀ padded to [r16, N])`` in
+    bf16; ``out`` reuses buffers whose padding is already zero."""
     r, K = A.shape
     N = B.shape[0]
     if out is None:
         out = (torch.zeros(64, K, dtype=torch.bfloat16, device=A.device),
-               torch.zeros(N, 64, dtype=torch.bfloat16, device=A.device))
-    a_pad, b_pad = out
+               torch.zeros(N, 64, dtype=torch.bfloat16, device=A.device),
+               torch.zeros(lora_k.round16(r), N, dtype=torch.bfloat16, device=A.device))
+    a_pad, b_pad, b_t = out
     if A.is_cuda and A.dtype == torch.float32 and B.dtype == torch.float32:
-        _ext.ext().lora_pack(A.contiguous(), B.contiguous(), float(scaling), a_pad, b_pad)
+        _ext.ext().lora_pack(A.contiguous(), B.contiguous(), float(scaling), a_pad, b_pad, b_t)
     else:
         a_pad[:r].copy_(A.float() * scaling)
         b_pad[:, :r].copy_(B)
-    return a_pad, b_pad
+        b_t[:r].copy_(B.t())
+    return a_pad, b_pad, b_t
 
 
 def nf4_linear(x, packed, absmax, out_features: int, in_features: int, bias=None,
@@ -556,6 +582,8 @@ class Linear4bit(nn.Module):
             reuse = self._lora_ops
             if reuse is not None and (reuse[0].shape != (64, A.shape[1])
                                       or reuse[1].shape != (B.shape[0], 64)
+                                      or reuse[2].shape != (lora_k.round16(A.shape[0]),
+                                                            B.shape[0])
                                       or reuse[0].device != A.device):
                 reuse = None
             with torch.no_grad():
