@@ -116,6 +116,9 @@ def main():
                     help="run the steps eagerly instead of as one CUDA graph replay each")
     ap.add_argument("--torch-profile", default=None,
                     help="after timing, profile one more step and write a per-kernel table here")
+    ap.add_argument("--metrics-jsonl", default=None,
+                    help="per-step JSONL (loss, device ms and tokens/s max over ranks, bytes "
+                         "gathered / synced) written by the Trainer during the end-to-end pass")
     args = ap.parse_args()
     if args.warmup < 3:
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
@@ -131,6 +134,7 @@ def main():
     from zeroq_b200.models import DecoderLM, get_config
     from zeroq_b200.ops import _ext
     from zeroq_b200.train import ClockSampler, Trainer, device_time_ms, synthetic_batch
+    from zeroq_b200.utils import metrics
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -178,11 +182,20 @@ def main():
     torch.cuda.synchronize()
     graphed = trainer._graph is not None
 
+    metrics.reset_counters()
     with ClockSampler(local) as clk, _ext.LaunchCounter() as lc:
         ms = device_time_ms(lambda: trainer.step_device(x_dev, y_dev), args.steps)
+    moved = {k: v // args.steps for k, v in metrics.snapshot().items()}
     e2e_ms = None
     if not args.no_e2e:
+        if args.metrics_jsonl:
+            trainer.logger = metrics.StepLogger(args.metrics_jsonl, flush_every=args.steps,
+                                                flops_per_token=model.flops_per_token(S),
+                                                peak_tflops=_measured_peaks()["bf16_tflops_sustained"])
         e2e_ms = device_time_ms(lambda: losses.append(trainer.step(x_host, y_host)), args.steps)
+        if trainer.logger is not None:
+            trainer.logger.flush()
+            trainer.logger = None
 
     if args.torch_profile and rank == 0:
         from torch.profiler import ProfilerActivity, profile
@@ -199,7 +212,10 @@ def main():
     peaks = _measured_peaks()
     fpt = model.flops_per_token(S)
     tflops_per_gpu = fpt * value / world / 1e12
-    mem_gb = torch.cuda.max_memory_allocated(device) / 1e9
+    mem = torch.tensor([torch.cuda.max_memory_allocated(device) / 1e9], device=device)
+    if world > 1:
+        dist.all_reduce(mem, op=dist.ReduceOp.MAX)
+    mem_gb = float(mem.item())
     first_loss = float(losses[0]) if losses else float("nan")
     last_loss = float(losses[-1]) if losses else float("nan")
     out = {
@@ -239,7 +255,9 @@ def main():
         "clocks": clk.summary(),
         "achieved_tflops_per_gpu": round(tflops_per_gpu, 1),
         "frac_of_measured_bf16_sustained": round(tflops_per_gpu / peaks["bf16_tflops_sustained"], 3),
-        "peak_mem_gb": round(mem_gb, 1),
+        "peak_mem_gb": round(mem_gb, 1),   # max over ranks
+        "gather_bytes_per_step": moved.get("gather_bytes", 0),   # rank 0: read from other ranks
+        "sync_bytes_per_step": moved.get("sync_bytes", 0),
         "loss_first_last": [round(first_loss, 4), round(last_loss, 4)],
     }
     if rank == 0:

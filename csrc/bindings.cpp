@@ -56,7 +56,8 @@ void ce_bwd(at::Tensor logits, at::Tensor targets, at::Tensor lse, at::Tensor sc
             int64_t ignore_index);
 void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> pbf16,
                 double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
-                double gscale, c10::optional<at::Tensor> bc);
+                double gscale, c10::optional<at::Tensor> bc, c10::optional<at::Tensor> clip_sq,
+                double max_norm);
 void opt_tick(at::Tensor clk, at::Tensor bc, double b1, double b2, bool bump_epoch);
 void lion_step(at::Tensor master, at::Tensor grad, at::Tensor mom, double lr, double b1, double b2,
                double wd, int64_t seed);
@@ -73,7 +74,11 @@ void rs_adamw(std::vector<int64_t> grads, std::vector<int64_t> params, std::vect
               int64_t rank, int64_t epoch, int64_t lo, int64_t n, at::Tensor m, at::Tensor v,
               int64_t grad_is_bf16, double lr, double b1, double b2, double eps, double wd,
               double bc1, double bc2, double gscale, bool push, int64_t timeout_ms,
-              c10::optional<at::Tensor> clk, c10::optional<at::Tensor> bc);
+              c10::optional<at::Tensor> clk, c10::optional<at::Tensor> bc,
+              c10::optional<at::Tensor> clip_sq, double max_norm, int64_t epoch_mul, int64_t epoch_add);
+void rs_sumsq(std::vector<int64_t> grads, std::vector<int64_t> flags, int64_t rank, int64_t epoch, int64_t lo,
+              int64_t n, at::Tensor sq, int64_t grad_is_bf16, double gscale, int64_t timeout_ms,
+              c10::optional<at::Tensor> clk, int64_t epoch_mul, int64_t epoch_add);
 void plan_gather(std::vector<int64_t> src, std::vector<int64_t> flags, int64_t rank, int64_t epoch,
                  std::vector<int64_t> offsets, std::vector<int64_t> lengths, at::Tensor out,
                  int64_t timeout_ms);
@@ -148,10 +153,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", [](at::Tensor p, at::Tensor g, at::Tensor m_, at::Tensor v,
                          c10::optional<at::Tensor> pbf16, double lr, double b1, double b2, double eps,
                          double wd, double bc1, double bc2, double gscale) {
-    adamw_step(p, g, m_, v, pbf16, lr, b1, b2, eps, wd, bc1, bc2, gscale, c10::nullopt);
+    adamw_step(p, g, m_, v, pbf16, lr, b1, b2, eps, wd, bc1, bc2, gscale, c10::nullopt, c10::nullopt, 0.0);
   });
-  // bias corrections read from the device-side optimizer clock (bc, see opt_tick)
-  m.def("adamw_step_dev", &adamw_step);
+  // bias corrections read from the device-side optimizer clock (bc, see opt_tick);
+  // optional device-side gradient clipping (clip_sq = squared global norm, max_norm)
+  m.def("adamw_step_dev", &adamw_step, py::arg("p"), py::arg("g"), py::arg("m"), py::arg("v"),
+        py::arg("pbf16"), py::arg("lr"), py::arg("b1"), py::arg("b2"), py::arg("eps"), py::arg("wd"),
+        py::arg("bc1"), py::arg("bc2"), py::arg("gscale"), py::arg("bc") = py::none(),
+        py::arg("clip_sq") = py::none(), py::arg("max_norm") = 0.0);
   m.def("opt_tick", &opt_tick, "advance the device-side optimizer clock");
   m.def("lion_step", &lion_step);
   m.def("peer_alloc", &peer_alloc);
@@ -167,10 +176,20 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                        int64_t grad_is_bf16, double lr, double b1, double b2, double eps, double wd,
                        double bc1, double bc2, double gscale, bool push, int64_t timeout_ms) {
     rs_adamw(grads, params, flags, rank, epoch, lo, n, m_, v, grad_is_bf16, lr, b1, b2, eps, wd, bc1,
-             bc2, gscale, push, timeout_ms, c10::nullopt, c10::nullopt);
+             bc2, gscale, push, timeout_ms, c10::nullopt, c10::nullopt, c10::nullopt, 0.0, 1, 0);
   });
-  // epoch and bias corrections from the device-side optimizer clock
-  m.def("rs_adamw_dev", &rs_adamw);
+  // epoch and bias corrections from the device-side optimizer clock (clk, bc);
+  // optional device-side gradient clipping (clip_sq, max_norm)
+  m.def("rs_adamw_dev", &rs_adamw, py::arg("grads"), py::arg("params"), py::arg("flags"), py::arg("rank"),
+        py::arg("epoch"), py::arg("lo"), py::arg("n"), py::arg("m"), py::arg("v"), py::arg("grad_is_bf16"),
+        py::arg("lr"), py::arg("b1"), py::arg("b2"), py::arg("eps"), py::arg("wd"), py::arg("bc1"),
+        py::arg("bc2"), py::arg("gscale"), py::arg("push"), py::arg("timeout_ms"),
+        py::arg("clk") = py::none(), py::arg("bc") = py::none(), py::arg("clip_sq") = py::none(),
+        py::arg("max_norm") = 0.0, py::arg("epoch_mul") = 1, py::arg("epoch_add") = 0);
+  m.def("rs_sumsq", &rs_sumsq, py::arg("grads"), py::arg("flags"), py::arg("rank"), py::arg("epoch"),
+        py::arg("lo"), py::arg("n"), py::arg("sq"), py::arg("grad_is_bf16"), py::arg("gscale"),
+        py::arg("timeout_ms"), py::arg("clk") = py::none(), py::arg("epoch_mul") = 1,
+        py::arg("epoch_add") = 0);
   m.def("plan_gather", &plan_gather);
   m.def("plan_gather_dequant", &plan_gather_dequant);
   m.def("ag_gemm_f32", &ag_gemm_f32, "gather of fp32 pieces + bf16 cast + tcgen05 GEMM in one kernel",

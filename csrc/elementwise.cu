@@ -479,11 +479,14 @@ template <typename G>
 __global__ void adamw_kernel(float* __restrict__ p, const G* __restrict__ g, float* __restrict__ m,
                              float* __restrict__ v, __nv_bfloat16* __restrict__ pbf, int64_t n,
                              float lr, float b1, float b2, float eps, float wd, float bc1,
-                             float bc2, float gscale, const float* __restrict__ bcp) {
+                             float bc2, float gscale, const float* __restrict__ bcp,
+                             const float* __restrict__ clip_sq, float max_norm) {
   if (bcp != nullptr) {  // bias corrections from the device-side optimizer clock
     bc1 = bcp[0];
     bc2 = bcp[1];
   }
+  // gradient clipping with the squared global norm on the device (no host sync)
+  if (clip_sq != nullptr) gscale *= fminf(1.0f, max_norm / (sqrtf(*clip_sq) + 1e-6f));
   const float step_size = lr / bc1;
   const float inv_sqrt_bc2 = rsqrtf(bc2);
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -883,8 +886,15 @@ void ce_bwd(at::Tensor logits, at::Tensor targets, at::Tensor lse, at::Tensor sc
 
 void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v,
                 c10::optional<at::Tensor> pbf16, double lr, double b1, double b2, double eps,
-                double wd, double bc1, double bc2, double gscale, c10::optional<at::Tensor> bc) {
+                double wd, double bc1, double bc2, double gscale, c10::optional<at::Tensor> bc,
+                c10::optional<at::Tensor> clip_sq, double max_norm) {
   const float* bcp = nullptr;
+  const float* sqp = nullptr;
+  if (clip_sq.has_value() && clip_sq->defined()) {
+    TORCH_CHECK(clip_sq->is_cuda() && clip_sq->scalar_type() == at::kFloat && clip_sq->numel() >= 1 &&
+                    max_norm > 0.0, "adamw: clip_sq fp32[1] and a positive max_norm");
+    sqp = clip_sq->data_ptr<float>();
+  }
   if (bc.has_value() && bc->defined()) {
     TORCH_CHECK(bc->is_cuda() && bc->scalar_type() == at::kFloat && bc->numel() >= 2, "adamw: bc fp32[2]");
     bcp = bc->data_ptr<float>();
@@ -902,12 +912,12 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v,
   if (g.scalar_type() == at::kFloat) {
     adamw_kernel<float><<<grid, 256, 0, stream>>>(p.data_ptr<float>(), g.data_ptr<float>(),
         m.data_ptr<float>(), v.data_ptr<float>(), pb, n, (float)lr, (float)b1, (float)b2,
-        (float)eps, (float)wd, (float)bc1, (float)bc2, (float)gscale, bcp);
+        (float)eps, (float)wd, (float)bc1, (float)bc2, (float)gscale, bcp, sqp, (float)max_norm);
   } else {
     TORCH_CHECK(g.scalar_type() == at::kBFloat16, "adamw: grad fp32 or bf16");
     adamw_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(p.data_ptr<float>(), cbf(g),
         m.data_ptr<float>(), v.data_ptr<float>(), pb, n, (float)lr, (float)b1, (float)b2,
-        (float)eps, (float)wd, (float)bc1, (float)bc2, (float)gscale, bcp);
+        (float)eps, (float)wd, (float)bc1, (float)bc2, (float)gscale, bcp, sqp, (float)max_norm);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

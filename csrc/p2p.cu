@@ -164,14 +164,20 @@ __global__ void __launch_bounds__(256) rs_adamw_kernel(PeerTable grads, PeerTabl
                                                        float bc2, float gscale, int push,
                                                        unsigned long long wait_ns,
                                                        const int64_t* __restrict__ clk,
-                                                       const float* __restrict__ bcp) {
+                                                       const float* __restrict__ bcp,
+                                                       const float* __restrict__ clip_sq, float max_norm,
+                                                       int epoch_mul, int epoch_add) {
   // device-side optimizer clock (CUDA-graph replays): epoch and bias corrections
-  // written by opt_tick earlier on this stream instead of launch arguments
-  if (clk != nullptr) epoch = (int)clk[1];
+  // written by opt_tick earlier on this stream instead of launch arguments (a
+  // step that runs two peer kernels takes epochs clk * 2 and clk * 2 + 1)
+  if (clk != nullptr) epoch = (int)clk[1] * epoch_mul + epoch_add;
   if (bcp != nullptr) {
     bc1 = bcp[0];
     bc2 = bcp[1];
   }
+  // gradient clipping: clip_sq holds the squared norm of the averaged gradient
+  // (rs_sumsq, then summed over the ranks); scale by min(1, max_norm / norm)
+  if (clip_sq != nullptr) gscale *= fminf(1.0f, max_norm / (sqrtf(*clip_sq) + 1e-6f));
   const bool ok = grid_start(flags, rank, world, epoch, wait_ns);
   if (ok) {
     const float step_size = lr / bc1;
@@ -230,6 +236,43 @@ __global__ void __launch_bounds__(256) rs_adamw_kernel(PeerTable grads, PeerTabl
         }
       }
     }
+  }
+  grid_end(flags, rank, world, epoch, wait_ns);
+}
+
+// sq[0] += sum over this rank's shard [lo, lo + n) of (gscale * sum_q grads[q][i])^2:
+// the squared norm of the averaged gradient's shard, read over NVLink like
+// rs_adamw reads it (same barriers), for gradient clipping without a host sync.
+template <typename G>
+__global__ void __launch_bounds__(256) rs_sumsq_kernel(PeerTable grads, PeerTable flags, int rank, int world,
+                                                       int epoch, int64_t lo, int64_t n, float gscale,
+                                                       float* __restrict__ sq, unsigned long long wait_ns,
+                                                       const int64_t* __restrict__ clk, int epoch_mul,
+                                                       int epoch_add) {
+  if (clk != nullptr) epoch = (int)clk[1] * epoch_mul + epoch_add;
+  __shared__ float red[8];
+  const bool ok = grid_start(flags, rank, world, epoch, wait_ns);
+  float acc = 0.0f;
+  if (ok) {
+    const int64_t n4 = n >> 2;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      float4 g = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int q = 0; q < world; ++q) {
+        const float4 t = load4<G>(reinterpret_cast<const G*>(grads.ptr[q]) + lo + i * 4);
+        g.x += t.x; g.y += t.y; g.z += t.z; g.w += t.w;
+      }
+      g.x *= gscale; g.y *= gscale; g.z *= gscale; g.w *= gscale;
+      acc += g.x * g.x + g.y * g.y + g.z * g.z + g.w * g.w;
+    }
+  }
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0 && v != 0.0f) atomicAdd(sq, v);
   }
   grid_end(flags, rank, world, epoch, wait_ns);
 }
@@ -446,7 +489,8 @@ void rs_adamw(std::vector<int64_t> grads, std::vector<int64_t> params, std::vect
               int64_t rank, int64_t epoch, int64_t lo, int64_t n, at::Tensor m, at::Tensor v,
               int64_t grad_is_bf16, double lr, double b1, double b2, double eps, double wd,
               double bc1, double bc2, double gscale, bool push, int64_t timeout_ms,
-              c10::optional<at::Tensor> clk, c10::optional<at::Tensor> bc) {
+              c10::optional<at::Tensor> clk, c10::optional<at::Tensor> bc,
+              c10::optional<at::Tensor> clip_sq, double max_norm, int64_t epoch_mul, int64_t epoch_add) {
   const int world = (int)grads.size();
   TORCH_CHECK(world >= 1 && world <= kMaxRanks && (int)params.size() == world &&
                   (int)flags.size() == world, "rs_adamw: one pointer per rank");
@@ -463,18 +507,57 @@ void rs_adamw(std::vector<int64_t> grads, std::vector<int64_t> params, std::vect
     clkp = clk->data_ptr<int64_t>();
     bcp = bc->data_ptr<float>();
   }
+  const float* sqp = nullptr;
+  if (clip_sq.has_value() && clip_sq->defined()) {
+    TORCH_CHECK(clip_sq->is_cuda() && clip_sq->scalar_type() == at::kFloat && clip_sq->numel() >= 1,
+                "rs_adamw: clip_sq fp32[1]");
+    TORCH_CHECK(max_norm > 0.0, "rs_adamw: max_norm must be positive");
+    sqp = clip_sq->data_ptr<float>();
+  }
   const int grid = grad_is_bf16 ? resident_grid(rs_adamw_kernel<__nv_bfloat16>, 256)
                                 : resident_grid(rs_adamw_kernel<float>, 256);
   if (grad_is_bf16) {
     rs_adamw_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
         table_from(grads), table_from(params), table_from(flags), (int)rank, world, (int)epoch, lo, n,
         m.data_ptr<float>(), v.data_ptr<float>(), (float)lr, (float)b1, (float)b2, (float)eps,
-        (float)wd, (float)bc1, (float)bc2, (float)gscale, push ? 1 : 0, wait_ns(timeout_ms), clkp, bcp);
+        (float)wd, (float)bc1, (float)bc2, (float)gscale, push ? 1 : 0, wait_ns(timeout_ms), clkp, bcp,
+        sqp, (float)max_norm, (int)epoch_mul, (int)epoch_add);
   } else {
     rs_adamw_kernel<float><<<grid, 256, 0, stream>>>(
         table_from(grads), table_from(params), table_from(flags), (int)rank, world, (int)epoch, lo, n,
         m.data_ptr<float>(), v.data_ptr<float>(), (float)lr, (float)b1, (float)b2, (float)eps,
-        (float)wd, (float)bc1, (float)bc2, (float)gscale, push ? 1 : 0, wait_ns(timeout_ms), clkp, bcp);
+        (float)wd, (float)bc1, (float)bc2, (float)gscale, push ? 1 : 0, wait_ns(timeout_ms), clkp, bcp,
+        sqp, (float)max_norm, (int)epoch_mul, (int)epoch_add);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// sq[0] += squared norm of this rank's shard of the averaged gradient (see
+// rs_sumsq_kernel); sq must be zeroed by the caller.  clk: device clock epochs.
+void rs_sumsq(std::vector<int64_t> grads, std::vector<int64_t> flags, int64_t rank, int64_t epoch, int64_t lo,
+              int64_t n, at::Tensor sq, int64_t grad_is_bf16, double gscale, int64_t timeout_ms,
+              c10::optional<at::Tensor> clk, int64_t epoch_mul, int64_t epoch_add) {
+  const int world = (int)grads.size();
+  TORCH_CHECK(world >= 1 && world <= kMaxRanks && (int)flags.size() == world, "rs_sumsq: one pointer per rank");
+  TORCH_CHECK(n % 4 == 0 && lo % 4 == 0, "rs_sumsq: shard offset/length must be multiples of 4");
+  TORCH_CHECK(sq.is_cuda() && sq.scalar_type() == at::kFloat && sq.numel() >= 1, "rs_sumsq: sq fp32[1]");
+  const at::cuda::CUDAGuard guard(sq.device());
+  const int64_t* clkp = nullptr;
+  if (clk.has_value() && clk->defined()) {
+    TORCH_CHECK(clk->scalar_type() == at::kLong && clk->numel() >= 2 && clk->is_cuda(), "rs_sumsq: clk int64[2]");
+    clkp = clk->data_ptr<int64_t>();
+  }
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (grad_is_bf16) {
+    const int grid = resident_grid(rs_sumsq_kernel<__nv_bfloat16>, 256);
+    rs_sumsq_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+        table_from(grads), table_from(flags), (int)rank, world, (int)epoch, lo, n, (float)gscale,
+        sq.data_ptr<float>(), wait_ns(timeout_ms), clkp, (int)epoch_mul, (int)epoch_add);
+  } else {
+    const int grid = resident_grid(rs_sumsq_kernel<float>, 256);
+    rs_sumsq_kernel<float><<<grid, 256, 0, stream>>>(
+        table_from(grads), table_from(flags), (int)rank, world, (int)epoch, lo, n, (float)gscale,
+        sq.data_ptr<float>(), wait_ns(timeout_ms), clkp, (int)epoch_mul, (int)epoch_add);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

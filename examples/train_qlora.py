@@ -55,6 +55,8 @@ def parse_args(argv=None):
     p.add_argument("--steps", type=int, default=100)
     p.add_argument("--lr", type=float, default=2e-4)
     p.add_argument("--weight-decay", type=float, default=0.0)
+    p.add_argument("--max-grad-norm", type=float, default=None,
+                   help="global-norm gradient clipping (computed on the device, every backend)")
     p.add_argument("--lora-r", type=int, default=16)
     p.add_argument("--lora-alpha", type=float, default=32.0)
     p.add_argument("--lora-targets", default=None, help="comma list (default: the preset's)")
@@ -155,7 +157,8 @@ def main(argv=None) -> int:
     weights = [float(w) for w in args.hetero_weights.split(",")] if args.hetero_weights else None
     zq.prepare_model_for_zeroq(model, zcfg, trainable_patterns=("lora_",), rank_weights=weights,
                                checkpoint=args.checkpoint)
-    opt = zq.ShardedAdamW(model.trainable_parameters(), lr=args.lr, weight_decay=args.weight_decay)
+    opt = zq.ShardedAdamW(model.trainable_parameters(), lr=args.lr, weight_decay=args.weight_decay,
+                          max_grad_norm=args.max_grad_norm)
     start = 0
     if args.resume:
         start = load_sharded_checkpoint(args.resume, model, opt)

@@ -156,23 +156,27 @@ def w_reduce_scatter(rank, world):
 def w_sharded_adamw(rank, world):
     import zeroq_b200 as zq
 
-    torch.manual_seed(0)
-    ps = [torch.nn.Parameter(torch.randn(7, 3)), torch.nn.Parameter(torch.randn(5))]
-    ref = [torch.nn.Parameter(p.detach().clone()) for p in ps]
-    opt = zq.ShardedAdamW(ps, lr=1e-2, weight_decay=0.1)
-    ref_opt = torch.optim.AdamW(ref, lr=1e-2, weight_decay=0.1)
-    for step in range(3):
-        gens = [torch.Generator().manual_seed(100 * step + r) for r in range(world)]
-        grads = [[torch.randn(p.shape, generator=gens[r]) for p in ps] for r in range(world)]
-        for p, g in zip(ps, grads[rank]):
-            p.grad.copy_(g)
-        opt.step()
-        opt.zero_grad()
-        for i, p in enumerate(ref):
-            p.grad = sum(grads[r][i] for r in range(world)) / world
-        ref_opt.step()
-    for p, r in zip(ps, ref):
-        assert torch.allclose(p.detach(), r.detach(), atol=1e-5), (p, r)
+    for clip in (None, 0.5):  # with clipping: the averaged gradient's global norm
+        torch.manual_seed(0)
+        ps = [torch.nn.Parameter(torch.randn(7, 3)), torch.nn.Parameter(torch.randn(5))]
+        ref = [torch.nn.Parameter(p.detach().clone()) for p in ps]
+        opt = zq.ShardedAdamW(ps, lr=1e-2, weight_decay=0.1, max_grad_norm=clip)
+        ref_opt = torch.optim.AdamW(ref, lr=1e-2, weight_decay=0.1)
+        for step in range(3):
+            gens = [torch.Generator().manual_seed(100 * step + r) for r in range(world)]
+            grads = [[torch.randn(p.shape, generator=gens[r]) for p in ps] for r in range(world)]
+            for p, g in zip(ps, grads[rank]):
+                p.grad.copy_(g)
+            opt.step()
+            opt.zero_grad()
+            for i, p in enumerate(ref):
+                p.grad = sum(grads[r][i] for r in range(world)) / world
+            if clip is not None:
+                norm = torch.nn.utils.clip_grad_norm_(ref, clip)
+                assert abs(opt.grad_norm() - float(norm)) < 1e-4 * float(norm)
+            ref_opt.step()
+        for p, r in zip(ps, ref):
+            assert torch.allclose(p.detach(), r.detach(), atol=1e-5), (clip, p, r)
 
 
 def w_tiny_decoder_training(rank, world):

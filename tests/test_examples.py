@@ -69,7 +69,7 @@ def test_train_qlora_example_cpu_save_resume(tmp_path):
     env = dict(os.environ, CUDA_VISIBLE_DEVICES="", PYTHONPATH=ROOT)
     ex = os.path.join(ROOT, "examples", "train_qlora.py")
     base = [sys.executable, ex, "--model", "tiny", "--layers", "2", "--seq", "64", "--batch", "2",
-            "--lr", "1e-3", "--lora-r", "4", "--save", str(tmp_path / "run")]
+            "--lr", "1e-3", "--lora-r", "4", "--max-grad-norm", "1.0", "--save", str(tmp_path / "run")]
     r = subprocess.run(base + ["--steps", "3"], env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout + r.stderr
     logs = [json.loads(l) for l in r.stdout.splitlines() if l.startswith("{")]

@@ -144,3 +144,34 @@ class TestConfig:
         assert m.node_id and m.coordinator_port == 5555
         assert MultiNodeConfig.from_dict(m.to_dict()) == m
         assert PHOENIX_CLUSTER_CONFIG.gradient_compression
+
+
+@pytest.mark.parametrize("shape,world,weights", [((37, 129), 3, None), ((64, 64), 2, None),
+                                                 ((50, 77), 4, [2.0, 2.0, 1.0, 1.0]),
+                                                 ((8, 1000), 8, [2, 2, 1, 1, 1, 1, 1, 1])])
+def test_local_range_quantisation_equals_full_then_slice(shape, world, weights):
+    """Each rank quantises only the blocks covering its bytes; the shards are the
+    slices of one full quantisation (uniform and weighted plans, ragged sizes)."""
+    import zeroq_b200 as zq
+    from zeroq_b200.ops.nf4 import quantize_4bit
+    from zeroq_b200.parallel.coordinator import ZeroQParameter
+    from zeroq_b200.parallel.hetero import HeteroZeroQParameter
+
+    torch.manual_seed(0)
+    w = torch.randn(*shape) * 0.02
+    full_p, st = quantize_4bit(w.to(torch.float16), 64, "nf4")
+    full_a = st.absmax.reshape(-1)
+    cfg = zq.ZeroQConfig(exclude_modules=[])
+    for rank in range(world):
+        param = torch.nn.Parameter(w.clone(), requires_grad=False)
+        if weights is None:
+            p = ZeroQParameter(param=param, rank=rank, world_size=world, config=cfg, param_id=0)
+        else:
+            p = HeteroZeroQParameter(param=param, rank=rank, world_size=world, config=cfg,
+                                     param_id=0, rank_weights=weights)
+        p.partition_from_full_precision(w)
+        p0, p1 = p.packed_plan.range_of(rank)
+        a0, a1 = p.absmax_plan.range_of(rank)
+        assert torch.equal(p.local_packed, full_p[p0:p1])
+        assert torch.equal(p.local_absmax, full_a[a0:a1])
+        assert p._quant_meta["shape"] == tuple(shape)

@@ -57,7 +57,24 @@ def _run(fn_name, world=2):
         raise AssertionError("\n".join(msgs) or "worker failed")
 
 
+def _weights(world):
+    """Uneven rank weights: [3, 1] at two ranks, the [2, 2, 1, ...] plan beyond."""
+    return [3.0, 1.0] if world == 2 else [2.0, 2.0] + [1.0] * (world - 2)
+
+
+WORLDS = [2, 4, 8]
+
+
 def w_fused_adamw(rank, world):
+    for clip in (None, 1.0):
+        for graph in (False, True):
+            _fused_adamw_case(rank, world, clip, graph)
+
+
+def _fused_adamw_case(rank, world, clip, device_clock):
+    """Fused reduce-scatter + AdamW (+ device-side clipping: a sum-of-squares pass
+    over NVLink, one scalar all-reduce, the clip factor read by the kernel) against
+    NCCL reduce-scatter + AdamW, with host or device-side optimizer clock."""
     import zeroq_b200 as zq
 
     torch.manual_seed(0)
@@ -65,9 +82,12 @@ def w_fused_adamw(rank, world):
     init = [torch.randn(s, device="cuda") for s in shapes]
     pf = [torch.nn.Parameter(t.clone()) for t in init]
     pn = [torch.nn.Parameter(t.clone()) for t in init]
-    fused = zq.ShardedAdamW(pf, lr=1e-2, weight_decay=0.05, backend="fused")
-    nccl = zq.ShardedAdamW(pn, lr=1e-2, weight_decay=0.05, backend="nccl")
+    fused = zq.ShardedAdamW(pf, lr=1e-2, weight_decay=0.05, backend="fused", max_grad_norm=clip)
+    nccl = zq.ShardedAdamW(pn, lr=1e-2, weight_decay=0.05, backend="nccl", max_grad_norm=clip)
     assert fused.backend == "fused", fused._peer_error
+    if device_clock:
+        fused.use_device_clock()
+        nccl.use_device_clock()
     for step in range(3):
         g = torch.Generator(device="cuda").manual_seed(10 * step + rank)
         for a, b in zip(pf, pn):
@@ -78,6 +98,8 @@ def w_fused_adamw(rank, world):
         nccl.step()
         fused.zero_grad()
         nccl.zero_grad()
+        if clip is not None:
+            torch.testing.assert_close(fused.last_grad_norm, nccl.last_grad_norm, rtol=1e-5, atol=0)
     torch.cuda.synchronize()
     fused._peer.flags.check()
     for a, b in zip(pf, pn):
@@ -97,7 +119,7 @@ def w_peer_gather(rank, world):
                                                         device="cuda") * 0.02, requires_grad=False)
         cfg = zq.ZeroQConfig(exclude_modules=[], backend="nccl")
         if hetero:
-            coord = zq.HeteroZeroQCoordinator(cfg, rank_weights=[3.0, 1.0])
+            coord = zq.HeteroZeroQCoordinator(cfg, rank_weights=_weights(world))
             zq.HeteroZeroQModuleWrapper(m, coord).partition()
         else:
             coord = zq.ZeroQCoordinator(cfg)
@@ -142,7 +164,7 @@ def w_peer_ag_gemm(rank, world):
             m[0].lora_B.normal_(0, 0.02)
         cfg = zq.ZeroQConfig(exclude_modules=[], backend="fused", compute_in_4bit=True)
         if hetero:
-            coord = zq.HeteroZeroQCoordinator(cfg, rank_weights=[3.0, 1.0])
+            coord = zq.HeteroZeroQCoordinator(cfg, rank_weights=_weights(world))
             zq.HeteroZeroQModuleWrapper(m, coord).partition()
         else:
             coord = zq.ZeroQCoordinator(cfg)
@@ -240,20 +262,133 @@ def w_peer_master_gemm(rank, world):
     pool.close()
 
 
-def test_fused_reduce_scatter_adamw_matches_nccl():
-    _run("w_fused_adamw", 2)
+def _tiny_decoder(device):
+    from zeroq_b200.models import DecoderLM, get_config
+
+    cfg = get_config("4.7b", d_model=256, n_layers=2, n_heads=2, n_kv_heads=2, ffn_dim=1024,
+                     vocab_size=1000, lora_r=16, lora_alpha=32.0)
+    return cfg, DecoderLM(cfg, device=device).init_dense_(seed=0)
 
 
-def test_peer_gather_and_gather_dequant_match_nccl():
-    _run("w_peer_gather", 2)
+def _zcfg():
+    import zeroq_b200 as zq
+
+    return zq.ZeroQConfig(compute_dtype=torch.bfloat16, compute_in_4bit=True, gather_once=True,
+                          exclude_modules=["lm_head", "embed_tokens"], backend="fused")
 
 
-def test_peer_ag_gemm_one_kernel_matches_assembled():
-    _run("w_peer_ag_gemm", 2)
+def w_resident_local_copy(rank, world):
+    """4-bit compute with a peer pool registered: the one-time gather assembles a
+    local NF4 copy through the peer plan-gather kernel, byte-identical to the NCCL
+    assembly, and the resident forward equals the peer-source forward."""
+    import zeroq_b200 as zq
+    from zeroq_b200.ops.qlinear import Linear4bit
+    from zeroq_b200.parallel.varlen import all_gather_by_plan
+
+    _, model = _tiny_decoder("cuda")
+    zq.initialize(model, _zcfg(), trainable_patterns=("lora_", "norm"))
+    coord = model._zeroq_coordinator
+    pool = coord.peer_pool
+    assert pool is not None
+    n = 0
+    for p in coord._params.values():
+        mod = p.module
+        if not (isinstance(mod, Linear4bit) and p.param_name == "weight"):
+            continue
+        assert mod._peer is None and mod.weight_packed is not None
+        pk = all_gather_by_plan(p.local_packed, p.packed_plan)
+        am = all_gather_by_plan(p.local_absmax, p.absmax_plan)
+        assert torch.equal(mod.weight_packed, pk) and torch.equal(mod.weight_absmax, am)
+        x = (torch.randn(2, 128, mod.in_features, device="cuda") * 0.5).to(torch.bfloat16)
+        with torch.no_grad():
+            y_res = mod(x)
+            keep = (mod.weight_packed, mod.weight_absmax)
+            mod.set_peer_source(pool, p)
+            y_peer = mod(x)
+            mod.set_nf4(*keep)
+        assert torch.equal(y_res, y_peer)
+        n += 1
+    assert n == 2 * 6
+    torch.cuda.synchronize()
 
 
-def test_peer_master_gather_gemm_matches_nccl_path():
-    _run("w_peer_master_gemm", 2)
+def w_step_equals_single_process(rank, world):
+    """One fused-backend training step on ``world`` ranks (each on its slice of the
+    batch; fused reduce-scatter + AdamW + all-gather) leaves the LoRA and norm
+    parameters where one process stepping on the concatenated batch leaves them.
+    AdamW runs with eps = 1, so the update is ~lr * grad and compares linearly."""
+    import zeroq_b200 as zq
+
+    cfg, model = _tiny_decoder("cuda")
+    zq.initialize(model, _zcfg(), trainable_patterns=("lora_", "norm"))
+    with torch.no_grad():  # non-zero B so every adapter gets a gradient
+        g = torch.Generator(device="cuda").manual_seed(7)
+        for n_, p in model.named_parameters():
+            if "lora_B" in n_:
+                p.normal_(0.0, 0.02, generator=g)
+    opt = zq.ShardedAdamW(model.trainable_parameters(), lr=1e-3, eps=1.0, weight_decay=0.0)
+    assert opt.backend == "fused", opt._peer_error
+    gen = torch.Generator().manual_seed(11)
+    ids = torch.randint(0, cfg.vocab_size, (2 * world, 129), generator=gen)
+    x, y = ids[:, :-1].cuda(), ids[:, 1:].cuda()
+    names = [n_ for n_, p in model.named_parameters() if p.requires_grad]
+    before = {n_: p.detach().clone() for n_, p in model.named_parameters() if p.requires_grad}
+    loss = model(x[2 * rank:2 * rank + 2], y[2 * rank:2 * rank + 2])
+    loss.backward()
+    opt.step()
+    opt.zero_grad()
+    torch.cuda.synchronize()
+    after = {n_: p.detach().clone() for n_, p in model.named_parameters() if p.requires_grad}
+    # single process on the whole batch: same weights, plain fp32 AdamW
+    _, ref = _tiny_decoder("cuda")
+    ref.convert_to_4bit_()
+    for n_, p in ref.named_parameters():
+        p.requires_grad = n_ in before
+        if n_ in before:
+            with torch.no_grad():
+                p.copy_(before[n_])
+    ropt = torch.optim.AdamW([p for p in ref.parameters() if p.requires_grad], lr=1e-3, eps=1.0,
+                             weight_decay=0.0)
+    ref(x, y).backward()
+    ropt.step()
+    refp = dict(ref.named_parameters())
+    worst = 0.0
+    for n_ in names:
+        d_run = after[n_] - before[n_]
+        d_ref = refp[n_].detach() - before[n_]
+        scale = d_ref.abs().max().item() + 1e-12
+        worst = max(worst, (d_run - d_ref).abs().max().item() / scale)
+    assert worst < 5e-2, worst  # bf16 activations, different reduction orders
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_fused_reduce_scatter_adamw_matches_nccl(world):
+    _run("w_fused_adamw", world)
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_peer_gather_and_gather_dequant_match_nccl(world):
+    _run("w_peer_gather", world)
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_peer_ag_gemm_one_kernel_matches_assembled(world):
+    _run("w_peer_ag_gemm", world)
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_peer_master_gather_gemm_matches_nccl_path(world):
+    _run("w_peer_master_gemm", world)
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_resident_mode_assembles_local_nf4_copy_with_peer_pool(world):
+    _run("w_resident_local_copy", world)
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_fused_step_equals_single_process_on_concatenated_batch(world):
+    _run("w_step_equals_single_process", world)
 
 
 def test_peer_wait_times_out_with_error_status(cuda):

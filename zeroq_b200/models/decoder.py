@@ -40,6 +40,7 @@ from ..ops.norm import add_rmsnorm
 from ..ops.qlinear import Linear4bit
 from ..ops.qkv import qkv_fusable, qkv_projection
 from ..ops.rope import RopeSpec, apply_rope, rope_table
+from ..utils.metrics import nvtx_range
 
 
 @dataclass
@@ -329,8 +330,9 @@ class DecoderLM(nn.Module):
         B, S = input_ids.shape
         h = self.embed_tokens(input_ids)
         delta = None
-        for layer in self.layers:
-            h, delta = self._layer_call(layer, h, delta)
+        for i, layer in enumerate(self.layers):
+            with nvtx_range(f"layer{i}"):
+                h, delta = self._layer_call(layer, h, delta)
         x = self.norm(h) if delta is None else self.norm(h, delta)[1]
         W = self.head_weight()
         if W.numel() == 0:

@@ -25,22 +25,27 @@ def adamw_step(param: torch.Tensor, grad: torch.Tensor, exp_avg: torch.Tensor,
                exp_avg_sq: torch.Tensor, *, lr: float, beta1: float = 0.9,
                beta2: float = 0.999, eps: float = 1e-8, weight_decay: float = 0.0,
                step: int = 1, grad_scale: float = 1.0, param_bf16: torch.Tensor = None,
-               bc_dev: torch.Tensor = None):
+               bc_dev: torch.Tensor = None, clip_sq: torch.Tensor = None, max_norm: float = 0.0):
     """In-place AdamW on flat fp32 tensors (``grad`` may be fp32 or bf16).
     ``bc_dev``: fp32 [2] bias corrections on the device (device-side optimizer
-    clock), used instead of ``step``."""
+    clock), used instead of ``step``.  ``clip_sq``: fp32 [1] squared global
+    gradient norm on the device; the gradient is then also scaled by
+    ``min(1, max_norm / sqrt(clip_sq))`` inside the kernel."""
     bc1 = 1.0 - beta1 ** step
     bc2 = 1.0 - beta2 ** step
-    if param.is_cuda and bc_dev is not None:
+    if param.is_cuda and (bc_dev is not None or clip_sq is not None):
         _ext.ext().adamw_step_dev(param, grad, exp_avg, exp_avg_sq, param_bf16, float(lr),
                                   float(beta1), float(beta2), float(eps), float(weight_decay),
-                                  1.0, 1.0, float(grad_scale), bc_dev)
+                                  float(bc1), float(bc2), float(grad_scale), bc_dev, clip_sq,
+                                  float(max_norm))
         return
     if param.is_cuda:
         _ext.ext().adamw_step(param, grad, exp_avg, exp_avg_sq, param_bf16, float(lr),
                               float(beta1), float(beta2), float(eps), float(weight_decay),
                               float(bc1), float(bc2), float(grad_scale))
         return
+    if clip_sq is not None:
+        grad_scale = grad_scale * min(1.0, max_norm / (float(clip_sq.reshape(-1)[0]) ** 0.5 + 1e-6))
     g = grad.float() * grad_scale
     param.mul_(1.0 - lr * weight_decay)
     exp_avg.mul_(beta1).add_(g, alpha=1.0 - beta1)

@@ -19,6 +19,7 @@ from typing import Optional
 import torch
 import torch.distributed as dist
 
+from ..utils.metrics import count, nvtx_range
 from .varlen import all_gather_by_plan
 
 
@@ -58,6 +59,13 @@ def _backend(zq) -> str:
     return b
 
 
+def remote_nf4_bytes(zq) -> int:
+    """Bytes of ``zq``'s packed NF4 data and absmax held by the other ranks."""
+    p0, p1 = zq.packed_plan.range_of(zq.rank)
+    a0, a1 = zq.absmax_plan.range_of(zq.rank)
+    return (zq.packed_plan.total - (p1 - p0)) + 4 * (zq.absmax_plan.total - (a1 - a0))
+
+
 def gather_nf4(zq, group=None, async_op: bool = True) -> GatherHandle:
     """Gather the packed bytes and absmax of ``zq`` according to its plans."""
     if _world(group) == 1 or zq.world_size == 1:
@@ -65,9 +73,12 @@ def gather_nf4(zq, group=None, async_op: bool = True) -> GatherHandle:
         return GatherHandle([lambda: p, lambda: a])
     pool = getattr(zq, "_peer_pool", None)
     if _backend(zq) == "fused" and pool is not None:
-        return pool.gather(zq)
-    _, fin_p = all_gather_by_plan(zq.local_packed, zq.packed_plan, group=group, async_op=True)
-    _, fin_a = all_gather_by_plan(zq.local_absmax, zq.absmax_plan, group=group, async_op=True)
+        with nvtx_range("gather_nf4_peer"):
+            return pool.gather(zq)   # (counts its own bytes)
+    count("gather_bytes", remote_nf4_bytes(zq))
+    with nvtx_range("gather_nf4_nccl"):
+        _, fin_p = all_gather_by_plan(zq.local_packed, zq.packed_plan, group=group, async_op=True)
+        _, fin_a = all_gather_by_plan(zq.local_absmax, zq.absmax_plan, group=group, async_op=True)
     h = GatherHandle([fin_p, fin_a])
     if not async_op:
         h.wait()

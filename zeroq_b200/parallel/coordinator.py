@@ -145,28 +145,43 @@ class ZeroQParameter:
             self.param = new_param
 
     def _quantize_and_keep_shard(self, weight: torch.Tensor, device: torch.device):
-        w = weight.detach().contiguous().to(device=device)
-        if w.dtype != torch.float16:
-            # The reference quantises fp16-cast weights (src/coordinator.py:166-168);
-            # casting first keeps the stored bytes identical.
-            w = w.to(torch.float16)
-        packed, state = quantize_4bit(w, blocksize=self.config.blocksize,
-                                      quant_type=self.config.quant_type)
-        packed = packed.view(-1)
-        absmax = state.absmax.view(-1)
-        self._packed_total = packed.numel()
-        self._absmax_total = absmax.numel()
+        """Quantise only the 64-value blocks that cover this rank's bytes.
+
+        The plans depend only on the tensor's size, so this rank's packed-byte and
+        absmax ranges are known before quantising; NF4 blocks are independent, so
+        quantising the covering blocks gives exactly the bytes a full quantisation
+        would.  The reference quantises the whole tensor on every rank and slices
+        (``src/coordinator.py:166-212``); here no rank materialises more than its
+        own range (plus one block at each end) in fp16 or NF4."""
+        bs = int(self.config.blocksize)
+        flat = weight.detach().reshape(-1)
+        n = flat.numel()
+        self._packed_total = (n + 1) // 2
+        self._absmax_total = (n + bs - 1) // bs
         self.packed_plan, self.absmax_plan = self._make_plans(self._packed_total,
                                                               self._absmax_total)
         p0, p1 = self.packed_plan.range_of(self.rank)
         a0, a1 = self.absmax_plan.range_of(self.rank)
+        # blocks [b0, b1) cover elements [2 p0, 2 p1) and absmax entries [a0, a1)
+        b0 = min((2 * p0) // bs, a0) if p1 > p0 or a1 > a0 else 0
+        b1 = max((2 * p1 + bs - 1) // bs, a1)
+        e0, e1 = b0 * bs, min(n, b1 * bs)
+        # The reference quantises fp16-cast weights (src/coordinator.py:166-168);
+        # casting first keeps the stored bytes identical.
+        w = flat[e0:e1].to(device=device, dtype=torch.float16)
+        if e1 > e0:
+            packed, state = quantize_4bit(w, blocksize=bs, quant_type=self.config.quant_type)
+            packed, absmax = packed.view(-1), state.absmax.view(-1)
+        else:
+            packed = torch.empty(0, dtype=torch.uint8, device=device)
+            absmax = torch.empty(0, dtype=torch.float32, device=device)
         self.local_packed = comm.alloc_shard(p1 - p0, torch.uint8, device, self)
-        self.local_packed.copy_(packed[p0:p1])
+        self.local_packed.copy_(packed[p0 - e0 // 2:p1 - e0 // 2])
         self.local_absmax = comm.alloc_shard(a1 - a0, torch.float32, device, self)
-        self.local_absmax.copy_(absmax[a0:a1])
+        self.local_absmax.copy_(absmax[a0 - b0:a1 - b0])
         self._quant_meta = {
-            "shape": tuple(state.shape), "dtype": state.dtype,
-            "blocksize": state.blocksize, "quant_type": state.quant_type,
+            "shape": tuple(weight.shape), "dtype": torch.float16,
+            "blocksize": bs, "quant_type": self.config.quant_type,
         }
 
     def partition_from_full_precision(self, weight: torch.Tensor):

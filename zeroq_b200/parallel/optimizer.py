@@ -19,7 +19,12 @@ then steps torch's AdamW), restructured ZeRO-style:
   peer-memory kernel of ``zeroq_b200.parallel.peer`` (it sums the peers' slices
   over NVLink and applies AdamW in the same pass).
 
-Optional global-norm gradient clipping scales the gradient inside the kernel.
+Optional global-norm gradient clipping (``max_grad_norm``, as
+``torch.nn.utils.clip_grad_norm_`` in the reference's trainer) is computed on
+the device: the squared norm of the averaged gradient is summed (over NVLink for
+the fused backend, then one scalar all-reduce) and the update kernels read it
+and scale by ``min(1, max_norm / norm)`` themselves - no host synchronisation,
+so clipped steps also run as CUDA graph replays.
 """
 
 from __future__ import annotations
@@ -31,6 +36,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops.optim import adamw_step
+from ..utils.metrics import count, nvtx_range
 
 
 class FlatParams:
@@ -124,6 +130,7 @@ class ShardedAdamW:
         if backend == "fused" and self._peer is None:
             self.backend = "nccl"
         self.last_grad_norm: Optional[torch.Tensor] = None
+        self._sq = torch.zeros(1, dtype=torch.float32, device=dev)
         self.device_clock = None   # (clk int64 [step, epoch], bc fp32 [2]) once enabled
 
     def use_device_clock(self):
@@ -152,16 +159,32 @@ class ShardedAdamW:
     def zero_grad(self, set_to_none: bool = False):
         self.flat.zero_grad()
 
-    def _clip_scale(self, g: torch.Tensor, already_averaged_scale: float) -> float:
+    def _clip_sq(self, g: Optional[torch.Tensor] = None, scale: float = 1.0) -> Optional[torch.Tensor]:
+        """Squared global norm of the averaged gradient on the device (None without
+        clipping): the kernels scale by ``min(1, max_norm / norm)`` themselves, so
+        clipping costs no host synchronisation (and runs inside CUDA graphs).
+        ``g``: this rank's part of the averaged gradient times ``1/scale``."""
         if self.max_grad_norm is None:
-            return 1.0
-        sq = (g.float() * already_averaged_scale).pow(2).sum()
-        if self.world > 1:
+            return None
+        if g is not None:
+            sq = (g.float() * scale).pow(2).sum().reshape(1)
+            if self.world > 1:
+                dist.all_reduce(sq, group=self.pg)
+        else:  # fused backend: the shard is summed over NVLink by rs_sumsq
+            sq = self._sq
+            sq.zero_()
+            lo = self.rank * self.shard
+            self._peer.sumsq(self, lo, sq)
             dist.all_reduce(sq, group=self.pg)
-        norm = sq.sqrt()
-        self.last_grad_norm = norm
-        # device-side factor would avoid this sync; clipping is off on the bench path
-        return float(torch.clamp(self.max_grad_norm / (norm + 1e-6), max=1.0))
+        self.last_grad_norm = sq  # squared; see grad_norm()
+        return sq
+
+    def grad_norm(self) -> Optional[float]:
+        """Global L2 norm of the last clipped gradient (host read; call outside the
+        hot loop)."""
+        if self.last_grad_norm is None:
+            return None
+        return float(self.last_grad_norm.sqrt().item())
 
     @torch.no_grad()
     def step(self):
@@ -173,31 +196,33 @@ class ShardedAdamW:
         b1, b2 = self.betas
         bc_dev = None
         if self.device_clock is not None:
-            if self.max_grad_norm is not None:
-                raise NotImplementedError("gradient clipping syncs with the host; not with the device clock")
             self._tick()
             bc_dev = self.device_clock[1]
         if self.world == 1:
-            scale = self._clip_scale(self.flat.grad, 1.0)
+            sq = self._clip_sq(self.flat.grad)
             adamw_step(self.flat.data, self.flat.grad, self.exp_avg, self.exp_avg_sq, lr=self.lr,
                        beta1=b1, beta2=b2, eps=self.eps, weight_decay=self.wd,
-                       step=self.step_count, grad_scale=scale, bc_dev=bc_dev)
+                       step=self.step_count, bc_dev=bc_dev, clip_sq=sq,
+                       max_norm=self.max_grad_norm or 0.0)
             return
         lo = self.rank * self.shard
         mine = self.flat.data[lo:lo + self.shard]
+        count("sync_bytes", 4 * self.flat.padded)
         if self.backend == "fused":
-            if self.max_grad_norm is not None:
-                raise NotImplementedError("gradient clipping runs on the nccl backend")
-            # one kernel: peers' gradient slices summed over NVLink, AdamW, and the
-            # updated shard written into every peer's parameter buffer
-            self._peer.reduce_scatter_adamw(self, mine)
+            with nvtx_range("grad_sync_fused"):
+                # one kernel: peers' gradient slices summed over NVLink, AdamW, and the
+                # updated shard written into every peer's parameter buffer (with
+                # clipping, a sum-of-squares pass over the same slices comes first)
+                sq = self._clip_sq()
+                self._peer.reduce_scatter_adamw(self, mine, clip_sq=sq)
             return
         dist.reduce_scatter_tensor(self.grad_shard, self.flat.grad, op=dist.ReduceOp.SUM,
                                    group=self.pg)
-        scale = self._clip_scale(self.grad_shard, 1.0 / self.world) / self.world
+        sq = self._clip_sq(self.grad_shard, 1.0 / self.world)
         adamw_step(mine, self.grad_shard, self.exp_avg, self.exp_avg_sq, lr=self.lr,
                    beta1=b1, beta2=b2, eps=self.eps, weight_decay=self.wd,
-                   step=self.step_count, grad_scale=scale, bc_dev=bc_dev)
+                   step=self.step_count, grad_scale=1.0 / self.world, bc_dev=bc_dev, clip_sq=sq,
+                   max_norm=self.max_grad_norm or 0.0)
         # NCCL gathers in place when the input is this rank's slice of the output;
         # other backends get a private copy of the shard.
         src = mine if self.flat.data.is_cuda else mine.clone()

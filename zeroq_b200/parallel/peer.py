@@ -120,31 +120,51 @@ class PeerReduceScatterAdamW:
 
     def run(self, lo: int, n: int, m: torch.Tensor, v: torch.Tensor, *, lr, beta1, beta2, eps,
             weight_decay, step, grad_scale, push: bool = True, timeout_ms: int = 0,
-            clock=None):
+            clock=None, clip_sq: Optional[torch.Tensor] = None, max_norm: float = 0.0):
         """``clock = (clk, bc)``: take the barrier epoch and the bias corrections from
         the device-side optimizer clock (see :meth:`ShardedAdamW.use_device_clock`)
-        instead of launch arguments."""
+        instead of launch arguments.  ``clip_sq``: squared global gradient norm on
+        the device (:meth:`sumsq` + all-reduce); the kernel clips to ``max_norm``.
+        A clipped step runs two peer kernels, on epochs ``2e`` and ``2e + 1`` of the
+        device clock."""
         bc1 = 1.0 - beta1 ** step
         bc2 = 1.0 - beta2 ** step
+        mul, add = (2, 1) if clip_sq is not None else (1, 0)
         if clock is not None:
             _ext.ext().rs_adamw_dev(self.grad_buf.ptrs, self.param_buf.ptrs, self.flags.ptrs,
                                     self.flags.rank, 0, int(lo), int(n), m, v,
                                     1 if self.grad_is_bf16 else 0, float(lr), float(beta1),
                                     float(beta2), float(eps), float(weight_decay), 1.0, 1.0,
-                                    float(grad_scale), bool(push), int(timeout_ms), clock[0], clock[1])
+                                    float(grad_scale), bool(push), int(timeout_ms), clock[0], clock[1],
+                                    clip_sq, float(max_norm), mul, add)
             return
-        _ext.ext().rs_adamw(self.grad_buf.ptrs, self.param_buf.ptrs, self.flags.ptrs,
-                            self.flags.rank, self.flags.next_epoch(), int(lo), int(n), m, v,
-                            1 if self.grad_is_bf16 else 0, float(lr), float(beta1), float(beta2),
-                            float(eps), float(weight_decay), float(bc1), float(bc2),
-                            float(grad_scale), bool(push), int(timeout_ms))
+        _ext.ext().rs_adamw_dev(self.grad_buf.ptrs, self.param_buf.ptrs, self.flags.ptrs,
+                                self.flags.rank, self.flags.next_epoch(), int(lo), int(n), m, v,
+                                1 if self.grad_is_bf16 else 0, float(lr), float(beta1), float(beta2),
+                                float(eps), float(weight_decay), float(bc1), float(bc2),
+                                float(grad_scale), bool(push), int(timeout_ms), None, None,
+                                clip_sq, float(max_norm))
 
-    def reduce_scatter_adamw(self, opt, mine: torch.Tensor):
+    def sumsq(self, opt, lo: int, sq: torch.Tensor, timeout_ms: int = 0):
+        """``sq += ‖shard of the averaged gradient‖²`` for this rank's shard, read from
+        every rank's gradient over NVLink (the first of a clipped step's two kernels)."""
+        clock = opt.device_clock
+        if clock is not None:
+            _ext.ext().rs_sumsq(self.grad_buf.ptrs, self.flags.ptrs, self.flags.rank, 0, int(lo),
+                                int(opt.shard), sq, 1 if self.grad_is_bf16 else 0, 1.0 / opt.world,
+                                int(timeout_ms), clock[0], 2, 0)
+            return
+        _ext.ext().rs_sumsq(self.grad_buf.ptrs, self.flags.ptrs, self.flags.rank,
+                            self.flags.next_epoch(), int(lo), int(opt.shard), sq,
+                            1 if self.grad_is_bf16 else 0, 1.0 / opt.world, int(timeout_ms))
+
+    def reduce_scatter_adamw(self, opt, mine: torch.Tensor, clip_sq: Optional[torch.Tensor] = None):
         b1, b2 = opt.betas
         lo = opt.rank * opt.shard
         self.run(lo, opt.shard, opt.exp_avg, opt.exp_avg_sq, lr=opt.lr, beta1=b1, beta2=b2,
                  eps=opt.eps, weight_decay=opt.wd, step=opt.step_count,
-                 grad_scale=1.0 / opt.world, push=True, clock=opt.device_clock)
+                 grad_scale=1.0 / opt.world, push=True, clock=opt.device_clock,
+                 clip_sq=clip_sq, max_norm=opt.max_grad_norm or 0.0)
 
 
 def peer_flat_allocator(group):
@@ -277,6 +297,10 @@ class PeerShardPool:
         from .comm import GatherHandle
 
         E = _ext.ext()
+        from ..utils.metrics import count
+        from .comm import remote_nf4_bytes
+
+        count("gather_bytes", remote_nf4_bytes(zq))
         packed = torch.empty(zq.packed_plan.total, dtype=torch.uint8, device=zq.local_packed.device)
         absmax = torch.empty(zq.absmax_plan.total, dtype=torch.float32, device=zq.local_packed.device)
         for which, out in ((0, packed), (1, absmax)):
@@ -291,6 +315,10 @@ class PeerShardPool:
         gather and the dequantisation are one kernel."""
         from ..ops.nf4 import QUANT_TYPE_ID
 
+        from ..utils.metrics import count
+        from .comm import remote_nf4_bytes
+
+        count("gather_bytes", remote_nf4_bytes(zq) * rows // max(1, zq.original_shape[0]))
         psrc, _, _ = self._segments(zq, 0)
         asrc, _, _ = self._segments(zq, 1)
         if out is None:
@@ -306,6 +334,10 @@ class PeerShardPool:
                 wbuf: Optional[torch.Tensor] = None, extra: Optional[tuple] = None):
         """``x Wᵀ`` with ``W`` read from the owners' NF4 shards inside the GEMM
         kernel (:func:`ag_gemm_pieces`); returns ``(y, wbuf)``."""
+        from ..utils.metrics import count
+        from .comm import remote_nf4_bytes
+
+        count("gather_bytes", remote_nf4_bytes(zq))
         psrc, _, _ = self._segments(zq, 0)
         asrc, _, _ = self._segments(zq, 1)
         N, K = zq.original_shape

@@ -7,6 +7,10 @@ optimizer (reduce-scatter + AdamW across ranks), and returns the loss as a
 Python float (one device -> host read).  ``step_device`` is the same step with
 device-resident inputs and the loss left on the device.
 
+``Trainer(..., logger=StepLogger(path))`` (``zeroq_b200.utils.metrics``) writes one
+JSON line per step on rank 0: loss, device-timed milliseconds and tokens/s (max
+over ranks), bytes gathered and synced, model-FLOP fraction of a peak.
+
 The reference's production trainer adds all-ranks-agree checks before each
 collective so a non-finite loss on one rank cannot desynchronise the others
 (``examples/train_32b_maxwell.py:522-547``); :meth:`Trainer.all_ranks_finite`
@@ -29,8 +33,9 @@ import torch.distributed as dist
 
 class Trainer:
     def __init__(self, model: torch.nn.Module, optimizer, device: torch.device,
-                 process_group=None):
+                 process_group=None, logger=None):
         self.model = model
+        self.logger = logger
         self.opt = optimizer
         self.device = device
         self.pg = process_group
@@ -38,6 +43,7 @@ class Trainer:
         self._tg = None
         self._graph_on = False
         self._graph = None
+        self._graph_bytes = {}
         self.graph_launches = 0   # this framework's kernels in one captured step
 
     def enable_cuda_graph(self):
@@ -70,10 +76,16 @@ class Trainer:
             loss = self._eager(self._gin, self._gtg)   # this call's step
         torch.cuda.current_stream(self.device).wait_stream(stream)
         torch.cuda.synchronize(self.device)
+        from .utils.metrics import snapshot
+
         graph = torch.cuda.CUDAGraph()
+        before = snapshot()
         with LaunchCounter() as lc:
             with torch.cuda.graph(graph, stream=stream):
                 self._gloss = self._eager(self._gin, self._gtg)
+        after = snapshot()
+        self._graph_bytes = {k: after[k] - before.get(k, 0) for k in after
+                             if after[k] != before.get(k, 0)}
         self.graph_launches = lc.count
         self._graph = graph
         return loss
@@ -85,14 +97,30 @@ class Trainer:
         return self._in, self._tg
 
     def step_device(self, input_ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        if self.logger is None:
+            return self._step_device(input_ids, targets)
+        self.logger.begin()
+        loss = self._step_device(input_ids, targets)
+        self.logger.end(loss, input_ids.numel())
+        return loss
+
+    def _step_device(self, input_ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        from .utils.metrics import nvtx_range
+
         if not self._graph_on:
-            return self._eager(input_ids, targets)
+            with nvtx_range("train_step"):
+                return self._eager(input_ids, targets)
         if self._graph is None:
             return self._capture(input_ids, targets)
         if input_ids.data_ptr() != self._gin.data_ptr():
             self._gin.copy_(input_ids, non_blocking=True)
             self._gtg.copy_(targets, non_blocking=True)
         self._graph.replay()
+        if self._graph_bytes:   # a replay moves what the captured step moved
+            from .utils.metrics import count
+
+            for k, v in self._graph_bytes.items():
+                count(k, v)
         return self._gloss
 
     def step(self, input_ids_host: torch.Tensor, targets_host: torch.Tensor) -> float:
