@@ -58,9 +58,9 @@ CONFIGS = {
              "projection + RMSNorm weights, AdamW"),
     "qwen7b-hetero": ("qwen2.5-7b", 16, ("q_proj", "k_proj", "v_proj", "o_proj"), 4, 2048,
                       "hetero",
-                      "Qwen2.5-7B shape, frozen NF4 base sharded by rank weights "
-                      "[2,2,1,1,1,1,1,1] and gathered per use (peer plan gather), LoRA r=16 "
-                      "alpha 32 on q/k/v/o, AdamW"),
+                      "Qwen2.5-7B shape, frozen NF4 base sharded by uneven rank weights "
+                      "(rank_weights: [2,2,1,1,1,1,1,1] at 8 ranks) and gathered per use "
+                      "(peer plan gather), LoRA r=16 alpha 32 on q/k/v/o, AdamW"),
     "qwen32b-gather": ("qwen2.5-32b", 64, ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj",
                                           "up_proj", "down_proj"), 2, 4096, "gather",
                        "Qwen2.5-32B shape, NF4 shards gathered per layer with one layer of "
@@ -197,13 +197,16 @@ def main():
             trainer.logger.flush()
             trainer.logger = None
 
-    if args.torch_profile and rank == 0:
+    if args.torch_profile:
+        # every rank runs the profiled step (its collectives need all ranks); rank r
+        # writes its table to PATH (rank 0) or PATH.rank<r>
         from torch.profiler import ProfilerActivity, profile
 
         with profile(activities=[ProfilerActivity.CUDA]) as prof:
             trainer.step_device(x_dev, y_dev)
             torch.cuda.synchronize()
-        with open(args.torch_profile, "w") as f:
+        path = args.torch_profile if rank == 0 else f"{args.torch_profile}.rank{rank}"
+        with open(path, "w") as f:
             f.write(prof.key_averages().table(sort_by="cuda_time_total", row_limit=60,
                                               max_name_column_width=90))
 

@@ -155,6 +155,16 @@ def w_reduce_scatter(rank, world):
 
 def w_sharded_adamw(rank, world):
     import zeroq_b200 as zq
+    import torch.distributed as dist
+
+    # replicas initialised from different random states start from rank 0's values
+    torch.manual_seed(100 + rank)
+    own = [torch.nn.Parameter(torch.randn(6, 4)), torch.nn.Parameter(torch.randn(3))]
+    zq.ShardedAdamW(own, lr=1e-2)
+    for p in own:
+        ref = p.detach().clone()
+        dist.broadcast(ref, src=0)
+        assert torch.equal(p.detach(), ref)
 
     for clip in (None, 0.5):  # with clipping: the averaged gradient's global norm
         torch.manual_seed(0)

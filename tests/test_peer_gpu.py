@@ -352,13 +352,16 @@ def w_step_equals_single_process(rank, world):
     ref(x, y).backward()
     ropt.step()
     refp = dict(ref.named_parameters())
-    worst = 0.0
+    rows = []
     for n_ in names:
         d_run = after[n_] - before[n_]
         d_ref = refp[n_].detach() - before[n_]
-        scale = d_ref.abs().max().item() + 1e-12
-        worst = max(worst, (d_run - d_ref).abs().max().item() / scale)
-    assert worst < 5e-2, worst  # bf16 activations, different reduction orders
+        rows.append((n_, d_ref.abs().max().item(), d_run.abs().max().item(),
+                     (d_run - d_ref).abs().max().item()))
+    scale = max(r[1] for r in rows)
+    bad = [r for r in rows if r[3] > 5e-2 * max(r[1], 1e-3 * scale)]
+    # bf16 activations and different reduction orders: a few percent
+    assert not bad, "\n".join(f"{r[0]}: ref {r[1]:.3e} run {r[2]:.3e} diff {r[3]:.3e}" for r in bad)
 
 
 @pytest.mark.parametrize("world", WORLDS)

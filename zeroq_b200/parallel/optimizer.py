@@ -96,7 +96,12 @@ class ShardedAdamW:
 
     def __init__(self, params, lr: float = 1e-4, betas=(0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 0.0, process_group: Optional[dist.ProcessGroup] = None,
-                 backend: str = "auto", max_grad_norm: Optional[float] = None):
+                 backend: str = "auto", max_grad_norm: Optional[float] = None,
+                 broadcast_initial: bool = True):
+        """``broadcast_initial``: start every rank from rank 0's parameters (one
+        broadcast of the flat buffer), as data-parallel training requires - layers
+        initialise adapters from each process's own random state (LoRA ``A``), and
+        the sharded update only keeps replicas equal if they start equal."""
         self.pg = process_group
         self.world = dist.get_world_size(process_group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(process_group) if dist.is_initialized() else 0
@@ -116,6 +121,10 @@ class ShardedAdamW:
                 backend = "nccl"
         # pad so that every rank's shard is a whole number of 16-byte vectors
         self.flat = FlatParams(params, pad_to=self.world * 4, alloc=alloc)
+        if broadcast_initial and self.world > 1:
+            src = dist.get_global_rank(process_group, 0) if process_group is not None else 0
+            dist.broadcast(self.flat.data, src=src, group=process_group)
+            self.flat.mark_updated()
         self.lr, self.betas, self.eps, self.wd = lr, betas, eps, weight_decay
         self.max_grad_norm = max_grad_norm
         self.shard = self.flat.padded // self.world
