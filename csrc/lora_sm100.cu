@@ -35,7 +35,7 @@
 //
 // All mbarrier waits are bounded (common.cuh); a timeout records an error code
 // in the device status word read by gemm_status(), the kernel drains its copies
-// in flight, frees TMEM and returns.  No load uses cluster multicast.
+// in flight, frees TMEM and returns.  Every TMA load targets this CTA only.
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
