@@ -103,6 +103,9 @@ def main():
     ap.add_argument("--bhsd", action="store_true", help="attn_trace: K/V as [B, H, S, D]")
     ap.add_argument("--reps", type=int, default=5)
     ap.add_argument("--r", type=int, default=16, help="lora: adapter rank (packed width)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="lora: time every launch shape (cluster size / splits, ring depth, "
+                         "K boxes per stage) of the three kernels, read-only L2 flush")
     ap.add_argument("--world", type=int, default=4, help="ag_gemm: emulated ranks (pieces)")
     ap.add_argument("--profile", action="store_true", help="print one call's kernels (torch profiler)")
     a = ap.parse_args()
@@ -359,6 +362,43 @@ def main():
         if L.vdb(gy, bt, ut, 64, [(0, N, 0)], [gB], r16, r) is not None:
             ms = _time(lambda: L.vdb(gy, bt, ut, 64, [(0, N, 0)], [gB], r16, r), a.reps)
             _report(f"lora_vdb V and dB {M}x{N} r={r}", ms, byts=M * N * 2 + M * (64 + 2 * r16) * 2)
+        if a.sweep:
+            flush = torch.ones(64 << 20, device=dev)  # 256 MB read between launches
+
+            def tro(fn, reps=10):
+                fn()
+                torch.cuda.synchronize()
+                tot = 0.0
+                for _ in range(reps):
+                    flush.sum()
+                    s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    s0.record()
+                    fn()
+                    e0.record()
+                    torch.cuda.synchronize()
+                    tot += s0.elapsed_time(e0)
+                return tot / reps
+
+            import itertools
+
+            ut2 = torch.empty(r16, M, device=dev, dtype=torch.bfloat16)
+            u2 = torch.empty(M, 64, device=dev, dtype=torch.bfloat16)
+            for cs, st, kb in itertools.product((1, 2, 4, 8), (4, 6), (1, 2)):
+                _report(f"sweep lora_down {M}x{K} cs={cs} stages={st} kb={kb}",
+                        tro(lambda: E.lora_down(x, sa, u2, ut2, cs, st, kb)), byts=M * K * 2)
+            for sp, st, kb in itertools.product((0, 6, 13, 26), (4, 6), (1, 2)):
+                _report(f"sweep lora_wgrad dA {M}x{K} splits={sp} stages={st} kb={kb}",
+                        tro(lambda: E.lora_wgrad(x, vt, r16, [0], [K], [0], [1.0], [gA], r16, r,
+                                                 True, sp, st, kb)), byts=M * K * 2)
+            for cs, st in itertools.product((1, 2, 4, 8), (4, 6)):
+                v2 = torch.empty(M, 64, device=dev, dtype=torch.bfloat16)
+                vt2 = torch.empty(r16, M, device=dev, dtype=torch.bfloat16)
+                if E.lora_vdb(gy, bt, ut, v2, vt2, r16, [0], [N], [0], [gB], r, cs, st):
+                    _report(f"sweep lora_vdb {M}x{N} cs={cs} stages={st}",
+                            tro(lambda: E.lora_vdb(gy, bt, ut, v2, vt2, r16, [0], [N], [0], [gB], r,
+                                                   cs, st)), byts=M * N * 2)
+                else:
+                    print(f"sweep lora_vdb {M}x{N} cs={cs} stages={st}: declined (TMEM)")
         if a.cublas:
             ap_, bp_ = torch.zeros(64, K, device=dev, dtype=torch.bfloat16), torch.zeros(
                 N, 64, device=dev, dtype=torch.bfloat16)

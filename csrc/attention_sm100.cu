@@ -47,6 +47,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 
 // defined in gemm_sm100.cu
@@ -1018,6 +1020,269 @@ attn_bwd_dkv_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_con
   if (warp == 8) { tc_fence_after(); tmem_dealloc(tmem, 512); }
 }
 
+// ============================================================================
+// dK/dV backward with 64-query iterations and double-buffered Sᵀ / dPᵀ.
+//
+// Per key tile (one CTA), iterating over (query head, 64-query tile):
+//   Sᵀ_t  = K Q_tᵀ,  dPᵀ_t = V dO_tᵀ       M = 128 keys, N = 64 queries (SS MMAs)
+//   Pᵀ_t  = exp2(Sᵀ·scale·log2e - lse2),  dSᵀ_t = Pᵀ ⊙ (dPᵀ - delta)   (compute warps)
+//   dV   += Pᵀ_t dO_t,  dK += dSᵀ_t Q_t     A = Pᵀ / dSᵀ from TMEM, B MN-major
+// Tensor memory: dV 0-127, dK 128-255, buffer b (= t & 1): Sᵀ at 256 + 128 b
+// (64 columns, then Pᵀ packed in its first 32) and dPᵀ at 320 + 128 b.
+// The MMA thread issues Sᵀ/dPᵀ of iteration t + 1 before it waits for the
+// compute warps' Pᵀ/dSᵀ of iteration t, so the score MMAs of the next tile run
+// while the exponentials of this one are computed; buffer b is rewritten only
+// by MMAs issued after the dV/dK MMAs that read it (tcgen05 MMAs of one CTA
+// execute in issue order).  Q and dO stream through 4-stage rings of 64-query
+// tiles (16 KB each), each dO stage with its 64 lse2 / delta values.
+// ============================================================================
+constexpr int kBwd64Q = 64;
+constexpr int kBwd64Stages = 4;
+
+struct BwdDkv64Smem {
+  static constexpr int kTile = AttSmem::kTile, kAtom = AttSmem::kAtom;  // 128-key K / V tiles
+  static constexpr int kQTile = kBwd64Q * kAttD * 2;                  // 16 KB
+  static constexpr int kQAtom = kQTile / 2;                            // 64 rows x 64 D, 8 KB
+  static constexpr int kK = 0, kV = kTile;
+  static constexpr int kQ = 2 * kTile;
+  static constexpr int kDO = kQ + kBwd64Stages * kQTile;
+  static constexpr int kLD = kDO + kBwd64Stages * kQTile;              // per stage: lse2[64], delta[64]
+  static constexpr int kBar = kLD + kBwd64Stages * 512;
+  static constexpr int kBytes = kBar + 256 + 1024;
+};
+
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
+attn_bwd_dkv64_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                         const float* __restrict__ lse2, const float* __restrict__ delta,
+                         __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv, int B, int S,
+                         int Hq, int Hk, float scale_log2, float scale, int causal,
+                         const float2* __restrict__ rope_cs, DeviceStatus* status, int64_t ld_dk,
+                         int64_t ld_dv) {
+  // tmQ / tmDO: 4-D maps with a box of 64 D x 1 head x 64 rows x 1 batch
+  using L = BwdDkv64Smem;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* kv_full = bars;                          // K and V landed
+  uint64_t* q_full = bars + 1;                       // [kBwd64Stages]
+  uint64_t* q_empty = q_full + kBwd64Stages;
+  uint64_t* o_full = q_empty + kBwd64Stages;         // dO + lse2/delta
+  uint64_t* o_empty = o_full + kBwd64Stages;
+  uint64_t* s_full = o_empty + kBwd64Stages;         // [2] Sᵀ / dPᵀ of buffer b
+  uint64_t* p_full = s_full + 2;                     // [2] Pᵀ / dSᵀ written (8 arrivals)
+  uint64_t* acc_done = p_full + 2;
+  uint64_t* drain = acc_done + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nkt = S / kAttKeys, nq64 = S / kBwd64Q;
+  const int bhk = (int)(blockIdx.x / (unsigned)nkt);
+  const int kt = (int)(blockIdx.x % (unsigned)nkt);
+  const int b = bhk / Hk, hk = bhk % Hk;
+  const int group = Hq / Hk;
+  const int i0 = causal ? 2 * kt : 0;        // first 64-query tile that sees this key tile
+  const int per_head = nq64 - i0;
+  const int n_it = group * per_head;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < kBwd64Stages; ++i) {
+      mbar_init(&q_full[i], 1); mbar_init(&q_empty[i], 1);
+      mbar_init(&o_full[i], 1); mbar_init(&o_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], kSoftmaxWarps);
+    }
+    mbar_init(acc_done, 1);
+    mbar_init(drain, 1);
+    fence_mbar_init();
+    prefetch_tmap(&tmQ); prefetch_tmap(&tmK); prefetch_tmap(&tmV); prefetch_tmap(&tmDO);
+  }
+  if (warp == 8) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp >= 9) {
+    // ------------------------------------------------------------ TMA loaders
+    if (lane == 0) {
+      const bool is_q = warp == 9;
+      if (is_q) {
+        mbar_arrive_expect_tx(kv_full, 2 * L::kTile);
+        tma_load_4d(smem + L::kK, &tmK, kv_full, 0, hk, kt * kAttKeys, b);
+        tma_load_4d(smem + L::kK + L::kAtom, &tmK, kv_full, 64, hk, kt * kAttKeys, b);
+        tma_load_4d(smem + L::kV, &tmV, kv_full, 0, hk, kt * kAttKeys, b);
+        tma_load_4d(smem + L::kV + L::kAtom, &tmV, kv_full, 64, hk, kt * kAttKeys, b);
+      }
+      const CUtensorMap* map = is_q ? &tmQ : &tmDO;
+      uint64_t* empty = is_q ? q_empty : o_empty;
+      uint64_t* full = is_q ? q_full : o_full;
+      uint8_t* ring = smem + (is_q ? L::kQ : L::kDO);
+      int issued = 0;
+      bool ok = true;
+      for (int t = 0; t < n_it; ++t) {
+        const int st = t % kBwd64Stages;
+        const int h = hk * group + t / per_head, it = i0 + t % per_head;
+        if (!mbar_wait(&empty[st], ((t / kBwd64Stages) & 1) ^ 1, status, kErrBwdLoad)) { ok = false; break; }
+        uint8_t* dst = ring + st * L::kQTile;
+        mbar_arrive_expect_tx(&full[st], L::kQTile + (is_q ? 0 : 512));
+        tma_load_4d(dst, map, &full[st], 0, h, it * kBwd64Q, b);
+        tma_load_4d(dst + L::kQAtom, map, &full[st], 64, h, it * kBwd64Q, b);
+        if (!is_q) {  // this query tile's lse2 and delta (256 B each)
+          const int64_t li = ((int64_t)b * Hq + h) * S + it * kBwd64Q;
+          bulk_load(smem + L::kLD + st * 512, lse2 + li, 256, &full[st]);
+          bulk_load(smem + L::kLD + st * 512 + 256, delta + li, 256, &full[st]);
+        }
+        issued = t + 1;
+      }
+      if (!ok) {  // let every copy this thread issued land before the CTA can exit
+        if (is_q) mbar_wait(kv_full, 0, nullptr, 0);
+        for (int t = (issued > kBwd64Stages ? issued - kBwd64Stages : 0); t < issued; ++t)
+          mbar_wait(&full[t % kBwd64Stages], (t / kBwd64Stages) & 1, nullptr, 0);
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_k = umma_idesc_bf16(kAttKeys, kBwd64Q);     // Sᵀ, dPᵀ
+      constexpr uint32_t idesc_mn = umma_idesc_bf16_bmn(kAttKeys, kAttD);  // dV, dK
+      const uint32_t k_addr = smem_u32(smem + L::kK), v_addr = smem_u32(smem + L::kV);
+      bool ok = mbar_wait(kv_full, 0, status, kErrBwdMma);
+      // Sᵀ_t and dPᵀ_t into buffer t & 1
+      auto issue_scores = [&](int t) -> bool {
+        const int st = t % kBwd64Stages;
+        const uint32_t ph = (t / kBwd64Stages) & 1;
+        if (!mbar_wait(&q_full[st], ph, status, kErrBwdMma)) return false;
+        if (!mbar_wait(&o_full[st], ph, status, kErrBwdMma)) return false;
+        tc_fence_after();
+        const uint32_t q_addr = smem_u32(smem + L::kQ + st * L::kQTile);
+        const uint32_t o_addr = smem_u32(smem + L::kDO + st * L::kQTile);
+        const uint32_t sc = 256u + 128u * (uint32_t)(t & 1);
+#pragma unroll
+        for (int kk = 0; kk < kAttD / 16; ++kk) {
+          const uint32_t ka = (uint32_t)((kk >> 2) * L::kAtom + (kk & 3) * 32);
+          const uint32_t qa = (uint32_t)((kk >> 2) * L::kQAtom + (kk & 3) * 32);
+          umma_f16_ss(tmem + sc, umma_desc_sw128_kmajor(k_addr + ka), umma_desc_sw128_kmajor(q_addr + qa),
+                      idesc_k, kk > 0 ? 1u : 0u);
+          umma_f16_ss(tmem + sc + 64u, umma_desc_sw128_kmajor(v_addr + ka),
+                      umma_desc_sw128_kmajor(o_addr + qa), idesc_k, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[t & 1]);
+        return true;
+      };
+      if (ok && n_it > 0) ok = issue_scores(0);
+      for (int t = 0; t < n_it && ok; ++t) {
+        if (t + 1 < n_it && !issue_scores(t + 1)) { ok = false; break; }
+        if (!mbar_wait(&p_full[t & 1], (t >> 1) & 1, status, kErrBwdMma)) { ok = false; break; }
+        tc_fence_after();
+        const int st = t % kBwd64Stages;
+        const uint32_t q_addr = smem_u32(smem + L::kQ + st * L::kQTile);
+        const uint32_t o_addr = smem_u32(smem + L::kDO + st * L::kQTile);
+        const uint32_t sc = 256u + 128u * (uint32_t)(t & 1);
+#pragma unroll
+        for (int kk = 0; kk < kBwd64Q / 16; ++kk) {   // dV += Pᵀ dO and dK += dSᵀ Q, interleaved
+          umma_f16_ts(tmem, tmem + sc + (uint32_t)(kk * 8),
+                      umma_desc_sw128_mnmajor(o_addr + (uint32_t)kk * 2048u, (uint32_t)L::kQAtom), idesc_mn,
+                      (t > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ts(tmem + 128u, tmem + sc + 64u + (uint32_t)(kk * 8),
+                      umma_desc_sw128_mnmajor(q_addr + (uint32_t)kk * 2048u, (uint32_t)L::kQAtom), idesc_mn,
+                      (t > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(&q_empty[st]);
+        umma_commit(&o_empty[st]);
+      }
+      umma_commit(acc_done);
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ Pᵀ, dSᵀ + epilogue
+    const int quad = warp & 3, half = warp >> 2;
+    const int row = quad * 32 + lane;                     // key row = TMEM lane
+    const int col0 = half * 32;                           // this half's 32 query columns
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    const int pair_bar = 1 + quad;
+    const int key = kt * kAttKeys + row;
+    bool ok = true;
+    for (int t = 0; t < n_it && ok; ++t) {
+      const int st = t % kBwd64Stages;
+      const int it = i0 + t % per_head;
+      const uint32_t sc = 256u + 128u * (uint32_t)(t & 1);
+      const float* sl = reinterpret_cast<const float*>(smem + L::kLD + st * 512) + col0;
+      // o_full also covers the staged lse2/delta (the bulk copies completed on it)
+      const bool got = mbar_wait(&s_full[t & 1], (t >> 1) & 1, status, kErrBwdCompute) &&
+                       mbar_wait(&o_full[st], (t / kBwd64Stages) & 1, status, kErrBwdCompute);
+      if (!named_barrier_and(pair_bar, 64, got)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t sv[32], dp[32];
+      tmem_ld_32x32b_x32(tmem + lane_base + sc + (uint32_t)col0, sv);
+      tmem_ld_32x32b_x32(tmem + lane_base + sc + 64u + (uint32_t)col0, dp);
+      tmem_ld_wait();
+      tc_fence_before();
+      named_barrier(pair_bar, 64);   // both halves hold their columns before either overwrites
+      tc_fence_after();
+      const bool diag = causal && it <= 2 * kt + 1;   // some key of this tile is after some query
+      const int q0 = it * kBwd64Q + col0;
+      uint32_t pp[16], dsp[16];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {   // 4 queries per step: shared-memory broadcasts
+        const float4 l4 = reinterpret_cast<const float4*>(sl)[i];
+        const float4 d4 = reinterpret_cast<const float4*>(sl + 64)[i];
+        const float lv[4] = {l4.x, l4.y, l4.z, l4.w}, dv4[4] = {d4.x, d4.y, d4.z, d4.w};
+        float p[4], ds[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int c = 4 * i + u;
+          p[u] = fast_exp2(fmaf(__uint_as_float(sv[c]), scale_log2, -lv[u]));
+          if (diag && key > q0 + c) p[u] = 0.0f;
+          ds[u] = p[u] * (__uint_as_float(dp[c]) - dv4[u]);
+        }
+        pp[2 * i] = pack_bf16x2(p[0], p[1]);
+        pp[2 * i + 1] = pack_bf16x2(p[2], p[3]);
+        dsp[2 * i] = pack_bf16x2(ds[0], ds[1]);
+        dsp[2 * i + 1] = pack_bf16x2(ds[2], ds[3]);
+      }
+      tmem_st_32x32b_x16(tmem + lane_base + sc + (uint32_t)(half * 16), pp);
+      tmem_st_32x32b_x16(tmem + lane_base + sc + 64u + (uint32_t)(half * 16), dsp);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t & 1]);
+    }
+    if (named_barrier_and(pair_bar, 64, ok)) {
+      const bool done = mbar_wait(acc_done, 0, status, kErrBwdCompute);
+      if (named_barrier_and(pair_bar, 64, done)) {
+        tc_fence_after();
+        const int ecol0 = half * 64;                      // epilogue: this half's 64 D columns
+        const int64_t tok = (int64_t)b * S + key, hoff = (int64_t)hk * kAttD + ecol0;
+#pragma unroll 1
+        for (int w = 0; w < 2; ++w) {   // w = 0: dV (scale 1), w = 1: dK (scale)
+          __nv_bfloat16* out = w == 0 ? dv + tok * ld_dv + hoff : dk + tok * ld_dk + hoff;
+          const float f = w == 0 ? 1.0f : scale;
+          bwd_store_half_row(tmem + lane_base + (uint32_t)(w * 128), ecol0, f,
+                             (w == 1 && rope_cs != nullptr) ? rope_cs + (int64_t)key * 64 : nullptr, out);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) { tc_fence_after(); tmem_dealloc(tmem, 512); }
+}
+
 }  // namespace zq
 
 using namespace zq;
@@ -1028,7 +1293,7 @@ using namespace zq;
 // With bhsd = true the tensor is [B, H, S, D] (heads outermost); the map keeps
 // the same coordinate order (D, H, S, B), only the strides differ, so the kernel
 // addresses both layouts alike.
-static CUtensorMap make_tmap_bshd(const at::Tensor& t, bool bhsd = false) {
+static CUtensorMap make_tmap_bshd(const at::Tensor& t, bool bhsd = false, int box_rows = kAttRows) {
   const int64_t B = t.size(0), S = bhsd ? t.size(2) : t.size(1), H = bhsd ? t.size(1) : t.size(2),
                 D = t.size(3);
   TORCH_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0, "attention: 16-byte aligned tensors");
@@ -1041,7 +1306,7 @@ static CUtensorMap make_tmap_bshd(const at::Tensor& t, bool bhsd = false) {
   CUtensorMap map;
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)S, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)(sH * 2), (cuuint64_t)(sS * 2), (cuuint64_t)(sB * 2)};
-  cuuint32_t box[4] = {64u, 1u, (cuuint32_t)kAttRows, 1u};
+  cuuint32_t box[4] = {64u, 1u, (cuuint32_t)box_rows, 1u};
   cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
   CUresult r = get_encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, t.data_ptr(), dims, strides,
                                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -1134,6 +1399,8 @@ void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::
                                         BwdDqSmem::kBytes));
     C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dkv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         BwdDkvSmem::kBytes));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dkv64_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        BwdDkv64Smem::kBytes));
     configured[dev] = true;
   }
   const float2* rcs = nullptr;
@@ -1171,10 +1438,26 @@ void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::
       reinterpret_cast<__nv_bfloat16*>(dq.data_ptr<at::BFloat16>()), (int)B, (int)S, (int)Hq, (int)Hk, sl2,
       (float)scale, causal ? 1 : 0, rcs, st, trp);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  attn_bwd_dkv_tc_kernel<<<(unsigned)g_dkv, kBwdThreads, BwdDkvSmem::kBytes, stream>>>(
-      tq, tk, tv, tdo, lse2.data_ptr<float>(), delta.data_ptr<float>(),
-      reinterpret_cast<__nv_bfloat16*>(dk.data_ptr<at::BFloat16>()),
-      reinterpret_cast<__nv_bfloat16*>(dv.data_ptr<at::BFloat16>()), (int)B, (int)S, (int)Hq, (int)Hk, sl2,
-      (float)scale, causal ? 1 : 0, rcs, st, trp ? trp + g_dq * 32 : nullptr, dk.stride(1), dv.stride(1));
+  // dK/dV: 64-query iterations with double-buffered scores (overlapping the score
+  // MMAs of the next tile with this tile's exponentials); ZEROQ_ATTN_DKV128=1 or a
+  // trace request selects the 128-query kernel
+  static const bool dkv128 = [] {
+    const char* e = std::getenv("ZEROQ_ATTN_DKV128");
+    return e != nullptr && e[0] == '1';
+  }();
+  if (dkv128 || trp != nullptr) {
+    attn_bwd_dkv_tc_kernel<<<(unsigned)g_dkv, kBwdThreads, BwdDkvSmem::kBytes, stream>>>(
+        tq, tk, tv, tdo, lse2.data_ptr<float>(), delta.data_ptr<float>(),
+        reinterpret_cast<__nv_bfloat16*>(dk.data_ptr<at::BFloat16>()),
+        reinterpret_cast<__nv_bfloat16*>(dv.data_ptr<at::BFloat16>()), (int)B, (int)S, (int)Hq, (int)Hk, sl2,
+        (float)scale, causal ? 1 : 0, rcs, st, trp ? trp + g_dq * 32 : nullptr, dk.stride(1), dv.stride(1));
+  } else {
+    const CUtensorMap tq64 = make_tmap_bshd(q, false, kBwd64Q), tdo64 = make_tmap_bshd(dout, false, kBwd64Q);
+    attn_bwd_dkv64_tc_kernel<<<(unsigned)g_dkv, kBwdThreads, BwdDkv64Smem::kBytes, stream>>>(
+        tq64, tk, tv, tdo64, lse2.data_ptr<float>(), delta.data_ptr<float>(),
+        reinterpret_cast<__nv_bfloat16*>(dk.data_ptr<at::BFloat16>()),
+        reinterpret_cast<__nv_bfloat16*>(dv.data_ptr<at::BFloat16>()), (int)B, (int)S, (int)Hq, (int)Hk, sl2,
+        (float)scale, causal ? 1 : 0, rcs, st, dk.stride(1), dv.stride(1));
+  }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
