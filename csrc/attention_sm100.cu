@@ -1067,8 +1067,13 @@ attn_bwd_dkv64_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_c
                          __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv, int B, int S,
                          int Hq, int Hk, float scale_log2, float scale, int causal,
                          const float2* __restrict__ rope_cs, DeviceStatus* status, int64_t ld_dk,
-                         int64_t ld_dv) {
+                         int64_t ld_dv, unsigned long long* __restrict__ trace) {
   // tmQ / tmDO: 4-D maps with a box of 64 D x 1 head x 64 rows x 1 batch
+  // trace (optional, [grid][32] ns): 0 start; iterations t = 1, 2 at 1 + 8(t-1) + i:
+  //   compute: i = 0 Sᵀ/dPᵀ seen, 1 loaded, 2 Pᵀ/dSᵀ computed, 3 arrived;
+  //   MMA: 4 Q/dO of t seen, 5 Sᵀ/dPᵀ of t issued, 6 Pᵀ/dSᵀ seen, 7 dV/dK issued;  30 end
+  unsigned long long* tr = trace ? trace + (size_t)blockIdx.x * 32 : nullptr;
+  if (tr && threadIdx.x == 0) tr[0] = globaltimer();
   using L = BwdDkv64Smem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -1162,10 +1167,12 @@ attn_bwd_dkv64_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_c
       bool ok = mbar_wait(kv_full, 0, status, kErrBwdMma);
       // Sᵀ_t and dPᵀ_t into buffer t & 1
       auto issue_scores = [&](int t) -> bool {
+        unsigned long long* tj = (tr && (t == 1 || t == 2)) ? tr + 1 + 8 * (t - 1) : nullptr;
         const int st = t % kBwd64Stages;
         const uint32_t ph = (t / kBwd64Stages) & 1;
         if (!mbar_wait(&q_full[st], ph, status, kErrBwdMma)) return false;
         if (!mbar_wait(&o_full[st], ph, status, kErrBwdMma)) return false;
+        if (tj) tj[4] = globaltimer();
         tc_fence_after();
         const uint32_t q_addr = smem_u32(smem + L::kQ + st * L::kQTile);
         const uint32_t o_addr = smem_u32(smem + L::kDO + st * L::kQTile);
@@ -1180,12 +1187,15 @@ attn_bwd_dkv64_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_c
                       umma_desc_sw128_kmajor(o_addr + qa), idesc_k, kk > 0 ? 1u : 0u);
         }
         umma_commit(&s_full[t & 1]);
+        if (tj) tj[5] = globaltimer();
         return true;
       };
       if (ok && n_it > 0) ok = issue_scores(0);
       for (int t = 0; t < n_it && ok; ++t) {
+        unsigned long long* tj = (tr && (t == 1 || t == 2)) ? tr + 1 + 8 * (t - 1) : nullptr;
         if (t + 1 < n_it && !issue_scores(t + 1)) { ok = false; break; }
         if (!mbar_wait(&p_full[t & 1], (t >> 1) & 1, status, kErrBwdMma)) { ok = false; break; }
+        if (tj) tj[6] = globaltimer();
         tc_fence_after();
         const int st = t % kBwd64Stages;
         const uint32_t q_addr = smem_u32(smem + L::kQ + st * L::kQTile);
@@ -1202,6 +1212,7 @@ attn_bwd_dkv64_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_c
         }
         umma_commit(&q_empty[st]);
         umma_commit(&o_empty[st]);
+        if (tj) tj[7] = globaltimer();
       }
       umma_commit(acc_done);
       umma_commit(drain);
@@ -1222,14 +1233,17 @@ attn_bwd_dkv64_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_c
       const uint32_t sc = 256u + 128u * (uint32_t)(t & 1);
       const float* sl = reinterpret_cast<const float*>(smem + L::kLD + st * 512) + col0;
       // o_full also covers the staged lse2/delta (the bulk copies completed on it)
+      unsigned long long* tj = (tr && threadIdx.x == 0 && (t == 1 || t == 2)) ? tr + 1 + 8 * (t - 1) : nullptr;
       const bool got = mbar_wait(&s_full[t & 1], (t >> 1) & 1, status, kErrBwdCompute) &&
                        mbar_wait(&o_full[st], (t / kBwd64Stages) & 1, status, kErrBwdCompute);
       if (!named_barrier_and(pair_bar, 64, got)) { ok = false; break; }
+      if (tj) tj[0] = globaltimer();
       tc_fence_after();
       uint32_t sv[32], dp[32];
       tmem_ld_32x32b_x32(tmem + lane_base + sc + (uint32_t)col0, sv);
       tmem_ld_32x32b_x32(tmem + lane_base + sc + 64u + (uint32_t)col0, dp);
       tmem_ld_wait();
+      if (tj) tj[1] = globaltimer();
       tc_fence_before();
       named_barrier(pair_bar, 64);   // both halves hold their columns before either overwrites
       tc_fence_after();
@@ -1254,12 +1268,14 @@ attn_bwd_dkv64_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_c
         dsp[2 * i] = pack_bf16x2(ds[0], ds[1]);
         dsp[2 * i + 1] = pack_bf16x2(ds[2], ds[3]);
       }
+      if (tj) tj[2] = globaltimer();
       tmem_st_32x32b_x16(tmem + lane_base + sc + (uint32_t)(half * 16), pp);
       tmem_st_32x32b_x16(tmem + lane_base + sc + 64u + (uint32_t)(half * 16), dsp);
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[t & 1]);
+      if (tj) tj[3] = globaltimer();
     }
     if (named_barrier_and(pair_bar, 64, ok)) {
       const bool done = mbar_wait(acc_done, 0, status, kErrBwdCompute);
@@ -1274,6 +1290,7 @@ attn_bwd_dkv64_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_c
           bwd_store_half_row(tmem + lane_base + (uint32_t)(w * 128), ecol0, f,
                              (w == 1 && rope_cs != nullptr) ? rope_cs + (int64_t)key * 64 : nullptr, out);
         }
+        if (tr && threadIdx.x == 0) tr[30] = globaltimer();
       }
     }
   }
@@ -1445,7 +1462,7 @@ void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::
     const char* e = std::getenv("ZEROQ_ATTN_DKV128");
     return e != nullptr && e[0] == '1';
   }();
-  if (dkv128 || trp != nullptr) {
+  if (dkv128) {
     attn_bwd_dkv_tc_kernel<<<(unsigned)g_dkv, kBwdThreads, BwdDkvSmem::kBytes, stream>>>(
         tq, tk, tv, tdo, lse2.data_ptr<float>(), delta.data_ptr<float>(),
         reinterpret_cast<__nv_bfloat16*>(dk.data_ptr<at::BFloat16>()),
@@ -1457,7 +1474,7 @@ void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::
         tq64, tk, tv, tdo64, lse2.data_ptr<float>(), delta.data_ptr<float>(),
         reinterpret_cast<__nv_bfloat16*>(dk.data_ptr<at::BFloat16>()),
         reinterpret_cast<__nv_bfloat16*>(dv.data_ptr<at::BFloat16>()), (int)B, (int)S, (int)Hq, (int)Hk, sl2,
-        (float)scale, causal ? 1 : 0, rcs, st, dk.stride(1), dv.stride(1));
+        (float)scale, causal ? 1 : 0, rcs, st, dk.stride(1), dv.stride(1), trp ? trp + g_dq * 32 : nullptr);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
