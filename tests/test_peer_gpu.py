@@ -183,33 +183,47 @@ def w_peer_ag_gemm(rank, world):
                 torch.cuda.synchronize()
                 assert torch.equal(wbuf.reshape(-1), full)
                 assert torch.equal(y, ref)
-        # module path: the pre-forward hook hands each Linear4bit its peer source
-        lin = m[0]
-        calls = []
-        fused_call = pool.ag_gemm
-        pool.ag_gemm = lambda *a, **k: (calls.append(1), fused_call(*a, **k))[1]
-        x = (torch.randn(2, 160, 512, device="cuda") * 0.5).to(torch.bfloat16).requires_grad_(True)
-        y = m(x)
-        assert len(calls) == 2  # both layers ran the one-kernel path
-        y.float().square().sum().backward()
-        gx, gA = x.grad.clone(), lin.lora_A.grad.clone()
-        # the same through assembled NF4 (set_nf4) with the hooks removed
-        ref_m = torch.nn.Sequential(*[Linear4bit(l.in_features, l.out_features, device="cuda",
-                                                 lora_r=l.lora_r) for l in m])
-        for src, dst, p in zip(m, ref_m, coord._params.values()):
-            pk, am = pool.gather(p).wait()
-            dst.set_nf4(pk, am)
-            if src.lora_r:
-                dst.lora_A.data.copy_(src.lora_A.data)
-                dst.lora_B.data.copy_(src.lora_B.data)
-        x2 = x.detach().clone().requires_grad_(True)
-        y2 = ref_m(x2)
-        y2.float().square().sum().backward()
-        assert torch.equal(y, y2)
-        assert torch.equal(gx, x2.grad)
-        torch.testing.assert_close(gA, ref_m[0].lora_A.grad, rtol=1e-4, atol=1e-5)
+        # module path: the pre-forward hook hands each Linear4bit its peer source;
+        # >= 2049 rows run the one-kernel gather-GEMM, fewer the two-kernel form
+        for rows, one_kernel in ((1100, True), (160, False)):
+            _module_path_case(m, coord, pool, rows, one_kernel)
         torch.cuda.synchronize()
         pool.close()
+
+
+def _module_path_case(m, coord, pool, rows, one_kernel):
+    """Forward/backward of the peer-sourced modules against assembled NF4 copies."""
+    from zeroq_b200.ops.qlinear import Linear4bit
+
+    lin = m[0]
+    for mod in m:
+        if mod.lora_A is not None:
+            mod.lora_A.grad = None
+            mod.lora_B.grad = None
+    calls = []
+    fused_call = pool.ag_gemm
+    pool.ag_gemm = lambda *a, **k: (calls.append(1), fused_call(*a, **k))[1]
+    x = (torch.randn(2, rows, 512, device="cuda") * 0.5).to(torch.bfloat16).requires_grad_(True)
+    y = m(x)
+    pool.ag_gemm = fused_call
+    assert len(calls) == (2 if one_kernel else 0), (rows, len(calls))
+    y.float().square().sum().backward()
+    gx, gA = x.grad.clone(), lin.lora_A.grad.clone()
+    # the same through assembled NF4 (set_nf4) with the hooks removed
+    ref_m = torch.nn.Sequential(*[Linear4bit(l.in_features, l.out_features, device="cuda",
+                                             lora_r=l.lora_r) for l in m])
+    for src, dst, p in zip(m, ref_m, coord._params.values()):
+        pk, am = pool.gather(p).wait()
+        dst.set_nf4(pk, am)
+        if src.lora_r:
+            dst.lora_A.data.copy_(src.lora_A.data)
+            dst.lora_B.data.copy_(src.lora_B.data)
+    x2 = x.detach().clone().requires_grad_(True)
+    y2 = ref_m(x2)
+    y2.float().square().sum().backward()
+    assert torch.equal(y, y2)
+    assert torch.equal(gx, x2.grad)
+    torch.testing.assert_close(gA, ref_m[0].lora_A.grad, rtol=1e-4, atol=1e-5)
 
 
 def w_peer_master_gemm(rank, world):

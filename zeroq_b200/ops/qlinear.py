@@ -56,6 +56,13 @@ from .nf4 import QUANT_TYPE_ID, QuantState, dequantize_4bit, quantize_4bit
 # in-kernel decode of the 4-bit weight inside the GEMM (off by default, see above)
 IN_KERNEL_DECODE = os.environ.get("ZEROQ_IN_KERNEL_DECODE", "0") == "1"
 
+# Peer-sourced weights: up to this many rows of x, the two-kernel form (peer
+# gather + dequantise into a bf16 operand, then the GEMM) is faster than the
+# one-kernel gather-GEMM (measured on 2 B200s at M = 1024: 0.055 / 0.159 /
+# 0.483 ms against 0.071 / 0.182 / 0.538 ms for K = N = 4096 / 8192 / 12288;
+# equal or slower from M = 4096 on).
+AG_ONE_KERNEL_MIN_M = int(os.environ.get("ZEROQ_AG_ONE_KERNEL_MIN_M", "2049"))
+
 
 def _in_kernel_ok(M: int, K: int, N: int) -> bool:
     return IN_KERNEL_DECODE and M >= 256 and K % 128 == 0 and N % 64 == 0
@@ -137,8 +144,19 @@ class NF4LinearFunction(torch.autograd.Function):
         # peer = (PeerShardPool, ZeroQParameter): W stays in its owners' shards and
         # the fused gather + dequantise + GEMM kernel reads it there
         peer_fused = peer is not None and fused and _peer_ag_ok(M, N, K, blocksize)
-        if peer is not None and not peer_fused:
+        w_peer = None
+        if peer_fused and M < AG_ONE_KERNEL_MIN_M:
+            # short inputs: dequantise straight from the owners' shards (one
+            # kernel), then the regular GEMM paths (epilogues included)
+            w_peer = peer[0].gather_dequant(peer[1], N, K)
+            peer_fused = False
+        elif peer is not None and not peer_fused:
             packed, absmax = peer[0].gather(peer[1]).wait()
+
+        def operand():  # bf16 W [N, K] for the GEMM paths below
+            if w_peer is not None:
+                return w_peer
+            return _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
         U = None
         Ut = None
         a_pad = b_pad = b_t = None
@@ -167,20 +185,20 @@ class NF4LinearFunction(torch.autograd.Function):
             elif (rope is not None and bias is None and _epi_ok(M, K) and N % 128 == 0
                   and rope_cs.shape[1] == 64 and M % rope_cs.shape[0] == 0
                   and not _in_kernel_ok(M, K, N)):
-                w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
+                w = operand()
                 E.gemm_rope(x2, w, y, rope_cs, U, b_pad)
                 rope_done = True
                 del w
             elif act_out == "gelu" and bias is None and _epi_ok(M, K) and not _in_kernel_ok(M, K, N):
-                w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
+                w = operand()
                 act = torch.empty_like(y)
                 E.gemm_gelu(x2, w, y, act, False, U, b_pad)
                 del w
-            elif _in_kernel_ok(M, K, N):
+            elif _in_kernel_ok(M, K, N) and w_peer is None:
                 E.gemm_nf4(x2, packed, absmax, N, K, blocksize, QUANT_TYPE_ID[quant_type], False, y,
                            U, b_pad)
             else:
-                w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
+                w = operand()
                 if has_lora:
                     E.gemm_bf16_tn_extra(x2, w, y, U, b_pad)
                 else:
