@@ -50,10 +50,11 @@ void gelu_cdf_pdf(at::Tensor x, at::Tensor cdf, at::Tensor pdf);
 void gelu_bwd(at::Tensor g, at::Tensor x, at::Tensor dx);
 void swiglu_fwd(at::Tensor gate, at::Tensor up, at::Tensor y);
 void swiglu_bwd(at::Tensor g, at::Tensor gate, at::Tensor up, at::Tensor dgate, at::Tensor dup);
-void ce_fwd(at::Tensor logits, at::Tensor targets, at::Tensor loss, at::Tensor lse, at::Tensor count,
-            int64_t vocab, int64_t ignore_index);
+void ce_fwd(at::Tensor logits, at::Tensor targets, at::Tensor loss, at::Tensor lse,
+            c10::optional<at::Tensor> count, int64_t vocab, int64_t ignore_index, int64_t col0,
+            int64_t vocab_total);
 void ce_bwd(at::Tensor logits, at::Tensor targets, at::Tensor lse, at::Tensor scale, int64_t vocab,
-            int64_t ignore_index);
+            int64_t ignore_index, int64_t col0, int64_t vocab_total);
 void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v, c10::optional<at::Tensor> pbf16,
                 double lr, double b1, double b2, double eps, double wd, double bc1, double bc2,
                 double gscale, c10::optional<at::Tensor> bc, c10::optional<at::Tensor> clip_sq,
@@ -148,8 +149,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gelu_cdf_pdf", &gelu_cdf_pdf);
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);
-  m.def("ce_fwd", &ce_fwd);
-  m.def("ce_bwd", &ce_bwd);
+  // (col0, vocab_total): the logits buffer holds vocabulary columns [col0, col0 + vocab)
+  m.def("ce_fwd", &ce_fwd, py::arg("logits"), py::arg("targets"), py::arg("loss"), py::arg("lse"),
+        py::arg("count"), py::arg("vocab"), py::arg("ignore_index"), py::arg("col0") = 0,
+        py::arg("vocab_total") = -1);
+  m.def("ce_bwd", &ce_bwd, py::arg("logits"), py::arg("targets"), py::arg("lse"), py::arg("scale"),
+        py::arg("vocab"), py::arg("ignore_index"), py::arg("col0") = 0, py::arg("vocab_total") = -1);
   m.def("adamw_step", [](at::Tensor p, at::Tensor g, at::Tensor m_, at::Tensor v,
                          c10::optional<at::Tensor> pbf16, double lr, double b1, double b2, double eps,
                          double wd, double bc1, double bc2, double gscale) {

@@ -396,7 +396,10 @@ constexpr int kCEThreads = 256;
 __global__ void __launch_bounds__(kCEThreads) ce_fwd_kernel(
     const __nv_bfloat16* __restrict__ logits, const int64_t* __restrict__ targets,
     float* __restrict__ loss, float* __restrict__ lse_out, float* __restrict__ count, int64_t Vpad,
-    int64_t vocab, int64_t ignore_index) {
+    int64_t vocab, int64_t ignore_index, int64_t col0, int64_t vocab_total) {
+  // The buffer holds columns [col0, col0 + vocab) of the vocabulary (col0 = 0 and
+  // vocab_total = vocab for whole rows): lse is over those columns, and a row
+  // whose target lies among them gets loss = lse - logit[target] and is counted.
   __shared__ float smax[kCEThreads / 32], ssum[kCEThreads / 32];
   const int64_t row = blockIdx.x;
   const __nv_bfloat16* lr = logits + row * Vpad;
@@ -437,11 +440,12 @@ __global__ void __launch_bounds__(kCEThreads) ce_fwd_kernel(
     const float lse = M + logf(S);
     lse_out[row] = lse;
     const int64_t t = targets[row];
-    if (t == ignore_index || t < 0 || t >= vocab) {
-      loss[row] = 0.0f;
+    const bool valid = !(t == ignore_index || t < 0 || t >= vocab_total);
+    if (valid && t >= col0 && t < col0 + vocab) {
+      loss[row] = lse - __bfloat162float(lr[t - col0]);
+      if (count != nullptr) atomicAdd(count, 1.0f);
     } else {
-      loss[row] = lse - __bfloat162float(lr[t]);
-      atomicAdd(count, 1.0f);
+      loss[row] = 0.0f;
     }
   }
 }
@@ -450,11 +454,13 @@ __global__ void __launch_bounds__(kCEThreads) ce_fwd_kernel(
 __global__ void __launch_bounds__(kCEThreads) ce_bwd_kernel(
     __nv_bfloat16* __restrict__ logits, const int64_t* __restrict__ targets,
     const float* __restrict__ lse, const float* __restrict__ scale_ptr, int64_t Vpad, int64_t vocab,
-    int64_t ignore_index) {
+    int64_t ignore_index, int64_t col0, int64_t vocab_total) {
+  // columns [col0, col0 + vocab) of the vocabulary; lse is the whole row's
   const int64_t row = blockIdx.x;
   __nv_bfloat16* lr = logits + row * Vpad;
-  const int64_t t = targets[row];
-  const bool ignored = (t == ignore_index || t < 0 || t >= vocab);
+  const int64_t t = targets[row] - col0;   // chunk-local target column (may be outside)
+  const int64_t tg = targets[row];
+  const bool ignored = (tg == ignore_index || tg < 0 || tg >= vocab_total);
   const float L = lse[row];
   const float sc = ignored ? 0.0f : scale_ptr[0];
   const int64_t nch = Vpad >> 3;
@@ -857,30 +863,37 @@ void swiglu_bwd(at::Tensor g, at::Tensor gate, at::Tensor up, at::Tensor dgate, 
 }
 
 void ce_fwd(at::Tensor logits, at::Tensor targets, at::Tensor loss, at::Tensor lse,
-            at::Tensor count, int64_t vocab, int64_t ignore_index) {
+            c10::optional<at::Tensor> count, int64_t vocab, int64_t ignore_index, int64_t col0,
+            int64_t vocab_total) {
   check_bf16(logits, "logits");
   TORCH_CHECK(targets.scalar_type() == at::kLong && targets.is_contiguous(), "targets int64");
   const int64_t M = logits.size(0), Vpad = logits.size(1);
   TORCH_CHECK(Vpad % 8 == 0 && vocab <= Vpad, "ce: Vpad % 8 and vocab <= Vpad");
   TORCH_CHECK(targets.numel() == M && loss.numel() >= M && lse.numel() >= M, "ce: one target per row");
   const at::cuda::CUDAGuard guard(logits.device());
+  float* cnt = nullptr;
+  if (count.has_value() && count->defined()) cnt = count->data_ptr<float>();
+  if (vocab_total < 0) vocab_total = vocab;
+  TORCH_CHECK(col0 >= 0 && col0 + vocab <= vocab_total, "ce: chunk outside the vocabulary");
   ce_fwd_kernel<<<(unsigned)M, kCEThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       cbf(logits), targets.data_ptr<int64_t>(), loss.data_ptr<float>(), lse.data_ptr<float>(),
-      count.data_ptr<float>(), Vpad, vocab, ignore_index);
+      cnt, Vpad, vocab, ignore_index, col0, vocab_total);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 void ce_bwd(at::Tensor logits, at::Tensor targets, at::Tensor lse, at::Tensor scale,
-            int64_t vocab, int64_t ignore_index) {
+            int64_t vocab, int64_t ignore_index, int64_t col0, int64_t vocab_total) {
   check_bf16(logits, "logits");
   const int64_t M = logits.size(0), Vpad = logits.size(1);
   TORCH_CHECK(Vpad % 8 == 0 && vocab <= Vpad && targets.numel() == M && lse.numel() >= M &&
                   targets.scalar_type() == at::kLong && scale.numel() >= 1,
               "ce_bwd: sizes");
   const at::cuda::CUDAGuard guard(logits.device());
+  if (vocab_total < 0) vocab_total = vocab;
+  TORCH_CHECK(col0 >= 0 && col0 + vocab <= vocab_total, "ce_bwd: chunk outside the vocabulary");
   ce_bwd_kernel<<<(unsigned)M, kCEThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       bf(logits), targets.data_ptr<int64_t>(), lse.data_ptr<float>(), scale.data_ptr<float>(),
-      Vpad, vocab, ignore_index);
+      Vpad, vocab, ignore_index, col0, vocab_total);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

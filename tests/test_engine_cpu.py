@@ -343,3 +343,15 @@ def test_linear4bit_rope_argument_matches_apply_rope_on_cpu():
     y2.square().sum().backward()
     torch.testing.assert_close(y.view(B, S, H, 128), y2, rtol=1e-5, atol=1e-6)
     torch.testing.assert_close(g1, x.grad, rtol=1e-4, atol=1e-6)
+
+
+def test_chunked_cross_entropy_falls_back_on_cpu():
+    from zeroq_b200.ops.cross_entropy import lm_head_cross_entropy
+
+    torch.manual_seed(0)
+    h = torch.randn(16, 64)
+    W = torch.randn(256, 64) * 0.1
+    t = torch.randint(0, 250, (16,))
+    loss = lm_head_cross_entropy(h, W, t, 250, chunk=128)
+    ref = torch.nn.functional.cross_entropy(h @ W[:250].t(), t)
+    assert abs(loss.item() - ref.item()) < 1e-4

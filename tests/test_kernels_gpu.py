@@ -1041,3 +1041,35 @@ def test_cuda_graph_training_steps_match_eager(cuda):
     spread_p = (pb - pa).abs().max().item()
     assert (lg - la).abs().max().item() <= 3 * spread_l + 2e-3, (lg, la, lb)
     assert (pg - pa).abs().max().item() <= 3 * spread_p + 1e-4
+
+
+@pytest.mark.parametrize("vocab,chunk", [(1000, 256), (50257, 16384), (2048, 2048)])
+def test_chunked_lm_head_cross_entropy_matches_full_logits(cuda, vocab, chunk):
+    """LM head + CE over vocabulary chunks (no [M, V] logits) against the full
+    logits path and an fp32 reference, with ignored rows."""
+    from zeroq_b200.ops.cross_entropy import cross_entropy, lm_head_cross_entropy
+    from zeroq_b200.ops.gemm import LMHeadFunction
+
+    torch.manual_seed(21)
+    M, d = 512, 256
+    Vp = (vocab + 127) // 128 * 128
+    W = (0.05 * torch.randn(Vp, d, device=cuda)).bfloat16()
+    W[vocab:] = 0
+    h = torch.randn(M, d, device=cuda).bfloat16()
+    t = torch.randint(0, vocab, (M,), device=cuda)
+    t[::7] = -100
+    h1 = h.clone().requires_grad_(True)
+    l1 = lm_head_cross_entropy(h1, W, t, vocab, chunk=chunk)
+    l1.backward()
+    h2 = h.clone().requires_grad_(True)
+    l2 = cross_entropy(LMHeadFunction.apply(h2, W), t, vocab=vocab)
+    l2.backward()
+    h3 = h.float().clone().requires_grad_(True)
+    l3 = torch.nn.functional.cross_entropy(h3 @ W.float()[:vocab].t(), t, ignore_index=-100)
+    l3.backward()
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    assert abs(l1.item() - l2.item()) < 2e-3 and abs(l1.item() - l3.item()) < 2e-2
+    scale = h3.grad.abs().max().item()
+    assert (h1.grad.float() - h2.grad.float()).abs().max().item() < 3e-2 * scale
+    assert (h1.grad.float() - h3.grad).abs().max().item() < 3e-2 * scale

@@ -34,7 +34,7 @@ import torch.utils.checkpoint as ckpt
 
 from ..ops.activations import gelu, swiglu
 from ..ops.attention import flash_attention
-from ..ops.cross_entropy import cross_entropy
+from ..ops.cross_entropy import cross_entropy, lm_head_cross_entropy
 from ..ops.gemm import LMHeadFunction
 from ..ops.norm import add_rmsnorm
 from ..ops.qlinear import Linear4bit
@@ -67,6 +67,11 @@ class DecoderConfig:
     quant_type: str = "nf4"
     # memory
     activation_checkpointing: bool = False
+    # > 0: LM head + cross-entropy over vocabulary chunks of this many columns
+    # (the [tokens, vocab] logits are never materialised; frozen head only).
+    # Off by default: it trades one extra head GEMM for the logits' memory
+    # (Qwen2.5-7B shape, 2 B200s: 29.4 vs 31.1 GB peak, 327 vs 314 ms/step)
+    ce_chunk: int = 0
     train_norms: bool = True
     train_embeddings: bool = False
 
@@ -338,6 +343,9 @@ class DecoderLM(nn.Module):
         if W.numel() == 0:
             raise RuntimeError("the LM head weight is sharded and not gathered here; keep "
                                "'embed_tokens' and 'lm_head' in exclude_modules")
+        if targets is not None and self.cfg.ce_chunk > 0:
+            return lm_head_cross_entropy(x, W, targets.reshape(-1), vocab=self.cfg.vocab_size,
+                                         ignore_index=ignore_index, chunk=self.cfg.ce_chunk)
         logits = LMHeadFunction.apply(x, W)
         if targets is None:
             return logits.view(B, S, -1)[..., : self.cfg.vocab_size]
