@@ -99,13 +99,6 @@ void plan_gather_dequant(std::vector<int64_t> psrc, std::vector<int64_t> pstarts
                          std::vector<int64_t> asrc, std::vector<int64_t> astarts, int64_t rows,
                          int64_t cols, int64_t row0, int64_t blocksize, int64_t qtype, bool transpose,
                          at::Tensor out);
-#ifdef ZQ_WITH_ATTENTION
-// attention.cu
-void attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse, bool causal,
-              double scale);
-void attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse,
-              at::Tensor dq, at::Tensor dk, at::Tensor dv, bool causal, double scale);
-#endif
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "zeroq_b200 sm_100a kernels";
@@ -215,8 +208,4 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("rank"), pybind11::arg("N"), pybind11::arg("K"), pybind11::arg("blocksize"),
         pybind11::arg("quant_type"), pybind11::arg("wbuf"), pybind11::arg("c"),
         pybind11::arg("a2") = pybind11::none(), pybind11::arg("b2") = pybind11::none());
-#ifdef ZQ_WITH_ATTENTION
-  m.def("attn_fwd", &attn_fwd);
-  m.def("attn_bwd", &attn_bwd);
-#endif
 }

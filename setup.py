@@ -12,7 +12,7 @@ from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 SOURCES = sorted(glob.glob(os.path.join("csrc", "*.cu"))) + ["csrc/bindings.cpp"]
-DEFINES = ["-DZQ_WITH_ATTENTION"] if os.path.exists(os.path.join(ROOT, "csrc", "attention.cu")) else []
+DEFINES = []
 
 NVCC_FLAGS = [
     "-O3", "-std=c++17", "-lineinfo",

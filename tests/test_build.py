@@ -15,6 +15,6 @@ def test_extension_loads_if_built():
     from zeroq_b200.ops import _ext
 
     assert _ext.available(), f"extension failed to load: {_ext._EXT_ERR!r}"
-    for name in ("gemm_bf16_tn", "gemm_bf16_nn", "add_rmsnorm_fwd", "rmsnorm_bwd", "attn_fwd",
+    for name in ("gemm_bf16_tn", "gemm_bf16_nn", "add_rmsnorm_fwd", "rmsnorm_bwd", "attn_fwd_tc",
                  "nf4_quantize", "rs_adamw", "plan_gather_dequant"):
         assert hasattr(_ext.ext(), name), name

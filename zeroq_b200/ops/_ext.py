@@ -39,7 +39,7 @@ def available() -> bool:
 
 
 # kernels launched per call of each binding (bindings not listed launch one)
-_KERNELS_PER_CALL = {"attn_bwd": 3, "attn_bwd_tc": 3, "gemm_status": 0, "set_gemm_pair_mode": 0,
+_KERNELS_PER_CALL = {"attn_bwd_tc": 3, "gemm_status": 0, "set_gemm_pair_mode": 0,
                      "peer_alloc": 0, "peer_handle": 0, "peer_open": 0, "peer_close": 0,
                      "peer_free": 0, "tensor_from_ptr": 0, "peer_status_read": 0,
                      "peer_flag_words": 0}

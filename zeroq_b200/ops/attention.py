@@ -1,19 +1,18 @@
 """Causal (GQA-capable) flash attention, forward and backward.
 
 Tensors keep the projection layout ``[B, S, H, D]`` so no transposes surround
-the kernels.  For ``D = 128`` the forward runs on the 5th-generation tensor
-cores (``csrc/attention_sm100.cu``: TMA-fed Q/K/V tiles, S and O accumulated in
-tensor memory, softmax in registers, P through shared memory); ``D = 64`` uses
-the ``mma.sync`` kernel in ``csrc/attention.cu``.  Both write ``O`` plus the row
-log-sum-exp ``L``.  The backward (``csrc/attention.cu``) recomputes
-probabilities from ``L``, accumulates ``dK``/``dV`` per key tile in registers and
-``dQ`` in fp32 with atomics, after a small kernel that forms
-``delta = rowsum(dO * O)``; for ``D = 128`` it runs on the tensor cores as well
-(``csrc/attention_sm100.cu``): a dQ kernel per query tile and a dK/dV kernel
-per key tile, both recomputing P from ``L`` with S, dP, P and dS held in
-tensor memory, no atomics.
+the kernels.  Forward and backward run on the 5th-generation tensor cores
+(``csrc/attention_sm100.cu``): the forward with TMA-fed Q/K/V tiles, S and O
+accumulated in tensor memory and softmax in registers, writing ``O`` and the
+row log-sum-exp ``L``; the backward as a ``delta = rowsum(dO * O)`` pass, a dQ
+kernel per query tile and a dK/dV kernel per key tile, both recomputing P from
+``L`` with S, dP, P and dS in tensor memory, no atomics.  The kernels are built
+for 128-wide heads; narrower heads (``D`` = 64 and other multiples of 16) are
+zero-padded to 128 - padded columns change no score and come out zero - so
+every head size up to 128 runs on the same kernels (at 128-wide cost).
 
-CPU tensors use PyTorch's SDPA (the oracle).
+CPU tensors, ``S`` not a multiple of 128 and heads wider than 128 use PyTorch's
+SDPA (the oracle).
 """
 
 from __future__ import annotations
@@ -47,42 +46,54 @@ def _tma_ok(t: torch.Tensor) -> bool:
             and t.data_ptr() % 16 == 0)
 
 
+def _pad128(t: torch.Tensor) -> torch.Tensor:
+    """``[B, S, H, D]`` (D < 128) zero-padded to ``[B, S, H, 128]``."""
+    out = t.new_zeros(*t.shape[:-1], 128)
+    out[..., : t.shape[-1]] = t
+    return out
+
+
+def _tc_ok(q: torch.Tensor) -> bool:
+    D = q.shape[-1]
+    return q.shape[1] % 128 == 0 and q.shape[1] > 0 and D <= 128 and D % 16 == 0
+
+
 class _FlashAttn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, causal, scale, rope=None):
         D = q.shape[-1]
+        ctx.d = D
+        if D < 128:   # narrower heads run zero-padded on the 128-wide kernels
+            q, k, v = _pad128(q), _pad128(k), _pad128(v)
         # the tcgen05 kernels read q/k/v through TMA maps and take strided views
         # (column slices of a fused q/k/v projection) as they are
-        q, k, v = (t if (D == 128 and _tma_ok(t)) else t.contiguous() for t in (q, k, v))
-        B, S, Hq, D = q.shape
+        q, k, v = (t if _tma_ok(t) else t.contiguous() for t in (q, k, v))
+        B, S, Hq, _ = q.shape
         o = torch.empty(q.shape, dtype=q.dtype, device=q.device)
         lse = torch.empty(B, Hq, S, dtype=torch.float32, device=q.device)
-        if D == 128:
-            _ext.ext().attn_fwd_tc(q, k, v, o, lse, bool(causal), float(scale))
-        else:
-            _ext.ext().attn_fwd(q, k, v, o, lse, bool(causal), float(scale))
+        _ext.ext().attn_fwd_tc(q, k, v, o, lse, bool(causal), float(scale))
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.causal, ctx.scale = causal, scale
         ctx.rope = rope if (rope is not None and hasattr(rope, "grads_unrotated")) else None
-        return o
+        return o if D == 128 else o[..., :D]
 
     @staticmethod
     def backward(ctx, do):
         q, k, v, o, lse = ctx.saved_tensors
-        do = do.contiguous()
+        D = ctx.d
+        do = do.contiguous() if D == 128 else _pad128(do)
         dq, dk = (torch.empty(t.shape, dtype=t.dtype, device=t.device) for t in (q, k))
-        dv = _like_token_pitched(v) if q.shape[-1] == 128 else None
+        dv = _like_token_pitched(v) if D == 128 else None
         if dv is None:
             dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
-        if q.shape[-1] == 128:
-            rope = ctx.rope
-            cs = rope.cs if rope is not None and rope.cs.shape[0] == q.shape[1] else None
-            _ext.ext().attn_bwd_tc(do, q, k, v, o, lse, dq, dk, dv, bool(ctx.causal), float(ctx.scale),
-                                   None, cs)
-            if cs is not None:
-                rope.grads_unrotated = True  # dQ/dK are gradients of the pre-rotation q/k
-        else:
-            _ext.ext().attn_bwd(do, q, k, v, o, lse, dq, dk, dv, bool(ctx.causal), float(ctx.scale))
+        rope = ctx.rope
+        cs = rope.cs if (rope is not None and D == 128 and rope.cs.shape[0] == q.shape[1]) else None
+        _ext.ext().attn_bwd_tc(do, q, k, v, o, lse, dq, dk, dv, bool(ctx.causal), float(ctx.scale),
+                               None, cs)
+        if cs is not None:
+            rope.grads_unrotated = True  # dQ/dK are gradients of the pre-rotation q/k
+        if D < 128:
+            dq, dk, dv = dq[..., :D], dk[..., :D], dv[..., :D]
         return dq, dk, dv, None, None, None
 
 
@@ -106,6 +117,6 @@ def flash_attention(q, k, v, causal: bool = True, scale=None, rope=None):
     (tcgen05 path) and marks the spec so the projections do not rotate again."""
     if scale is None:
         scale = 1.0 / math.sqrt(q.shape[-1])
-    if q.is_cuda and q.dtype == torch.bfloat16:
+    if q.is_cuda and q.dtype == torch.bfloat16 and _tc_ok(q):
         return _FlashAttn.apply(q, k, v, causal, scale, rope)
     return attention_reference(q, k, v, causal, scale)
