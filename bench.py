@@ -56,6 +56,11 @@ CONFIGS = {
     "4.7b": ("4.7b", 16, None, 8, 1024, "4bit-once",
              "NF4 4-bit compute (weights gathered once, resident), LoRA r=16 on every "
              "projection + RMSNorm weights, AdamW"),
+    "qwen7b-4bit": ("qwen2.5-7b", 16, ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj",
+                                       "up_proj", "down_proj"), 4, 2048, "4bit-once",
+                    "Qwen2.5-7B shape, NF4 4-bit compute (weights gathered once, resident), "
+                    "SwiGLU MLP with its GEMM epilogues, LoRA r=16 on all linears + RMSNorm "
+                    "weights, AdamW"),
     "qwen7b-hetero": ("qwen2.5-7b", 16, ("q_proj", "k_proj", "v_proj", "o_proj"), 4, 2048,
                       "hetero",
                       "Qwen2.5-7B shape, frozen NF4 base sharded by uneven rank weights "

@@ -87,7 +87,8 @@ void ag_gemm_nf4(at::Tensor a, std::vector<int64_t> psrc, std::vector<int64_t> p
                  std::vector<int64_t> asrc, std::vector<int64_t> astarts, int64_t packed_total,
                  int64_t absmax_total, int64_t rank, int64_t N, int64_t K, int64_t blocksize,
                  int64_t quant_type, at::Tensor wbuf, at::Tensor c, c10::optional<at::Tensor> a2,
-                 c10::optional<at::Tensor> b2);
+                 c10::optional<at::Tensor> b2, c10::optional<at::Tensor> swiglu_g,
+                 c10::optional<at::Tensor> swiglu_out);
 void ag_gemm_f32(at::Tensor a, std::vector<int64_t> src, std::vector<int64_t> starts, int64_t total,
                  int64_t rank, int64_t N, int64_t K, at::Tensor wbuf, at::Tensor c,
                  c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2);
@@ -95,6 +96,9 @@ void gemm_rope(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor cs,
                c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2, int64_t ncols);
 void gemm_gelu(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor aux, bool b_mn,
                c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2);
+void gemm_swiglu(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor c2, at::Tensor g,
+                 c10::optional<at::Tensor> u, bool b_mn, c10::optional<at::Tensor> a2,
+                 c10::optional<at::Tensor> b2);
 void plan_gather_dequant(std::vector<int64_t> psrc, std::vector<int64_t> pstarts,
                          std::vector<int64_t> asrc, std::vector<int64_t> astarts, int64_t rows,
                          int64_t cols, int64_t row0, int64_t blocksize, int64_t qtype, bool transpose,
@@ -207,5 +211,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("astarts"), pybind11::arg("packed_total"), pybind11::arg("absmax_total"),
         pybind11::arg("rank"), pybind11::arg("N"), pybind11::arg("K"), pybind11::arg("blocksize"),
         pybind11::arg("quant_type"), pybind11::arg("wbuf"), pybind11::arg("c"),
+        pybind11::arg("a2") = pybind11::none(), pybind11::arg("b2") = pybind11::none(),
+        pybind11::arg("swiglu_g") = pybind11::none(), pybind11::arg("swiglu_out") = pybind11::none());
+  m.def("gemm_swiglu", &gemm_swiglu,
+        "tcgen05 GEMM with the SwiGLU output (b_mn=false) / SwiGLU-gradient (b_mn=true) epilogue",
+        pybind11::arg("a"), pybind11::arg("b"), pybind11::arg("c"), pybind11::arg("c2"),
+        pybind11::arg("g"), pybind11::arg("u"), pybind11::arg("b_mn"),
         pybind11::arg("a2") = pybind11::none(), pybind11::arg("b2") = pybind11::none());
 }

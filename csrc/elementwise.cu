@@ -9,6 +9,7 @@
 
 #include "common.cuh"
 #include "gelu.cuh"
+#include "swiglu.cuh"
 
 namespace zq {
 
@@ -362,7 +363,7 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gate,
   bf16x8_to_f32(reinterpret_cast<const uint4*>(gate)[t], a);
   bf16x8_to_f32(reinterpret_cast<const uint4*>(up)[t], b);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) o[i] = a[i] / (1.0f + expf(-a[i])) * b[i];
+  for (int i = 0; i < 8; ++i) o[i] = swiglu_fwd_val(a[i], b[i]);
   reinterpret_cast<uint4*>(y)[t] = f32_to_bf16x8(o);
 }
 
@@ -378,12 +379,7 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ g,
   bf16x8_to_f32(reinterpret_cast<const uint4*>(gate)[t], a);
   bf16x8_to_f32(reinterpret_cast<const uint4*>(up)[t], b);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float sg = 1.0f / (1.0f + expf(-a[i]));
-    const float silu = a[i] * sg;
-    db[i] = gg[i] * silu;
-    da[i] = gg[i] * b[i] * sg * (1.0f + a[i] * (1.0f - sg));
-  }
+  for (int i = 0; i < 8; ++i) swiglu_bwd_vals(gg[i], a[i], b[i], da[i], db[i]);
   reinterpret_cast<uint4*>(dgate)[t] = f32_to_bf16x8(da);
   reinterpret_cast<uint4*>(dup)[t] = f32_to_bf16x8(db);
 }

@@ -32,6 +32,7 @@
 #include "common.cuh"
 #include "peer_gather.cuh"
 #include "gelu.cuh"
+#include "swiglu.cuh"
 
 namespace zq {
 
@@ -75,9 +76,13 @@ struct GemmArgs {
   __nv_bfloat16* ag_w;
   int* ag_sync;
   int ag_rot, ag_kchunks, ag_cols;  // ag_cols: columns per gather item
-  // epilogue input (kEpiGeluBwd): the pre-activation h [M, N], row pitch epi_ld
+  // epilogue input (kEpiGeluBwd): the pre-activation h [M, N], row pitch epi_ld;
+  // (kEpiSwigluFwd / kEpiSwigluBwd): the gate pre-activation g [M, N]
   const __nv_bfloat16* epi_src;
   int64_t epi_ld;
+  // second epilogue input (kEpiSwigluBwd): the up-projection output u [M, N]
+  const __nv_bfloat16* epi_src2;
+  int64_t epi_ld2;
   // epilogue input (kEpiRope): (cos, sin) table [epi_S, 64] of float2
   const float2* epi_cs;
   int epi_S;
@@ -95,7 +100,17 @@ struct GemmArgs {
 // every 128-wide head) to the bf16-rounded output: row m is position m % S and
 // epi_cs holds (cos, sin) of each position and pair (fp32, [S, 64, 2]) - the
 // arithmetic of the standalone RoPE kernel, so q/k projections need no RoPE pass.
-enum PairEpi { kEpiPlain = 0, kEpiGeluFwd = 1, kEpiGeluBwd = 2, kEpiRope = 3 };
+//
+// SwiGLU MLP halves (gate g and up u are separate projections of the same x):
+// kEpiSwigluFwd is the up-projection: it stores u = bf16(acc) through tmC and
+// silu(g)·u through tmC2, reading g [M, N] (epi_src) - the activation kernel's
+// three passes over [M, N] become one extra read.  kEpiSwigluBwd is the input
+// gradient of the down-projection, dact = bf16(acc): it reads g (epi_src) and
+// u (epi_src2) and stores dg = dact·u·silu'(g) through tmC and du = dact·silu(g)
+// through tmC2, so dact is never stored.  Both use the arithmetic of the
+// standalone SwiGLU kernels on the bf16-rounded values (swiglu.cuh).
+enum PairEpi { kEpiPlain = 0, kEpiGeluFwd = 1, kEpiGeluBwd = 2, kEpiRope = 3, kEpiSwigluFwd = 4,
+               kEpiSwigluBwd = 5 };
 
 constexpr int kAgMaxTilesN = 4096;
 constexpr int kAgClaim = kAgMaxTilesN, kAgExit = kAgMaxTilesN + 1, kAgSyncWords = kAgMaxTilesN + 2;
@@ -704,22 +719,62 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
       }
       ++chunk_no;
     };
-    // pre-activation values of this thread's row for columns n_col .. n_col+31
-    auto load_h = [&](int n_col, int m0, uint4 (&hv)[4]) {
+    // epilogue inputs of this thread's row for columns n_col .. n_col+31
+    constexpr bool kSide = EPI == kEpiGeluBwd || EPI == kEpiSwigluFwd || EPI == kEpiSwigluBwd;
+    constexpr bool kSide2 = EPI == kEpiSwigluBwd;
+    auto load_side = [&](const __nv_bfloat16* src, int64_t ld, int n_col, int m0, uint4 (&hv)[4]) {
       const int64_t grow = m0 + row;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int c = n_col + 8 * j;
         hv[j] = (grow < args.M && c < args.N)
-                    ? *reinterpret_cast<const uint4*>(args.epi_src + grow * args.epi_ld + c)
+                    ? *reinterpret_cast<const uint4*>(src + grow * ld + c)
                     : make_uint4(0u, 0u, 0u, 0u);
       }
     };
+    auto load_h = [&](int n_col, int m0, uint4 (&hv)[4], uint4 (&hv2)[4]) {
+      if constexpr (kSide) load_side(args.epi_src, args.epi_ld, n_col, m0, hv);
+      if constexpr (kSide2) load_side(args.epi_src2, args.epi_ld2, n_col, m0, hv2);
+    };
     // fp32 chunk of 32 columns -> epilogue -> staging -> TMA store(s)
-    auto store_chunk = [&](const float (&v)[32], int n_col, int m0, const uint4 (&hv)[4]) {
+    auto store_chunk = [&](const float (&v)[32], int n_col, int m0, const uint4 (&hv)[4],
+                           const uint4 (&hv2)[4]) {
       uint32_t o[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) o[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+      if constexpr (EPI == kEpiSwigluFwd || EPI == kEpiSwigluBwd) {
+        const uint32_t gw[16] = {hv[0].x, hv[0].y, hv[0].z, hv[0].w, hv[1].x, hv[1].y, hv[1].z, hv[1].w,
+                                 hv[2].x, hv[2].y, hv[2].z, hv[2].w, hv[3].x, hv[3].y, hv[3].z, hv[3].w};
+        if constexpr (EPI == kEpiSwigluFwd) {
+          stage_store(o, &tmC, n_col, m0);   // u
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float2 g = bf16x2_to_f2(gw[i]);
+            const float2 u = bf16x2_to_f2(o[i]);
+            o[i] = pack_bf16x2(swiglu_fwd_val(g.x, u.x), swiglu_fwd_val(g.y, u.y));
+          }
+          stage_store(o, &tmC2, n_col, m0);  // silu(g)·u
+        } else {
+          const uint32_t uw[16] = {hv2[0].x, hv2[0].y, hv2[0].z, hv2[0].w, hv2[1].x, hv2[1].y,
+                                   hv2[1].z, hv2[1].w, hv2[2].x, hv2[2].y, hv2[2].z, hv2[2].w,
+                                   hv2[3].x, hv2[3].y, hv2[3].z, hv2[3].w};
+          uint32_t du[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float2 d = bf16x2_to_f2(o[i]);
+            const float2 g = bf16x2_to_f2(gw[i]);
+            const float2 u = bf16x2_to_f2(uw[i]);
+            float dg0, du0, dg1, du1;
+            swiglu_bwd_vals(d.x, g.x, u.x, dg0, du0);
+            swiglu_bwd_vals(d.y, g.y, u.y, dg1, du1);
+            du[i] = pack_bf16x2(du0, du1);
+            o[i] = pack_bf16x2(dg0, dg1);
+          }
+          stage_store(o, &tmC, n_col, m0);    // dg
+          stage_store(du, &tmC2, n_col, m0);  // du
+        }
+        return;
+      }
       if constexpr (EPI == kEpiGeluBwd) {
         const uint32_t hw[16] = {hv[0].x, hv[0].y, hv[0].z, hv[0].w, hv[1].x, hv[1].y, hv[1].z, hv[1].w,
                                  hv[2].x, hv[2].y, hv[2].z, hv[2].w, hv[3].x, hv[3].y, hv[3].z, hv[3].w};
@@ -779,37 +834,38 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             ob[i + 1] = rope_hi(a.y, b.y, v.z, v.w);
           }
           if (n0 + c0 * 32 < args.epi_ncols) {
-            store_chunk(oa, n0 + c0 * 32, m0, none);
-            store_chunk(ob, n0 + c1 * 32, m0, none);
+            store_chunk(oa, n0 + c0 * 32, m0, none, none);
+            store_chunk(ob, n0 + c1 * 32, m0, none, none);
           } else {  // a head past the rotated columns (v of a fused q/k/v GEMM): as is
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
               oa[i] = __uint_as_float(ra[i]);
               ob[i] = __uint_as_float(rb[i]);
             }
-            store_chunk(oa, n0 + c0 * 32, m0, none);
-            store_chunk(ob, n0 + c1 * 32, m0, none);
+            store_chunk(oa, n0 + c0 * 32, m0, none, none);
+            store_chunk(ob, n0 + c1 * 32, m0, none, none);
           }
         }
       } else if (pw.sk < 0) {
-        uint4 hnext[4] = {};
-        if constexpr (EPI == kEpiGeluBwd) load_h(n0, m0, hnext);
+        uint4 hnext[4] = {}, hnext2[4] = {};
+        load_h(n0, m0, hnext, hnext2);
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
-          uint4 hv[4];
+          uint4 hv[4], hv2[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) hv[j] = hnext[j];
-          // the next chunk's pre-activation loads overlap this chunk's work
-          if constexpr (EPI == kEpiGeluBwd) {
-            if (c + 1 < BN / 32) load_h(n0 + (c + 1) * 32, m0, hnext);
+          for (int j = 0; j < 4; ++j) {
+            hv[j] = hnext[j];
+            hv2[j] = hnext2[j];
           }
+          // the next chunk's epilogue-input loads overlap this chunk's work
+          if (c + 1 < BN / 32) load_h(n0 + (c + 1) * 32, m0, hnext, hnext2);
           uint32_t r[32];
           tmem_ld_32x32b_x32(trow + (uint32_t)(c * 32), r);
           tmem_ld_wait();
           float v[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          store_chunk(v, n0 + c * 32, m0, hv);
+          store_chunk(v, n0 + c * 32, m0, hv, hv2);
         }
       } else {
         // stream-K part: add this part's fp32 block into the tile's accumulation
@@ -848,8 +904,8 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             for (int i = 0; i < 16; ++i) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);  // clean for the next GEMM
 #pragma unroll
             for (int h2 = 0; h2 < 2; ++h2) {
-              uint4 hv[4] = {};
-              if constexpr (EPI == kEpiGeluBwd) load_h(n0 + (c + h2) * 32, m0, hv);
+              uint4 hv[4] = {}, hv2[4] = {};
+              load_h(n0 + (c + h2) * 32, m0, hv, hv2);
               float v[32];
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
@@ -858,7 +914,7 @@ gemm_tn_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 v[4 * i + 2] = x[8 * h2 + i].z;
                 v[4 * i + 3] = x[8 * h2 + i].w;
               }
-              store_chunk(v, n0 + (c + h2) * 32, m0, hv);
+              store_chunk(v, n0 + (c + h2) * 32, m0, hv, hv2);
             }
           }
         }
@@ -1181,7 +1237,8 @@ void set_gemm_pair_mode(int64_t mode) { g_pair_mode = (int)mode; }
 static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
                       const c10::optional<at::Tensor>& a2, const c10::optional<at::Tensor>& b2,
                       bool b_mn = false, int epi = kEpiPlain, const at::Tensor* aux = nullptr,
-                      int64_t rope_ncols = -1) {
+                      int64_t rope_ncols = -1, const at::Tensor* aux2 = nullptr,
+                      const at::Tensor* c2 = nullptr) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: CUDA tensors");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 &&
                   c.scalar_type() == at::kBFloat16, "gemm: bf16 operands");
@@ -1249,7 +1306,9 @@ static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
   if (pair) {
     const CUtensorMap tc = make_tmap_store_bf16(c.data_ptr(), M, N, c.stride(0));
     const bool k128 = (K % 128) == 0;
-    if (epi != kEpiRope) setup_streamk(args, (int)(K / (k128 ? 128 : 64)), sms, dev, stream);
+    // (the SwiGLU epilogues take their shapes' many waves without a stream-K tail)
+    if (epi != kEpiRope && epi != kEpiSwigluFwd && epi != kEpiSwigluBwd)
+      setup_streamk(args, (int)(K / (k128 ? 128 : 64)), sms, dev, stream);
     if (epi == kEpiRope) {
       const at::Tensor& t = *aux;
       TORCH_CHECK(!b_mn && N % 128 == 0, "gemm: the RoPE epilogue needs [N, K] weights and 128-wide heads");
@@ -1264,12 +1323,37 @@ static void gemm_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& c,
       else launch_gemm_pair<128, 4, 2, false, false, false, kEpiRope>(ta, tb, ta2, tb2, tc, args, stream, sms);
       return;
     }
-    if (epi != kEpiPlain) {
-      const at::Tensor& x = *aux;
+    auto check_mn = [&](const at::Tensor& x) {
       TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.size(0) == M &&
                       x.size(1) == N && x.stride(1) == 1 && (x.stride(0) % 8) == 0 &&
                       (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0,
-                  "gemm: epilogue tensor must be bf16 [M, N], 16-byte aligned rows");
+                  "gemm: epilogue tensors must be bf16 [M, N], 16-byte aligned rows");
+    };
+    if (epi == kEpiSwigluFwd || epi == kEpiSwigluBwd) {
+      TORCH_CHECK(c2 != nullptr, "gemm: the SwiGLU epilogues need a second output");
+      check_mn(*aux);
+      check_mn(*c2);
+      args.epi_src = reinterpret_cast<const __nv_bfloat16*>(aux->data_ptr<at::BFloat16>());
+      args.epi_ld = aux->stride(0);
+      const CUtensorMap tc2 = make_tmap_store_bf16(c2->data_ptr(), M, N, c2->stride(0));
+      if (epi == kEpiSwigluFwd) {
+        TORCH_CHECK(!b_mn, "gemm: the SwiGLU-output epilogue is for the [N, K] weight layout");
+        if (bn == 256) launch_gemm_pair<256, 3, 2, false, false, false, kEpiSwigluFwd>(ta, tb, ta2, tb2, tc, args, stream, sms, &tc2);
+        else launch_gemm_pair<128, 4, 2, false, false, false, kEpiSwigluFwd>(ta, tb, ta2, tb2, tc, args, stream, sms, &tc2);
+      } else {
+        TORCH_CHECK(b_mn && aux2 != nullptr, "gemm: the SwiGLU-gradient epilogue is for the [K, N] "
+                    "weight layout and needs g and u");
+        check_mn(*aux2);
+        args.epi_src2 = reinterpret_cast<const __nv_bfloat16*>(aux2->data_ptr<at::BFloat16>());
+        args.epi_ld2 = aux2->stride(0);
+        if (bn == 256) launch_gemm_pair<256, 3, 2, true, false, false, kEpiSwigluBwd>(ta, tb, ta2, tb2, tc, args, stream, sms, &tc2);
+        else launch_gemm_pair<128, 4, 2, true, false, false, kEpiSwigluBwd>(ta, tb, ta2, tb2, tc, args, stream, sms, &tc2);
+      }
+      return;
+    }
+    if (epi != kEpiPlain) {
+      const at::Tensor& x = *aux;
+      check_mn(x);
       if (epi == kEpiGeluFwd) {
         TORCH_CHECK(!b_mn, "gemm: the GELU-output epilogue is for the [N, K] weight layout");
         const CUtensorMap tc2 = make_tmap_store_bf16(x.data_ptr(), M, N, x.stride(0));
@@ -1328,6 +1412,16 @@ void gemm_bf16_nn(at::Tensor a, at::Tensor b, at::Tensor c, c10::optional<at::Te
 void gemm_gelu(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor aux, bool b_mn,
                c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2) {
   gemm_impl(a, b, c, a2, b2, b_mn, b_mn ? kEpiGeluBwd : kEpiGeluFwd, &aux);
+}
+
+// GEMM with the SwiGLU epilogues (needs M >= 256 and K % 128 == 0):
+//   b_mn = false: c = U = A·Bᵀ (+ A2·B2ᵀ) and c2 = silu(g)·U   (u unused);
+//   b_mn = true:  D = A·B (+ A2·B2); c = D·u·silu'(g) (dg), c2 = D·silu(g) (du).
+void gemm_swiglu(at::Tensor a, at::Tensor b, at::Tensor c, at::Tensor c2, at::Tensor g,
+                 c10::optional<at::Tensor> u, bool b_mn, c10::optional<at::Tensor> a2,
+                 c10::optional<at::Tensor> b2) {
+  const at::Tensor* up = (u.has_value() && u->defined()) ? &*u : nullptr;
+  gemm_impl(a, b, c, a2, b2, b_mn, b_mn ? kEpiSwigluBwd : kEpiSwigluFwd, &g, -1, up, &c2);
 }
 
 // C = rope(A·Bᵀ (+ A2·B2ᵀ)) for 128-wide heads; cs: fp32 [S, 64, 2] (cos, sin) per
@@ -1441,7 +1535,8 @@ static void ag_gemm_impl(int kind, at::Tensor a, std::vector<int64_t> psrc, std:
                          std::vector<int64_t> asrc, std::vector<int64_t> astarts, int64_t packed_total,
                          int64_t absmax_total, int64_t rank, int64_t N, int64_t K, int64_t blocksize,
                          int64_t quant_type, at::Tensor wbuf, at::Tensor c, c10::optional<at::Tensor> a2,
-                         c10::optional<at::Tensor> b2) {
+                         c10::optional<at::Tensor> b2, const at::Tensor* swiglu_g = nullptr,
+                         const at::Tensor* swiglu_out = nullptr) {
   const int world = (int)psrc.size();
   TORCH_CHECK(world >= 1 && world <= kAgMaxRanks && (int)pstarts.size() == world &&
                   (int)asrc.size() == world && (int)astarts.size() == world,
@@ -1535,8 +1630,21 @@ static void ag_gemm_impl(int kind, at::Tensor a, std::vector<int64_t> psrc, std:
   }
   auto stream = at::cuda::getCurrentCUDAStream();
   args.ag_sync = ag_sync_buffer(dev, stream);
-  setup_streamk(args, (int)(K / 128), sms, dev, stream);
   const CUtensorMap tc = make_tmap_store_bf16(c.data_ptr(), M, N, c.stride(0));
+  if (swiglu_g != nullptr) {  // c = u, swiglu_out = silu(g)·u
+    for (const at::Tensor* x : {swiglu_g, swiglu_out})
+      TORCH_CHECK(x->scalar_type() == at::kBFloat16 && x->dim() == 2 && x->size(0) == M &&
+                      x->size(1) == N && x->stride(1) == 1 && (x->stride(0) % 8) == 0 &&
+                      (reinterpret_cast<uintptr_t>(x->data_ptr()) & 15) == 0,
+                  "ag_gemm_nf4: SwiGLU tensors must be bf16 [M, N], 16-byte aligned rows");
+    args.epi_src = reinterpret_cast<const __nv_bfloat16*>(swiglu_g->data_ptr<at::BFloat16>());
+    args.epi_ld = swiglu_g->stride(0);
+    const CUtensorMap tc2 = make_tmap_store_bf16(swiglu_out->data_ptr(), M, N, swiglu_out->stride(0));
+    if (bn == 256) launch_gemm_pair<256, 3, 2, false, false, true, kEpiSwigluFwd>(ta, tb, ta2, tb2, tc, args, stream, sms, &tc2);
+    else launch_gemm_pair<128, 4, 2, false, false, true, kEpiSwigluFwd>(ta, tb, ta2, tb2, tc, args, stream, sms, &tc2);
+    return;
+  }
+  setup_streamk(args, (int)(K / 128), sms, dev, stream);
   if (bn == 256) launch_gemm_pair<256, 3, 2, false, false, true>(ta, tb, ta2, tb2, tc, args, stream, sms);
   else launch_gemm_pair<128, 4, 2, false, false, true>(ta, tb, ta2, tb2, tc, args, stream, sms);
 }
@@ -1545,9 +1653,14 @@ void ag_gemm_nf4(at::Tensor a, std::vector<int64_t> psrc, std::vector<int64_t> p
                  std::vector<int64_t> asrc, std::vector<int64_t> astarts, int64_t packed_total,
                  int64_t absmax_total, int64_t rank, int64_t N, int64_t K, int64_t blocksize,
                  int64_t quant_type, at::Tensor wbuf, at::Tensor c, c10::optional<at::Tensor> a2,
-                 c10::optional<at::Tensor> b2) {
+                 c10::optional<at::Tensor> b2, c10::optional<at::Tensor> swiglu_g,
+                 c10::optional<at::Tensor> swiglu_out) {
+  const bool sw = swiglu_g.has_value() && swiglu_g->defined();
+  TORCH_CHECK(!sw || (swiglu_out.has_value() && swiglu_out->defined()),
+              "ag_gemm_nf4: the SwiGLU epilogue needs g and an output");
   ag_gemm_impl(kAgNf4, a, psrc, pstarts, asrc, astarts, packed_total, absmax_total, rank, N, K,
-               blocksize, quant_type, wbuf, c, a2, b2);
+               blocksize, quant_type, wbuf, c, a2, b2, sw ? &*swiglu_g : nullptr,
+               sw ? &*swiglu_out : nullptr);
 }
 
 // The same with W [N, K] held as fp32 pieces (flat elements [starts[q],

@@ -322,6 +322,45 @@ def test_gelu_mlp_split_form_matches_plain_form_on_cpu():
         up.lora_A.grad = None
 
 
+def test_swiglu_mlp_split_form_matches_plain_form_on_cpu():
+    """The split SwiGLU MLP (up returns u and a non-differentiable silu(g)·u, down
+    takes the gradients through g and u) gives the plain form's values and
+    gradients off the fused path, including with a full-precision down weight."""
+    from zeroq_b200.ops.activations import swiglu
+    from zeroq_b200.ops.qlinear import Linear4bit
+
+    torch.manual_seed(2)
+    gate = Linear4bit(64, 96, lora_r=4, backend="torch", device="cpu")
+    up = Linear4bit(64, 96, lora_r=4, backend="torch", device="cpu")
+    down = Linear4bit(96, 64, lora_r=4, backend="torch", device="cpu")
+    for m, shape in ((gate, (96, 64)), (up, (96, 64)), (down, (64, 96))):
+        m.quantize_from(torch.randn(*shape) * 0.05)
+        with torch.no_grad():
+            m.lora_B.normal_(0, 0.05)
+    x = torch.randn(3, 7, 64, requires_grad=True)
+    for full_precision_down in (False, True):
+        if full_precision_down:
+            w = down.dequantized_weight()
+            down.clear_nf4()
+            down.weight = torch.nn.Parameter(w, requires_grad=False)
+        x.grad = None
+        g = gate(x)
+        u, a = up(x, act_out="swiglu", gate=g)
+        assert not a.requires_grad
+        y = down(a, pre=(g, u))
+        y.square().sum().backward()
+        g1, gA1, uA1 = x.grad.clone(), gate.lora_A.grad.clone(), up.lora_A.grad.clone()
+        x.grad = None
+        gate.lora_A.grad = up.lora_A.grad = None
+        y2 = down(swiglu(gate(x), up(x)))
+        y2.square().sum().backward()
+        torch.testing.assert_close(y, y2, rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(g1, x.grad, rtol=1e-4, atol=1e-6)
+        torch.testing.assert_close(gA1, gate.lora_A.grad, rtol=1e-4, atol=1e-6)
+        torch.testing.assert_close(uA1, up.lora_A.grad, rtol=1e-4, atol=1e-6)
+        gate.lora_A.grad = up.lora_A.grad = None
+
+
 def test_linear4bit_rope_argument_matches_apply_rope_on_cpu():
     """Off the fused path (CPU) the rope= argument rotates the projection's output
     like apply_rope, values and input gradients."""

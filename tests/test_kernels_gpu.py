@@ -750,6 +750,141 @@ def test_fused_gelu_mlp_matches_unfused(cuda, lora_r):
         torch.testing.assert_close(g1, g2, rtol=1e-4, atol=1e-5)
 
 
+@pytest.mark.parametrize("M,K,N", [(512, 384, 1024), (300, 1536, 640), (2048, 3584, 4736)])
+@pytest.mark.parametrize("extra", [False, True])
+def test_gemm_swiglu_epilogues_match_separate_kernels(cuda, M, K, N, extra):
+    """SwiGLU-output epilogue (u and silu(g)·u from the up-projection GEMM) and
+    SwiGLU-gradient epilogue (dg, du from the down-projection's input-gradient
+    GEMM) against the plain GEMMs followed by the SwiGLU kernels (bit-identical:
+    the epilogues round the accumulator to bf16 first) and against fp32 torch."""
+    E = _ext.ext()
+    torch.manual_seed(15)
+    x = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=cuda) * 0.05).to(torch.bfloat16)
+    g = (torch.randn(M, N, device=cuda) * 2).to(torch.bfloat16)
+    a2 = b2 = None
+    if extra:
+        a2 = (torch.randn(M, 64, device=cuda) * 0.1).to(torch.bfloat16)
+        b2 = (torch.randn(N, 64, device=cuda) * 0.1).to(torch.bfloat16)
+    u = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    act = torch.empty_like(u)
+    E.gemm_swiglu(x, w, u, act, g, None, False, a2, b2)
+    u_ref = torch.empty_like(u)
+    if extra:
+        E.gemm_bf16_tn_extra(x, w, u_ref, a2, b2)
+    else:
+        E.gemm_bf16_tn(x, w, u_ref)
+    act_ref = torch.empty_like(u)
+    E.swiglu_fwd(g, u_ref, act_ref)
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    assert torch.equal(u, u_ref) and torch.equal(act, act_ref)
+    want = torch.nn.functional.silu(g.float()) * u_ref.float()
+    torch.testing.assert_close(act.float(), want, rtol=1e-2, atol=1e-2)
+    # backward: D = dY [M, K'] · Wd [K', N]; dg = D·u·silu'(g), du = D·silu(g)
+    gy = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    wd = (torch.randn(K, N, device=cuda) * 0.05).to(torch.bfloat16)
+    a3 = b3 = None
+    if extra:
+        a3 = (torch.randn(M, 64, device=cuda) * 0.1).to(torch.bfloat16)
+        b3 = (torch.randn(64, N, device=cuda) * 0.1).to(torch.bfloat16)
+    dg = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    du = torch.empty_like(dg)
+    E.gemm_swiglu(gy, wd, dg, du, g, u_ref, True, a3, b3)
+    d = torch.empty_like(dg)
+    E.gemm_bf16_nn(gy, wd, d, a3, b3)
+    dg_ref, du_ref = torch.empty_like(dg), torch.empty_like(dg)
+    E.swiglu_bwd(d, g, u_ref, dg_ref, du_ref)
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    assert torch.equal(dg, dg_ref), (dg.float() - dg_ref.float()).abs().max().item()
+    assert torch.equal(du, du_ref), (du.float() - du_ref.float()).abs().max().item()
+    gf, uf, df = g.float(), u_ref.float(), d.float()
+    sg = torch.sigmoid(gf)
+    torch.testing.assert_close(du.float(), df * gf * sg, rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(dg.float(), df * uf * sg * (1 + gf * (1 - sg)), rtol=1e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("lora_r", [0, 16])
+def test_fused_swiglu_mlp_matches_unfused(cuda, lora_r):
+    """gate(x); up(x, act_out='swiglu', gate=g); down(f, pre=(g, u)) equals
+    swiglu between plain NF4 layers, values and gradients (input and LoRA)."""
+    from zeroq_b200.ops.activations import swiglu
+    from zeroq_b200.ops.qlinear import Linear4bit
+
+    torch.manual_seed(16)
+    d, f = 512, 1408
+    gate = Linear4bit(d, f, lora_r=lora_r, device=cuda)
+    up = Linear4bit(d, f, lora_r=lora_r, device=cuda)
+    down = Linear4bit(f, d, lora_r=lora_r, device=cuda)
+    for m, shape in ((gate, (f, d)), (up, (f, d)), (down, (d, f))):
+        m.quantize_from(torch.randn(*shape, device=cuda) * 0.03)
+        if lora_r:
+            with torch.no_grad():
+                m.lora_B.normal_(0, 0.02)
+    mods = (gate, up, down)
+    x = (torch.randn(2, 200, d, device=cuda)).to(torch.bfloat16).requires_grad_(True)
+    g = gate(x)
+    u, a = up(x, act_out="swiglu", gate=g)
+    assert not a.requires_grad
+    y = down(a, pre=(g, u))
+    (y.float() ** 2).sum().backward()
+
+    def take():
+        out = [x.grad.clone()]
+        for m in mods:
+            if lora_r:
+                out += [m.lora_A.grad.clone(), m.lora_B.grad.clone()]
+                m.lora_A.grad = m.lora_B.grad = None
+        x.grad = None
+        return out
+
+    grads = take()
+    y2 = down(swiglu(gate(x), up(x)))
+    (y2.float() ** 2).sum().backward()
+    grads2 = take()
+    torch.cuda.synchronize()
+    _status_ok(cuda)
+    assert torch.equal(y, y2)
+    torch.testing.assert_close(grads[0], grads2[0], rtol=1e-2, atol=1e-3)  # summed in another order
+    for g1, g2 in zip(grads[1:], grads2[1:]):  # LoRA grads: atomic fp32 sums, no fixed order
+        torch.testing.assert_close(g1, g2, rtol=1e-3, atol=1e-5)
+
+
+def test_ag_gemm_swiglu_epilogue_matches_separate_kernels(cuda):
+    """The gather-mode GEMM with the SwiGLU-output epilogue (u and silu(g)·u, the
+    weight assembled from pieces inside the kernel) against the plain GEMM on the
+    dequantised weight and the SwiGLU kernel, for every rank's tile rotation."""
+    from zeroq_b200.parallel.peer import ag_gemm_pieces
+
+    torch.manual_seed(17)
+    M, N, K = 512, 1408, 512
+    W = torch.randn(N, K, device=cuda) * 0.02
+    packed, st = quantize_4bit(W, 64, "nf4")
+    packed, absmax = packed.reshape(-1), st.absmax.reshape(-1)
+    pst = [0, packed.numel() // 3 + 1, 2 * packed.numel() // 3]
+    ast = [0, absmax.numel() // 3, 2 * absmax.numel() // 3]
+    ppieces, pptrs = _split_pieces(packed, pst)
+    apieces, aptrs = _split_pieces(absmax, ast)
+    full = torch.empty(N * K, dtype=torch.bfloat16, device=cuda)
+    _ext.ext().nf4_to_bf16(packed, absmax, full, N, K, 64, 0, False)
+    x = torch.randn(M, K, device=cuda).to(torch.bfloat16)
+    g = (torch.randn(M, N, device=cuda) * 2).to(torch.bfloat16)
+    ex = ((torch.randn(M, 64, device=cuda) * 0.1).to(torch.bfloat16),
+          (torch.randn(N, 64, device=cuda) * 0.1).to(torch.bfloat16))
+    u_ref = torch.empty(M, N, dtype=torch.bfloat16, device=cuda)
+    _ext.ext().gemm_bf16_tn_extra(x, full.view(N, K), u_ref, ex[0], ex[1])
+    act_ref = torch.empty_like(u_ref)
+    _ext.ext().swiglu_fwd(g, u_ref, act_ref)
+    for rank in range(3):
+        act = torch.empty_like(u_ref)
+        u, _ = ag_gemm_pieces(x, pptrs, pst, aptrs, ast, N, K, 64, "nf4", rank=rank, extra=ex,
+                              swiglu=(g, act))
+        torch.cuda.synchronize()
+        _status_ok(cuda)
+        assert torch.equal(u, u_ref) and torch.equal(act, act_ref), rank
+
+
 @pytest.mark.parametrize("M,N,K,starts_frac", [
     (512, 384, 512, [0.0, 0.5]),
     (768, 1000, 1536, [0.0, 0.3, 0.31, 0.8]),   # uneven pieces, odd element starts

@@ -25,6 +25,7 @@ zero and the loss ignores the padded columns.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import asdict, dataclass, field, replace
 from typing import Optional, Tuple
 
@@ -138,6 +139,11 @@ class RMSNorm(nn.Module):
         return add_rmsnorm(h, delta, self.weight, self.eps)
 
 
+# ZEROQ_FUSED_MLP=0 keeps the activation kernels between the MLP projections
+# (the split forms with GEMM-epilogue activations are the default)
+_FUSED_MLP = os.environ.get("ZEROQ_FUSED_MLP", "1") != "0"
+
+
 def _hooked(m: nn.Module) -> bool:
     return bool(m._forward_hooks or m._forward_pre_hooks or m._backward_hooks
                 or m._backward_pre_hooks)
@@ -214,6 +220,12 @@ class DecoderLayer(nn.Module):
         a = self.o_proj(o.view(B, S, cfg.n_heads * cfg.head_dim))
         h, x = self.mlp_norm(h, a)
         if self.gate_proj is not None:
+            if self._fused_mlp(with_gate=True):
+                # up-projection epilogue writes u and silu(g)·u; the down-projection's
+                # input-gradient epilogue writes dg and du: no SwiGLU kernels
+                g = self.gate_proj(x)
+                u, f = self.up_proj(x, act_out="swiglu", gate=g)
+                return h, self.down_proj(f, pre=(g, u))
             f = swiglu(self.gate_proj(x), self.up_proj(x))
         elif self._fused_gelu_mlp():
             # up-projection epilogue writes h and gelu(h); the down-projection's
@@ -232,13 +244,18 @@ class DecoderLayer(nn.Module):
                 and all(isinstance(m, Linear4bit) for m in mods)
                 and not any(_hooked(m) for m in mods))
 
-    def _fused_gelu_mlp(self) -> bool:
+    def _fused_mlp(self, with_gate: bool = False) -> bool:
+        """The MLP's projections are all ``Linear4bit`` without module hooks (the
+        split activation forms pass the pre-activations as keyword arguments and
+        return a non-differentiable activation, which per-module hooks do not see)."""
         from ..ops.qlinear import Linear4bit
 
-        mods = (self.up_proj, self.down_proj)
-        return (all(isinstance(m, Linear4bit) for m in mods)
-                and not any(m._forward_hooks or m._forward_pre_hooks or m._backward_hooks
-                            or m._backward_pre_hooks for m in mods))
+        mods = (self.up_proj, self.down_proj) + ((self.gate_proj,) if with_gate else ())
+        return (_FUSED_MLP and all(isinstance(m, Linear4bit) for m in mods)
+                and not any(_hooked(m) for m in mods))
+
+    def _fused_gelu_mlp(self) -> bool:
+        return self._fused_mlp()
 
 
 class DecoderLM(nn.Module):

@@ -125,6 +125,17 @@ class NF4LinearFunction(torch.autograd.Function):
       ``gelu'(h)``, so the gradient of ``gelu(h)`` is never stored.
     Off the fused path both fall back to the GELU kernels with the same results.
 
+    SwiGLU MLP fusion (``act_out="swiglu"`` with ``gate`` / ``pre`` with ``pre_u``):
+
+    * the up-projection with ``act_out="swiglu", gate=g`` returns ``(u, silu(g)·u)``:
+      its GEMM epilogue reads ``g`` and writes both; ``silu(g)·u`` carries no
+      gradient of its own (nor does ``gate`` through this function);
+    * the down-projection with ``pre=g, pre_u=u``: ``x`` is ``silu(g)·u`` and the
+      gradients are returned for ``g`` and ``u`` - the input-gradient GEMM's
+      epilogue writes ``dg`` and ``du`` and the gradient of the activation is
+      never stored.
+    Off the fused path both fall back to the SwiGLU kernels with the same results.
+
     ``rope=cs`` (a ``[S, D/2, 2]`` cos/sin table, D = 128): the output is returned
     rotary-embedded (row m at position m % S); the GEMM epilogue applies the
     rotation, and the backward un-rotates the incoming gradient first.
@@ -132,7 +143,8 @@ class NF4LinearFunction(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, x, packed, absmax, lora_A, lora_B, bias, N, K, blocksize, quant_type,
-                scaling, backend, lora_ops=None, peer=None, act_out=None, pre=None, rope=None):
+                scaling, backend, lora_ops=None, peer=None, act_out=None, pre=None, rope=None,
+                pre_u=None, gate=None):
         shp = x.shape
         x2 = x.reshape(-1, K)
         if not x2.is_contiguous():
@@ -167,8 +179,15 @@ class NF4LinearFunction(torch.autograd.Function):
             from .rope import rope_table_of
 
             rope_cs = rope_table_of(rope)
-        if act_out not in (None, "gelu"):
+        if act_out not in (None, "gelu", "swiglu"):
             raise ValueError(f"unsupported fused activation {act_out!r}")
+        gate2 = None
+        if act_out == "swiglu":
+            if gate is None:
+                raise ValueError('act_out="swiglu" needs the gate projection\'s output')
+            gate2 = gate.reshape(-1, N)
+            if not gate2.is_contiguous():
+                gate2 = gate2.contiguous()
         if fused:
             E = _ext.ext()
             y = torch.empty(M, N, dtype=x2.dtype, device=x2.device)
@@ -179,8 +198,12 @@ class NF4LinearFunction(torch.autograd.Function):
                 # U [M, 64] (zero past the rank) for the GEMM slab, Ut [r16, M] for dB
                 U, Ut = lora_k.down(x2, a_pad[:lora_k.round16(r)])
             if peer_fused:
+                sw = None
+                if act_out == "swiglu" and bias is None and gate2.dtype == torch.bfloat16:
+                    act = torch.empty_like(y)
+                    sw = (gate2, act)
                 _, wbuf = peer[0].ag_gemm(peer[1], x2, out=y,
-                                          extra=(U, b_pad) if has_lora else None)
+                                          extra=(U, b_pad) if has_lora else None, swiglu=sw)
                 del wbuf
             elif (rope is not None and bias is None and _epi_ok(M, K) and N % 128 == 0
                   and rope_cs.shape[1] == 64 and M % rope_cs.shape[0] == 0
@@ -193,6 +216,12 @@ class NF4LinearFunction(torch.autograd.Function):
                 w = operand()
                 act = torch.empty_like(y)
                 E.gemm_gelu(x2, w, y, act, False, U, b_pad)
+                del w
+            elif (act_out == "swiglu" and bias is None and _epi_ok(M, K)
+                  and gate2.dtype == torch.bfloat16 and not _in_kernel_ok(M, K, N)):
+                w = operand()
+                act = torch.empty_like(y)
+                E.gemm_swiglu(x2, w, y, act, gate2, None, False, U, b_pad)
                 del w
             elif _in_kernel_ok(M, K, N) and w_peer is None:
                 E.gemm_nf4(x2, packed, absmax, N, K, blocksize, QUANT_TYPE_ID[quant_type], False, y,
@@ -220,20 +249,24 @@ class NF4LinearFunction(torch.autograd.Function):
         ctx.rope = rope
         if peer is not None:
             packed = absmax = None  # re-read from the owners in backward
-        pre2 = None
+        pre2 = preu2 = None
         if pre is not None:
             pre2 = pre.reshape(-1, K)
             if not pre2.is_contiguous():
                 pre2 = pre2.contiguous()
+        if pre_u is not None:
+            preu2 = pre_u.reshape(-1, K)
+            if not preu2.is_contiguous():
+                preu2 = preu2.contiguous()
         # fused path: the transposed rank-space product is what the backward reads
         ctx.save_for_backward(x2 if has_lora else None, packed, absmax, lora_A, lora_B,
-                              Ut if fused else U, a_pad, b_pad, b_t, pre2)
+                              Ut if fused else U, a_pad, b_pad, b_t, pre2, preu2)
         ctx.meta = (shp, N, K, blocksize, quant_type, scaling, fused, bias is not None, has_lora, r)
         ctx.peer = peer
         y = y.view(*shp[:-1], N)
-        if act_out == "gelu":
+        if act_out in ("gelu", "swiglu"):
             if act is None:
-                act = _gelu_kernel(y)
+                act = _gelu_kernel(y) if act_out == "gelu" else _swiglu_kernel(gate2, y.view(-1, N))
             act = act.view(*shp[:-1], N)
             ctx.mark_non_differentiable(act)
             # no zero-filled gradient for gelu(h) (it never has one): saves a
@@ -245,8 +278,9 @@ class NF4LinearFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, gy, g_act=None):
         if gy is None:  # (grads are not materialised for the act_out form)
-            return (None,) * 17
-        x2, packed, absmax, lora_A, lora_B, U, a_pad, b_pad, b_t, pre2 = ctx.saved_tensors
+            return (None,) * 19
+        x2, packed, absmax, lora_A, lora_B, U, a_pad, b_pad, b_t, pre2, preu2 = ctx.saved_tensors
+        swiglu_in = preu2 is not None
         shp, N, K, blocksize, quant_type, scaling, fused, has_bias, has_lora, r = ctx.meta
         gy2 = gy.reshape(-1, N)
         if not gy2.is_contiguous():
@@ -258,14 +292,19 @@ class NF4LinearFunction(torch.autograd.Function):
                 gy2 = rope_rows(gy2, rope_table_of(ctx.rope), -1.0)
         M = gy2.shape[0]
         gx = gA = gB = gbias = None
-        # with pre=h the input gradient is taken for h (through gelu'(h))
-        want_gx = ctx.needs_input_grad[15] if pre2 is not None else ctx.needs_input_grad[0]
+        # with pre=h the input gradient is taken for h (through gelu'(h)); with
+        # pre=g, pre_u=u for g and u (through the SwiGLU derivative)
+        if swiglu_in:
+            want_gx = ctx.needs_input_grad[15] or ctx.needs_input_grad[17]
+        else:
+            want_gx = ctx.needs_input_grad[15] if pre2 is not None else ctx.needs_input_grad[0]
         peer = ctx.peer
         peer_operand = (peer is not None and fused and M >= 256 and want_gx
                         and not _in_kernel_ok(M, N, K))
         if peer is not None and not peer_operand and want_gx:
             packed, absmax = peer[0].gather(peer[1]).wait()
         gelu_done = False
+        g_swiglu = None   # (dg, du) from the SwiGLU-gradient epilogue
         if fused:
             E = _ext.ext()
             gy2 = gy2.to(torch.bfloat16)
@@ -289,14 +328,22 @@ class NF4LinearFunction(torch.autograd.Function):
                 V, Vt = res
             if want_gx:
                 gx = torch.empty(M, K, dtype=torch.bfloat16, device=gy2.device)
-                if pre2 is not None and _epi_ok(M, N) and not _in_kernel_ok(M, N, K):
-                    # dH = (dY·W + V·(s·A)) * gelu'(H) in the GEMM epilogue
+                if (pre2 is not None and _epi_ok(M, N) and not _in_kernel_ok(M, N, K)
+                        and pre2.dtype == torch.bfloat16
+                        and (not swiglu_in or preu2.dtype == torch.bfloat16)):
                     if peer_operand:
                         w = peer[0].gather_dequant(peer[1], N, K)
                     else:
                         w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
-                    E.gemm_gelu(gy2, w, gx, pre2, True, V, a_pad)
-                    gelu_done = True
+                    if swiglu_in:
+                        # D = dY·W + V·(s·A); dg = D·u·silu'(g), du = D·silu(g) in the epilogue
+                        du = torch.empty_like(gx)
+                        E.gemm_swiglu(gy2, w, gx, du, pre2, preu2, True, V, a_pad)
+                        g_swiglu = (gx.view(*shp[:-1], K), du.view(*shp[:-1], K))
+                    else:
+                        # dH = (dY·W + V·(s·A)) * gelu'(H) in the GEMM epilogue
+                        E.gemm_gelu(gy2, w, gx, pre2, True, V, a_pad)
+                        gelu_done = True
                     del w
                 elif _in_kernel_ok(M, N, K):  # dX = dY·W + V·(s·A), W decoded in the kernel
                     E.gemm_nf4(gy2, packed, absmax, N, K, blocksize, QUANT_TYPE_ID[quant_type],
@@ -350,14 +397,22 @@ class NF4LinearFunction(torch.autograd.Function):
                     gB = (gy2.float().t() @ U.float()).to(lora_B.dtype)
         if has_bias and ctx.needs_input_grad[5]:
             gbias = gy2.float().sum(0)
+        if swiglu_in:
+            dg = du = None
+            if gx is not None:
+                if g_swiglu is None:
+                    g_swiglu = _swiglu_grad_kernel(gx, pre2.view(gx.shape), preu2.view(gx.shape))
+                dg, du = g_swiglu
+            return (None, None, None, gA, gB, gbias, None, None, None, None, None, None, None,
+                    None, None, dg, None, du, None)
         if pre2 is not None:
             g_pre = None
             if gx is not None:
                 g_pre = gx if gelu_done else _gelu_grad_kernel(gx, pre2.view(gx.shape))
             return (None, None, None, gA, gB, gbias, None, None, None, None, None, None, None,
-                    None, None, g_pre, None)
+                    None, None, g_pre, None, None, None)
         return (gx, None, None, gA, gB, gbias, None, None, None, None, None, None, None, None,
-                None, None, None)
+                None, None, None, None, None)
 
 
 def _epi_ok(M: int, K: int) -> bool:
@@ -370,6 +425,28 @@ def _gelu_kernel(h: torch.Tensor) -> torch.Tensor:
 
     with torch.no_grad():
         return gelu(h)
+
+
+def _swiglu_kernel(g: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    """``silu(g)·u`` with no autograd graph (the standalone SwiGLU kernel on CUDA)."""
+    with torch.no_grad():
+        if g.is_cuda and g.dtype == torch.bfloat16 and u.dtype == torch.bfloat16:
+            out = torch.empty_like(u)
+            _ext.ext().swiglu_fwd(g.contiguous(), u.contiguous(), out)
+            return out
+        return (torch.nn.functional.silu(g.float()) * u.float()).to(u.dtype)
+
+
+def _swiglu_grad_kernel(d: torch.Tensor, g: torch.Tensor, u: torch.Tensor):
+    """``(d·u·silu'(g), d·silu(g))``: the gradients of ``silu(g)·u`` for ``g`` and ``u``."""
+    if d.is_cuda and d.dtype == torch.bfloat16 and g.dtype == torch.bfloat16:
+        dg = torch.empty_like(g)
+        du = torch.empty_like(u)
+        _ext.ext().swiglu_bwd(d.contiguous(), g.contiguous(), u.contiguous(), dg, du)
+        return dg, du
+    gf, uf, df = g.float(), u.float(), d.float()
+    sg = torch.sigmoid(gf)
+    return ((df * uf * sg * (1.0 + gf * (1.0 - sg))).to(g.dtype), (df * gf * sg).to(u.dtype))
 
 
 def _gelu_grad_kernel(g: torch.Tensor, h: torch.Tensor) -> torch.Tensor:
@@ -472,12 +549,12 @@ def _pack_lora(A: torch.Tensor, B: torch.Tensor, scaling: float, out=None):
 def nf4_linear(x, packed, absmax, out_features: int, in_features: int, bias=None,
                lora_A=None, lora_B=None, scaling: float = 1.0, blocksize: int = 64,
                quant_type: str = "nf4", backend: str = "auto", lora_ops=None, peer=None,
-               act_out=None, pre=None, rope=None):
+               act_out=None, pre=None, rope=None, pre_u=None, gate=None):
     if backend == "auto":
         backend = "fused" if x.is_cuda else "torch"
     return NF4LinearFunction.apply(x, packed, absmax, lora_A, lora_B, bias, out_features,
                                    in_features, blocksize, quant_type, scaling, backend, lora_ops,
-                                   peer, act_out, pre, rope)
+                                   peer, act_out, pre, rope, pre_u, gate)
 
 
 class Linear4bit(nn.Module):
@@ -611,12 +688,18 @@ class Linear4bit(nn.Module):
 
     # -- forward -------------------------------------------------------------
     def forward(self, x: torch.Tensor, act_out: Optional[str] = None,
-                pre: Optional[torch.Tensor] = None, rope=None):
+                pre=None, rope=None, gate: Optional[torch.Tensor] = None):
         """``act_out="gelu"``: return ``(y, gelu(y))`` with ``gelu(y)`` carrying no
         gradient of its own; ``pre=h``: ``x`` is ``gelu(h)`` and the gradient goes to
-        ``h`` (the two halves of a GELU MLP; see :class:`NF4LinearFunction`);
+        ``h`` (the two halves of a GELU MLP; see :class:`NF4LinearFunction`).
+        ``act_out="swiglu", gate=g``: return ``(y, silu(g)·y)``, the second carrying
+        no gradient; ``pre=(g, u)``: ``x`` is ``silu(g)·u`` and the gradients go to
+        ``g`` and ``u`` (the SwiGLU MLP).
         ``rope``: a cos/sin table or a :class:`~zeroq_b200.ops.rope.RopeSpec` - return
         the output rotary-embedded."""
+        pre_u = None
+        if isinstance(pre, tuple):
+            pre, pre_u = pre
         master = getattr(self, "_master", None)
         if master is not None:
             pool, zq = master
@@ -631,15 +714,16 @@ class Linear4bit(nn.Module):
             ops = self._lora_operands() if (self.lora_r and x.is_cuda) else None
             return nf4_linear(x, None, None, self.out_features, self.in_features, self.bias,
                               self.lora_A, self.lora_B, self.scaling, self.blocksize,
-                              self.quant_type, self.backend, ops, peer, act_out, pre, rope)
+                              self.quant_type, self.backend, ops, peer, act_out, pre, rope,
+                              pre_u, gate)
         if self.weight_packed is None:
             if self.weight.numel() == 0:
                 raise RuntimeError("Linear4bit has no weight: neither NF4 data nor a "
                                    "gathered full-precision weight is present")
-            if pre is not None:  # same gradient path as the fused form: through h
-                from .activations import gelu
+            if pre is not None:  # same gradient path as the fused form: through h (g, u)
+                from .activations import gelu, swiglu
 
-                x = gelu(pre)
+                x = swiglu(pre, pre_u) if pre_u is not None else gelu(pre)
             y = torch.nn.functional.linear(x, self.weight.to(x.dtype),
                                            None if self.bias is None else self.bias.to(x.dtype))
             if self.lora_r:
@@ -650,12 +734,14 @@ class Linear4bit(nn.Module):
                 y = rope_rows_autograd(y.reshape(-1, y.shape[-1]), rope).view(y.shape)
             if act_out == "gelu":
                 return y, _gelu_kernel(y.detach())
+            if act_out == "swiglu":
+                return y, _swiglu_kernel(gate.detach(), y.detach())
             return y
         ops = self._lora_operands() if (self.lora_r and x.is_cuda) else None
         return nf4_linear(x, self.weight_packed, self.weight_absmax, self.out_features,
                           self.in_features, self.bias, self.lora_A, self.lora_B,
                           self.scaling, self.blocksize, self.quant_type, self.backend, ops,
-                          None, act_out, pre, rope)
+                          None, act_out, pre, rope, pre_u, gate)
 
     def extra_repr(self) -> str:
         return (f"in_features={self.in_features}, out_features={self.out_features}, "

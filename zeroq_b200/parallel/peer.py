@@ -194,7 +194,7 @@ def ag_gemm_pieces(x: torch.Tensor, packed_ptrs: List[int], packed_starts: List[
                    absmax_ptrs: List[int], absmax_starts: List[int], N: int, K: int,
                    blocksize: int, quant_type: str = "nf4", rank: int = 0,
                    out: Optional[torch.Tensor] = None, wbuf: Optional[torch.Tensor] = None,
-                   extra: Optional[tuple] = None):
+                   extra: Optional[tuple] = None, swiglu: Optional[tuple] = None):
     """``y [M, N] = x [M, K] · Wᵀ`` for a 4-bit ``W [N, K]`` whose flat packed
     bytes and absmax are split into per-rank pieces (piece ``q`` starts at flat
     index ``*_starts[q]`` and lives at device address ``*_ptrs[q]``: local memory
@@ -205,8 +205,10 @@ def ag_gemm_pieces(x: torch.Tensor, packed_ptrs: List[int], packed_starts: List[
     ``wbuf`` (bf16 ``[N, K]``) and publish a per-N-tile counter; the TMA producer
     loads an N tile's B once its counter is full, and each rank starts on the N
     tiles of its own rows.  ``extra = (x2 [M, 64], w2 [N, 64])`` adds the 64-wide
-    K slab of the LoRA up-projection.  Returns ``(y, wbuf)``; ``wbuf`` holds the
-    assembled bf16 weight afterwards.  Needs :func:`ag_gemm_ok`.
+    K slab of the LoRA up-projection.  ``swiglu = (g [M, N], act [M, N])``: the
+    epilogue also writes ``act = silu(g)·y`` (the up-projection of a SwiGLU MLP).
+    Returns ``(y, wbuf)``; ``wbuf`` holds the assembled bf16 weight afterwards.
+    Needs :func:`ag_gemm_ok`.
     """
     from ..ops.nf4 import QUANT_TYPE_ID
 
@@ -218,10 +220,11 @@ def ag_gemm_pieces(x: torch.Tensor, packed_ptrs: List[int], packed_starts: List[
     if wbuf is None:
         wbuf = torch.empty(N, K, dtype=torch.bfloat16, device=x.device)
     a2, b2 = extra if extra is not None else (None, None)
+    sg, sa = swiglu if swiglu is not None else (None, None)
     _ext.ext().ag_gemm_nf4(x, [int(p) for p in packed_ptrs], [int(v) for v in packed_starts],
                            [int(p) for p in absmax_ptrs], [int(v) for v in absmax_starts],
                            N * K // 2, -(-N * K // blocksize), int(rank), int(N), int(K),
-                           int(blocksize), QUANT_TYPE_ID[quant_type], wbuf, out, a2, b2)
+                           int(blocksize), QUANT_TYPE_ID[quant_type], wbuf, out, a2, b2, sg, sa)
     return out, wbuf
 
 
@@ -331,9 +334,11 @@ class PeerShardPool:
         return out.view(cols, rows) if transpose else out.view(rows, cols)
 
     def ag_gemm(self, zq, x: torch.Tensor, out: Optional[torch.Tensor] = None,
-                wbuf: Optional[torch.Tensor] = None, extra: Optional[tuple] = None):
+                wbuf: Optional[torch.Tensor] = None, extra: Optional[tuple] = None,
+                swiglu: Optional[tuple] = None):
         """``x Wᵀ`` with ``W`` read from the owners' NF4 shards inside the GEMM
-        kernel (:func:`ag_gemm_pieces`); returns ``(y, wbuf)``."""
+        kernel (:func:`ag_gemm_pieces`, SwiGLU epilogue with ``swiglu``); returns
+        ``(y, wbuf)``."""
         from ..utils.metrics import count
         from .comm import remote_nf4_bytes
 
@@ -344,7 +349,7 @@ class PeerShardPool:
         m = zq._quant_meta
         return ag_gemm_pieces(x, psrc, list(zq.packed_plan.offsets), asrc,
                               list(zq.absmax_plan.offsets), N, K, int(m["blocksize"]),
-                              m["quant_type"], self.rank, out, wbuf, extra)
+                              m["quant_type"], self.rank, out, wbuf, extra, swiglu)
 
     def sync_after_update(self):
         """Barrier after shards were re-quantised in place (training mode)."""
