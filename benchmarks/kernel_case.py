@@ -86,7 +86,7 @@ def _report(name, ms, byts=None, flops=None, extra=""):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["gemm", "attention", "attn_trace", "attn_bwd_trace",
+    ap.add_argument("case", choices=["gemm", "attention", "attn_trace", "attn2_trace", "attn_bwd_trace",
                                      "nf4_operand", "rmsnorm", "gelu", "q4gemm", "gelu_gemm",
                                      "ag_gemm", "lora"])
     ap.add_argument("--m", type=int, default=8192)
@@ -247,6 +247,45 @@ def main():
                 print(f"  tile {j} (us from S ready): " + ", ".join(row) + f"; next S ready +{nxt:.3f}")
         last_end = t[:, 30]
         print(f"  CTA duration mean {((last_end - t[:, 0]) / 1e3).mean():.2f} us")
+    elif a.case == "attn2_trace":
+        # per-CTA timeline of the two-query-tile forward (S a multiple of 256)
+        q = torch.randn(a.b, a.s, a.h, a.d, device=dev, dtype=torch.bfloat16)
+        k, v = torch.randn_like(q), torch.randn_like(q)
+        o = torch.empty_like(q)
+        lse = torch.empty(a.b, a.h, a.s, device=dev)
+        grid = a.b * a.h * (a.s // 256)
+        tr = torch.zeros(grid, 32, dtype=torch.int64, device=dev)
+        scale = a.d ** -0.5
+        for _ in range(3):
+            E.attn_fwd_tc(q, k, v, o, lse, True, scale)
+        torch.cuda.synchronize()
+        ms = _time(lambda: E.attn_fwd_tc(q, k, v, o, lse, True, scale), a.reps)
+        _report("attn_fwd_tc (two query tiles)", ms, flops=4.0 * a.b * a.h * a.s * a.s * a.d / 2)
+        E.attn_fwd_tc(q, k, v, o, lse, True, scale, tr)
+        torch.cuda.synchronize()
+        t = tr.cpu().double()
+        n = t[:, 31].long()
+        print(f"attn2 trace B={a.b} S={a.s} H={a.h}: kernel span "
+              f"{(t[:, 30].max() - t[:, 0].min()) / 1e3:.1f} us over {grid} CTAs")
+        base = t[n >= 4]
+        names = ["in registers", "row max", "exps", "P stored", "p_full arrived"]
+        for x, tile in ((0, "A"), (1, "B")):
+            for j in (1, 2):
+                o0 = 1 + 6 * (2 * x + j - 1)
+                s0 = base[:, o0]
+                row = [f"{nm} {((base[:, o0 + i + 1] - s0) / 1e3).mean():+.3f}" for i, nm in enumerate(names)]
+                print(f"  tile {tile} key {j} (us from S ready): " + ", ".join(row))
+            per = ((base[:, 1 + 6 * (2 * x + 1)] - base[:, 1 + 6 * (2 * x)]) / 1e3).mean()
+            print(f"  tile {tile}: S ready(2) - S ready(1) = {per:.3f} us")
+        a1, b1 = base[:, 6], base[:, 18]
+        print(f"  MMA: p_full A(1) seen {((base[:, 25] - a1) / 1e3).mean():+.3f} us after the arrival, "
+              f"PV A(1) + S A(2) issued {((base[:, 26] - a1) / 1e3).mean():+.3f}; "
+              f"S A(2) ready {((base[:, 7] - a1) / 1e3).mean():+.3f}")
+        print(f"  MMA: p_full B(1) seen {((base[:, 27] - b1) / 1e3).mean():+.3f} us after the arrival, "
+              f"PV B(1) + S B(2) issued {((base[:, 28] - b1) / 1e3).mean():+.3f}; "
+              f"S B(2) ready {((base[:, 19] - b1) / 1e3).mean():+.3f}")
+        print(f"  CTA duration mean {((t[:, 30] - t[:, 0]) / 1e3).mean():.2f} us, "
+              f"start -> S A(1) ready {((base[:, 1] - base[:, 0]) / 1e3).mean():.2f} us")
     elif a.case == "attn_bwd_trace":
         # per-CTA timelines of the tcgen05 backward kernels (dQ, then dK/dV)
         q = torch.randn(a.b, a.s, a.h, a.d, device=dev, dtype=torch.bfloat16)

@@ -415,6 +415,432 @@ attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constan
 }
 
 // ============================================================================
+// Forward over two query tiles per CTA (256 queries of one head).
+//
+// Tensor memory holds S and O of both tiles: S_A 0-127, S_B 128-255, O_A
+// 256-383, O_B 384-511; P (bf16 pairs) is written over the first 64 columns of
+// its tile's S.  Q_A and Q_B stay in shared memory (the score MMAs read both
+// operands there), K and V stream through two-stage TMA rings shared by both
+// tiles, so every K/V tile is loaded once for 256 queries.
+//
+// 320 threads: warps 0-3 are the softmax/epilogue warpgroup of tile A, warps
+// 4-7 that of tile B (thread = one query row = one TMEM lane, the whole
+// 128-key row in registers), warp 8 issues the MMAs, warp 9 loads.  The MMA
+// order per key tile j is
+//     PV_A(j), S_A(j+1) | PV_B(j), S_B(j+1) | PV_A(j+1), S_A(j+2) | ...
+// so tile A's exponentials of key tile j+1 run while the tensor core does tile
+// B's PV and next scores, and the other way round.
+//
+// Ten warps put three on some SMSP, whose 16K registers then cap a thread at
+// 168 registers: the row (128 fp32 scores) fits, with the O rescale moved
+// after the P store so the two are never live together.
+//
+// Softmax arithmetic uses Blackwell's packed fp32 pairs (fma/add .f32x2) and
+// 3-input maxima.  Exponentials: 2^x by ex2.approx on the special-function
+// unit, and for every POLY_EVERY-th pair of columns by a polynomial on the FMA
+// pipes (Cody-Waite range reduction x = j + f, f in [-1/2, 1/2], 2^f by a
+// degree-3 polynomial, 2^j added to the exponent field).  The coefficients are
+// a relative-error least-squares fit on 4000 Chebyshev nodes of [-1/2, 1/2]
+// (max relative error 7.8e-5 in fp32, against 2^-9 for the bf16 P).
+//
+// Causal: the CTA takes query tiles 2p and 2p+1 (key tiles 0..2p and 0..2p+1);
+// CTAs are ordered longest first over all heads.  Other rules (lazy rescale by
+// more than 2^8, bounded waits, draining before TMEM is freed) as above.
+// ============================================================================
+constexpr int kF2Threads = 320;
+constexpr int kF2KStages = 2;
+constexpr int kF2VStages = 2;
+
+struct Fwd2Smem {
+  static constexpr int kTile = AttSmem::kTile, kAtom = AttSmem::kAtom;
+  static constexpr int kQ = 0;                               // Q_A, Q_B
+  static constexpr int kK = 2 * kTile;                       // kF2KStages stages
+  static constexpr int kV = kK + kF2KStages * kTile;         // kF2VStages stages
+  static constexpr int kBar = kV + kF2VStages * kTile;
+  static constexpr int kBytes = kBar + 256 + 1024;
+};
+
+// Packed fp32 pairs (Blackwell f32x2 arithmetic: one instruction for two values).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair, x <= 64, by range reduction and a degree-3 polynomial (see
+// above); x below -120 is clamped there (2^-120 ~ 7.5e-37 instead of 0).
+__device__ __forceinline__ void exp2_poly3_x2(float a0, float a1, float& p0, float& p1) {
+  const uint64_t x = f2_pack(fmaxf(a0, -120.0f), fmaxf(a1, -120.0f));
+  const uint64_t magic = f2_pack(12582912.0f, 12582912.0f);   // 1.5 * 2^23
+  const uint64_t t = f2_add(x, magic);        // round(x) in the low mantissa bits
+  const uint64_t f = f2_sub(x, f2_sub(t, magic));   // [-1/2, 1/2]
+  uint64_t p = f2_fma(f2_pack(0.05508868396282196f, 0.05508868396282196f), f,
+                      f2_pack(0.24260404706001282f, 0.24260404706001282f));
+  p = f2_fma(p, f, f2_pack(0.6932762265205383f, 0.6932762265205383f));
+  p = f2_fma(p, f, f2_pack(0.9999289512634277f, 0.9999289512634277f));
+  float q0, q1, t0, t1;
+  f2_unpack(p, q0, q1);
+  f2_unpack(t, t0, t1);
+  // the bits of t are (0x4B400000 + round(x)); shifted by 23 only round(x) << 23 remains
+  p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+  p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
+}
+
+template <int POLY_EVERY, bool TRACE>
+__global__ void __launch_bounds__(kF2Threads, 1)
+attn_fwd2_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, __nv_bfloat16* __restrict__ O,
+                    float* __restrict__ lse, int B, int S, int Hq, int Hk, float scale_log2,
+                    int causal, DeviceStatus* status, unsigned long long* __restrict__ trace) {
+  // trace (TRACE builds only, [grid][kTraceSlots] ns from %globaltimer): 0 CTA
+  // start; for tile x (0: A, 1: B) and key tile j = 1, 2, slots
+  // 1 + 6 (2x + j - 1) + i from warp 4x lane 0: i = 0 S_j ready, 1 S_j in
+  // registers, 2 row max done, 3 exponentials done, 4 P stored, 5 p_full
+  // arrived; MMA thread: 25 / 27 p_full A(1) / B(1) seen, 26 / 28 PV A(1) +
+  // S A(2) / PV B(1) + S B(2) issued; 29 / 30 tile A / B epilogue end, 31 key
+  // tiles of B
+  unsigned long long* tr = (TRACE && trace) ? trace + (size_t)blockIdx.x * kTraceSlots : nullptr;
+  using L = Fwd2Smem;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBar);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;     // [kF2KStages]
+  uint64_t* k_empty = bars + 3;    // [kF2KStages]
+  uint64_t* v_full = bars + 5;     // [kF2VStages]
+  uint64_t* v_empty = bars + 7;    // [kF2VStages]
+  uint64_t* s_full = bars + 9;     // [tile]
+  uint64_t* p_full = bars + 11;    // [tile], one arrival per softmax warp
+  uint64_t* pv_done = bars + 13;   // [tile]
+  uint64_t* drain = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nqt = S / kAttRows;
+  const int npairs = nqt / 2;
+  const int BH = B * Hq;
+  // longest pairs first over all heads (causal), then any order
+  const int pr = causal ? npairs - 1 - (int)(blockIdx.x / (unsigned)BH) : (int)(blockIdx.x / (unsigned)BH);
+  const int bh = (int)(blockIdx.x % (unsigned)BH);
+  const int b = bh / Hq, h = bh % Hq;
+  const int hk = h / (Hq / Hk);
+  const int qt_a = 2 * pr, qt_b = 2 * pr + 1;
+  const int n_a = causal ? qt_a + 1 : nqt;
+  const int n_b = causal ? qt_b + 1 : nqt;
+
+  if (tr && threadIdx.x == 0) tr[0] = globaltimer();
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kF2KStages; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < kF2VStages; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&pv_done[i], 1);
+    }
+    mbar_init(drain, 1);
+    fence_mbar_init();
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  if (warp == 8) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 9) {
+    // ------------------------------------------------------------ TMA loader (one thread)
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * L::kTile);
+      for (int x = 0; x < 2; ++x) {
+        uint8_t* dst = smem + L::kQ + x * L::kTile;
+        const int row0 = (x == 0 ? qt_a : qt_b) * kAttRows;
+        tma_load_4d(dst, &tmQ, q_full, 0, h, row0, b);
+        tma_load_4d(dst + L::kAtom, &tmQ, q_full, 64, h, row0, b);
+      }
+      // K_j and V_j in key order: a K stage frees when S_B(j) has read it, a V
+      // stage when PV_B(j) has, and S_B(j+1) comes after PV_B(j), so loads are
+      // issued in the order their stages free up
+      int k_issued = 0, v_issued = 0;
+      bool ok = true;
+      for (int j = 0; j < n_b && ok; ++j) {
+        for (int kv = 0; kv < 2; ++kv) {
+          const int nst = kv == 0 ? kF2KStages : kF2VStages;
+          const int st = j % nst;
+          uint64_t* empty = kv == 0 ? k_empty : v_empty;
+          uint64_t* full = kv == 0 ? k_full : v_full;
+          if (!mbar_wait(&empty[st], ((j / nst) & 1) ^ 1, status, kErrAttLoad)) { ok = false; break; }
+          uint8_t* dst = smem + (kv == 0 ? L::kK : L::kV) + st * L::kTile;
+          const CUtensorMap* map = kv == 0 ? &tmK : &tmV;
+          mbar_arrive_expect_tx(&full[st], L::kTile);
+          tma_load_4d(dst, map, &full[st], 0, hk, j * kAttKeys, b);
+          tma_load_4d(dst + L::kAtom, map, &full[st], 64, hk, j * kAttKeys, b);
+          if (kv == 0) k_issued = j + 1; else v_issued = j + 1;
+        }
+      }
+      if (!ok) {  // let every copy this thread issued land before the CTA can exit
+        mbar_wait(q_full, 0, nullptr, 0);
+        for (int j = (k_issued > kF2KStages ? k_issued - kF2KStages : 0); j < k_issued; ++j)
+          mbar_wait(&k_full[j % kF2KStages], (j / kF2KStages) & 1, nullptr, 0);
+        for (int j = (v_issued > kF2VStages ? v_issued - kF2VStages : 0); j < v_issued; ++j)
+          mbar_wait(&v_full[j % kF2VStages], (j / kF2VStages) & 1, nullptr, 0);
+      }
+    }
+  } else if (warp == 8) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = umma_idesc_bf16(kAttRows, kAttKeys);
+      constexpr uint32_t idesc_pv = umma_idesc_bf16_bmn(kAttRows, kAttD);
+      auto wait_k = [&](int j) {
+        return mbar_wait(&k_full[j % kF2KStages], (j / kF2KStages) & 1, status, kErrAttMma);
+      };
+      // S_x = Q_x K_jᵀ: both operands K-major in shared memory
+      auto issue_s = [&](int x, int j) {
+        const uint32_t k_addr = smem_u32(smem + L::kK + (j % kF2KStages) * L::kTile);
+        const uint32_t q_addr = smem_u32(smem + L::kQ + x * L::kTile);
+#pragma unroll
+        for (int kk = 0; kk < kAttD / 16; ++kk) {
+          const uint32_t off = (uint32_t)((kk >> 2) * L::kAtom + (kk & 3) * 32);
+          umma_f16_ss(tmem + (uint32_t)(x * 128), umma_desc_sw128_kmajor(q_addr + off),
+                      umma_desc_sw128_kmajor(k_addr + off), idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[x]);
+      };
+      // O_x += P_x V_j: P from tensor memory (bf16 pairs over S_x), V read MN-major
+      auto issue_pv = [&](int x, int j) {
+        const uint32_t v_addr = smem_u32(smem + L::kV + (j % kF2VStages) * L::kTile);
+#pragma unroll
+        for (int kk = 0; kk < kAttKeys / 16; ++kk)
+          umma_f16_ts(tmem + 256u + (uint32_t)(x * 128), tmem + (uint32_t)(x * 128 + kk * 8),
+                      umma_desc_sw128_mnmajor(v_addr + (uint32_t)kk * 2048u, (uint32_t)L::kAtom),
+                      idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&pv_done[x]);
+      };
+      bool ok = mbar_wait(q_full, 0, status, kErrAttMma) && wait_k(0);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        umma_commit(&k_empty[0]);
+      }
+      for (int j = 0; j < n_b && ok; ++j) {
+        const bool a_on = j < n_a;
+        if (!mbar_wait(&v_full[j % kF2VStages], (j / kF2VStages) & 1, status, kErrAttMma)) { ok = false; break; }
+        bool k_next = false;   // K_{j+1} already waited for
+        const bool trj = tr && j == 1;
+        if (a_on) {
+          if (!mbar_wait(&p_full[0], j & 1, status, kErrAttMma)) { ok = false; break; }
+          if (trj) tr[25] = globaltimer();
+          tc_fence_after();
+          issue_pv(0, j);
+          if (j + 1 < n_a) {
+            if (!wait_k(j + 1)) { ok = false; break; }
+            k_next = true;
+            tc_fence_after();
+            issue_s(0, j + 1);
+          }
+          if (trj) tr[26] = globaltimer();
+        }
+        if (!mbar_wait(&p_full[1], j & 1, status, kErrAttMma)) { ok = false; break; }
+        if (trj) tr[27] = globaltimer();
+        tc_fence_after();
+        issue_pv(1, j);
+        umma_commit(&v_empty[j % kF2VStages]);   // V_j consumed by both tiles
+        if (j + 1 < n_b) {
+          if (!k_next && !wait_k(j + 1)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(1, j + 1);
+          umma_commit(&k_empty[(j + 1) % kF2KStages]);   // K_{j+1} consumed by both tiles
+        }
+        if (trj) tr[28] = globaltimer();
+      }
+      // every MMA issued by this thread has completed before TMEM can be freed
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int x = warp >> 2;                        // 0: tile A, 1: tile B
+    const int quad = warp & 3;                      // TMEM lane quadrant
+    const int row = quad * 32 + lane;               // query row in the tile = TMEM lane
+    const int qt = x == 0 ? qt_a : qt_b;
+    const int n_kv = x == 0 ? n_a : n_b;
+    const uint32_t t_s = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(x * 128);
+    const uint32_t t_o = t_s + 256u;
+    float m_used = -INFINITY;
+    float l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      // every exit is decided by a warp vote: the TMEM loads/stores are warp-wide
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[x], j & 1, status, kErrAttSoftmax))) { ok = false; break; }
+      unsigned long long* tj =
+          (tr && quad == 0 && lane == 0 && (j == 1 || j == 2)) ? tr + 1 + 6 * (2 * x + j - 1) : nullptr;
+      if (tj) tj[0] = globaltimer();
+      tc_fence_after();
+      uint32_t r[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        tmem_ld_32x32b_x32(t_s + (uint32_t)(c * 32), *reinterpret_cast<uint32_t(*)[32]>(&r[32 * c]));
+      tmem_ld_wait();
+      if (tj) tj[1] = globaltimer();
+      if (causal && j == qt) {  // diagonal tile: keys after the query -> -inf
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (c > row) r[c] = __float_as_uint(-INFINITY);
+      }
+      // row max: 8 independent chains of 3-input maxima over columns 8..119, then the rest
+      float pm[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) pm[i] = __uint_as_float(r[i]);
+#pragma unroll
+      for (int c = 8; c < 120; c += 16)
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          pm[i] = fmax3(pm[i], __uint_as_float(r[c + i]), __uint_as_float(r[c + 8 + i]));
+      const float mx = fmax3(fmax3(pm[0], pm[1], __uint_as_float(r[120])),
+                             fmax3(pm[2], pm[3], __uint_as_float(r[121])),
+                             fmax3(fmax3(pm[4], pm[5], __uint_as_float(r[122])),
+                                   fmax3(pm[6], pm[7], __uint_as_float(r[123])),
+                                   fmax3(__uint_as_float(r[124]), __uint_as_float(r[125]),
+                                         fmaxf(__uint_as_float(r[126]), __uint_as_float(r[127]))))) *
+                       scale_log2;
+      if (tj) tj[2] = globaltimer();
+      const bool need = mx > m_used + kRescaleThreshold;
+      const bool rescale = __any_sync(0xffffffffu, need);
+      float factor = 1.0f;
+      if (rescale) {
+        const float m_new = need ? mx : m_used;
+        factor = (m_used == -INFINITY) ? 0.0f : fast_exp2(m_used - m_new);
+        m_used = m_new;
+      }
+      // P_j (bf16 pairs) over the first 64 columns of S_j; exponent arguments and
+      // row sums in packed pairs
+      const uint64_t sc2 = f2_pack(scale_log2, scale_log2), nm2 = f2_pack(-m_used, -m_used);
+      uint64_t ps2[4] = {0ull, 0ull, 0ull, 0ull};
+      uint32_t pk[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {  // masked keys hold -inf: ex2 gives exactly 0
+        float a0, a1;
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nm2), a0, a1);
+        float p0 = 0.0f, p1 = 0.0f;
+        bool poly = false;
+        if constexpr (POLY_EVERY > 0) poly = (i % POLY_EVERY) == POLY_EVERY - 1;
+        if (poly) {
+          exp2_poly3_x2(a0, a1, p0, p1);
+        } else {
+          p0 = fast_exp2(a0);
+          p1 = fast_exp2(a1);
+        }
+        ps2[i & 3] = f2_add(ps2[i & 3], f2_pack(p0, p1));
+        pk[i] = pack_bf16x2(p0, p1);
+      }
+      if (tj) tj[3] = globaltimer();
+      tmem_st_32x32b_x32(t_s, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+      tmem_st_32x32b_x32(t_s + 32u, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
+      float ps[4];
+      f2_unpack(f2_add(ps2[0], ps2[1]), ps[0], ps[1]);
+      f2_unpack(f2_add(ps2[2], ps2[3]), ps[2], ps[3]);
+      l = l * factor + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
+      if (rescale && j > 0) {
+        // O holds PV_0..PV_{j-1}: wait for PV_{j-1}, then scale this thread's row
+        // (before the arrival below lets PV_j add into it)
+        if (!__all_sync(0xffffffffu, mbar_wait(&pv_done[x], (j - 1) & 1, status, kErrAttSoftmax))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(t_o + (uint32_t)(c * 32), o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+          tmem_st_32x32b_x32(t_o + (uint32_t)(c * 32), o);
+        }
+      }
+      tmem_st_wait();
+      if (tj) tj[4] = globaltimer();
+      tc_fence_before();          // TMEM loads/stores of this step ordered before the arrive
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[x]);
+      if (tj) tj[5] = globaltimer();
+    }
+    if (ok) {
+      const int jl = n_kv - 1;
+      if (__all_sync(0xffffffffu, mbar_wait(&pv_done[x], jl & 1, status, kErrAttSoftmax))) {
+        tc_fence_after();
+        const float inv = 1.0f / l;
+        const int q = qt * kAttRows + row;
+        __nv_bfloat16* orow = O + (((int64_t)b * S + q) * Hq + h) * kAttD;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(t_o + (uint32_t)(c * 32), o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4 v;
+            v.x = pack_bf16x2(__uint_as_float(o[8 * i + 0]) * inv, __uint_as_float(o[8 * i + 1]) * inv);
+            v.y = pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv);
+            v.z = pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv);
+            v.w = pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + i * 8) = v;
+          }
+        }
+        lse[((int64_t)b * Hq + h) * S + q] = (m_used + __log2f(l)) * 0.69314718055994531f;
+        if (tr && quad == 0 && lane == 0) {
+          tr[29 + x] = globaltimer();
+          if (x == 1) tr[31] = (unsigned long long)n_b;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ============================================================================
 // Backward: delta pre-pass, dQ kernel (per query tile) and dK/dV kernel (per
 // key tile), all on the 5th-generation tensor cores.
 //
@@ -1363,6 +1789,43 @@ void attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Ten
   }
   const CUtensorMap tq = make_tmap_bshd(q), tk = make_tmap_bshd(k, kv_bhsd),
                     tv = make_tmap_bshd(v, kv_bhsd);
+  const bool want_trace = trace.has_value() && trace->defined();
+  // two query tiles per CTA when S is a multiple of 256 (ZEROQ_ATTN_FWD1=1: the
+  // one-tile kernel); ZEROQ_ATTN_POLY = 0 / 4: every how many column pairs the
+  // polynomial exponential takes (default 4)
+  static const bool fwd1 = [] {
+    const char* e = std::getenv("ZEROQ_ATTN_FWD1");
+    return e != nullptr && e[0] == '1';
+  }();
+  static const int poly = [] {
+    const char* e = std::getenv("ZEROQ_ATTN_POLY");
+    return e == nullptr ? 4 : std::atoi(e);
+  }();
+  if (!fwd1 && S % (2 * kAttRows) == 0) {
+    static bool configured2[64] = {false};
+    if (!configured2[dev]) {
+      for (auto k2 : {attn_fwd2_tc_kernel<0, false>, attn_fwd2_tc_kernel<4, false>,
+                      attn_fwd2_tc_kernel<0, true>, attn_fwd2_tc_kernel<4, true>})
+        C10_CUDA_CHECK(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, Fwd2Smem::kBytes));
+      configured2[dev] = true;
+    }
+    const unsigned grid2 = (unsigned)(B * Hq * (S / (2 * kAttRows)));
+    unsigned long long* trp2 = nullptr;
+    if (want_trace) {
+      TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->is_contiguous() &&
+                      trace->numel() >= (int64_t)grid2 * kTraceSlots,
+                  "attention trace: int64 CUDA tensor of [grid, 32]");
+      trp2 = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+    }
+    auto kern = want_trace ? (poly == 4 ? attn_fwd2_tc_kernel<4, true> : attn_fwd2_tc_kernel<0, true>)
+                           : (poly == 4 ? attn_fwd2_tc_kernel<4, false> : attn_fwd2_tc_kernel<0, false>);
+    kern<<<grid2, kF2Threads, Fwd2Smem::kBytes, at::cuda::getCurrentCUDAStream()>>>(
+        tq, tk, tv, reinterpret_cast<__nv_bfloat16*>(o.data_ptr<at::BFloat16>()), lse.data_ptr<float>(),
+        (int)B, (int)S, (int)Hq, (int)Hk, (float)(scale * 1.4426950408889634), causal ? 1 : 0,
+        status_buffer(dev), trp2);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   const unsigned grid = (unsigned)(B * Hq * (S / kAttRows));
   unsigned long long* trp = nullptr;
   if (trace.has_value() && trace->defined()) {

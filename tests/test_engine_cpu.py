@@ -322,6 +322,31 @@ def test_gelu_mlp_split_form_matches_plain_form_on_cpu():
         up.lora_A.grad = None
 
 
+def test_exp2_polynomial_range_reduction_error_bound():
+    """The attention forward's polynomial 2^x (csrc/attention_sm100.cu
+    exp2_poly3_x2), emulated step by step in float32: round-to-nearest by the
+    1.5 * 2^23 addition, degree-3 Horner on [-1/2, 1/2], 2^j added to the
+    exponent bits.  Relative error <= 8e-5 over the kernel's input range
+    (-120, 8], far below the bf16 rounding of P."""
+    import numpy as np
+
+    c3, c2, c1, c0 = (np.float32(0.05508868396282196), np.float32(0.24260404706001282),
+                      np.float32(0.6932762265205383), np.float32(0.9999289512634277))
+    magic = np.float32(12582912.0)
+    x = np.concatenate([np.linspace(-120.0, 8.0, 400001), np.arange(-120, 9)]).astype(np.float32)
+    t = (x + magic).astype(np.float32)
+    j = (t - magic).astype(np.float32)
+    f = (x - j).astype(np.float32)
+    assert np.abs(f).max() <= 0.5
+    p = c3
+    for c in (c2, c1, c0):
+        p = (p * f + c).astype(np.float32)   # (the kernel's fma rounds once; this rounds twice)
+    bits = p.view(np.int32) + (t.view(np.int32) << 23)
+    y = bits.view(np.float32).astype(np.float64)
+    rel = np.abs(y / np.exp2(x.astype(np.float64)) - 1.0)
+    assert rel.max() < 8e-5, rel.max()
+
+
 def test_swiglu_mlp_split_form_matches_plain_form_on_cpu():
     """The split SwiGLU MLP (up returns u and a non-differentiable silu(g)·u, down
     takes the gradients through g and u) gives the plain form's values and

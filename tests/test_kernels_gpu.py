@@ -478,10 +478,12 @@ def test_gemm_nf4_fp4_and_block_sizes(cuda, quant_type, blocksize):
 
 
 
-@pytest.mark.parametrize("B,S,Hq,Hk", [(2, 256, 4, 4), (1, 1024, 8, 2), (2, 512, 3, 1), (1, 2048, 2, 2)])
+@pytest.mark.parametrize("B,S,Hq,Hk", [(2, 256, 4, 4), (1, 1024, 8, 2), (2, 512, 3, 1), (1, 2048, 2, 2),
+                                       (2, 384, 4, 2)])
 @pytest.mark.parametrize("causal", [True, False])
 def test_attention_forward_tcgen05_vs_fp32(cuda, B, S, Hq, Hk, causal):
-    """tcgen05 forward: output and row log-sum-exp against an fp32 reference."""
+    """tcgen05 forward: output and row log-sum-exp against an fp32 reference (S a
+    multiple of 256: the two-query-tile kernel; S = 384: the one-tile kernel)."""
     torch.manual_seed(31)
     D = 128
     q = torch.randn(B, S, Hq, D, device=cuda, dtype=torch.bfloat16)
