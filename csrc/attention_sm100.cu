@@ -479,6 +479,11 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
 __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
   uint64_t r;
   asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
@@ -1176,15 +1181,23 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_cons
       named_barrier(pair_bar, 64);
       tc_fence_after();
       const bool diag = causal && j == qt;
+      // dS = P (dP - delta) with P = 2^(S scale - lse): exponent arguments,
+      // differences and products in packed fp32 pairs
+      const uint64_t sc2 = f2_pack(scale_log2, scale_log2), nl2 = f2_pack(-l2, -l2), dl2 = f2_pack(dl, dl);
       uint32_t pk[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const int c = 2 * i;
-        float p0 = fast_exp2(fmaf(__uint_as_float(s[c]), scale_log2, -l2));
-        float p1 = fast_exp2(fmaf(__uint_as_float(s[c + 1]), scale_log2, -l2));
+        float a0, a1;
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(s[c]), __uint_as_float(s[c + 1])), sc2, nl2), a0, a1);
+        float p0 = fast_exp2(a0);
+        float p1 = fast_exp2(a1);
         if (diag && col0 + c > row) p0 = 0.0f;
         if (diag && col0 + c + 1 > row) p1 = 0.0f;
-        pk[i] = pack_bf16x2(p0 * (__uint_as_float(dp[c]) - dl), p1 * (__uint_as_float(dp[c + 1]) - dl));
+        float g0, g1;
+        f2_unpack(f2_mul(f2_pack(p0, p1),
+                         f2_sub(f2_pack(__uint_as_float(dp[c]), __uint_as_float(dp[c + 1])), dl2)), g0, g1);
+        pk[i] = pack_bf16x2(g0, g1);
       }
       if (tj) tj[2] = globaltimer();
       tmem_st_32x32b_x32(tmem + lane_base + (uint32_t)(half * 32), pk);
