@@ -30,6 +30,7 @@ import torch
 from . import _ext
 from . import lora as lora_k
 from .nf4 import QUANT_TYPE_ID
+from .qlinear import KEEP_OPERANDS
 
 
 def _decode_into(mods, w: torch.Tensor):
@@ -99,6 +100,8 @@ class QKVFunction(torch.autograd.Function):
             U, Ut = lora_k.down(x2, A_cat[:3 * g], upad=A_cat.shape[0])
         y = torch.empty(M, Nt, dtype=torch.bfloat16, device=x2.device)
         E.gemm_rope(x2, w, y, cs, U, B_blk, Ns[0] + Ns[1])
+        # the input-gradient GEMM reads the same operand (see qlinear.KEEP_OPERANDS)
+        ctx.w_kept = w if (KEEP_OPERANDS and ctx.needs_input_grad[0]) else None
         del w, U
         ctx.save_for_backward(x2 if lora else None, Ut, A_cat, B_blk, B_catT)
         ctx.g = g
@@ -162,8 +165,11 @@ class QKVFunction(torch.autograd.Function):
                 res = lora_k.down(g, B_catT, upad=A_cat.shape[0])
             V, Vt = res
         if ctx.needs_input_grad[0]:
-            w = torch.empty(Nt, d, dtype=torch.bfloat16, device=dev)
-            _decode_into(mods, w)
+            w = ctx.w_kept
+            if w is None:
+                w = torch.empty(Nt, d, dtype=torch.bfloat16, device=dev)
+                _decode_into(mods, w)
+            ctx.w_kept = None
             gx = torch.empty(M, d, dtype=torch.bfloat16, device=dev)
             E.gemm_bf16_nn(g, w, gx, V, A_cat)     # dX = dY·W + V·[sA] in one GEMM
             del w

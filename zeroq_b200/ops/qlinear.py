@@ -79,6 +79,16 @@ def _dequant_weight(packed, absmax, N, K, blocksize, quant_type, dtype):
     return dequantize_4bit(packed, st, out_dtype=dtype)
 
 
+# The bf16 operand a resident projection decodes for its forward GEMM is the one
+# its input-gradient GEMM reads (W [N, K], MN-major there): keeping it from the
+# forward to the backward halves the decode launches of a step, for the memory of
+# one bf16 copy of the resident weights held between the two (4.7B: ~9.4 GB).
+# The weights stay NF4-resident and are decoded every step.  Peer-sourced
+# operands are never kept (that would pin every gathered layer).
+# ZEROQ_KEEP_OPERANDS=0 decodes again in the backward.
+KEEP_OPERANDS = os.environ.get("ZEROQ_KEEP_OPERANDS", "1") != "0"
+
+
 def _nf4_operand(packed, absmax, N, K, blocksize, quant_type, transpose: bool):
     """bf16 GEMM operand from NF4: ``W [N, K]`` or ``Wᵀ [K, N]`` (``csrc/gemm_sm100.cu``)."""
     w = torch.empty(N * K, dtype=torch.bfloat16, device=packed.device)
@@ -165,10 +175,18 @@ class NF4LinearFunction(torch.autograd.Function):
         elif peer is not None and not peer_fused:
             packed, absmax = peer[0].gather(peer[1]).wait()
 
+        # the backward reads the same W [N, K] for inputs of at least 256 rows
+        keep_ok = (KEEP_OPERANDS and peer is None and M >= 256
+                   and (ctx.needs_input_grad[0] or pre is not None))
+        kept = []
+
         def operand():  # bf16 W [N, K] for the GEMM paths below
             if w_peer is not None:
                 return w_peer
-            return _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
+            w_ = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
+            if keep_ok:
+                kept.append(w_)
+            return w_
         U = None
         Ut = None
         a_pad = b_pad = b_t = None
@@ -247,6 +265,7 @@ class NF4LinearFunction(torch.autograd.Function):
 
             y = rope_rows(y, rope_cs, 1.0)
         ctx.rope = rope
+        ctx.w_kept = kept[0] if kept else None
         if peer is not None:
             packed = absmax = None  # re-read from the owners in backward
         pre2 = preu2 = None
@@ -278,6 +297,7 @@ class NF4LinearFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, gy, g_act=None):
         if gy is None:  # (grads are not materialised for the act_out form)
+            ctx.w_kept = None
             return (None,) * 19
         x2, packed, absmax, lora_A, lora_B, U, a_pad, b_pad, b_t, pre2, preu2 = ctx.saved_tensors
         swiglu_in = preu2 is not None
@@ -331,7 +351,9 @@ class NF4LinearFunction(torch.autograd.Function):
                 if (pre2 is not None and _epi_ok(M, N) and not _in_kernel_ok(M, N, K)
                         and pre2.dtype == torch.bfloat16
                         and (not swiglu_in or preu2.dtype == torch.bfloat16)):
-                    if peer_operand:
+                    if ctx.w_kept is not None:
+                        w = ctx.w_kept
+                    elif peer_operand:
                         w = peer[0].gather_dequant(peer[1], N, K)
                     else:
                         w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
@@ -349,7 +371,9 @@ class NF4LinearFunction(torch.autograd.Function):
                     E.gemm_nf4(gy2, packed, absmax, N, K, blocksize, QUANT_TYPE_ID[quant_type],
                                True, gx, V, a_pad)
                 elif M >= 256:  # W [N, K] read MN-major from the operand kernel's copy
-                    if peer_operand:  # straight from the owners' shards (one kernel)
+                    if ctx.w_kept is not None:   # the forward's operand
+                        w = ctx.w_kept
+                    elif peer_operand:  # straight from the owners' shards (one kernel)
                         w = peer[0].gather_dequant(peer[1], N, K)
                     else:
                         w = _nf4_operand(packed, absmax, N, K, blocksize, quant_type, False)
@@ -363,6 +387,7 @@ class NF4LinearFunction(torch.autograd.Function):
                         E.gemm_bf16_tn(gy2, w, gx)
                     del w
                 gx = gx.view(*shp[:-1], K)
+            ctx.w_kept = None
             if has_lora:
                 # dA += s·Vᵀ·X, dB += dYᵀ·U: bf16 operands, fp32 accumulation straight
                 # into the bound gradient (or a zeroed buffer), U read as Ut [r16, M]
