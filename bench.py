@@ -119,6 +119,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-graph", action="store_true",
                     help="run the steps eagerly instead of as one CUDA graph replay each")
+    ap.add_argument("--overlap-sync", action="store_true",
+                    help="sync the trainable gradients per decoder layer during the backward "
+                         "(fused backend, several GPUs)")
     ap.add_argument("--torch-profile", default=None,
                     help="after timing, profile one more step and write a per-kernel table here")
     ap.add_argument("--metrics-jsonl", default=None,
@@ -167,8 +170,13 @@ def main():
     trainable = ("lora_", "norm") if mode == "4bit-once" else ("lora_",)
     initialize(model, zq, trainable_patterns=trainable, rank_weights=rank_weights)
     torch.cuda.empty_cache()
+    # --overlap-sync: one fused reduce-scatter + AdamW + all-gather per decoder layer,
+    # launched during the backward (several ranks)
+    okw = dict(overlap_buckets=model.layer_parameter_groups()) if args.overlap_sync else {}
     opt = ShardedAdamW(model.trainable_parameters(), lr=1e-4, betas=(0.9, 0.999),
-                       weight_decay=0.0)
+                       weight_decay=0.0, **okw)
+    if getattr(opt, "overlap", False):
+        model.set_layer_grad_callback(opt.bucket_ready)
     trainer = Trainer(model, opt, device)
 
     B = args.batch or B0

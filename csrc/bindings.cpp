@@ -76,7 +76,8 @@ void rs_adamw(std::vector<int64_t> grads, std::vector<int64_t> params, std::vect
               int64_t grad_is_bf16, double lr, double b1, double b2, double eps, double wd,
               double bc1, double bc2, double gscale, bool push, int64_t timeout_ms,
               c10::optional<at::Tensor> clk, c10::optional<at::Tensor> bc,
-              c10::optional<at::Tensor> clip_sq, double max_norm, int64_t epoch_mul, int64_t epoch_add);
+              c10::optional<at::Tensor> clip_sq, double max_norm, int64_t epoch_mul, int64_t epoch_add,
+              int64_t max_ctas);
 void rs_sumsq(std::vector<int64_t> grads, std::vector<int64_t> flags, int64_t rank, int64_t epoch, int64_t lo,
               int64_t n, at::Tensor sq, int64_t grad_is_bf16, double gscale, int64_t timeout_ms,
               c10::optional<at::Tensor> clk, int64_t epoch_mul, int64_t epoch_add);
@@ -178,7 +179,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                        int64_t grad_is_bf16, double lr, double b1, double b2, double eps, double wd,
                        double bc1, double bc2, double gscale, bool push, int64_t timeout_ms) {
     rs_adamw(grads, params, flags, rank, epoch, lo, n, m_, v, grad_is_bf16, lr, b1, b2, eps, wd, bc1,
-             bc2, gscale, push, timeout_ms, c10::nullopt, c10::nullopt, c10::nullopt, 0.0, 1, 0);
+             bc2, gscale, push, timeout_ms, c10::nullopt, c10::nullopt, c10::nullopt, 0.0, 1, 0, 0);
   });
   // epoch and bias corrections from the device-side optimizer clock (clk, bc);
   // optional device-side gradient clipping (clip_sq, max_norm)
@@ -187,7 +188,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("lr"), py::arg("b1"), py::arg("b2"), py::arg("eps"), py::arg("wd"), py::arg("bc1"),
         py::arg("bc2"), py::arg("gscale"), py::arg("push"), py::arg("timeout_ms"),
         py::arg("clk") = py::none(), py::arg("bc") = py::none(), py::arg("clip_sq") = py::none(),
-        py::arg("max_norm") = 0.0, py::arg("epoch_mul") = 1, py::arg("epoch_add") = 0);
+        py::arg("max_norm") = 0.0, py::arg("epoch_mul") = 1, py::arg("epoch_add") = 0,
+        py::arg("max_ctas") = 0);
   m.def("rs_sumsq", &rs_sumsq, py::arg("grads"), py::arg("flags"), py::arg("rank"), py::arg("epoch"),
         py::arg("lo"), py::arg("n"), py::arg("sq"), py::arg("grad_is_bf16"), py::arg("gscale"),
         py::arg("timeout_ms"), py::arg("clk") = py::none(), py::arg("epoch_mul") = 1,

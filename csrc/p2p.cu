@@ -490,7 +490,8 @@ void rs_adamw(std::vector<int64_t> grads, std::vector<int64_t> params, std::vect
               int64_t grad_is_bf16, double lr, double b1, double b2, double eps, double wd,
               double bc1, double bc2, double gscale, bool push, int64_t timeout_ms,
               c10::optional<at::Tensor> clk, c10::optional<at::Tensor> bc,
-              c10::optional<at::Tensor> clip_sq, double max_norm, int64_t epoch_mul, int64_t epoch_add) {
+              c10::optional<at::Tensor> clip_sq, double max_norm, int64_t epoch_mul, int64_t epoch_add,
+              int64_t max_ctas) {
   const int world = (int)grads.size();
   TORCH_CHECK(world >= 1 && world <= kMaxRanks && (int)params.size() == world &&
                   (int)flags.size() == world, "rs_adamw: one pointer per rank");
@@ -514,8 +515,13 @@ void rs_adamw(std::vector<int64_t> grads, std::vector<int64_t> params, std::vect
     TORCH_CHECK(max_norm > 0.0, "rs_adamw: max_norm must be positive");
     sqp = clip_sq->data_ptr<float>();
   }
-  const int grid = grad_is_bf16 ? resident_grid(rs_adamw_kernel<__nv_bfloat16>, 256)
-                                : resident_grid(rs_adamw_kernel<float>, 256);
+  // max_ctas > 0 caps the grid: a launch that runs beside other kernels (a
+  // bucket synchronised during the backward) takes a few CTAs, which share SMs
+  // with the compute kernels instead of filling them (CTA 0 runs the cross-rank
+  // barrier and the others wait for its flag, so a partly resident grid is fine)
+  int grid = grad_is_bf16 ? resident_grid(rs_adamw_kernel<__nv_bfloat16>, 256)
+                          : resident_grid(rs_adamw_kernel<float>, 256);
+  if (max_ctas > 0) grid = std::max(1, std::min(grid, (int)max_ctas));
   if (grad_is_bf16) {
     rs_adamw_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
         table_from(grads), table_from(params), table_from(flags), (int)rank, world, (int)epoch, lo, n,

@@ -322,6 +322,28 @@ def test_gelu_mlp_split_form_matches_plain_form_on_cpu():
         up.lora_A.grad = None
 
 
+def test_flat_params_groups_layout_padding_and_binding():
+    """FlatParams with groups: each group contiguous and padded to pad_to, every
+    parameter (and its .grad) a view at its offset, values preserved."""
+    from zeroq_b200.parallel.optimizer import FlatParams
+
+    torch.manual_seed(3)
+    ps = [torch.nn.Parameter(torch.randn(n)) for n in (5, 7, 3, 9)]
+    vals = [p.detach().clone() for p in ps]
+    groups = [[ps[2], ps[0]], [ps[3]], [ps[1]]]
+    flat = FlatParams(ps, pad_to=8, groups=groups)
+    assert flat.group_ranges == [(0, 8), (8, 24), (24, 32)] and flat.padded == 32
+    assert [p is q for p, q in zip(flat.params, [ps[2], ps[0], ps[3], ps[1]])] == [True] * 4
+    assert flat.offsets == [0, 3, 8, 24]
+    for p, v, off in zip(flat.params, [vals[2], vals[0], vals[3], vals[1]], flat.offsets):
+        assert torch.equal(p.detach(), v)
+        assert p.data.data_ptr() == flat.data[off:].data_ptr()
+        assert p.grad.data_ptr() == flat.grad[off:].data_ptr()
+    assert float(flat.data[17:24].abs().sum()) == 0.0   # padding
+    with pytest.raises(ValueError):
+        FlatParams(ps, groups=[[ps[0]], [ps[0], ps[1], ps[2], ps[3]]])
+
+
 def test_exp2_polynomial_range_reduction_error_bound():
     """The attention forward's polynomial 2^x (csrc/attention_sm100.cu
     exp2_poly3_x2), emulated step by step in float32: round-to-nearest by the

@@ -378,6 +378,49 @@ def w_step_equals_single_process(rank, world):
     assert not bad, "\n".join(f"{r[0]}: ref {r[1]:.3e} run {r[2]:.3e} diff {r[3]:.3e}" for r in bad)
 
 
+def w_overlap_matches_step_end(rank, world):
+    """Gradient sync overlapped with the backward (one reduce-scatter + AdamW +
+    all-gather bucket per decoder layer, launched on a side stream from the layer's
+    input-gradient hook) leaves the parameters where the step-end sync leaves them,
+    over eager steps and CUDA-graph replays (device clock, per-launch epochs)."""
+    import zeroq_b200 as zq
+    from zeroq_b200.train import Trainer
+
+    runs = []
+    for overlap in (True, False):
+        torch.manual_seed(1234)   # the same LoRA initialisation in both runs
+        cfg, model = _tiny_decoder("cuda")
+        n_layers = len(model.layers)
+        zq.initialize(model, _zcfg(), trainable_patterns=("lora_", "norm"))
+        with torch.no_grad():
+            g = torch.Generator(device="cuda").manual_seed(7)
+            for n_, p in model.named_parameters():
+                if "lora_B" in n_:
+                    p.normal_(0.0, 0.02, generator=g)
+        kw = dict(overlap_buckets=model.layer_parameter_groups()) if overlap else {}
+        opt = zq.ShardedAdamW(model.trainable_parameters(), lr=1e-3, eps=1.0, weight_decay=0.0, **kw)
+        assert opt.backend == "fused", opt._peer_error
+        assert opt.overlap == overlap and len(opt._parts) == (n_layers + 1 if overlap else 1)
+        if overlap:
+            model.set_layer_grad_callback(opt.bucket_ready)
+        tr = Trainer(model, opt, torch.device("cuda"))
+        gen = torch.Generator().manual_seed(11 + rank)
+        ids = torch.randint(0, cfg.vocab_size, (2, 129), generator=gen)
+        x, y = ids[:, :-1].cuda(), ids[:, 1:].cuda()
+        for i in range(5):
+            if i == 1:
+                tr.enable_cuda_graph()
+            tr.step_device(x, y)
+        torch.cuda.synchronize()
+        runs.append({n_: p.detach().clone() for n_, p in model.named_parameters() if p.requires_grad})
+        tr._graph = None
+        del tr, opt, model
+    a, b = runs
+    assert a.keys() == b.keys()
+    for n_ in a:
+        torch.testing.assert_close(a[n_], b[n_], rtol=1e-5, atol=1e-6, msg=n_)
+
+
 @pytest.mark.parametrize("world", WORLDS)
 def test_fused_reduce_scatter_adamw_matches_nccl(world):
     _run("w_fused_adamw", world)
@@ -406,6 +449,11 @@ def test_resident_mode_assembles_local_nf4_copy_with_peer_pool(world):
 @pytest.mark.parametrize("world", WORLDS)
 def test_fused_step_equals_single_process_on_concatenated_batch(world):
     _run("w_step_equals_single_process", world)
+
+
+@pytest.mark.parametrize("world", WORLDS)
+def test_overlapped_bucket_sync_matches_step_end_sync(world):
+    _run("w_overlap_matches_step_end", world)
 
 
 def test_peer_wait_times_out_with_error_status(cuda):

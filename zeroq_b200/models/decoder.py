@@ -352,7 +352,12 @@ class DecoderLM(nn.Module):
         B, S = input_ids.shape
         h = self.embed_tokens(input_ids)
         delta = None
+        cb = getattr(self, "_layer_grad_cb", None)
         for i, layer in enumerate(self.layers):
+            if cb is not None and torch.is_grad_enabled() and h.requires_grad:
+                # the gradient of a layer's input is complete once every kernel of
+                # that layer's backward (its parameter gradients included) is queued
+                h.register_hook(lambda g, i=i: cb(i))
             with nvtx_range(f"layer{i}"):
                 h, delta = self._layer_call(layer, h, delta)
         x = self.norm(h) if delta is None else self.norm(h, delta)[1]
@@ -372,6 +377,18 @@ class DecoderLM(nn.Module):
     # -- bookkeeping ---------------------------------------------------------------
     def trainable_parameters(self):
         return [p for p in self.parameters() if p.requires_grad]
+
+    def layer_parameter_groups(self):
+        """The trainable parameters of each decoder layer (``overlap_buckets`` of
+        :class:`~zeroq_b200.parallel.optimizer.ShardedAdamW`)."""
+        return [[p for p in layer.parameters() if p.requires_grad] for layer in self.layers]
+
+    def set_layer_grad_callback(self, fn):
+        """``fn(i)`` runs in the backward when layer ``i``'s input gradient is
+        computed - every gradient of layer ``i`` is written by then (e.g.
+        ``ShardedAdamW.bucket_ready``).  Layer 0's input (the frozen embedding)
+        takes no gradient, so layer 0 gets no call.  ``None`` removes it."""
+        self._layer_grad_cb = fn
 
     def flops_per_token(self, seq_len: int) -> float:
         """Training FLOPs per token: frozen projections run forward + input-grad

@@ -120,30 +120,35 @@ class PeerReduceScatterAdamW:
 
     def run(self, lo: int, n: int, m: torch.Tensor, v: torch.Tensor, *, lr, beta1, beta2, eps,
             weight_decay, step, grad_scale, push: bool = True, timeout_ms: int = 0,
-            clock=None, clip_sq: Optional[torch.Tensor] = None, max_norm: float = 0.0):
+            clock=None, clip_sq: Optional[torch.Tensor] = None, max_norm: float = 0.0,
+            epoch: Optional[tuple] = None, max_ctas: int = 0):
         """``clock = (clk, bc)``: take the barrier epoch and the bias corrections from
         the device-side optimizer clock (see :meth:`ShardedAdamW.use_device_clock`)
         instead of launch arguments.  ``clip_sq``: squared global gradient norm on
         the device (:meth:`sumsq` + all-reduce); the kernel clips to ``max_norm``.
         A clipped step runs two peer kernels, on epochs ``2e`` and ``2e + 1`` of the
-        device clock."""
+        device clock; ``epoch = (mul, add)`` sets that pair for other schedules
+        (``k`` launches per step: ``(k, i)`` for the i-th).  ``max_ctas`` caps the
+        grid (a launch beside compute kernels)."""
         bc1 = 1.0 - beta1 ** step
         bc2 = 1.0 - beta2 ** step
         mul, add = (2, 1) if clip_sq is not None else (1, 0)
+        if epoch is not None:
+            mul, add = epoch
         if clock is not None:
             _ext.ext().rs_adamw_dev(self.grad_buf.ptrs, self.param_buf.ptrs, self.flags.ptrs,
                                     self.flags.rank, 0, int(lo), int(n), m, v,
                                     1 if self.grad_is_bf16 else 0, float(lr), float(beta1),
                                     float(beta2), float(eps), float(weight_decay), 1.0, 1.0,
                                     float(grad_scale), bool(push), int(timeout_ms), clock[0], clock[1],
-                                    clip_sq, float(max_norm), mul, add)
+                                    clip_sq, float(max_norm), mul, add, int(max_ctas))
             return
         _ext.ext().rs_adamw_dev(self.grad_buf.ptrs, self.param_buf.ptrs, self.flags.ptrs,
                                 self.flags.rank, self.flags.next_epoch(), int(lo), int(n), m, v,
                                 1 if self.grad_is_bf16 else 0, float(lr), float(beta1), float(beta2),
                                 float(eps), float(weight_decay), float(bc1), float(bc2),
                                 float(grad_scale), bool(push), int(timeout_ms), None, None,
-                                clip_sq, float(max_norm))
+                                clip_sq, float(max_norm), 1, 0, int(max_ctas))
 
     def sumsq(self, opt, lo: int, sq: torch.Tensor, timeout_ms: int = 0):
         """``sq += ‖shard of the averaged gradient‖²`` for this rank's shard, read from

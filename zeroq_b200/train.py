@@ -60,6 +60,8 @@ class Trainer:
 
     def _eager(self, input_ids: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
         loss = self.model(input_ids, targets)
+        if hasattr(self.opt, "arm_overlap"):   # one backward per step: sync buckets may start
+            self.opt.arm_overlap()
         loss.backward()
         self.opt.step()
         self.opt.zero_grad()
