@@ -252,6 +252,25 @@ def w_train_mode_rs(rank, world):
     x = torch.randn(4, 64, generator=torch.Generator().manual_seed(rank))
     m(x).pow(2).mean().backward()
     assert all(p.grad is not None for p in masters)
+    # the reduce-scatters started in the gradient hooks were finished at the end of
+    # the backward: each master shard holds its slice of the rank-averaged gradient
+    torch.manual_seed(0)
+    ref = TinyMLP()          # the same initial weights, not sharded
+    ref(x).pow(2).mean().backward()
+    refp = dict(ref.named_parameters())
+    checked = 0
+    for zq_ in coord._params.values():
+        if getattr(zq_, "master_shard", None) is None or zq_.master_shard.grad is None:
+            continue
+        checked += 1
+        full = refp[f"{zq_.module_path}.{zq_.param_name}"].grad.detach().reshape(-1).clone()
+        dist.all_reduce(full)
+        full /= world
+        n = zq_.master_shard.numel()
+        want = torch.nn.functional.pad(full, (0, n * world - full.numel()))[rank * n:(rank + 1) * n]
+        torch.testing.assert_close(zq_.master_shard.grad, want.to(zq_.master_shard.dtype),
+                                   rtol=1e-5, atol=1e-6)
+    assert checked > 0
     opt.step()
     st = coord.gather_full_state_dict()
     if rank == 0:

@@ -40,7 +40,7 @@ import torch.nn.functional as F
 from ..config import ZeroQConfig
 from ..ops.nf4 import QuantState, code_table, dequantize_4bit, quantize_4bit
 from . import comm
-from .gradient_sync import reduce_scatter_grads
+from .gradient_sync import reduce_scatter_grads, reduce_scatter_grads_async
 from .shard_plan import ShardPlan, ceil_plan, uniform_remainder_plan
 
 
@@ -374,12 +374,21 @@ class ZeroQParameter:
         zq = self
 
         def _grad_hook(grad):
-            local = reduce_scatter_grads(grad, zq.world_size, zq.rank, group=zq.process_group)
-            local = local[: zq.master_shard.numel()].to(zq.master_shard.dtype)
-            if zq.master_shard.grad is None:
-                zq.master_shard.grad = local
-            else:
-                zq.master_shard.grad.add_(local)
+            # the reduce-scatter starts now and overlaps the rest of the backward;
+            # it is finished (and added into the master shard's .grad) by a
+            # callback at the end of this backward pass, so .grad is complete when
+            # backward() returns, as with the synchronous form
+            coord = getattr(zq, "coordinator", None)
+            if coord is None:   # a parameter used outside a coordinator: synchronous
+                local = reduce_scatter_grads(grad, zq.world_size, zq.rank, group=zq.process_group)
+                local = local[: zq.master_shard.numel()].to(zq.master_shard.dtype)
+                if zq.master_shard.grad is None:
+                    zq.master_shard.grad = local
+                else:
+                    zq.master_shard.grad.add_(local)
+                return grad
+            coord._pending_grad_sync(zq, reduce_scatter_grads_async(
+                grad, zq.world_size, zq.rank, group=zq.process_group))
             return grad
 
         new_param.register_hook(_grad_hook)
@@ -499,6 +508,28 @@ class ZeroQCoordinator:
         self._param_to_module: Dict[int, torch.nn.Module] = {}
         self._next_param_id = 0
         self._collective_seq = 0
+        self._grad_sync_pending = []     # (ZeroQParameter, finish) of this backward
+        self._grad_sync_queued = False
+
+    # -- train mode: reduce-scatters overlapped with the backward -----------------
+    def _pending_grad_sync(self, zq, finish):
+        """Called from a gradient hook: remember the started reduce-scatter and, once
+        per backward pass, queue the callback that finishes them all when the
+        autograd engine is done (how DDP overlaps its buckets with the backward)."""
+        self._grad_sync_pending.append((zq, finish))
+        if not self._grad_sync_queued:
+            self._grad_sync_queued = True
+            torch.autograd.Variable._execution_engine.queue_callback(self._finish_grad_sync)
+
+    def _finish_grad_sync(self):
+        pending, self._grad_sync_pending = self._grad_sync_pending, []
+        self._grad_sync_queued = False
+        for zq, finish in pending:
+            local = finish()[: zq.master_shard.numel()].to(zq.master_shard.dtype)
+            if zq.master_shard.grad is None:
+                zq.master_shard.grad = local
+            else:
+                zq.master_shard.grad.add_(local)
 
     def _new_param(self, param, module, param_name, param_id):
         return self.param_cls(param=param, rank=self.rank, world_size=self.world_size,
@@ -512,6 +543,7 @@ class ZeroQCoordinator:
         pid = self._next_param_id
         self._next_param_id += 1
         zq = self._new_param(param, module, param_name, pid)
+        zq.coordinator = self
         self._params[pid] = zq
         self._params_by_obj_id[id(param)] = zq
         if module is not None:

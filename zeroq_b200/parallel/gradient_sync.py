@@ -48,6 +48,37 @@ class GradSyncConfig:
     timeout_sec: float = 60.0
 
 
+def reduce_scatter_grads_async(param_full_grad: torch.Tensor, world_size: int, rank: int,
+                               group: Optional[dist.ProcessGroup] = None):
+    """Start the averaging reduce-scatter of :func:`reduce_scatter_grads` without
+    waiting for it (the collective runs on the backend's stream while the caller's
+    work goes on); returns ``finish()``, which waits and returns this rank's shard."""
+    if not dist.is_initialized() or world_size == 1:
+        out = param_full_grad.contiguous().view(-1).clone()
+        return lambda: out
+    flat = param_full_grad.contiguous().view(-1)
+    chunk = (flat.numel() + world_size - 1) // world_size
+    if flat.numel() != chunk * world_size:
+        flat = F.pad(flat, (0, chunk * world_size - flat.numel()))
+    out = torch.empty(chunk, device=flat.device, dtype=flat.dtype)
+    try:
+        work = dist.reduce_scatter_tensor(out, flat, op=dist.ReduceOp.SUM, group=group,
+                                          async_op=True)
+
+        def finish():
+            work.wait()
+            return out.div_(world_size)
+    except (RuntimeError, AttributeError):
+        # gloo builds without reduce_scatter: all-reduce a copy, then slice
+        full = flat.clone()
+        work = dist.all_reduce(full, op=dist.ReduceOp.SUM, group=group, async_op=True)
+
+        def finish():
+            work.wait()
+            return full[rank * chunk:(rank + 1) * chunk].div_(world_size)
+    return finish
+
+
 def reduce_scatter_grads(param_full_grad: torch.Tensor, world_size: int, rank: int,
                          group: Optional[dist.ProcessGroup] = None) -> torch.Tensor:
     """Average a full gradient across ranks and return this rank's ceil-split shard."""
