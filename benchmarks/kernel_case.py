@@ -88,7 +88,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["gemm", "attention", "attn_trace", "attn2_trace", "attn_bwd_trace",
                                      "nf4_operand", "rmsnorm", "gelu", "q4gemm", "gelu_gemm",
-                                     "ag_gemm", "lora"])
+                                     "ag_gemm", "lora", "rs_adamw"])
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=3072)
     ap.add_argument("--k", type=int, default=3072)
@@ -352,6 +352,24 @@ def main():
                 ms_b = _time(lambda: E.attn_bwd_tc(go, qd, kd, vd, o, lse, dq, dk, dv, True,
                                                    a.d ** -0.5, None, t), a.reps)
                 _report(f"attention bwd kernels ({name})", ms_b, flops=fwd_fl * 2.5)
+    elif a.case == "rs_adamw":
+        # the fused reduce-scatter + AdamW (+ all-gather) kernel on one GPU: world 1,
+        # epoch 0 (no cross-rank barrier), so it runs its memory traffic alone:
+        # per element it reads the gradient, master, m and v and writes master, m,
+        # v and the pushed parameter copy (here the same buffer)
+        n = a.n * a.k
+        g = torch.randn(n, device=dev) * 1e-3
+        master = torch.randn(n, device=dev)
+        m_ = torch.zeros(n, device=dev)
+        v_ = torch.zeros(n, device=dev)
+        flags = torch.zeros(64, dtype=torch.int32, device=dev)
+
+        def run():
+            E.rs_adamw([g.data_ptr()], [master.data_ptr()], [flags.data_ptr()], 0, 0, 0, n,
+                       m_, v_, 0, 1e-4, 0.9, 0.999, 1e-8, 0.0, 0.1, 0.001, 1.0, True, 0)
+
+        ms = _time(run, a.reps, a.profile)
+        _report(f"rs_adamw world 1, {n} fp32 elements", ms, byts=7 * 4 * n)
     elif a.case == "nf4_operand":
         from zeroq_b200.ops.nf4 import quantize_4bit
 
