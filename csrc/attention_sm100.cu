@@ -846,8 +846,8 @@ attn_fwd2_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
 }
 
 // ============================================================================
-// Backward: delta pre-pass, dQ kernel (per query tile) and dK/dV kernel (per
-// key tile), all on the 5th-generation tensor cores.
+// Backward: dQ kernel (per query tile, also producing delta and lse2) and dK/dV
+// kernel (per key tile), both on the 5th-generation tensor cores.
 //
 //   P  = exp(scale·Q Kᵀ - lse)            (recomputed from the saved lse)
 //   dP = dO Vᵀ,   dS = P ∘ (dP - delta),   delta = rowsum(dO ∘ O)
@@ -859,6 +859,9 @@ attn_fwd2_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
 // independent accumulation chains), eight compute warps turn them into dS
 // (bf16, written over S's own columns) and the MMA thread adds dS·K into the
 // dQ accumulator (K read MN-major).  dQ is written once, in bf16: no atomics.
+// Before the loop the compute warps form delta = rowsum(dO ∘ O) of their rows
+// (dO from the staged tile, O from global) and store delta and lse·log2(e) for
+// the dK/dV kernel, which runs after this one on the same stream.
 // Tensor memory: S 0-127, dP 128-255, dQ 256-383, Q 384-447, dO 448-511.
 //
 // dK/dV kernel: one CTA per (128-key tile, kv head, batch), looping over the
@@ -877,61 +880,6 @@ constexpr int kBwdKStages = 3;     // dQ kernel K ring
 constexpr int kBwdVStages = 2;     // dQ kernel V ring
 constexpr int kBwdQStages = 2;     // dK/dV kernel Q and dO rings
 enum AttBwdErr { kErrBwdLoad = 311, kErrBwdMma = 312, kErrBwdCompute = 313 };
-
-// delta[b, h, s] = sum_d dO[b, s, h, d] * O[b, s, h, d]  (one warp per row, D = 128)
-// and lse2 = lse * log2(e) (the exponent offset in the exp2 form)
-// delta = rowsum(dO * O) per (b, h, s) and lse2 = lse * log2(e), in [B, H, S]
-// order.  Grid-stride: 16 lanes x 16-byte loads per 128-wide row, two rows per
-// warp, two row pairs per iteration in flight (a warp per row with 8-byte loads
-// and a block per 8 rows was bound by block scheduling).
-__global__ void __launch_bounds__(256) attn_delta_kernel(const __nv_bfloat16* __restrict__ dout,
-                                  const __nv_bfloat16* __restrict__ o, const float* __restrict__ lse,
-                                  float* __restrict__ delta, float* __restrict__ lse2,
-                                  int64_t rows, int S, int Hq) {
-  const int lane = threadIdx.x & 31;
-  const int half = lane >> 4, l16 = lane & 15;
-  const int64_t nw = (int64_t)gridDim.x * (blockDim.x >> 5);
-  const int64_t pairs = (rows + 1) >> 1;
-  for (int64_t p0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p0 < pairs; p0 += 2 * nw) {
-    float acc[2] = {0.0f, 0.0f};
-    uint4 a[2], c[2];
-    int64_t row[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      row[u] = (p0 + u * nw) * 2 + half;
-      if (p0 + u * nw < pairs && row[u] < rows) {
-        a[u] = *reinterpret_cast<const uint4*>(dout + row[u] * kAttD + l16 * 8);
-        c[u] = *reinterpret_cast<const uint4*>(o + row[u] * kAttD + l16 * 8);
-      } else {
-        a[u] = c[u] = make_uint4(0u, 0u, 0u, 0u);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const uint32_t aw[4] = {a[u].x, a[u].y, a[u].z, a[u].w};
-      const uint32_t cw[4] = {c[u].x, c[u].y, c[u].z, c[u].w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 x = bf16x2_to_f2(aw[j]), y = bf16x2_to_f2(cw[j]);
-        acc[u] = fmaf(x.x, y.x, acc[u]);
-        acc[u] = fmaf(x.y, y.y, acc[u]);
-      }
-#pragma unroll
-      for (int off = 8; off > 0; off >>= 1) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], off);
-    }
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      if (l16 == 0 && p0 + u * nw < pairs && row[u] < rows) {
-        const int h = (int)(row[u] % Hq);
-        const int64_t bs = row[u] / Hq;
-        const int s = (int)(bs % S), b = (int)(bs / S);
-        const int64_t li = ((int64_t)b * Hq + h) * S + s;
-        delta[li] = acc[u];
-        lse2[li] = lse[li] * 1.4426950408889634f;
-      }
-    }
-  }
-}
 
 // 64 consecutive columns of one TMEM row (this thread's lane) -> registers
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t (&r)[64]) {
@@ -958,7 +906,8 @@ struct BwdDqSmem {
   static constexpr int kQ = 0, kDO = kTile;
   static constexpr int kK = 2 * kTile;                        // kBwdKStages stages
   static constexpr int kV = kK + kBwdKStages * kTile;         // kBwdVStages stages
-  static constexpr int kBar = kV + kBwdVStages * kTile;
+  static constexpr int kX = kV + kBwdVStages * kTile;         // [2 halves][128 rows] fp32
+  static constexpr int kBar = kX + 2 * 128 * 4;
   static constexpr int kBytes = kBar + 256 + 1024;
 };
 
@@ -1018,7 +967,8 @@ __device__ __forceinline__ void bwd_store_half_row(uint32_t tblk, int col0, floa
 __global__ void __launch_bounds__(kBwdThreads, 1)
 attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                      const float* __restrict__ lse, const float* __restrict__ delta,
+                      const float* __restrict__ lse, const __nv_bfloat16* __restrict__ o,
+                      float* __restrict__ delta, float* __restrict__ lse2,
                       __nv_bfloat16* __restrict__ dq, int B, int S, int Hq, int Hk, float scale_log2,
                       float scale, int causal, const float2* __restrict__ rope_cs, DeviceStatus* status,
                       unsigned long long* __restrict__ trace) {
@@ -1153,8 +1103,40 @@ attn_bwd_dq_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_cons
     const int q = qt * kAttRows + row;
     const int64_t lrow = ((int64_t)b * Hq + h) * S + q;
     const float l2 = lse[lrow] * 1.4426950408889634f;      // lse in log2 units
-    const float dl = delta[lrow];
+    // delta = rowsum(dO ∘ O) of this query row, computed here (and written for
+    // the dK/dV kernel with lse2): this half's 64 columns of O from global
+    // (loads issued before the tile wait), of dO from the tile in shared memory
+    uint4 ov[8];
+    {
+      const uint4* orow = reinterpret_cast<const uint4*>(o + (((int64_t)b * S + q) * Hq + h) * kAttD + col0);
+#pragma unroll
+      for (int c = 0; c < 8; ++c) ov[c] = orow[c];
+    }
+    float dl = 0.0f;
     bool ok = named_barrier_and(pair_bar, 64, mbar_wait(q_full, 0, status, kErrBwdCompute));
+    if (ok) {
+      const uint8_t* drow = smem + L::kDO + half * L::kAtom + row * 128;
+      float acc = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {   // dO chunk c (8 columns) sits at swizzled slot c ^ (row & 7)
+        const uint4 du = *reinterpret_cast<const uint4*>(drow + ((c ^ (row & 7)) << 4));
+        const uint32_t dw[4] = {du.x, du.y, du.z, du.w}, ow[4] = {ov[c].x, ov[c].y, ov[c].z, ov[c].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 x = bf16x2_to_f2(dw[j]), y = bf16x2_to_f2(ow[j]);
+          acc = fmaf(x.x, y.x, acc);
+          acc = fmaf(x.y, y.y, acc);
+        }
+      }
+      float* xs = reinterpret_cast<float*>(smem + L::kX);
+      xs[half * 128 + row] = acc;
+      named_barrier(pair_bar, 64);
+      dl = xs[row] + xs[128 + row];
+      if (half == 0) {
+        delta[lrow] = dl;
+        lse2[lrow] = l2;
+      }
+    }
     if (ok) {  // Q and dO rows into tensor memory (A operands of S and dP)
       copy_row_to_tmem(smem + L::kQ + half * L::kAtom + row * 128, row,
                        tmem + lane_base + 384u + (uint32_t)(half * 32));
@@ -1855,7 +1837,8 @@ void attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Ten
 }
 
 // Backward of attn_fwd_tc: dq, dk, dv [B, S, H, D] bf16 from dout, q, k, v, o and
-// the forward's lse.  Three launches: delta, dQ (per query tile), dK/dV (per key tile).
+// the forward's lse.  Two launches: dQ (per query tile; writes delta and lse2 too),
+// then dK/dV (per key tile).
 // trace (optional): int64 [dQ grid + dK/dV grid, 32] per-CTA timestamps.
 void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o,
                  at::Tensor lse, at::Tensor dq, at::Tensor dk, at::Tensor dv, bool causal,
@@ -1906,14 +1889,8 @@ void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::
   }
   auto delta = at::empty({B, Hq, S}, q.options().dtype(at::kFloat));
   auto lse2 = at::empty({B, Hq, S}, q.options().dtype(at::kFloat));
-  const int64_t rows = B * S * Hq;
-  const int64_t delta_blocks = std::max<int64_t>(
-      1, std::min<int64_t>((rows / 2 + 7) / 8, (int64_t)at::cuda::getCurrentDeviceProperties()->multiProcessorCount * 8));
-  attn_delta_kernel<<<(unsigned)delta_blocks, 256, 0, stream>>>(
-      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr<at::BFloat16>()),
-      reinterpret_cast<const __nv_bfloat16*>(o.data_ptr<at::BFloat16>()), lse.data_ptr<float>(),
-      delta.data_ptr<float>(), lse2.data_ptr<float>(), rows, (int)S, (int)Hq);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  // delta = rowsum(dO ∘ O) and lse2 = lse·log2(e) are produced by the dQ kernel
+  // (each query row by the CTA that owns it) for the dK/dV kernel launched after it
   const CUtensorMap tq = make_tmap_bshd(q), tk = make_tmap_bshd(k), tv = make_tmap_bshd(v),
                     tdo = make_tmap_bshd(dout);
   const float sl2 = (float)(scale * 1.4426950408889634);
@@ -1927,7 +1904,9 @@ void attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::
     trp = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
   }
   attn_bwd_dq_tc_kernel<<<(unsigned)g_dq, kBwdThreads, BwdDqSmem::kBytes, stream>>>(
-      tq, tk, tv, tdo, lse.data_ptr<float>(), delta.data_ptr<float>(),
+      tq, tk, tv, tdo, lse.data_ptr<float>(),
+      reinterpret_cast<const __nv_bfloat16*>(o.data_ptr<at::BFloat16>()), delta.data_ptr<float>(),
+      lse2.data_ptr<float>(),
       reinterpret_cast<__nv_bfloat16*>(dq.data_ptr<at::BFloat16>()), (int)B, (int)S, (int)Hq, (int)Hk, sl2,
       (float)scale, causal ? 1 : 0, rcs, st, trp);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
