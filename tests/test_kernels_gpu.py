@@ -1108,6 +1108,26 @@ def test_fused_qkv_projection_matches_separate_projections(cuda, lora_r):
             assert torch.equal(a, b)
         else:  # LoRA grads: atomic fp32 sums over token ranges, no fixed order
             torch.testing.assert_close(a, b, rtol=1e-4, atol=1e-5)
+    if lora_r:
+        # an in-place update of the adapters (what an optimizer step does) must
+        # repack the cached q/k/v blocks
+        with torch.no_grad():
+            for m in mods:
+                m.lora_A.mul_(1.5)
+                m.lora_B.add_(0.01)
+        outs = []
+        for fused in (True, False):
+            if fused:
+                q, k, v = qkv_projection(x, mods, cs, cache)
+            else:
+                q, k = apply_rope(mods[0](x).view(B, S, Hq, 128), mods[1](x).view(B, S, Hk, 128),
+                                  10000.0)
+                v = mods[2](x).view(B, S, Hk, 128)
+            outs.append(flash_attention(q, k, v, causal=True).detach().float())
+        torch.cuda.synchronize()
+        scale = outs[1].abs().max().item() + 1e-6
+        assert (outs[0] - outs[1]).abs().max().item() <= 2e-2 * scale
+        assert (outs[0] - results[0][0].float()).abs().max().item() > 1e-3 * scale  # it changed
 
 
 @pytest.mark.parametrize("E", [128, 192, 256])

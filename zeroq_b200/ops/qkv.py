@@ -46,10 +46,12 @@ def _decode_into(mods, w: torch.Tensor):
 def _lora_blocks(mods, cache: dict):
     """``(g, A_cat [W, d], B_blk [Nq+Nk+Nv, W], B_catT [3g, Nq+Nk+Nv])`` with ``g`` the
     per-adapter column stride in rank space and ``W`` the slab width (64 when the
-    three ranks pack into one slab, else 3 x 64), rebuilt only when a module's
-    LoRA operands change."""
-    ops = [m._lora_operands() for m in mods]
-    key = tuple(m._lora_key for m in mods)
+    three ranks pack into one slab, else 3 x 64).  The three buffers persist (their
+    padding stays zero); when an adapter changes (every optimizer step) each one
+    is packed straight into its slices from the fp32 parameters - one pack kernel
+    per adapter, no per-step allocation or slice copies."""
+    key = tuple((m.lora_A._version, m.lora_B._version, m.lora_A.data_ptr(), m.lora_B.data_ptr(),
+                 float(m.scaling)) for m in mods)
     if cache.get("key") != key:
         r = mods[0].lora_r
         g = lora_k.round16(r)
@@ -58,18 +60,28 @@ def _lora_blocks(mods, cache: dict):
         W = 64 if 3 * g <= 64 else 3 * 64
         Nt = sum(m.out_features for m in mods)
         d = mods[0].in_features
-        dev = ops[0][0].device
-        A_cat = torch.zeros(W, d, dtype=torch.bfloat16, device=dev)
-        B_blk = torch.zeros(Nt, W, dtype=torch.bfloat16, device=dev)
-        B_catT = torch.zeros(3 * g, Nt, dtype=torch.bfloat16, device=dev)
+        dev = mods[0].lora_A.device
+        if cache.get("shape") != (g, W, Nt, d, r, dev):
+            cache.update(shape=(g, W, Nt, d, r, dev),
+                         A_cat=torch.zeros(W, d, dtype=torch.bfloat16, device=dev),
+                         B_blk=torch.zeros(Nt, W, dtype=torch.bfloat16, device=dev),
+                         B_catT=torch.zeros(3 * g, Nt, dtype=torch.bfloat16, device=dev))
+        A_cat, B_blk, B_catT = cache["A_cat"], cache["B_blk"], cache["B_catT"]
         off = 0
-        for i, (m, o) in enumerate(zip(mods, ops)):
-            n = m.out_features
-            A_cat[g * i:g * i + r] = o[0][:r]
-            B_blk[off:off + n, g * i:g * i + r] = o[1][:, :r]
-            B_catT[g * i:g * i + r, off:off + n] = o[2][:r]
-            off += n
-        cache.update(key=key, g=g, A_cat=A_cat, B_blk=B_blk, B_catT=B_catT)
+        with torch.no_grad():
+            for i, m in enumerate(mods):
+                n = m.out_features
+                A, B = m.lora_A.detach(), m.lora_B.detach()
+                a_v, b_v = A_cat[g * i:g * i + r], B_blk[off:off + n, g * i:g * i + r]
+                t_v = B_catT[g * i:g * i + r, off:off + n]
+                if A.is_cuda and A.dtype == torch.float32 and B.dtype == torch.float32:
+                    _ext.ext().lora_pack(A.contiguous(), B.contiguous(), float(m.scaling), a_v, b_v, t_v)
+                else:
+                    a_v.copy_(A.float() * m.scaling)
+                    b_v.copy_(B)
+                    t_v.copy_(B.t())
+                off += n
+        cache.update(key=key, g=g)
     return cache["g"], cache["A_cat"], cache["B_blk"], cache["B_catT"]
 
 
