@@ -35,6 +35,8 @@ void gemm_bf16_nn(at::Tensor a, at::Tensor b, at::Tensor c, c10::optional<at::Te
                   c10::optional<at::Tensor> b2);
 std::vector<int64_t> gemm_status(int64_t device);
 void set_gemm_pair_mode(int64_t mode);
+void nf4_to_bf16_segments(std::vector<at::Tensor> packed, std::vector<at::Tensor> absmax,
+                          std::vector<int64_t> numel, at::Tensor out, int64_t blocksize, int64_t qtype);
 void nf4_to_bf16(at::Tensor packed, at::Tensor absmax, at::Tensor out, int64_t rows, int64_t cols,
                  int64_t blocksize, int64_t qtype, bool transpose);
 // elementwise.cu
@@ -45,6 +47,7 @@ void rmsnorm_bwd(at::Tensor gy, at::Tensor x, at::Tensor w, at::Tensor rstd,
 void colsum_accum(at::Tensor part, at::Tensor out);
 void rope(at::Tensor x, at::Tensor out, at::Tensor cs, double sign);
 void rope_into(at::Tensor x, at::Tensor out, at::Tensor cs, double sign);
+void rope_into2(at::Tensor x1, at::Tensor out1, at::Tensor x2, at::Tensor out2, at::Tensor cs, double sign);
 void gelu_fwd(at::Tensor x, at::Tensor y);
 void gelu_cdf_pdf(at::Tensor x, at::Tensor cdf, at::Tensor pdf);
 void gelu_bwd(at::Tensor g, at::Tensor x, at::Tensor dx);
@@ -137,11 +140,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_status", &gemm_status);
   m.def("set_gemm_pair_mode", &set_gemm_pair_mode);
   m.def("nf4_to_bf16", &nf4_to_bf16);
+  m.def("nf4_to_bf16_segments", &nf4_to_bf16_segments,
+        "several 4-bit weights into consecutive ranges of one bf16 buffer, one launch");
   m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("colsum_accum", &colsum_accum);
   m.def("rope", &rope);
   m.def("rope_into", &rope_into);
+  m.def("rope_into2", &rope_into2, "rope_into for two (x, out) pairs in one launch");
   m.def("gelu_fwd", &gelu_fwd);
   m.def("gelu_bwd", &gelu_bwd);
   m.def("gelu_cdf_pdf", &gelu_cdf_pdf);

@@ -257,13 +257,40 @@ __global__ void __launch_bounds__(kNormThreads, (PF && NC <= 3) ? 2 : 1) rmsnorm
 // cs: [S, D/2] float2 (cos, sin) table; each thread rotates 8 pairs with
 // 16-byte loads/stores from both halves of the row.
 // ----------------------------------------------------------------------------
+__device__ __forceinline__ void rope_chunk(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ out,
+                                           const float2* __restrict__ cs, int64_t t, int S, int H, int D,
+                                           float sign, int64_t out_ld);
+
 __global__ void rope_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ out,
                             const float2* __restrict__ cs, int64_t rows, int S, int H, int D,
                             float sign, int64_t out_ld) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= rows * ((D >> 1) >> 3)) return;
+  rope_chunk(x, out, cs, t, S, H, D, sign, out_ld);
+}
+
+// Two tensors in one launch (the q and k gradients of a fused projection):
+// threads past the first tensor's chunks take the second's.
+__global__ void rope2_kernel(const __nv_bfloat16* __restrict__ x1, __nv_bfloat16* __restrict__ out1,
+                             int64_t rows1, int H1, int64_t ld1, const __nv_bfloat16* __restrict__ x2,
+                             __nv_bfloat16* __restrict__ out2, int64_t rows2, int H2, int64_t ld2,
+                             const float2* __restrict__ cs, int S, int D, float sign) {
+  const int64_t groups = (D >> 1) >> 3;
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t n1 = rows1 * groups;
+  if (t < n1) {
+    rope_chunk(x1, out1, cs, t, S, H1, D, sign, ld1);
+  } else if (t - n1 < rows2 * groups) {
+    rope_chunk(x2, out2, cs, t - n1, S, H2, D, sign, ld2);
+  }
+}
+
+// chunk t = (row, 8 rotary pairs) of x [rows = B*S*H, D] rotated into out
+__device__ __forceinline__ void rope_chunk(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ out,
+                                           const float2* __restrict__ cs, int64_t t, int S, int H, int D,
+                                           float sign, int64_t out_ld) {
   const int half = D >> 1;
   const int groups = half >> 3;
-  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= rows * groups) return;
   const int64_t row = t / groups;
   const int i0 = (int)(t % groups) * 8;
   const int pos = (int)((row / H) % S);
@@ -769,6 +796,35 @@ void rope(at::Tensor x, at::Tensor out, at::Tensor cs, double sign) {
 
 // RoPE of x [B, S, H, D] written into the first H*D columns of the rows of
 // out [B*S, >= H*D] (row pitch out.stride(0)): a slice of a wider buffer.
+// rope_into for two (x, out) pairs in one launch (same positions and table)
+void rope_into2(at::Tensor x1, at::Tensor out1, at::Tensor x2, at::Tensor out2, at::Tensor cs, double sign) {
+  for (auto pr : {std::make_pair(&x1, &out1), std::make_pair(&x2, &out2)}) {
+    const at::Tensor& x = *pr.first;
+    const at::Tensor& out = *pr.second;
+    check_bf16(x, "x");
+    TORCH_CHECK(x.dim() == 4, "rope_into2: x must be [B, S, H, D]");
+    TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.dim() == 2 &&
+                    out.size(0) == x.size(0) * x.size(1) && out.size(1) >= x.size(2) * x.size(3) &&
+                    out.stride(1) == 1 && out.stride(0) % 8 == 0 &&
+                    (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0,
+                "rope_into2: out must be bf16 [B*S, >= H*D] with 16-byte aligned rows");
+  }
+  const int64_t S = x1.size(1), D = x1.size(3);
+  TORCH_CHECK(x2.size(1) == S && x2.size(3) == D && x2.size(0) == x1.size(0), "rope_into2: shapes");
+  TORCH_CHECK(D % 16 == 0, "rope_into2: head dim must be a multiple of 16");
+  TORCH_CHECK(cs.scalar_type() == at::kFloat && cs.is_contiguous() && cs.numel() >= S * D,
+              "rope_into2: cos/sin table must be fp32 [S, D/2, 2]");
+  const at::cuda::CUDAGuard guard(x1.device());
+  const int64_t rows1 = x1.size(0) * S * x1.size(2), rows2 = x2.size(0) * S * x2.size(2);
+  const int64_t total = (rows1 + rows2) * (D / 16);
+  rope2_kernel<<<(unsigned)((total + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      cbf(x1), reinterpret_cast<__nv_bfloat16*>(out1.data_ptr<at::BFloat16>()), rows1, (int)x1.size(2),
+      out1.stride(0), cbf(x2), reinterpret_cast<__nv_bfloat16*>(out2.data_ptr<at::BFloat16>()), rows2,
+      (int)x2.size(2), out2.stride(0), reinterpret_cast<const float2*>(cs.data_ptr<float>()), (int)S,
+      (int)D, (float)sign);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void rope_into(at::Tensor x, at::Tensor out, at::Tensor cs, double sign) {
   check_bf16(x, "x");
   TORCH_CHECK(x.dim() == 4, "rope_into: x must be [B, S, H, D]");

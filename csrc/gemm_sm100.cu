@@ -1712,6 +1712,93 @@ __global__ void __launch_bounds__(256) nf4_to_bf16_flat_kernel(
   }
 }
 
+// Several 4-bit weights decoded into consecutive ranges of one bf16 buffer in one
+// launch (the operand of a fused projection, e.g. q/k/v): segment s covers flat
+// 8-code units [start[s], start[s+1]) of the output, reading its own packed
+// bytes and absmax.  Same per-unit arithmetic as nf4_to_bf16_flat_kernel.
+constexpr int kMaxDecodeSegs = 4;
+struct DecodeSegs {
+  const uint32_t* packed[kMaxDecodeSegs];
+  const float* absmax[kMaxDecodeSegs];
+  int64_t start[kMaxDecodeSegs + 1];   // in 8-code units
+  int nseg;
+};
+
+__global__ void __launch_bounds__(256) nf4_to_bf16_segments_kernel(const __grid_constant__ DecodeSegs sg,
+                                                                   uint4* __restrict__ out, int blocksize,
+                                                                   int qtype) {
+  __shared__ float lut[16];
+  if (threadIdx.x < 16) lut[threadIdx.x] = qtype == 0 ? c_code_nf4[threadIdx.x] : c_code_fp4[threadIdx.x];
+  __syncthreads();
+  const int64_t n8 = sg.start[sg.nseg];
+  const int64_t base = (int64_t)blockIdx.x * blockDim.x * kFlatIlp + threadIdx.x;
+  uint32_t raw[kFlatIlp];
+  float am[kFlatIlp];
+#pragma unroll
+  for (int j = 0; j < kFlatIlp; ++j) {
+    const int64_t i = base + (int64_t)j * blockDim.x;
+    if (i < n8) {
+      int s = 0;
+      while (s + 1 < sg.nseg && i >= sg.start[s + 1]) ++s;
+      const int64_t li = i - sg.start[s];
+      raw[j] = __ldg(sg.packed[s] + li);
+      am[j] = __ldg(sg.absmax[s] + (li * 8) / blocksize);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kFlatIlp; ++j) {
+    const int64_t i = base + (int64_t)j * blockDim.x;
+    if (i < n8) {
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t byte = (raw[j] >> (8 * q)) & 0xFFu;
+        o[q] = pack_bf16x2(lut[byte >> 4] * am[j], lut[byte & 15u] * am[j]);
+      }
+      out[i] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+// out (bf16, contiguous) = the weights of `packed[s]` / `absmax[s]` (numel[s]
+// elements each, row-major) one after the other; every numel a multiple of the
+// block size and of 8, at most 4 segments.
+void nf4_to_bf16_segments(std::vector<at::Tensor> packed, std::vector<at::Tensor> absmax,
+                          std::vector<int64_t> numel, at::Tensor out, int64_t blocksize, int64_t qtype) {
+  const int ns = (int)packed.size();
+  TORCH_CHECK(ns >= 1 && ns <= kMaxDecodeSegs && (int)absmax.size() == ns && (int)numel.size() == ns,
+              "nf4_to_bf16_segments: 1-4 segments with packed, absmax and numel each");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() &&
+                  (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0,
+              "nf4_to_bf16_segments: out must be contiguous, 16-byte aligned bf16");
+  TORCH_CHECK(blocksize > 0 && blocksize % 8 == 0 && (qtype == 0 || qtype == 1),
+              "nf4_to_bf16_segments: block size a multiple of 8, qtype 0 or 1");
+  DecodeSegs sg{};
+  sg.nseg = ns;
+  int64_t total = 0;
+  for (int s = 0; s < ns; ++s) {
+    TORCH_CHECK(numel[s] % 8 == 0 && numel[s] % blocksize == 0, "nf4_to_bf16_segments: numel % 8 and % blocksize");
+    TORCH_CHECK(packed[s].is_cuda() && packed[s].scalar_type() == at::kByte && packed[s].numel() * 2 >= numel[s] &&
+                    (reinterpret_cast<uintptr_t>(packed[s].data_ptr()) & 3) == 0,
+                "nf4_to_bf16_segments: packed must be 4-byte aligned uint8 covering numel");
+    TORCH_CHECK(absmax[s].scalar_type() == at::kFloat && absmax[s].numel() * blocksize >= numel[s],
+                "nf4_to_bf16_segments: absmax must be fp32 covering numel");
+    sg.packed[s] = reinterpret_cast<const uint32_t*>(packed[s].data_ptr<uint8_t>());
+    sg.absmax[s] = absmax[s].data_ptr<float>();
+    sg.start[s] = total / 8;
+    total += numel[s];
+  }
+  sg.start[ns] = total / 8;
+  TORCH_CHECK(out.numel() >= total, "nf4_to_bf16_segments: out too small");
+  const at::cuda::CUDAGuard guard(out.device());
+  const int64_t n8 = total / 8;
+  const int64_t blocks = (n8 + 256 * kFlatIlp - 1) / (256 * kFlatIlp);
+  if (blocks == 0) return;
+  nf4_to_bf16_segments_kernel<<<(unsigned)blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      sg, reinterpret_cast<uint4*>(out.data_ptr<at::BFloat16>()), (int)blocksize, (int)qtype);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void nf4_to_bf16(at::Tensor packed, at::Tensor absmax, at::Tensor out, int64_t rows, int64_t cols,
                  int64_t blocksize, int64_t qtype, bool transpose) {
   TORCH_CHECK(packed.is_cuda() && packed.scalar_type() == at::kByte, "nf4_to_bf16: uint8 packed");

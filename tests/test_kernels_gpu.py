@@ -646,6 +646,46 @@ def test_ag_gemm_one_kernel_matches_dequant_then_gemm(cuda, M, N, K, starts_frac
     assert (y.float() - want).abs().max().item() < 2e-2 * want.abs().max().item() + 1e-2
 
 
+def test_rope_into2_matches_two_rope_into(cuda):
+    """The q and k gradients un-rotated by one launch equal two separate launches,
+    into column slices of one fused gradient buffer."""
+    from zeroq_b200.ops.rope import rope_table
+
+    torch.manual_seed(22)
+    B, S, Hq, Hk, D = 2, 256, 4, 2, 128
+    dq = torch.randn(B, S, Hq, D, device=cuda).to(torch.bfloat16)
+    dk = torch.randn(B, S, Hk, D, device=cuda).to(torch.bfloat16)
+    cs = rope_table(S, D, 10000.0, cuda)
+    Nt = (Hq + 2 * Hk) * D
+    g1 = torch.zeros(B * S, Nt, dtype=torch.bfloat16, device=cuda)
+    g2 = torch.zeros_like(g1)
+    o1, o2 = Hq * D, (Hq + Hk) * D
+    _ext.ext().rope_into2(dq, g1[:, :o1], dk, g1[:, o1:o2], cs, -1.0)
+    _ext.ext().rope_into(dq, g2[:, :o1], cs, -1.0)
+    _ext.ext().rope_into(dk, g2[:, o1:o2], cs, -1.0)
+    torch.cuda.synchronize()
+    assert torch.equal(g1, g2)
+    assert float(g1[:, o2:].abs().sum()) == 0.0
+
+
+def test_nf4_segments_decode_matches_per_weight_decodes(cuda):
+    """Three 4-bit weights decoded into one buffer by one launch equal the three
+    separate decodes, byte for byte (the fused q/k/v operand)."""
+    torch.manual_seed(21)
+    shapes = [(1024, 512), (256, 512), (256, 512)]
+    qs = [quantize_4bit(torch.randn(n, k, device=cuda) * 0.02, 64, "nf4") for n, k in shapes]
+    total = sum(n * k for n, k in shapes)
+    out = torch.empty(total, dtype=torch.bfloat16, device=cuda)
+    _ext.ext().nf4_to_bf16_segments([p.reshape(-1) for p, _ in qs], [st.absmax.reshape(-1) for _, st in qs],
+                                    [n * k for n, k in shapes], out, 64, 0)
+    ref, off = torch.empty_like(out), 0
+    for (n, k), (p, st) in zip(shapes, qs):
+        _ext.ext().nf4_to_bf16(p.reshape(-1), st.absmax.reshape(-1), ref[off:off + n * k], n, k, 64, 0, False)
+        off += n * k
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+
+
 def test_gather_dequant_fast_path_matches_full(cuda):
     """The warp-per-item peer gather + dequantise (standalone kernel) over uneven
     pieces equals the full dequantise, for a row window too."""

@@ -34,7 +34,15 @@ from .qlinear import KEEP_OPERANDS
 
 
 def _decode_into(mods, w: torch.Tensor):
+    """The modules' 4-bit weights, one after the other, into ``w`` (one launch when
+    they share block size and code)."""
     E = _ext.ext()
+    if (len({m.blocksize for m in mods}) == 1 and len({m.quant_type for m in mods}) == 1
+            and len(mods) <= 4 and w.is_contiguous()):
+        E.nf4_to_bf16_segments([m.weight_packed for m in mods], [m.weight_absmax for m in mods],
+                               [m.out_features * m.in_features for m in mods], w,
+                               mods[0].blocksize, QUANT_TYPE_ID[mods[0].quant_type])
+        return
     off = 0
     for m in mods:
         n, d = m.out_features, m.in_features
@@ -149,11 +157,15 @@ class QKVFunction(torch.autograd.Function):
                 dv.untyped_storage(), 0, (M, Nt), (Nt, 1))
         else:
             g = torch.empty(M, Nt, dtype=torch.bfloat16, device=dev)
+        both = dq is not None and dk is not None
+        if both:   # gradients of the pre-rotation q and k columns: one launch
+            E.rope_into2(dq.contiguous(), g[:, :o1], dk.contiguous(), g[:, o1:o2], cs, -1.0)
         for grad, lo, hi, rot in ((dq, 0, o1, True), (dk, o1, o2, True), (dv, o2, Nt, False)):
             if grad is None:
                 g[:, lo:hi].zero_()
             elif rot:   # gradient of the pre-rotation columns, straight into its slice
-                E.rope_into(grad.contiguous(), g[:, lo:hi], cs, -1.0)
+                if not both:
+                    E.rope_into(grad.contiguous(), g[:, lo:hi], cs, -1.0)
             elif not in_place:
                 g[:, lo:hi].copy_(grad.reshape(M, hi - lo))
         d = mods[0].in_features
