@@ -127,8 +127,9 @@ class StepLogger:
             rec = {"step": step, "loss": loss, "ms": round(ms, 3), "tokens_per_s": round(tps, 1),
                    "gather_bytes": moved["gather_bytes"], "sync_bytes": moved["sync_bytes"]}
             if self.fpt is not None and self.peak:
-                rec["model_tflops_per_gpu"] = round(self.fpt * tps / self.world / 1e12, 1)
-                rec["frac_of_peak"] = round(self.fpt * tps / self.world / 1e12 / self.peak, 3)
+                rec["model_tflops_per_gpu"] = round(self.fpt * tps / self.world / 1e12, 3)
+                # (6 decimals: small models sit far below a B200's peak)
+                rec["frac_of_peak"] = round(self.fpt * tps / self.world / 1e12 / self.peak, 6)
             out.append(rec)
         self._pending = []
         self.records.extend(out)
