@@ -190,7 +190,7 @@ def w_sharded_adamw(rank, world):
 
 
 def w_tiny_decoder_training(rank, world):
-    """tiny decoder, NF4 shards in gather/release mode, 20 AdamW steps."""
+    """The tiny-decoder plumbing workload: NF4 shards in gather/release mode, 20 AdamW steps."""
     import zeroq_b200 as zq
     from zeroq_b200.models import DecoderLM, get_config
 
