@@ -19,6 +19,7 @@ void gemm_nf4(at::Tensor a, at::Tensor packed, at::Tensor absmax, int64_t rows, 
               c10::optional<at::Tensor> a2, c10::optional<at::Tensor> b2);
 void lora_pack(at::Tensor A, at::Tensor B, double scaling, at::Tensor a_pad, at::Tensor b_pad,
                c10::optional<at::Tensor> b_t);
+void lora_pack_many(at::Tensor table, int64_t max_elems);
 // lora_sm100.cu
 void lora_down(at::Tensor p, at::Tensor w, at::Tensor u, c10::optional<at::Tensor> ut, int64_t cs,
                int64_t stages, int64_t kb);
@@ -127,6 +128,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("kv_bhsd") = false);
   m.def("lora_pack", &lora_pack, py::arg("A"), py::arg("B"), py::arg("scaling"), py::arg("a_pad"),
         py::arg("b_pad"), py::arg("b_t") = py::none());
+  m.def("lora_pack_many", &lora_pack_many, "many LoRA operand packs in one launch (a table of jobs)");
   m.def("lora_down", &lora_down, py::arg("p"), py::arg("w"), py::arg("u"), py::arg("ut") = py::none(),
         py::arg("cs") = 0, py::arg("stages") = 0, py::arg("kb") = 0);
   m.def("lora_wgrad", &lora_wgrad, py::arg("p"), py::arg("qt"), py::arg("nq"), py::arg("i_begin"),

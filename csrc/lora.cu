@@ -40,9 +40,57 @@ __global__ void lora_pack_kernel(const float* __restrict__ A, const float* __res
   }
 }
 
+// Many lora_pack jobs in one launch: job j = blockIdx.y reads its row of `table`
+// (kPackFields int64 words: A, B, a_pad, a_ld, b_pad, b_ld, b_t, t_ld, r, K, N,
+// scaling as fp32 bits; b_t may be 0) and runs the same element loop.
+constexpr int kPackFields = 12;
+
+__global__ void lora_pack_many_kernel(const int64_t* __restrict__ table) {
+  const int64_t* e = table + (int64_t)blockIdx.y * kPackFields;
+  const float* A = reinterpret_cast<const float*>(e[0]);
+  const float* B = reinterpret_cast<const float*>(e[1]);
+  __nv_bfloat16* a_pad = reinterpret_cast<__nv_bfloat16*>(e[2]);
+  __nv_bfloat16* b_pad = reinterpret_cast<__nv_bfloat16*>(e[4]);
+  __nv_bfloat16* b_t = reinterpret_cast<__nv_bfloat16*>(e[6]);
+  const int64_t a_ld = e[3], b_ld = e[5], t_ld = e[7], K = e[9], N = e[10];
+  const int r = (int)e[8];
+  const float s = __int_as_float((int)e[11]);
+  const int64_t na = (int64_t)r * K, nb = N * r, nt = b_t != nullptr ? N * r : 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < na + nb + nt;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    if (i < na) {
+      const int64_t row = i / K, col = i % K;
+      a_pad[row * a_ld + col] = __float2bfloat16_rn(s * A[i]);
+    } else if (i < na + nb) {
+      const int64_t j = i - na, row = j / r, col = j % r;
+      b_pad[row * b_ld + col] = __float2bfloat16_rn(B[j]);
+    } else {
+      const int64_t j = i - na - nb, row = j / N, col = j % N;
+      b_t[row * t_ld + col] = __float2bfloat16_rn(B[col * r + row]);
+    }
+  }
+}
+
 }  // namespace zq
 
 using namespace zq;
+
+// table: int64 CUDA tensor [jobs, 12] (see lora_pack_many_kernel); max_elems: the
+// largest job's element count (sizes the grid).  The caller validated every job
+// the way lora_pack does.
+void lora_pack_many(at::Tensor table, int64_t max_elems) {
+  TORCH_CHECK(table.is_cuda() && table.scalar_type() == at::kLong && table.is_contiguous() &&
+                  table.dim() == 2 && table.size(1) == kPackFields,
+              "lora_pack_many: table must be a contiguous int64 CUDA tensor [jobs, 12]");
+  const int64_t jobs = table.size(0);
+  if (jobs == 0 || max_elems <= 0) return;
+  TORCH_CHECK(jobs <= 65535, "lora_pack_many: at most 65535 jobs");
+  const at::cuda::CUDAGuard guard(table.device());
+  const int64_t bx = std::min<int64_t>((max_elems + 255) / 256, 16);
+  lora_pack_many_kernel<<<dim3((unsigned)bx, (unsigned)jobs), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      table.data_ptr<int64_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 
 void lora_pack(at::Tensor A, at::Tensor B, double scaling, at::Tensor a_pad, at::Tensor b_pad,
                c10::optional<at::Tensor> b_t) {

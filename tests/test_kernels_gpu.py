@@ -646,6 +646,75 @@ def test_ag_gemm_one_kernel_matches_dequant_then_gemm(cuda, M, N, K, starts_frac
     assert (y.float() - want).abs().max().item() < 2e-2 * want.abs().max().item() + 1e-2
 
 
+def test_lora_pack_batch_matches_per_module_packs(cuda):
+    """One lora_pack_many launch over several adapters writes exactly what the
+    per-adapter lora_pack launches write (padding stays zero)."""
+    from zeroq_b200.ops import lora as lora_k
+    from zeroq_b200.ops.qlinear import LoraPackBatch, _pack_lora
+
+    torch.manual_seed(23)
+    jobs, refs, bufs = [], [], []
+    for r, K, N, sc in [(16, 512, 1024, 2.0), (16, 1024, 512, 0.5), (8, 256, 768, 1.0)]:
+        A = torch.randn(r, K, device=cuda)
+        B = torch.randn(N, r, device=cuda)
+        out = (torch.zeros(64, K, dtype=torch.bfloat16, device=cuda),
+               torch.zeros(N, 64, dtype=torch.bfloat16, device=cuda),
+               torch.zeros(lora_k.round16(r), N, dtype=torch.bfloat16, device=cuda))
+        jobs.append((A, B, sc, out[0], out[1], out[2], lambda: None))
+        bufs.append(out)
+        refs.append(_pack_lora(A, B, sc))
+    assert LoraPackBatch().run(jobs)
+    torch.cuda.synchronize()
+    for out, ref in zip(bufs, refs):
+        for a, b in zip(out, ref):
+            assert torch.equal(a, b)
+
+
+def test_trainer_batch_pack_keeps_lora_operands_current(cuda):
+    """After Trainer steps (each ending with one batched repack) every cached LoRA
+    operand - the fused q/k/v blocks and each projection's own - equals a fresh
+    pack of the adapter's current parameters."""
+    import zeroq_b200 as zq
+    from zeroq_b200.models import DecoderLM, get_config
+    from zeroq_b200.ops.qkv import _lora_blocks
+    from zeroq_b200.ops.qlinear import _pack_lora
+    from zeroq_b200.train import Trainer, synthetic_batch
+
+    cfg = get_config("4.7b", d_model=256, n_layers=2, n_heads=2, n_kv_heads=2, ffn_dim=1024,
+                     vocab_size=1000, lora_r=16, lora_alpha=32.0)
+    model = DecoderLM(cfg, device=cuda).init_dense_(seed=0)
+    zq.initialize(model, zq.ZeroQConfig(compute_dtype=torch.bfloat16, compute_in_4bit=True,
+                                        gather_once=True,
+                                        exclude_modules=["lm_head", "embed_tokens"]),
+                  trainable_patterns=("lora_", "norm"))
+    with torch.no_grad():
+        for n_, p in model.named_parameters():
+            if "lora_B" in n_:
+                p.normal_(0.0, 0.02)
+    opt = zq.ShardedAdamW(model.trainable_parameters(), lr=1e-2)
+    tr = Trainer(model, opt, cuda)
+    x, y = synthetic_batch(2, 256, cfg.vocab_size, seed=0)
+    for _ in range(3):
+        tr.step(x, y)
+    torch.cuda.synchronize()
+    checked = 0
+    for layer in model.layers:
+        for _, m in layer.projections():
+            if m._lora_ops is not None:
+                assert m._lora_key == m._lora_state_key()     # marked current by the batch
+                for a, b in zip(m._lora_ops, _pack_lora(m.lora_A.detach(), m.lora_B.detach(), m.scaling)):
+                    assert torch.equal(a, b)
+                checked += 1
+        cache = layer._qkv_cache
+        mods = (layer.q_proj, layer.k_proj, layer.v_proj)
+        got = [t.clone() for t in _lora_blocks(mods, cache)[1:]]   # current key: no repack
+        cache["key"] = None                                           # force a fresh pack
+        fresh = _lora_blocks(mods, cache)[1:]
+        for a, b in zip(got, fresh):
+            assert torch.equal(a, b)
+    assert checked > 0
+
+
 def test_rope_into2_matches_two_rope_into(cuda):
     """The q and k gradients un-rotated by one launch equal two separate launches,
     into column slices of one fused gradient buffer."""

@@ -383,6 +383,41 @@ class DecoderLM(nn.Module):
         :class:`~zeroq_b200.parallel.optimizer.ShardedAdamW`)."""
         return [[p for p in layer.parameters() if p.requires_grad] for layer in self.layers]
 
+    def pack_lora_operands(self) -> bool:
+        """Repack the bf16 LoRA operands of every adapter that already has them (the
+        fused q/k/v blocks and each other projection's own) in ONE launch, and mark
+        those caches current, so the next forward packs nothing.  Call after an
+        optimizer step (the :class:`~zeroq_b200.train.Trainer` does).  Adapters
+        without operands yet pack themselves on first use.  Returns False when
+        nothing was launched (the lazy per-module packs then run)."""
+        from ..ops.qkv import lora_block_views, lora_blocks_key
+        from ..ops.qlinear import Linear4bit, LoraPackBatch
+
+        jobs = []
+        for layer in self.layers:
+            cache = getattr(layer, "_qkv_cache", None)
+            mods = (layer.q_proj, layer.k_proj, layer.v_proj)
+            if cache and "A_cat" in cache and all(m.lora_r for m in mods):
+                views = lora_block_views(mods, cache)
+
+                def done_qkv(cache=cache, mods=mods):
+                    cache["key"] = lora_blocks_key(mods)
+
+                for i, (m, a_v, b_v, t_v) in enumerate(views):
+                    jobs.append((m.lora_A.detach(), m.lora_B.detach(), m.scaling, a_v, b_v, t_v,
+                                 done_qkv if i == len(views) - 1 else (lambda: None)))
+            for _, m in layer.projections():
+                ops = getattr(m, "_lora_ops", None) if isinstance(m, Linear4bit) else None
+                if m.lora_r and ops is not None:
+                    jobs.append((m.lora_A.detach(), m.lora_B.detach(), m.scaling, ops[0], ops[1], ops[2],
+                                 lambda m=m: setattr(m, "_lora_key", m._lora_state_key())))
+        if not jobs:
+            return False
+        if not hasattr(self, "_lora_batch"):
+            self._lora_batch = LoraPackBatch()
+        with torch.no_grad():
+            return self._lora_batch.run(jobs)
+
     def set_layer_grad_callback(self, fn):
         """``fn(i)`` runs in the backward when layer ``i``'s input gradient is
         computed - every gradient of layer ``i`` is written by then (e.g.

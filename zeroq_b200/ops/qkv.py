@@ -58,8 +58,7 @@ def _lora_blocks(mods, cache: dict):
     padding stays zero); when an adapter changes (every optimizer step) each one
     is packed straight into its slices from the fp32 parameters - one pack kernel
     per adapter, no per-step allocation or slice copies."""
-    key = tuple((m.lora_A._version, m.lora_B._version, m.lora_A.data_ptr(), m.lora_B.data_ptr(),
-                 float(m.scaling)) for m in mods)
+    key = lora_blocks_key(mods)
     if cache.get("key") != key:
         r = mods[0].lora_r
         g = lora_k.round16(r)
@@ -74,23 +73,38 @@ def _lora_blocks(mods, cache: dict):
                          A_cat=torch.zeros(W, d, dtype=torch.bfloat16, device=dev),
                          B_blk=torch.zeros(Nt, W, dtype=torch.bfloat16, device=dev),
                          B_catT=torch.zeros(3 * g, Nt, dtype=torch.bfloat16, device=dev))
-        A_cat, B_blk, B_catT = cache["A_cat"], cache["B_blk"], cache["B_catT"]
-        off = 0
+        cache["g"] = g
         with torch.no_grad():
-            for i, m in enumerate(mods):
-                n = m.out_features
+            for m, a_v, b_v, t_v in lora_block_views(mods, cache):
                 A, B = m.lora_A.detach(), m.lora_B.detach()
-                a_v, b_v = A_cat[g * i:g * i + r], B_blk[off:off + n, g * i:g * i + r]
-                t_v = B_catT[g * i:g * i + r, off:off + n]
                 if A.is_cuda and A.dtype == torch.float32 and B.dtype == torch.float32:
                     _ext.ext().lora_pack(A.contiguous(), B.contiguous(), float(m.scaling), a_v, b_v, t_v)
                 else:
                     a_v.copy_(A.float() * m.scaling)
                     b_v.copy_(B)
                     t_v.copy_(B.t())
-                off += n
         cache.update(key=key, g=g)
     return cache["g"], cache["A_cat"], cache["B_blk"], cache["B_catT"]
+
+
+def lora_blocks_key(mods):
+    """What the cached q/k/v block operands were packed from."""
+    return tuple((m.lora_A._version, m.lora_B._version, m.lora_A.data_ptr(), m.lora_B.data_ptr(),
+                  float(m.scaling)) for m in mods)
+
+
+def lora_block_views(mods, cache: dict):
+    """``(module, s·A slice, B slice, Bᵀ slice)`` of each adapter inside the cached
+    block buffers (their layout is fixed by ``_lora_blocks``)."""
+    g, r = cache["g"], mods[0].lora_r
+    A_cat, B_blk, B_catT = cache["A_cat"], cache["B_blk"], cache["B_catT"]
+    out, off = [], 0
+    for i, m in enumerate(mods):
+        n = m.out_features
+        out.append((m, A_cat[g * i:g * i + r], B_blk[off:off + n, g * i:g * i + r],
+                    B_catT[g * i:g * i + r, off:off + n]))
+        off += n
+    return out
 
 
 def _direct(p) -> bool:

@@ -571,6 +571,64 @@ def _pack_lora(A: torch.Tensor, B: torch.Tensor, scaling: float, out=None):
     return a_pad, b_pad, b_t
 
 
+class LoraPackBatch:
+    """Repack many adapters' bf16 operands in one launch (``lora_pack_many``).
+
+    ``run(jobs)``: each job is ``(A, B, scaling, a_view, b_view, bt_view, done)``
+    with the same shapes ``lora_pack`` takes; ``done()`` marks the owner's cache as
+    current.  The job table lives on the device and is rebuilt only when a pointer
+    or shape changes; a rebuild needs a host-to-device copy, so during stream
+    capture a changed table makes ``run`` return False without launching (the
+    owners then pack themselves on first use, as without the batch)."""
+
+    def __init__(self):
+        self._sig = None
+        self._table = None
+        self._max = 0
+
+    @staticmethod
+    def _check(A, B, a, b, t):
+        r, K = A.shape
+        N = B.shape[0]
+        ok = (A.is_cuda and A.dtype == torch.float32 and A.is_contiguous()
+              and B.dtype == torch.float32 and B.is_contiguous() and B.shape[1] == r
+              and a.dtype == torch.bfloat16 and a.shape[0] >= r and a.shape[1] == K and a.stride(1) == 1
+              and b.dtype == torch.bfloat16 and b.shape[0] == N and b.shape[1] >= r and b.stride(1) == 1
+              and (t is None or (t.dtype == torch.bfloat16 and t.shape[0] >= r and t.shape[1] == N
+                                 and t.stride(1) == 1)))
+        if not ok:
+            raise ValueError("LoraPackBatch: a job's operands do not have lora_pack's shapes")
+
+    def run(self, jobs) -> bool:
+        import struct
+
+        if not jobs:
+            return True
+        sig = tuple((A.data_ptr(), B.data_ptr(), tuple(A.shape), tuple(B.shape), float(s),
+                     a.data_ptr(), a.stride(0), b.data_ptr(), b.stride(0),
+                     0 if t is None else t.data_ptr(), 0 if t is None else t.stride(0))
+                    for A, B, s, a, b, t, _ in jobs)
+        if sig != self._sig:
+            if torch.cuda.is_current_stream_capturing():
+                return False
+            rows = []
+            for A, B, s, a, b, t, _ in jobs:
+                self._check(A, B, a, b, t)
+                r, K = A.shape
+                N = B.shape[0]
+                rows.append([A.data_ptr(), B.data_ptr(), a.data_ptr(), a.stride(0), b.data_ptr(),
+                             b.stride(0), 0 if t is None else t.data_ptr(),
+                             0 if t is None else t.stride(0), r, K, N,
+                             struct.unpack("<i", struct.pack("<f", float(s)))[0]])
+            self._table = torch.tensor(rows, dtype=torch.int64, device=jobs[0][0].device)
+            self._max = max(A.shape[0] * A.shape[1] + 2 * B.numel() for A, B, *_ in jobs)
+            self._sig = sig
+        _ext.ext().lora_pack_many(self._table, int(self._max))
+        for *_, done in jobs:
+            done()
+        return True
+
+
 def nf4_linear(x, packed, absmax, out_features: int, in_features: int, bias=None,
                lora_A=None, lora_B=None, scaling: float = 1.0, blocksize: int = 64,
                quant_type: str = "nf4", backend: str = "auto", lora_ops=None, peer=None,
@@ -692,12 +750,18 @@ class Linear4bit(nn.Module):
         """Drop the cached padded LoRA operands (after writes through ``.data``)."""
         self._lora_key = None
 
+    def _lora_state_key(self):
+        """What the cached LoRA operands were packed from (versions change on every
+        in-place update, e.g. an optimizer step)."""
+        A, B = self.lora_A, self.lora_B
+        return (A._version, B._version, A.data_ptr(), B.data_ptr(), float(self.scaling),
+                tuple(A.shape), tuple(B.shape))
+
     def _lora_operands(self):
         A, B = self.lora_A, self.lora_B
         if A is None or B is None or not A.is_cuda or A.shape[0] > 64:
             return None
-        key = (A._version, B._version, A.data_ptr(), B.data_ptr(), float(self.scaling),
-               tuple(A.shape), tuple(B.shape))
+        key = self._lora_state_key()
         if self._lora_key != key:
             reuse = self._lora_ops
             if reuse is not None and (reuse[0].shape != (64, A.shape[1])

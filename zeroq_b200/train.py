@@ -64,6 +64,9 @@ class Trainer:
             self.opt.arm_overlap()
         loss.backward()
         self.opt.step()
+        pack = getattr(self.model, "pack_lora_operands", None)
+        if pack is not None:   # every adapter's bf16 operands in one launch
+            pack()
         self.opt.zero_grad()
         return loss.detach()
 
