@@ -344,6 +344,31 @@ def test_flat_params_groups_layout_padding_and_binding():
         FlatParams(ps, groups=[[ps[0]], [ps[0], ps[1], ps[2], ps[3]]])
 
 
+def test_sharded_adamw_overlap_buckets_fall_back_off_the_fused_backend():
+    """overlap_buckets without the fused multi-rank backend (here: one CPU
+    process) keeps the single-shard layout; arm_overlap / bucket_ready are
+    no-ops and the step equals torch's AdamW."""
+    from zeroq_b200.parallel.optimizer import ShardedAdamW
+    from zeroq_b200.parallel.gradient_sync import reduce_scatter_grads_async
+
+    torch.manual_seed(4)
+    ps = [torch.nn.Parameter(torch.randn(n)) for n in (6, 10)]
+    ref = [torch.nn.Parameter(p.detach().clone()) for p in ps]
+    opt = ShardedAdamW(ps, lr=1e-2, overlap_buckets=[[ps[1]], [ps[0]]])
+    assert not opt.overlap and len(opt._parts) == 1
+    opt.arm_overlap()
+    opt.bucket_ready(0)   # no-op
+    for p, r in zip(ps, ref):
+        p.grad.copy_(torch.randn(p.shape))
+        r.grad = p.grad.detach().clone()
+    opt.step()
+    torch.optim.AdamW(ref, lr=1e-2, weight_decay=0.0).step()
+    for p, r in zip(ps, ref):
+        torch.testing.assert_close(p.detach(), r.detach(), rtol=1e-5, atol=1e-6)
+    g = torch.randn(7)
+    torch.testing.assert_close(reduce_scatter_grads_async(g, 1, 0)(), g)
+
+
 def test_exp2_polynomial_range_reduction_error_bound():
     """The attention forward's polynomial 2^x (csrc/attention_sm100.cu
     exp2_poly3_x2), emulated step by step in float32: round-to-nearest by the
