@@ -397,7 +397,7 @@ class DecoderLM(nn.Module):
         for layer in self.layers:
             cache = getattr(layer, "_qkv_cache", None)
             mods = (layer.q_proj, layer.k_proj, layer.v_proj)
-            if cache and "A_cat" in cache and all(m.lora_r for m in mods):
+            if cache and "A_cat" in cache and all(getattr(m, "lora_r", 0) for m in mods):
                 views = lora_block_views(mods, cache)
 
                 def done_qkv(cache=cache, mods=mods):
@@ -408,7 +408,7 @@ class DecoderLM(nn.Module):
                                  done_qkv if i == len(views) - 1 else (lambda: None)))
             for _, m in layer.projections():
                 ops = getattr(m, "_lora_ops", None) if isinstance(m, Linear4bit) else None
-                if m.lora_r and ops is not None:
+                if ops is not None and m.lora_r:
                     jobs.append((m.lora_A.detach(), m.lora_B.detach(), m.scaling, ops[0], ops[1], ops[2],
                                  lambda m=m: setattr(m, "_lora_key", m._lora_state_key())))
         if not jobs:
